@@ -1,0 +1,239 @@
+"""Torch-facing functional API over the C ABI.
+
+PyTorch only provides device memory (through its caching allocator) and the
+current CUDA stream here; all computation happens in lib/libplstm.so.
+
+* ``PackedWeights``: the device image of an LSTM stack + Linear head in the
+  layout the selected backend reads (``plstm_pack``).  It replaces the
+  per-weight-version caches of the reference's Python wrappers
+  (persistent_lstm_hip/persistent_lstm_hip/model.py:542-582,
+  miopen_adaptive_lstm_hip/miopen_adaptive_lstm_hip/model.py:403-430).
+* ``lstm_linear_forward``: x[B,T,I] + per-layer weights + Linear head ->
+  (out, h_n, c_n), the north-star entry point.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from typing import Optional, Sequence, Tuple
+
+import torch
+
+from . import _lib
+
+_DTYPES = {torch.float32: _lib.F32, torch.float16: _lib.F16, torch.bfloat16: _lib.BF16}
+_BACKENDS = {"auto": _lib.BACKEND_AUTO, "simt": _lib.BACKEND_SIMT, "tc": _lib.BACKEND_TC}
+_OUT_FLAGS = {"seq": _lib.FLAG_OUT_SEQ, "last": _lib.FLAG_OUT_LAST, "hseq": _lib.FLAG_NO_LINEAR}
+
+
+def _env_check() -> bool:
+    return os.environ.get("PLSTM_SYNC_CHECK", "0") not in ("", "0", "false", "off")
+
+
+def _ptr(t: Optional[torch.Tensor]):
+    return None if t is None else t.data_ptr()
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _require_cuda(t: torch.Tensor, name: str, device: torch.device, dtype=None) -> torch.Tensor:
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a torch.Tensor")
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor (this path has no CPU implementation)")
+    if t.device != device:
+        raise ValueError(f"{name} is on {t.device}, expected {device}")
+    if dtype is not None and t.dtype != dtype:
+        raise ValueError(f"{name} has dtype {t.dtype}, expected {dtype}")
+    return t.contiguous()
+
+
+def make_desc(*, batch: int, seq_len: int, input_size: int, hidden_size: int, num_layers: int,
+              output_size: int, dtype: torch.dtype, flags: int, backend: str = "auto",
+              w_layout: int = _lib.W_NATIVE, timeout_ms: int = 0, device: int = 0) -> _lib.Desc:
+    if dtype not in _DTYPES:
+        raise ValueError(f"unsupported dtype {dtype}; use float32, float16 or bfloat16")
+    if backend not in _BACKENDS:
+        raise ValueError(f"backend must be one of {sorted(_BACKENDS)}")
+    return _lib.Desc(batch, seq_len, input_size, hidden_size, num_layers, output_size, _DTYPES[dtype],
+                     w_layout, flags, _BACKENDS[backend], timeout_ms, device)
+
+
+def select_backend(*, input_size: int, hidden_size: int, num_layers: int, output_size: int,
+                   dtype: torch.dtype, out_mode: str = "seq", backend: str = "auto",
+                   device: int = 0) -> str:
+    """Name of the backend ("tc" or "simt") plstm_forward would run."""
+    d = make_desc(batch=1, seq_len=1, input_size=input_size, hidden_size=hidden_size,
+                  num_layers=num_layers, output_size=output_size, dtype=dtype,
+                  flags=_OUT_FLAGS[out_mode], backend=backend, device=device)
+    b = _lib.load().plstm_select_backend(ctypes.byref(d))
+    if b < 0:
+        _lib.check(-b)
+    return {_lib.BACKEND_SIMT: "simt", _lib.BACKEND_TC: "tc"}[b]
+
+
+class PackedWeights:
+    """Device image of the weights for one (shape, dtype, output mode, backend)."""
+
+    def __init__(self, w_ih: Sequence[torch.Tensor], w_hh: Sequence[torch.Tensor],
+                 b_ih: Optional[Sequence[Optional[torch.Tensor]]], b_hh: Optional[Sequence[Optional[torch.Tensor]]],
+                 w_lin: Optional[torch.Tensor], b_lin: Optional[torch.Tensor], *, out_mode: str = "seq",
+                 backend: str = "auto", w_layout: int = _lib.W_NATIVE, input_size: Optional[int] = None,
+                 hidden_size: Optional[int] = None):
+        if out_mode not in _OUT_FLAGS:
+            raise ValueError(f"out_mode must be one of {sorted(_OUT_FLAGS)}")
+        if len(w_ih) == 0 or len(w_ih) != len(w_hh):
+            raise ValueError("w_ih and w_hh must be non-empty lists of the same length")
+        lib = _lib.load()
+        dev = w_ih[0].device
+        dtype = w_ih[0].dtype
+        L = len(w_ih)
+        if hidden_size is None:
+            if w_layout != _lib.W_NATIVE:
+                raise ValueError("hidden_size is required for non-native weight layouts")
+            hidden_size = int(w_hh[0].shape[1])
+        if input_size is None:
+            if w_layout != _lib.W_NATIVE:
+                raise ValueError("input_size is required for non-native weight layouts")
+            input_size = int(w_ih[0].shape[1])
+        H = hidden_size
+        if w_layout == _lib.W_NATIVE:
+            for l in range(L):
+                k = input_size if l == 0 else H
+                if tuple(w_ih[l].shape) != (4 * H, k):
+                    raise ValueError(f"w_ih[{l}] must be [{4 * H}, {k}], got {tuple(w_ih[l].shape)}")
+                if tuple(w_hh[l].shape) != (4 * H, H):
+                    raise ValueError(f"w_hh[{l}] must be [{4 * H}, {H}], got {tuple(w_hh[l].shape)}")
+        O = 0
+        if out_mode != "hseq":
+            if w_lin is None:
+                raise ValueError("w_lin is required unless out_mode='hseq'")
+            if w_lin.dim() != 2 or w_lin.shape[1] != H:
+                raise ValueError(f"w_lin must be [O, {H}], got {tuple(w_lin.shape)}")
+            O = int(w_lin.shape[0])
+        keep = []
+
+        def conv(t, name):
+            if t is None:
+                return None
+            t = _require_cuda(t, name, dev, dtype)
+            keep.append(t)
+            return t
+
+        w_ih = [conv(t, f"w_ih[{i}]") for i, t in enumerate(w_ih)]
+        w_hh = [conv(t, f"w_hh[{i}]") for i, t in enumerate(w_hh)]
+        flags = _OUT_FLAGS[out_mode]
+        if b_ih is not None:
+            b_ih = [conv(t, f"b_ih[{i}]") for i, t in enumerate(b_ih)]
+        if b_hh is not None:
+            b_hh = [conv(t, f"b_hh[{i}]") for i, t in enumerate(b_hh)]
+        elif b_ih is not None:
+            flags |= _lib.FLAG_BIAS_SUMMED
+        w_lin = conv(w_lin, "w_lin") if out_mode != "hseq" else None
+        b_lin = conv(b_lin, "b_lin") if out_mode != "hseq" else None
+        self.device = dev
+        self.dtype = dtype
+        self.input_size, self.hidden_size, self.num_layers, self.output_size = input_size, H, L, O
+        self.out_mode = out_mode
+        self.backend_request = backend
+        self._flags = flags
+        d = self.desc(batch=1, seq_len=1)
+        d.w_layout = w_layout
+        nbytes = ctypes.c_size_t(0)
+        with torch.cuda.device(dev):
+            _lib.check(lib.plstm_packed_size(ctypes.byref(d), ctypes.byref(nbytes)))
+            self.blob = torch.empty(int(nbytes.value), dtype=torch.uint8, device=dev)
+            a_ih, _k1 = _lib.ptr_array([_ptr(t) for t in w_ih])
+            a_hh, _k2 = _lib.ptr_array([_ptr(t) for t in w_hh])
+            a_bih = _lib.ptr_array([_ptr(t) for t in b_ih])[0] if b_ih is not None else None
+            a_bhh = _lib.ptr_array([_ptr(t) for t in b_hh])[0] if b_hh is not None else None
+            keep.append((_k1, _k2, a_bih, a_bhh))
+            _lib.check(lib.plstm_pack(ctypes.byref(d), a_ih, a_hh, a_bih, a_bhh, _ptr(w_lin), _ptr(b_lin),
+                                      self.blob.data_ptr(), self.blob.numel(), _stream(dev)))
+        # The pack kernels read the source tensors asynchronously on the current stream.
+        for t in keep:
+            if isinstance(t, torch.Tensor):
+                t.record_stream(torch.cuda.current_stream(dev))
+        self.backend = select_backend(input_size=input_size, hidden_size=H, num_layers=L, output_size=max(O, 1),
+                                      dtype=dtype, out_mode=out_mode, backend=backend, device=dev.index)
+
+    def desc(self, *, batch: int, seq_len: int, extra_flags: int = 0, timeout_ms: int = 0) -> _lib.Desc:
+        return make_desc(batch=batch, seq_len=seq_len, input_size=self.input_size, hidden_size=self.hidden_size,
+                         num_layers=self.num_layers, output_size=max(self.output_size, 1), dtype=self.dtype,
+                         flags=self._flags | extra_flags, backend=self.backend_request, timeout_ms=timeout_ms,
+                         device=self.device.index or 0)
+
+    def forward(self, x: torch.Tensor, *, lengths: Optional[torch.Tensor] = None,
+                hx: Optional[Tuple[torch.Tensor, torch.Tensor]] = None, need_state: bool = True,
+                check: Optional[bool] = None, timeout_ms: int = 0, extra_flags: int = 0,
+                c_n_f32: bool = False):
+        """Runs the LSTM + Linear forward on x[B,T,I]; returns (out, h_n, c_n)."""
+        lib = _lib.load()
+        dev = self.device
+        x = _require_cuda(x, "x", dev, self.dtype)
+        if x.dim() != 3 or x.shape[2] != self.input_size:
+            raise ValueError(f"x must be [B, T, {self.input_size}], got {tuple(x.shape)}")
+        B, T, _ = (int(v) for v in x.shape)
+        L, H, O = self.num_layers, self.hidden_size, self.output_size
+        lens = None
+        if lengths is not None:
+            lens = lengths.to(device=dev, dtype=torch.int32).contiguous()
+            if lens.shape != (B,):
+                raise ValueError(f"lengths must be [{B}], got {tuple(lens.shape)}")
+        h0 = c0 = None
+        if hx is not None:
+            h0 = _require_cuda(hx[0], "h0", dev, self.dtype)
+            c0 = _require_cuda(hx[1], "c0", dev, self.dtype)
+            if tuple(h0.shape) != (L, B, H) or tuple(c0.shape) != (L, B, H):
+                raise ValueError(f"hx tensors must be [{L}, {B}, {H}]")
+        if self.out_mode == "seq":
+            out = torch.empty(B, T, O, dtype=self.dtype, device=dev)
+        elif self.out_mode == "last":
+            out = torch.empty(B, O, dtype=self.dtype, device=dev)
+        else:
+            out = torch.empty(B, T, H, dtype=self.dtype, device=dev)
+        h_n = c_n = None
+        if need_state:
+            h_n = torch.empty(L, B, H, dtype=self.dtype, device=dev)
+            c_n = torch.empty(L, B, H, dtype=torch.float32 if c_n_f32 else self.dtype, device=dev)
+        flags = extra_flags | (_lib.FLAG_CN_F32 if c_n_f32 else 0)
+        if check if check is not None else _env_check():
+            flags |= _lib.FLAG_SYNC_CHECK
+        d = self.desc(batch=B, seq_len=T, extra_flags=flags, timeout_ms=timeout_ms)
+        nbytes = ctypes.c_size_t(0)
+        _lib.check(lib.plstm_workspace_size(ctypes.byref(d), ctypes.byref(nbytes)))
+        ws = torch.empty(max(int(nbytes.value), 256), dtype=torch.uint8, device=dev)
+        with torch.cuda.device(dev):
+            rc = lib.plstm_forward_packed(ctypes.byref(d), self.blob.data_ptr(), _ptr(x), _ptr(lens), _ptr(h0),
+                                          _ptr(c0), _ptr(out), _ptr(h_n), _ptr(c_n), ws.data_ptr(), ws.numel(),
+                                          _stream(dev))
+        _lib.check(rc)
+        return out, h_n, c_n
+
+
+def lstm_linear_forward(x: torch.Tensor, w_ih: Sequence[torch.Tensor], w_hh: Sequence[torch.Tensor],
+                        b_ih: Optional[Sequence[torch.Tensor]], b_hh: Optional[Sequence[torch.Tensor]],
+                        w_lin: Optional[torch.Tensor] = None, b_lin: Optional[torch.Tensor] = None, *,
+                        lengths: Optional[torch.Tensor] = None,
+                        hx: Optional[Tuple[torch.Tensor, torch.Tensor]] = None, out_mode: str = "seq",
+                        backend: str = "auto", check: Optional[bool] = None):
+    """x[B,T,I] with nn.LSTM(batch_first=True)-layout weights -> (out, h_n, c_n).
+
+    out is [B,T,O] for out_mode="seq" (zero past each row's length), [B,O] for
+    "last" (Linear on each row's last valid step) and the last layer's h
+    sequence [B,T,H] for "hseq".  h_n / c_n are [L,B,H] at each row's last
+    valid step.
+    """
+    packed = PackedWeights(w_ih, w_hh, b_ih, b_hh, w_lin, b_lin, out_mode=out_mode, backend=backend,
+                           input_size=int(x.shape[-1]))
+    return packed.forward(x, lengths=lengths, hx=hx, check=check)
+
+
+def read_status(ws: torch.Tensor) -> Tuple[int, int]:
+    lib = _lib.load()
+    st = ctypes.c_int32(0)
+    detail = ctypes.c_int32(0)
+    _lib.check(lib.plstm_read_status(ws.data_ptr(), _stream(ws.device), ctypes.byref(st), ctypes.byref(detail)))
+    return st.value, detail.value

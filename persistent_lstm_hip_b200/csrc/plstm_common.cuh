@@ -1,0 +1,144 @@
+// plstm_common.cuh — shared definitions of the B200 LSTM + Linear library.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "../../include/plstm.h"
+
+namespace plstm {
+
+// ---- error reporting -------------------------------------------------------
+// Thread-local message of the last failure; plstm_last_error() returns it.
+void set_error(const std::string& msg);
+void clear_error();
+
+struct Error {
+  int32_t code;
+  std::string msg;
+};
+
+#define PLSTM_TRY_CUDA(expr)                                                          \
+  do {                                                                                \
+    cudaError_t _e = (expr);                                                          \
+    if (_e != cudaSuccess) {                                                          \
+      ::plstm::set_error(std::string(#expr) + ": " + cudaGetErrorString(_e));         \
+      return PLSTM_ECUDA;                                                             \
+    }                                                                                 \
+  } while (0)
+
+#define PLSTM_CHECK_ARG(cond, msg)           \
+  do {                                       \
+    if (!(cond)) {                           \
+      ::plstm::set_error(std::string(msg));  \
+      return PLSTM_EINVAL;                   \
+    }                                        \
+  } while (0)
+
+// ---- instrumentation ----------------------------------------------------------
+// Counts every kernel launch of the library (plstm_launch_count).
+void note_launches(int n);
+// Records the start / end of the dominant (recurrent) kernel when profiling is on.
+void profile_begin(cudaStream_t s);
+void profile_end(cudaStream_t s);
+
+// ---- workspace status block ------------------------------------------------
+// The first kStatusBytes of every workspace hold the device status the
+// kernels write when a bounded wait gives up: word 0 = PLSTM_* code (0 = ok),
+// word 1 = detail (cta << 16 | step & 0xffff) of the first failure.
+constexpr size_t kStatusBytes = 256;
+
+inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+inline size_t dtype_size(int32_t dt) { return dt == PLSTM_F32 ? 4 : 2; }
+
+// ---- element conversion ----------------------------------------------------
+template <typename T>
+__device__ __forceinline__ float to_f32(T v);
+template <>
+__device__ __forceinline__ float to_f32<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ float to_f32<__half>(__half v) { return __half2float(v); }
+template <>
+__device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+template <typename T>
+__device__ __forceinline__ T from_f32(float v);
+template <>
+__device__ __forceinline__ float from_f32<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ __half from_f32<__half>(float v) { return __float2half_rn(v); }
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+
+// Gate nonlinearities, written with CUDA's accurate expf / tanhf (the
+// reference computes sigmoid as 1 / (1 + expf(-x)) and tanh with tanhf,
+// persistent_lstm_hip.cu:96-98 and :316-324).
+__device__ __forceinline__ float sigmoid_acc(float v) { return 1.0f / (1.0f + expf(-v)); }
+__device__ __forceinline__ float tanh_acc(float v) { return tanhf(v); }
+
+// Records the first failure in the workspace status block.
+__device__ __forceinline__ void report_status(int* status, int code, int detail) {
+  if (status != nullptr && atomicCAS(status, 0, code) == 0) status[1] = detail;
+}
+
+// ---- entry points implemented per backend ---------------------------------
+struct Problem {
+  int B, T, I, H, L, O;
+  int dtype;
+  int flags;
+  int timeout_ms;
+  int device;
+  bool has_linear() const { return (flags & PLSTM_FLAG_NO_LINEAR) == 0; }
+  bool out_seq() const { return (flags & PLSTM_FLAG_OUT_SEQ) != 0; }
+  bool out_last() const { return (flags & PLSTM_FLAG_OUT_LAST) != 0; }
+};
+
+// Generic layer-sequential FFMA backend (any shape, f32/f16/bf16).
+size_t simt_packed_size(const Problem& p);
+size_t simt_workspace_size(const Problem& p);
+int32_t simt_pack(const Problem& p, int ih_layout, int hh_layout, const void* const* w_ih, const void* const* w_hh,
+                  const void* const* b_ih, const void* const* b_hh, const void* w_lin,
+                  const void* b_lin, void* packed, cudaStream_t s);
+int32_t simt_forward(const Problem& p, const void* packed, const void* x, const int32_t* lengths,
+                     const void* h0, const void* c0, void* out, void* h_n, void* c_n, void* ws,
+                     cudaStream_t s);
+
+// tcgen05 cluster wavefront backend (H = 128, L <= 4, I <= 16, O <= 32, f16/bf16).
+bool tc_supported(const Problem& p, std::string* why);
+size_t tc_packed_size(const Problem& p);
+size_t tc_workspace_size(const Problem& p);
+int32_t tc_pack(const Problem& p, int ih_layout, int hh_layout, const void* const* w_ih, const void* const* w_hh,
+                const void* const* b_ih, const void* const* b_hh, const void* w_lin,
+                const void* b_lin, void* packed, cudaStream_t s);
+int32_t tc_forward(const Problem& p, const void* packed, const void* x, const int32_t* lengths,
+                   const void* h0, const void* c0, void* out, void* h_n, void* c_n, void* ws,
+                   cudaStream_t s);
+
+// Reads element (r, k) of a [4H or O][K] weight given in any PLSTM_W_* layout.
+__device__ __forceinline__ int64_t weight_src_index(int layout, int rows, int K, int r, int k) {
+  if (layout == PLSTM_W_TRANSPOSED) return (int64_t)k * rows + r;
+  if (layout == PLSTM_W_KPAIR) return ((int64_t)(k >> 1) * rows + r) * 2 + (k & 1);
+  return (int64_t)r * K + k;
+}
+
+__device__ __forceinline__ float load_any(const void* src, int dtype, int64_t idx) {
+  if (dtype == PLSTM_F32) return static_cast<const float*>(src)[idx];
+  if (dtype == PLSTM_F16) return __half2float(static_cast<const __half*>(src)[idx]);
+  return __bfloat162float(static_cast<const __nv_bfloat16*>(src)[idx]);
+}
+
+__device__ __forceinline__ void store_any(void* dst, int dtype, int64_t idx, float v) {
+  if (dtype == PLSTM_F32)
+    static_cast<float*>(dst)[idx] = v;
+  else if (dtype == PLSTM_F16)
+    static_cast<__half*>(dst)[idx] = __float2half_rn(v);
+  else
+    static_cast<__nv_bfloat16*>(dst)[idx] = __float2bfloat16_rn(v);
+}
+
+}  // namespace plstm

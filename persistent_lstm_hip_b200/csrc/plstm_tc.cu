@@ -1,0 +1,959 @@
+// plstm_tc.cu — tcgen05 cluster wavefront backend for H = 128 LSTM stacks.
+//
+// What it replaces.  The reference runs this path as a chain of persistent
+// per-layer-pair kernels with weights re-read from global memory every step
+// (persistent_lstm_pair01_interleaved_kernel / pair23_last_interleaved_kernel,
+// persistent_lstm_hip.cu:457-662, host :2126-2254), a 4-layer "monolithic"
+// variant (:664-806) and a separate linear_head_kernel (:1662-1682).
+//
+// Design (B200-first).
+//   * One thread-block cluster of 2L CTAs per tile of N batch rows.  CTA rank
+//     r = 2l + s owns layer l, hidden units [64 s, 64 s + 64): 256 gate rows.
+//   * Its slice of [W_ih | W_hh] (256 rows x K, K = 256 for l >= 1,
+//     16 + 128 for l = 0 with x zero-padded to 16 columns) stays resident in
+//     shared memory for the whole sequence as the A operand (K-major, 128-byte
+//     swizzle).  The per-step contraction gates^T[256 x N] = W . [x_t | h_{t-1}]^T
+//     runs as tcgen05.mma kind::f16 (f16/bf16 in, f32 accumulate in TMEM),
+//     M = 128 per instruction, N = batch tile.
+//   * Layers run as a wavefront: layer l works on step t while layer l+1 works
+//     on step t-1.  The new h tile (64 units x N rows, 16-bit) is written once
+//     into this CTA's next B buffer and pushed to the sibling CTA (recurrent
+//     half) and to both CTAs of layer l+1 (input half) with shared::cta ->
+//     shared::cluster bulk copies that complete as transaction bytes on the
+//     destination's mbarrier.  Back-pressure from layer l+1 arrives through a
+//     multicast tcgen05.commit on this CTA's "empty" barriers.  No grid-wide
+//     barrier, no global-memory round trip for h.
+//   * Gate rows are ordered inside each 32-lane TMEM quadrant as
+//     [i x 8 units | f x 8 | g x 8 | o x 8], so one tcgen05.ld 16x256b per
+//     half-quadrant hands every thread the i, f, g, o values of the same
+//     (unit, batch) cells; bias, sigmoid / tanh and the c / h update run in
+//     registers with c kept in f32 (the reference keeps c in f32 registers and
+//     rounds h to 16 bits between steps, persistent_lstm_hip.cu:316-324).
+//   * The Linear head is one more M = 128 MMA (rows >= O are zero) on the last
+//     layer's recurrent half of the next step's B buffer, i.e. on h_{t-1}; it
+//     is added to the step-t MMA batch, and a final "drain" step handles
+//     h_{T-1}.  OUT_LAST only runs the drain.
+//   * Variable lengths: rows are sorted by length (descending) into tiles, a
+//     tile runs max(len) steps, finished rows freeze their state and write
+//     zeros.
+//   * Every wait is bounded (globaltimer deadline); a wait that gives up
+//     records PLSTM_ETIMEOUT in the workspace status word, raises the abort
+//     flag of every CTA of the cluster and the kernel unwinds without trapping.
+#include <algorithm>
+#include <cstdlib>
+#include <mutex>
+#include <string>
+
+#include "plstm_common.cuh"
+#include "sm100_ptx.cuh"
+
+namespace plstm {
+namespace tc {
+
+constexpr int kH = 128;          // hidden size served (64 units per CTA)
+constexpr int kXK = 16;        // padded layer-0 input width (one MMA K step)
+constexpr int kComputeWarps = 8;
+constexpr int kThreads = (kComputeWarps + 1) * 32;  // + one control warp
+constexpr int kABytes = 128 * 1024;                 // A image slot per CTA
+constexpr int kALinBytes = 32 * 1024;               // Linear head A image (2 K blocks)
+constexpr int kATileKB = 128 * 128;                 // one (M tile, 64-wide K block): 16 KB
+constexpr int kModeSeq = 0, kModeLast = 1, kModeHSeq = 2;
+
+// Packed image layout (global): [2L slots of kABytes][A_lin][bias f32 [2L][256]][b_lin f32 [32]]
+__host__ __device__ inline size_t packed_alin_off(int L) { return (size_t)2 * L * kABytes; }
+__host__ __device__ inline size_t packed_bias_off(int L) { return packed_alin_off(L) + kALinBytes; }
+__host__ __device__ inline size_t packed_blin_off(int L) { return packed_bias_off(L) + (size_t)2 * L * 256 * 4; }
+__host__ __device__ inline size_t packed_total(int L) { return packed_blin_off(L) + 32 * 4; }
+
+// Shared memory layout (offsets from a 1024-byte aligned base).
+template <int N>
+struct Smem {
+  static constexpr int kBKB = N * 128;  // one 64-wide K block of the B operand
+  static constexpr int kXBytes = N * 32;
+  static constexpr int kA = 0;
+  static constexpr int kALin = kABytes;
+  static constexpr int kB = kALin + kALinBytes;
+  static constexpr int kBufBytes = 4 * kBKB;  // slots: [in0 | in1 | rec0 | rec1]
+  static constexpr int kBar = kB + 2 * kBufBytes;
+  // barriers: full[2] empty[2] hready[2] mma ; then tmem base, abort flag, perm[N], lens[N]
+  static constexpr int kFull = kBar, kEmpty = kBar + 16, kHReady = kBar + 32, kMma = kBar + 48;
+  static constexpr int kTmemSlot = kBar + 64, kAbort = kBar + 68;
+  static constexpr int kPerm = kBar + 128, kLens = kPerm + 4 * N;
+  static constexpr int kEnd = kLens + 4 * N;
+  static constexpr int kDynBytes = kEnd + 1024;  // + alignment slack
+  static constexpr int kNL = N >= 32 ? N / 2 : N;  // Linear columns per CTA
+  static constexpr int kTmemCols = (2 * N + kNL) <= 64 ? 64 : ((2 * N + kNL) <= 128 ? 128 : 256);
+};
+
+struct Params {
+  const uint8_t* packed;
+  const uint8_t* xp;        // [tiles][T][N * 32 bytes]
+  const int32_t* perm;      // [tiles * N], -1 = padding row
+  const int32_t* lengths;   // [B] (varlen) or null
+  const int32_t* tile_len;  // [tiles]
+  const void* h0;
+  const void* c0;
+  void* out;
+  void* h_n;
+  void* c_n;
+  int* status;
+  int B, T, L, O, flags;
+  unsigned long long timeout_ns;
+  int drop_rank, drop_step;  // fault injection: rank that skips one sibling hand-off (-1 = off)
+};
+
+// 128-byte swizzled K-major offset of element (row, k) of a 64-wide K block.
+__device__ __forceinline__ uint32_t sw128_off(int row, int k) {
+  return (uint32_t)(row * 128 + ((((k >> 3) ^ (row & 7)) & 7) << 4) + (k & 7) * 2);
+}
+// No-swizzle K-major offset (core matrices 8 rows x 16 bytes, LBO 128, SBO 256) for K = 16.
+__device__ __forceinline__ uint32_t none16_off(int row, int k) {
+  return (uint32_t)((row >> 3) * 256 + (k >> 3) * 128 + (row & 7) * 16 + (k & 7) * 2);
+}
+
+template <bool BF16>
+__device__ __forceinline__ uint16_t to_bits(float v) {
+  if (BF16) {
+    __nv_bfloat16 h = __float2bfloat16_rn(v);
+    return *reinterpret_cast<uint16_t*>(&h);
+  } else {
+    __half h = __float2half_rn(v);
+    return *reinterpret_cast<uint16_t*>(&h);
+  }
+}
+template <bool BF16>
+__device__ __forceinline__ float from_bits(uint16_t b) {
+  if (BF16) {
+    return __bfloat162float(*reinterpret_cast<__nv_bfloat16*>(&b));
+  } else {
+    return __half2float(*reinterpret_cast<__half*>(&b));
+  }
+}
+
+// sigmoid(x) = 1 / (1 + e^-x) and tanh(x) = 2 sigmoid(2x) - 1, from the
+// exponential intrinsic and the fast reciprocal-divide; the argument is
+// clamped so that e^-x stays finite.
+__device__ __forceinline__ float gate_sigmoid(float x) {
+  x = fminf(fmaxf(x, -80.0f), 80.0f);
+  return __fdividef(1.0f, 1.0f + __expf(-x));
+}
+__device__ __forceinline__ float gate_tanh(float x) { return 2.0f * gate_sigmoid(2.0f * x) - 1.0f; }
+
+// Bounded wait on an mbarrier phase; false = gave up (timeout or cluster abort).
+__device__ __forceinline__ bool wait_phase(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                           unsigned long long timeout_ns) {
+  if (ptx::mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = ptx::globaltimer();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 32; ++i)
+      if (ptx::mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (ptx::globaltimer() - t0 > timeout_ns) return false;
+  }
+}
+
+// Raises the abort flag in every CTA of the cluster and records the failure.
+__device__ __forceinline__ void raise_abort(const Params& p, uint8_t* sm_abort, int ncta, int step) {
+  const uint32_t local = ptx::smem_u32(sm_abort);
+  for (int r = 0; r < ncta; ++r) ptx::st_cluster_u32(ptx::mapa(local, (uint32_t)r), 1u);
+  report_status(p.status, PLSTM_ETIMEOUT, (int)((blockIdx.x & 0x7fff) << 16) | (step & 0xffff));
+}
+
+template <int N, bool BF16, bool VARLEN, int MODE>
+__global__ void __launch_bounds__(kThreads, 1) wavefront_kernel(const Params p) {
+  using S = Smem<N>;
+  constexpr int CPW = N / 16;  // 256-bit column chunks per compute warp
+  constexpr int NL = S::kNL;
+  constexpr bool kHasLinear = MODE != kModeHSeq;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = ptx::smem_u32(sm);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int ncta = 2 * p.L;
+  const int rank = (int)ptx::cluster_ctarank();
+  const int l = rank >> 1, s = rank & 1;
+  const int tile = blockIdx.x / ncta;
+  const bool last_layer = l == p.L - 1;
+  const bool drain = kHasLinear && last_layer;
+  const bool does_linear = drain && (N >= 32 || s == 0);
+  const int Tt = p.tile_len[tile];
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + S::kAbort);
+  int32_t* perm_s = reinterpret_cast<int32_t*>(sm + S::kPerm);
+  int32_t* lens_s = reinterpret_cast<int32_t*>(sm + S::kLens);
+
+  const uint32_t bar_full = sbase + S::kFull, bar_empty = sbase + S::kEmpty;
+  const uint32_t bar_hready = sbase + S::kHReady, bar_mma = sbase + S::kMma;
+  auto bbuf = [&](int b) -> uint32_t { return sbase + S::kB + b * S::kBufBytes; };
+
+  // ---- set-up ------------------------------------------------------------------
+  if (tid == 0) {
+    ptx::mbar_init(bar_full + 0, 1);
+    ptx::mbar_init(bar_full + 8, 1);
+    ptx::mbar_init(bar_empty + 0, 2);
+    ptx::mbar_init(bar_empty + 8, 2);
+    ptx::mbar_init(bar_hready + 0, kComputeWarps);
+    ptx::mbar_init(bar_hready + 8, kComputeWarps);
+    ptx::mbar_init(bar_mma, 1);
+    *abort_flag = 0;
+    ptx::fence_mbar_init_cluster();
+  }
+  if (warp == 0) {
+    ptx::tmem_alloc(sbase + S::kTmemSlot, S::kTmemCols);
+    ptx::tmem_relinquish();
+  }
+  for (int i = tid; i < N; i += kThreads) {
+    const int b = p.perm[tile * N + i];
+    perm_s[i] = b;
+    int len = 0;
+    if (b >= 0) len = VARLEN ? min(max(p.lengths[b], 0), p.T) : p.T;
+    lens_s[i] = len;
+  }
+  {
+    const uint4* src = reinterpret_cast<const uint4*>(p.packed + (size_t)rank * kABytes);
+    uint4* dst = reinterpret_cast<uint4*>(sm + S::kA);
+    const int n16 = (l == 0 ? (64 + 8) * 1024 : kABytes) / 16;
+    for (int i = tid; i < n16; i += kThreads) dst[i] = src[i];
+    if (does_linear) {
+      const uint4* srcl = reinterpret_cast<const uint4*>(p.packed + packed_alin_off(p.L));
+      uint4* dstl = reinterpret_cast<uint4*>(sm + S::kALin);
+      for (int i = tid; i < kALinBytes / 16; i += kThreads) dstl[i] = srcl[i];
+    }
+  }
+  __syncthreads();  // perm_s / lens_s / tmem slot visible
+  // Initial recurrent state h0 -> both recurrent K blocks of B buffer 0.
+  {
+    uint8_t* b0 = sm + S::kB;
+    for (int i = tid; i < N * kH; i += kThreads) {
+      const int n = i / kH, k = i % kH;
+      float v = 0.0f;
+      const int b = perm_s[n];
+      if (p.h0 != nullptr && b >= 0) {
+        const uint16_t* h0 = static_cast<const uint16_t*>(p.h0);
+        v = from_bits<BF16>(h0[((size_t)l * p.B + b) * kH + k]);
+      }
+      *reinterpret_cast<uint16_t*>(b0 + (2 + (k >> 6)) * S::kBKB + sw128_off(n, k & 63)) = to_bits<BF16>(v);
+    }
+  }
+  ptx::fence_proxy_async_smem();
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(sm + S::kTmemSlot);
+  ptx::cluster_sync();  // every CTA's barriers are initialised before any remote operation
+
+  const int steps = Tt + (drain ? 1 : 0);
+  uint32_t n_commits = 0;
+
+  if (warp == kComputeWarps) {
+    // =========================== control warp ===========================
+    if (lane == 0) {
+      const uint32_t xbytes = S::kXBytes, bkb = S::kBKB;
+      auto in_bytes = [&](int t) -> uint32_t {
+        uint32_t nb = 0;
+        if (t < Tt) nb += (l == 0) ? xbytes : 2 * bkb;
+        if (t >= 1 && t <= Tt && (t < Tt || drain)) nb += bkb;  // sibling's h_{t-1}
+        return nb;
+      };
+      constexpr uint32_t idesc_g = ptx::idesc_f16(128, N, BF16);
+      constexpr uint32_t idesc_l = ptx::idesc_f16(128, NL, BF16);
+      const uint16_t up_mask = l > 0 ? (uint16_t)(3u << (2 * (l - 1))) : 0;
+      if (steps > 0) {
+        ptx::mbar_arrive_expect_tx(bar_full, in_bytes(0));
+        if (l == 0 && Tt > 0)
+          ptx::bulk_g2s(bbuf(0), p.xp + ((size_t)tile * p.T) * xbytes, xbytes, bar_full);
+      }
+      for (int t = 0; t < steps; ++t) {
+        const int b = t & 1;
+        if (*abort_flag) break;
+        if (!wait_phase(bar_full + 8 * b, (t >> 1) & 1, abort_flag, p.timeout_ns)) {
+          raise_abort(p, sm + S::kAbort, ncta, t);
+          break;
+        }
+        ptx::tc_fence_after();
+        const bool gates = t < Tt;
+        const uint32_t B0 = bbuf(b);
+        if (gates) {
+#pragma unroll
+          for (int tau = 0; tau < 2; ++tau) {
+            const uint32_t d = tmem + (uint32_t)(tau * N);
+            if (l == 0) {
+              const uint32_t a_x = sbase + S::kA + 64 * 1024 + tau * 4096;
+              ptx::mma_f16_ss(d, ptx::desc_k_none(a_x, 128, 256), ptx::desc_k_none(B0, 128, 256), idesc_g, 0u);
+#pragma unroll
+              for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk) {
+                  const uint32_t a = sbase + S::kA + tau * 2 * kATileKB + kb * kATileKB + kk * 32;
+                  const uint32_t bb = B0 + (2 + kb) * bkb + kk * 32;
+                  ptx::mma_f16_ss(d, ptx::desc_k_sw128(a), ptx::desc_k_sw128(bb), idesc_g, 1u);
+                }
+            } else {
+#pragma unroll
+              for (int kb = 0; kb < 4; ++kb)
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk) {
+                  const uint32_t a = sbase + S::kA + tau * 4 * kATileKB + kb * kATileKB + kk * 32;
+                  const uint32_t bb = B0 + kb * bkb + kk * 32;
+                  ptx::mma_f16_ss(d, ptx::desc_k_sw128(a), ptx::desc_k_sw128(bb), idesc_g,
+                                  (kb | kk) != 0 ? 1u : 0u);
+                }
+            }
+          }
+        }
+        const bool lin = does_linear && (t == Tt || (MODE == kModeSeq && t >= 1));
+        if (lin) {
+          const uint32_t d = tmem + (uint32_t)(2 * N);
+          const uint32_t row_off = (N >= 32 ? (uint32_t)(s * NL) : 0u) * 128u;
+#pragma unroll
+          for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              const uint32_t a = sbase + S::kALin + kb * kATileKB + kk * 32;
+              const uint32_t bb = B0 + (2 + kb) * bkb + row_off + kk * 32;
+              ptx::mma_f16_ss(d, ptx::desc_k_sw128(a), ptx::desc_k_sw128(bb), idesc_l,
+                              (kb | kk) != 0 ? 1u : 0u);
+            }
+        }
+        ptx::mma_commit(bar_mma);
+        ++n_commits;
+        if (l > 0 && gates && t + 2 < Tt) ptx::mma_commit_mc(bar_empty + 8 * b, up_mask);
+        if (t + 1 < steps) {
+          ptx::mbar_arrive_expect_tx(bar_full + 8 * (b ^ 1), in_bytes(t + 1));
+          if (l == 0 && t + 1 < Tt)
+            ptx::bulk_g2s(bbuf(b ^ 1), p.xp + ((size_t)tile * p.T + t + 1) * xbytes, xbytes,
+                          bar_full + 8 * (b ^ 1));
+        }
+        if (gates) {
+          if (!wait_phase(bar_hready + 8 * b, (t >> 1) & 1, abort_flag, p.timeout_ns)) {
+            raise_abort(p, sm + S::kAbort, ncta, t);
+            break;
+          }
+          const uint32_t src = bbuf(b ^ 1) + (2 + s) * bkb;
+          const bool to_sibling = (t + 1 < Tt) || (drain && t + 1 == Tt);
+          const bool dropped = rank == p.drop_rank && t == p.drop_step;
+          if (to_sibling && !dropped) {
+            const uint32_t peer = (uint32_t)(rank ^ 1);
+            ptx::bulk_s2c(ptx::mapa(src, peer), src, bkb, ptx::mapa(bar_full + 8 * (b ^ 1), peer));
+          }
+          if (l + 1 < p.L) {
+            const uint32_t dst_local = bbuf(b) + s * bkb;
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+              const uint32_t peer = (uint32_t)(2 * (l + 1) + j);
+              ptx::bulk_s2c(ptx::mapa(dst_local, peer), src, bkb, ptx::mapa(bar_full + 8 * b, peer));
+            }
+          }
+        }
+      }
+      // All MMAs must have completed before TMEM is released.
+      if (n_commits > 0) wait_phase(bar_mma, (n_commits - 1) & 1, abort_flag, p.timeout_ns);
+    }
+  } else {
+    // =========================== compute warps ===========================
+    const int q = warp & 3, half = warp >> 2;
+    const int j8 = lane >> 2;        // unit within the quadrant's group of 8
+    const int cpair = (lane & 3) * 2;  // first of the two batch columns in a chunk
+    const float* bias_img = reinterpret_cast<const float*>(p.packed + packed_bias_off(p.L)) + rank * 256;
+    float bi[2], bf[2], bg[2], bo[2];
+#pragma unroll
+    for (int tau = 0; tau < 2; ++tau) {
+      const int r = tau * 128 + 32 * q + j8;
+      bi[tau] = bias_img[r];
+      bf[tau] = bias_img[r + 8];
+      bg[tau] = bias_img[r + 16];
+      bo[tau] = bias_img[r + 24];
+    }
+    // cells: [tau][chunk j][e]
+    float c_st[2][CPW][2], h_st[2][CPW][2];
+    int ncol[CPW][2], len_c[CPW][2], bidx[CPW][2];
+#pragma unroll
+    for (int jc = 0; jc < CPW; ++jc)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int n = 8 * (half * CPW + jc) + cpair + e;
+        ncol[jc][e] = n;
+        len_c[jc][e] = lens_s[n];
+        bidx[jc][e] = perm_s[n];
+      }
+#pragma unroll
+    for (int tau = 0; tau < 2; ++tau) {
+      const int u = 64 * s + 8 * (4 * tau + q) + j8;
+#pragma unroll
+      for (int jc = 0; jc < CPW; ++jc)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int b = bidx[jc][e];
+          float hv = 0.0f, cv = 0.0f;
+          if (b >= 0 && p.h0 != nullptr) {
+            hv = from_bits<BF16>(static_cast<const uint16_t*>(p.h0)[((size_t)l * p.B + b) * kH + u]);
+            cv = from_bits<BF16>(static_cast<const uint16_t*>(p.c0)[((size_t)l * p.B + b) * kH + u]);
+          }
+          h_st[tau][jc][e] = hv;
+          c_st[tau][jc][e] = cv;
+        }
+    }
+    const float* blin = reinterpret_cast<const float*>(p.packed + packed_blin_off(p.L));
+    const bool lin_warp = does_linear && q == 0;
+    const int o = lane;  // Linear output row handled by this lane (lin_warp only)
+    const float blin_o = (lin_warp && o < p.O) ? blin[o] : 0.0f;
+    uint16_t* out16 = static_cast<uint16_t*>(p.out);
+
+    // Stores Linear outputs of step `ts` from D_lin (lanes 0..31 = output rows).
+    auto store_linear = [&](int ts, bool last_mode) {
+      uint32_t r[8];
+      const uint32_t taddr = tmem + (uint32_t)(2 * N + half * (NL / 2));
+      ptx::tmem_ld_32x32b_x8(taddr, r);
+      ptx::tmem_wait_ld();
+      if (o < p.O) {
+#pragma unroll
+        for (int i = 0; i < NL / 2; ++i) {
+          const int n = (N >= 32 ? s * NL : 0) + half * (NL / 2) + i;
+          const int b = perm_s[n];
+          if (b < 0) continue;
+          const float v = __uint_as_float(r[i]) + blin_o;
+          if (last_mode) {
+            out16[(size_t)b * p.O + o] = to_bits<BF16>(v);
+          } else {
+            const bool live = ts < lens_s[n];
+            out16[((size_t)b * p.T + ts) * p.O + o] = to_bits<BF16>(live ? v : 0.0f);
+          }
+        }
+      }
+    };
+
+    for (int t = 0; t < Tt; ++t) {
+      const int b = t & 1;
+      if (*abort_flag) break;
+      if (!wait_phase(bar_mma, t & 1, abort_flag, p.timeout_ns)) {
+        if (lane == 0) raise_abort(p, sm + S::kAbort, ncta, t);
+        break;
+      }
+      ptx::tc_fence_after();
+      uint32_t rif[2][4 * CPW], rgo[2][4 * CPW];
+#pragma unroll
+      for (int tau = 0; tau < 2; ++tau) {
+        const uint32_t col = (uint32_t)(tau * N + half * CPW * 8);
+        const uint32_t a0 = tmem + ((uint32_t)(32 * q) << 16) + col;
+        const uint32_t a1 = tmem + ((uint32_t)(32 * q + 16) << 16) + col;
+        if constexpr (CPW == 1) {
+          uint32_t(&x0)[4] = *reinterpret_cast<uint32_t(*)[4]>(rif[tau]);
+          uint32_t(&x1)[4] = *reinterpret_cast<uint32_t(*)[4]>(rgo[tau]);
+          ptx::tmem_ld_16x256b_x1(a0, x0);
+          ptx::tmem_ld_16x256b_x1(a1, x1);
+        } else {
+          uint32_t(&x0)[8] = *reinterpret_cast<uint32_t(*)[8]>(rif[tau]);
+          uint32_t(&x1)[8] = *reinterpret_cast<uint32_t(*)[8]>(rgo[tau]);
+          ptx::tmem_ld_16x256b_x2(a0, x0);
+          ptx::tmem_ld_16x256b_x2(a1, x1);
+        }
+      }
+      ptx::tmem_wait_ld();
+      if (MODE == kModeSeq && lin_warp && t >= 1) store_linear(t - 1, false);
+      ptx::tc_fence_before();
+
+      // Layer l+1 must have consumed h_{t-2} (same buffer and copy source) before it is overwritten.
+      if (l + 1 < p.L && t >= 2) {
+        if (!wait_phase(bar_empty + 8 * b, ((t - 2) >> 1) & 1, abort_flag, p.timeout_ns)) {
+          if (lane == 0) raise_abort(p, sm + S::kAbort, ncta, t);
+          break;
+        }
+      }
+      uint8_t* dst = sm + S::kB + (b ^ 1) * S::kBufBytes + (2 + s) * S::kBKB;
+#pragma unroll
+      for (int tau = 0; tau < 2; ++tau) {
+        const int ul = 8 * (4 * tau + q) + j8;  // unit within this CTA's 64
+#pragma unroll
+        for (int jc = 0; jc < CPW; ++jc)
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const float gi = __uint_as_float(rif[tau][4 * jc + e]) + bi[tau];
+            const float gf = __uint_as_float(rif[tau][4 * jc + 2 + e]) + bf[tau];
+            const float gg = __uint_as_float(rgo[tau][4 * jc + e]) + bg[tau];
+            const float go = __uint_as_float(rgo[tau][4 * jc + 2 + e]) + bo[tau];
+            const float c_new = gate_sigmoid(gf) * c_st[tau][jc][e] + gate_sigmoid(gi) * gate_tanh(gg);
+            const float h_new = gate_sigmoid(go) * gate_tanh(c_new);
+            const uint16_t hb = to_bits<BF16>(h_new);
+            bool live = true;
+            if (VARLEN) live = t < len_c[jc][e];
+            uint16_t wb;
+            if (live) {
+              c_st[tau][jc][e] = c_new;
+              h_st[tau][jc][e] = from_bits<BF16>(hb);
+              wb = hb;
+            } else {
+              wb = to_bits<BF16>(h_st[tau][jc][e]);
+            }
+            const int n = ncol[jc][e];
+            *reinterpret_cast<uint16_t*>(dst + sw128_off(n, ul)) = wb;
+            if (MODE == kModeHSeq && last_layer && bidx[jc][e] >= 0)
+              out16[((size_t)bidx[jc][e] * p.T + t) * kH + 64 * s + ul] = live ? hb : (uint16_t)0;
+          }
+      }
+      ptx::fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(bar_hready + 8 * b);
+    }
+    // Drain: Linear of the last step's h.
+    if (drain && lin_warp && !*abort_flag) {
+      if (wait_phase(bar_mma, Tt & 1, abort_flag, p.timeout_ns)) {
+        ptx::tc_fence_after();
+        if (MODE == kModeSeq) {
+          if (Tt >= 1) store_linear(Tt - 1, false);
+        } else {
+          store_linear(0, true);
+        }
+        ptx::tc_fence_before();
+      } else if (lane == 0) {
+        raise_abort(p, sm + S::kAbort, ncta, Tt);
+      }
+    }
+    // Outputs past the tile's last step are zero.
+    if (MODE == kModeSeq && lin_warp && o < p.O) {
+      for (int i = 0; i < NL / 2; ++i) {
+        const int n = (N >= 32 ? s * NL : 0) + half * (NL / 2) + i;
+        const int b = perm_s[n];
+        if (b < 0) continue;
+        for (int ts = Tt; ts < p.T; ++ts) out16[((size_t)b * p.T + ts) * p.O + o] = 0;
+      }
+    }
+    if (MODE == kModeHSeq && last_layer) {
+#pragma unroll
+      for (int tau = 0; tau < 2; ++tau) {
+        const int u = 64 * s + 8 * (4 * tau + q) + j8;
+#pragma unroll
+        for (int jc = 0; jc < CPW; ++jc)
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int bb = bidx[jc][e];
+            if (bb < 0) continue;
+            for (int ts = Tt; ts < p.T; ++ts) out16[((size_t)bb * p.T + ts) * kH + u] = 0;
+          }
+      }
+    }
+    // Final state.
+#pragma unroll
+    for (int tau = 0; tau < 2; ++tau) {
+      const int u = 64 * s + 8 * (4 * tau + q) + j8;
+#pragma unroll
+      for (int jc = 0; jc < CPW; ++jc)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int bb = bidx[jc][e];
+          if (bb < 0) continue;
+          const size_t idx = ((size_t)l * p.B + bb) * kH + u;
+          if (p.h_n != nullptr) static_cast<uint16_t*>(p.h_n)[idx] = to_bits<BF16>(h_st[tau][jc][e]);
+          if (p.c_n != nullptr) {
+            if (p.flags & PLSTM_FLAG_CN_F32)
+              static_cast<float*>(p.c_n)[idx] = c_st[tau][jc][e];
+            else
+              static_cast<uint16_t*>(p.c_n)[idx] = to_bits<BF16>(c_st[tau][jc][e]);
+          }
+        }
+    }
+  }
+
+  // ---- teardown -----------------------------------------------------------------
+  if (*abort_flag) {
+    // Let bulk copies already in flight toward peers land before any CTA leaves.
+    const unsigned long long t0 = ptx::globaltimer();
+    while (ptx::globaltimer() - t0 < 50000ull) {
+    }
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem, S::kTmemCols);
+  }
+  ptx::cluster_sync();
+}
+
+// ---- packing ----------------------------------------------------------------------
+// Writes the per-CTA A images, the Linear A image, the permuted bias and b_lin.
+struct PackArgs {
+  const void* w_ih[4];
+  const void* w_hh[4];
+  const void* b_ih[4];
+  const void* b_hh[4];
+  const void* w_lin;
+  const void* b_lin;
+  int ih_layout, hh_layout, dtype, L, I, O;
+};
+
+__device__ __forceinline__ int gate_row(int s, int tau, int r) {
+  const int q = r >> 5, rr = r & 31, gate = rr >> 3, j = rr & 7;
+  return gate * kH + 64 * s + 8 * (4 * tau + q) + j;
+}
+
+__global__ void tc_pack_kernel(const PackArgs a, uint8_t* packed) {
+  const int ncta = 2 * a.L;
+  const int64_t n_a = (int64_t)ncta * (kABytes / 2);
+  const int64_t n_lin = kALinBytes / 2;
+  const int64_t n_bias = (int64_t)ncta * 256;
+  const int64_t total = n_a + n_lin + n_bias + 32;
+  uint16_t* img = reinterpret_cast<uint16_t*>(packed);
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    if (i < n_a) {
+      const int rank = (int)(i / (kABytes / 2));
+      const int off = (int)(i % (kABytes / 2)) * 2;  // byte offset within slot
+      const int l = rank >> 1, s = rank & 1;
+      float v = 0.0f;
+      if (l == 0) {
+        if (off < 64 * 1024) {  // W_hh part: [tau][kb][128 rows x 128 B]
+          const int tau = off / (2 * kATileKB), kb = (off / kATileKB) & 1, within = off % kATileKB;
+          const int r = within / 128, chunk = (within % 128) >> 4, e = (within & 15) >> 1;
+          const int kk = ((chunk ^ (r & 7)) << 3) + e;
+          v = load_any(a.w_hh[0], a.dtype, weight_src_index(a.hh_layout, 4 * kH, kH, gate_row(s, tau, r), kb * 64 + kk));
+        } else if (off < 72 * 1024) {  // x part: [tau][128 rows x 16 k], no swizzle
+          const int o2 = off - 64 * 1024;
+          const int tau = o2 / 4096, w = o2 % 4096;
+          const int r = (w / 256) * 8 + (w % 128) / 16;
+          const int k = ((w % 256) / 128) * 8 + (w % 16) / 2;
+          if (k < a.I) v = load_any(a.w_ih[0], a.dtype, weight_src_index(a.ih_layout, 4 * kH, a.I, gate_row(s, tau, r), k));
+        }
+      } else {  // [tau][kb 0..3][128 rows x 128 B]; kb 0,1 = W_ih, kb 2,3 = W_hh
+        const int tau = off / (4 * kATileKB), kb = (off / kATileKB) & 3, within = off % kATileKB;
+        const int r = within / 128, chunk = (within % 128) >> 4, e = (within & 15) >> 1;
+        const int kk = ((chunk ^ (r & 7)) << 3) + e;
+        const int k = (kb & 1) * 64 + kk;
+        const int row = gate_row(s, tau, r);
+        v = kb < 2 ? load_any(a.w_ih[l], a.dtype, weight_src_index(a.ih_layout, 4 * kH, kH, row, k))
+                   : load_any(a.w_hh[l], a.dtype, weight_src_index(a.hh_layout, 4 * kH, kH, row, k));
+      }
+      const uint16_t bits = a.dtype == PLSTM_BF16 ? to_bits<true>(v) : to_bits<false>(v);
+      img[i] = bits;
+    } else if (i < n_a + n_lin) {
+      const int off = (int)(i - n_a) * 2;
+      const int kb = off / kATileKB, within = off % kATileKB;
+      const int r = within / 128, chunk = (within % 128) >> 4, e = (within & 15) >> 1;
+      const int kk = ((chunk ^ (r & 7)) << 3) + e;
+      float v = 0.0f;
+      if (r < a.O && a.w_lin != nullptr) v = load_any(a.w_lin, a.dtype, (int64_t)r * kH + kb * 64 + kk);
+      img[i] = a.dtype == PLSTM_BF16 ? to_bits<true>(v) : to_bits<false>(v);
+    } else if (i < n_a + n_lin + n_bias) {
+      const int64_t j = i - n_a - n_lin;
+      const int rank = (int)(j / 256), rr = (int)(j % 256);
+      const int l = rank >> 1, s = rank & 1;
+      const int row = gate_row(s, rr >> 7, rr & 127);
+      float v = 0.0f;
+      if (a.b_ih[l] != nullptr) v += load_any(a.b_ih[l], a.dtype, row);
+      if (a.b_hh[l] != nullptr) v += load_any(a.b_hh[l], a.dtype, row);
+      reinterpret_cast<float*>(packed + packed_bias_off(a.L))[j] = v;
+    } else {
+      const int o = (int)(i - n_a - n_lin - n_bias);
+      float v = 0.0f;
+      if (o < a.O && a.b_lin != nullptr) v = load_any(a.b_lin, a.dtype, o);
+      reinterpret_cast<float*>(packed + packed_blin_off(a.L))[o] = v;
+    }
+  }
+}
+
+// ---- per-call preparation -----------------------------------------------------------
+// Uniform lengths: tile rows are consecutive batch rows.
+__global__ void tc_perm_uniform_kernel(int32_t* perm, int32_t* tile_len, int B, int T, int N, int tiles) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < tiles * N; i += gridDim.x * blockDim.x) {
+    perm[i] = i < B ? i : -1;
+    if (i < tiles) tile_len[i] = T;
+  }
+}
+// Variable lengths: counting sort by length, longest first.
+__global__ void tc_len_hist_kernel(const int32_t* lengths, int B, int T, int32_t* hist) {
+  for (int b = blockIdx.x * blockDim.x + threadIdx.x; b < B; b += gridDim.x * blockDim.x) {
+    const int len = min(max(lengths[b], 0), T);
+    atomicAdd(&hist[T - len], 1);
+  }
+}
+__global__ void tc_len_scan_kernel(int32_t* hist, int nbins) {
+  if (threadIdx.x == 0 && blockIdx.x == 0) {
+    int acc = 0;
+    for (int i = 0; i < nbins; ++i) {
+      const int v = hist[i];
+      hist[i] = acc;
+      acc += v;
+    }
+  }
+}
+__global__ void tc_len_scatter_kernel(const int32_t* lengths, int B, int T, int32_t* offs, int32_t* sorted) {
+  for (int b = blockIdx.x * blockDim.x + threadIdx.x; b < B; b += gridDim.x * blockDim.x) {
+    const int len = min(max(lengths[b], 0), T);
+    sorted[atomicAdd(&offs[T - len], 1)] = b;
+  }
+}
+__global__ void tc_perm_varlen_kernel(const int32_t* sorted, const int32_t* lengths, int32_t* perm,
+                                      int32_t* tile_len, int B, int T, int N, int tiles) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < tiles * N; i += gridDim.x * blockDim.x) {
+    perm[i] = i < B ? sorted[i] : -1;
+    if (i < tiles) tile_len[i] = min(max(lengths[sorted[i * N]], 0), T);
+  }
+}
+// x[B][T][I] -> per-tile, per-step K-major no-swizzle 16-column tiles.
+template <typename T16>
+__global__ void tc_xpack_kernel(const T16* __restrict__ x, const int32_t* __restrict__ perm,
+                                uint8_t* __restrict__ xp, int B, int T, int I, int N, int tiles) {
+  const int64_t total = (int64_t)tiles * T * N;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int n = (int)(i % N);
+    const int64_t tt = i / N;
+    const int t = (int)(tt % T);
+    const int tile = (int)(tt / T);
+    const int b = perm[tile * N + n];
+    uint16_t v[16];
+#pragma unroll
+    for (int k = 0; k < 16; ++k) v[k] = 0;
+    if (b >= 0) {
+      const uint16_t* src = reinterpret_cast<const uint16_t*>(x) + ((size_t)b * T + t) * I;
+      for (int k = 0; k < I && k < 16; ++k) v[k] = src[k];
+    }
+    uint8_t* dst = xp + (size_t)tt * N * 32 + (n >> 3) * 256 + (n & 7) * 16;
+    uint4 lo, hi;
+    lo.x = v[0] | (v[1] << 16); lo.y = v[2] | (v[3] << 16); lo.z = v[4] | (v[5] << 16); lo.w = v[6] | (v[7] << 16);
+    hi.x = v[8] | (v[9] << 16); hi.y = v[10] | (v[11] << 16); hi.z = v[12] | (v[13] << 16); hi.w = v[14] | (v[15] << 16);
+    *reinterpret_cast<uint4*>(dst) = lo;
+    *reinterpret_cast<uint4*>(dst + 128) = hi;
+  }
+}
+
+// ---- host side ----------------------------------------------------------------------
+struct Plan {
+  int N, tiles;
+};
+
+template <int N, bool BF16, bool VARLEN, int MODE>
+void* kernel_ptr() {
+  return reinterpret_cast<void*>(&wavefront_kernel<N, BF16, VARLEN, MODE>);
+}
+
+template <int N>
+void* pick_kernel(bool bf16, bool varlen, int mode) {
+#define PLSTM_TC_K(B, V, M) \
+  if (bf16 == B && varlen == V && mode == M) return kernel_ptr<N, B, V, M>();
+  PLSTM_TC_K(false, false, kModeSeq) PLSTM_TC_K(false, false, kModeLast) PLSTM_TC_K(false, false, kModeHSeq)
+  PLSTM_TC_K(false, true, kModeSeq) PLSTM_TC_K(false, true, kModeLast) PLSTM_TC_K(false, true, kModeHSeq)
+  PLSTM_TC_K(true, false, kModeSeq) PLSTM_TC_K(true, false, kModeLast) PLSTM_TC_K(true, false, kModeHSeq)
+  PLSTM_TC_K(true, true, kModeSeq) PLSTM_TC_K(true, true, kModeLast) PLSTM_TC_K(true, true, kModeHSeq)
+#undef PLSTM_TC_K
+  return nullptr;
+}
+
+int mode_of(const Problem& p) {
+  if (!p.has_linear()) return kModeHSeq;
+  return p.out_seq() ? kModeSeq : kModeLast;
+}
+
+int smem_bytes_for(int N) { return N == 16 ? Smem<16>::kDynBytes : Smem<32>::kDynBytes; }
+
+// Max clusters of 2L CTAs (one per SM) co-resident on `device`; cached.
+int max_active_clusters(int device, int L, int N) {
+  static std::mutex mu;
+  static int cache[64][5][2];
+  static bool init = false;
+  std::lock_guard<std::mutex> g(mu);
+  if (!init) {
+    for (auto& a : cache)
+      for (auto& b : a)
+        for (auto& c : b) c = -1;
+    init = true;
+  }
+  const int ni = N == 16 ? 0 : 1;
+  if (device < 0 || device >= 64 || L < 1 || L > 4) return 1;
+  int& slot = cache[device][L][ni];
+  if (slot >= 0) return slot;
+  void* k = N == 16 ? pick_kernel<16>(false, false, kModeLast) : pick_kernel<32>(false, false, kModeLast);
+  cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes_for(N));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * L * 64, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem_bytes_for(N);
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeClusterDimension;
+  attr.val.clusterDim.x = 2 * L;
+  attr.val.clusterDim.y = 1;
+  attr.val.clusterDim.z = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, k, &cfg) != cudaSuccess || n < 1) {
+    cudaGetLastError();
+    n = 1;
+  }
+  slot = n;
+  return n;
+}
+
+Plan make_plan(const Problem& p) {
+  Plan pl;
+  int N = 32;
+  if (const char* e = std::getenv("PLSTM_TC_NTILE")) {
+    const int v = std::atoi(e);
+    if (v == 16 || v == 32) N = v;
+  } else {
+    const int clusters = max_active_clusters(p.device, p.L, 16);
+    if ((p.B + 15) / 16 <= clusters) N = 16;
+  }
+  pl.N = N;
+  pl.tiles = (p.B + N - 1) / N;
+  return pl;
+}
+
+struct TcWs {
+  size_t xp, perm, tile_len, hist, sorted, total;
+};
+
+TcWs tc_ws(const Problem& p, const Plan& pl) {
+  TcWs w;
+  size_t off = kStatusBytes;
+  w.xp = off;
+  off = align_up(off + (size_t)pl.tiles * std::max(p.T, 1) * pl.N * 32, 256);
+  w.perm = off;
+  off = align_up(off + (size_t)pl.tiles * pl.N * 4, 256);
+  w.tile_len = off;
+  off = align_up(off + (size_t)pl.tiles * 4, 256);
+  w.hist = off;
+  off = align_up(off + (size_t)(p.T + 1) * 4, 256);
+  w.sorted = off;
+  off = align_up(off + (size_t)std::max(p.B, 1) * 4, 256);
+  w.total = off;
+  return w;
+}
+
+}  // namespace tc
+
+using namespace tc;
+
+bool tc_supported(const Problem& p, std::string* why) {
+  auto no = [&](const char* m) {
+    if (why) *why = m;
+    return false;
+  };
+  if (p.dtype != PLSTM_F16 && p.dtype != PLSTM_BF16) return no("activation type must be f16 or bf16");
+  if (p.H != kH) return no("hidden_size must be 128");
+  if (p.L < 1 || p.L > 4) return no("num_layers must be 1..4 (one 2L-CTA cluster)");
+  if (p.I > kXK) return no("input_size must be <= 16");
+  if (p.has_linear() && p.O > 32) return no("output_size must be <= 32");
+  if (p.T > 65535) return no("seq_len must be <= 65535");
+  int dev = p.device, major = 0, minor = 0;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess) {
+    cudaGetLastError();
+    return no("no CUDA device");
+  }
+  if (major != 10 || minor != 0) return no("device is not sm_100 (B200)");
+  return true;
+}
+
+size_t tc_packed_size(const Problem& p) { return packed_total(p.L); }
+
+size_t tc_workspace_size(const Problem& p) { return tc_ws(p, make_plan(p)).total; }
+
+int32_t tc_pack(const Problem& p, int ih_layout, int hh_layout, const void* const* w_ih,
+                const void* const* w_hh, const void* const* b_ih, const void* const* b_hh,
+                const void* w_lin, const void* b_lin, void* packed, cudaStream_t s) {
+  PackArgs a = {};
+  for (int l = 0; l < p.L; ++l) {
+    a.w_ih[l] = w_ih[l];
+    a.w_hh[l] = w_hh[l];
+    a.b_ih[l] = b_ih ? b_ih[l] : nullptr;
+    a.b_hh[l] = b_hh ? b_hh[l] : nullptr;
+  }
+  a.w_lin = p.has_linear() ? w_lin : nullptr;
+  a.b_lin = p.has_linear() ? b_lin : nullptr;
+  a.ih_layout = ih_layout;
+  a.hh_layout = hh_layout;
+  a.dtype = p.dtype;
+  a.L = p.L;
+  a.I = p.I;
+  a.O = p.has_linear() ? p.O : 0;
+  tc_pack_kernel<<<148 * 4, 256, 0, s>>>(a, static_cast<uint8_t*>(packed));
+  PLSTM_TRY_CUDA(cudaGetLastError());
+  note_launches(1);
+  return PLSTM_OK;
+}
+
+int32_t tc_forward(const Problem& p, const void* packed, const void* x, const int32_t* lengths,
+                   const void* h0, const void* c0, void* out, void* h_n, void* c_n, void* ws,
+                   cudaStream_t s) {
+  const Plan pl = make_plan(p);
+  const TcWs w = tc_ws(p, pl);
+  uint8_t* wsb = static_cast<uint8_t*>(ws);
+  int32_t* perm = reinterpret_cast<int32_t*>(wsb + w.perm);
+  int32_t* tile_len = reinterpret_cast<int32_t*>(wsb + w.tile_len);
+  const int nthr = 256;
+  const int nperm = pl.tiles * pl.N;
+  if (lengths == nullptr) {
+    tc_perm_uniform_kernel<<<(nperm + nthr - 1) / nthr, nthr, 0, s>>>(perm, tile_len, p.B, p.T, pl.N, pl.tiles);
+    note_launches(1);
+  } else {
+    int32_t* hist = reinterpret_cast<int32_t*>(wsb + w.hist);
+    int32_t* sorted = reinterpret_cast<int32_t*>(wsb + w.sorted);
+    PLSTM_TRY_CUDA(cudaMemsetAsync(hist, 0, (size_t)(p.T + 1) * 4, s));
+    tc_len_hist_kernel<<<(p.B + nthr - 1) / nthr, nthr, 0, s>>>(lengths, p.B, p.T, hist);
+    tc_len_scan_kernel<<<1, 32, 0, s>>>(hist, p.T + 1);
+    tc_len_scatter_kernel<<<(p.B + nthr - 1) / nthr, nthr, 0, s>>>(lengths, p.B, p.T, hist, sorted);
+    tc_perm_varlen_kernel<<<(nperm + nthr - 1) / nthr, nthr, 0, s>>>(sorted, lengths, perm, tile_len, p.B, p.T,
+                                                                      pl.N, pl.tiles);
+    note_launches(4);
+  }
+  PLSTM_TRY_CUDA(cudaGetLastError());
+  if (p.T > 0) {
+    const int64_t total = (int64_t)pl.tiles * p.T * pl.N;
+    const int grid = (int)std::min<int64_t>((total + nthr - 1) / nthr, 148 * 32);
+    tc_xpack_kernel<uint16_t><<<grid, nthr, 0, s>>>(static_cast<const uint16_t*>(x), perm, wsb + w.xp, p.B,
+                                                    p.T, p.I, pl.N, pl.tiles);
+    PLSTM_TRY_CUDA(cudaGetLastError());
+    note_launches(1);
+  }
+  Params kp = {};
+  kp.packed = static_cast<const uint8_t*>(packed);
+  kp.xp = wsb + w.xp;
+  kp.perm = perm;
+  kp.lengths = lengths;
+  kp.tile_len = tile_len;
+  kp.h0 = h0;
+  kp.c0 = c0;
+  kp.out = out;
+  kp.h_n = h_n;
+  kp.c_n = c_n;
+  kp.status = reinterpret_cast<int*>(wsb);
+  kp.B = p.B;
+  kp.T = p.T;
+  kp.L = p.L;
+  kp.O = p.O;
+  kp.flags = p.flags;
+  kp.timeout_ns = (unsigned long long)p.timeout_ms * 1000000ull;
+  kp.drop_rank = -1;
+  kp.drop_step = -1;
+  if (p.flags & PLSTM_FLAG_TEST_DROP) {
+    kp.drop_rank = p.L >= 2 ? 2 : 0;
+    kp.drop_step = 0;
+  }
+  const bool bf16 = p.dtype == PLSTM_BF16;
+  const int mode = mode_of(p);
+  void* k = pl.N == 16 ? pick_kernel<16>(bf16, lengths != nullptr, mode)
+                       : pick_kernel<32>(bf16, lengths != nullptr, mode);
+  const int smem = smem_bytes_for(pl.N);
+  PLSTM_TRY_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(pl.tiles * 2 * p.L), 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeClusterDimension;
+  attr.val.clusterDim.x = 2 * p.L;
+  attr.val.clusterDim.y = 1;
+  attr.val.clusterDim.z = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  void* args[] = {&kp};
+  profile_begin(s);
+  PLSTM_TRY_CUDA(cudaLaunchKernelExC(&cfg, k, args));
+  profile_end(s);
+  note_launches(1);
+  return PLSTM_OK;
+}
+
+}  // namespace plstm

@@ -1,0 +1,91 @@
+"""Pins the CPU oracle to the reference's own outputs (tests/golden/*.npz).
+
+The ref_* fixtures were produced by the reference's reference_lstm_forward /
+reference_regressor_forward (persistent_lstm_hip/persistent_lstm_hip/reference.py:11-72);
+torch_varlen_f64 by torch.nn.LSTM over pack_padded_sequence.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from conftest import golden_weights, load_golden
+from oracle import oracle
+
+
+@pytest.mark.parametrize("name", ["ref_small_f64", "ref_state_f64", "ref_h128_f32"])
+@pytest.mark.parametrize("impl", ["c_f64", "numpy"])
+def test_oracle_matches_reference_sequence(name, impl):
+    g = load_golden(name)
+    B, T, I, H, L, O = (int(v) for v in g["dims"])
+    w_ih, w_hh, b_ih, b_hh, w_lin, b_lin = golden_weights(g, L)
+    kw = dict(h0=g.get("h0"), c0=g.get("c0"), out_mode="hseq")
+    if impl == "c_f64":
+        out, h_n, c_n = oracle.forward(g["x"], w_ih, w_hh, b_ih, b_hh, None, None, **kw)
+    else:
+        out, h_n, c_n = oracle.forward_numpy(g["x"], w_ih, w_hh, b_ih, b_hh, None, None, **kw)
+    tol = 1e-12 if g["x"].dtype == np.float64 else 2e-6
+    np.testing.assert_allclose(out, g["out_h"], atol=tol, rtol=0)
+    np.testing.assert_allclose(h_n, g["h_n"], atol=tol, rtol=0)
+    np.testing.assert_allclose(c_n, g["c_n"], atol=tol, rtol=0)
+
+
+@pytest.mark.parametrize("name", ["ref_small_f64", "ref_h128_f32"])
+def test_oracle_matches_reference_regressor(name):
+    g = load_golden(name)
+    B, T, I, H, L, O = (int(v) for v in g["dims"])
+    w_ih, w_hh, b_ih, b_hh, w_lin, b_lin = golden_weights(g, L)
+    out, _, _ = oracle.forward(g["x"], w_ih, w_hh, b_ih, b_hh, w_lin, b_lin, out_mode="last")
+    tol = 1e-12 if g["x"].dtype == np.float64 else 2e-6
+    np.testing.assert_allclose(out, g["regressor_out"], atol=tol, rtol=0)
+    seq, _, _ = oracle.forward(g["x"], w_ih, w_hh, b_ih, b_hh, w_lin, b_lin, out_mode="seq")
+    np.testing.assert_allclose(seq[:, -1, :], g["regressor_out"], atol=tol, rtol=0)
+
+
+def test_oracle_f32_close_to_reference():
+    g = load_golden("ref_h128_f32")
+    B, T, I, H, L, O = (int(v) for v in g["dims"])
+    w_ih, w_hh, b_ih, b_hh, w_lin, b_lin = golden_weights(g, L)
+    out, _, _ = oracle.forward(g["x"], w_ih, w_hh, b_ih, b_hh, w_lin, b_lin, out_mode="last",
+                               precision="f32")
+    np.testing.assert_allclose(out, g["regressor_out"], atol=1e-5, rtol=0)
+
+
+@pytest.mark.parametrize("impl", ["c_f64", "numpy"])
+def test_oracle_matches_torch_varlen(impl):
+    g = load_golden("torch_varlen_f64")
+    B, T, I, H, L, O = (int(v) for v in g["dims"])
+    w_ih, w_hh, b_ih, b_hh, w_lin, b_lin = golden_weights(g, L)
+    fn = oracle.forward if impl == "c_f64" else oracle.forward_numpy
+    seq, h_n, c_n = fn(g["x"], w_ih, w_hh, b_ih, b_hh, w_lin, b_lin, lengths=g["lengths"], out_mode="seq")
+    np.testing.assert_allclose(seq, g["out_seq"], atol=1e-12, rtol=0)
+    np.testing.assert_allclose(h_n, g["h_n"], atol=1e-12, rtol=0)
+    np.testing.assert_allclose(c_n, g["c_n"], atol=1e-12, rtol=0)
+    hs, _, _ = fn(g["x"], w_ih, w_hh, b_ih, b_hh, None, None, lengths=g["lengths"], out_mode="hseq")
+    np.testing.assert_allclose(hs, g["out_h"], atol=1e-12, rtol=0)
+    last, _, _ = fn(g["x"], w_ih, w_hh, b_ih, b_hh, w_lin, b_lin, lengths=g["lengths"], out_mode="last")
+    idx = g["lengths"] - 1
+    np.testing.assert_allclose(last, g["out_seq"][np.arange(B), idx], atol=1e-12, rtol=0)
+
+
+def test_oracle_zero_length_rows_keep_initial_state():
+    rng = np.random.default_rng(0)
+    B, T, I, H, L, O = 3, 4, 2, 4, 2, 3
+    w_ih = [rng.standard_normal((4 * H, I if l == 0 else H)) * 0.3 for l in range(L)]
+    w_hh = [rng.standard_normal((4 * H, H)) * 0.3 for _ in range(L)]
+    b = [rng.standard_normal(4 * H) * 0.1 for _ in range(L)]
+    h0 = rng.standard_normal((L, B, H))
+    c0 = rng.standard_normal((L, B, H))
+    x = rng.standard_normal((B, T, I))
+    lens = np.array([0, 2, 4], dtype=np.int32)
+    out, h_n, c_n = oracle.forward(x, w_ih, w_hh, b, None, rng.standard_normal((O, H)), np.zeros(O),
+                                   lengths=lens, h0=h0, c0=c0, out_mode="seq")
+    np.testing.assert_array_equal(out[0], 0.0)
+    np.testing.assert_array_equal(h_n[:, 0], h0[:, 0])
+    np.testing.assert_array_equal(c_n[:, 0], c0[:, 0])
+    np.testing.assert_array_equal(out[1, 2:], 0.0)
+    ref = oracle.forward_numpy(x, w_ih, w_hh, b, None, rng.standard_normal((O, H)), np.zeros(O),
+                               lengths=lens, h0=h0, c0=c0, out_mode="hseq")
+    got = oracle.forward(x, w_ih, w_hh, b, None, None, None, lengths=lens, h0=h0, c0=c0, out_mode="hseq")
+    for a, r in zip(got, ref):
+        np.testing.assert_allclose(a, r, atol=1e-12)

@@ -72,6 +72,10 @@ extern "C" {
 #define PLSTM_FLAG_SYNC_CHECK 0x10  /* synchronise `stream` and turn the device status into the return code */
 #define PLSTM_FLAG_CN_F32 0x20      /* c_n is written as f32 instead of the activation type */
 #define PLSTM_FLAG_TEST_DROP 0x100  /* fault injection: one producer CTA skips one h hand-off (tests only) */
+/* Diagnostics: the tensor-core kernel records SM clock (clock64) timestamps of
+ * 8 events for 64 steps starting at T/2, for every CTA of the first cluster,
+ * into the last 2L*64*8*8 bytes of the workspace (u64 [2L][64][8]). */
+#define PLSTM_FLAG_TRACE 0x200
 
 /* Problem descriptor.  All sizes are element counts. */
 typedef struct plstm_desc {

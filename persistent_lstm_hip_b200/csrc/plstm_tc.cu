@@ -15,6 +15,11 @@
 //     swizzle).  The per-step contraction gates^T[256 x N] = W . [x_t | h_{t-1}]^T
 //     runs as tcgen05.mma kind::f16 (f16/bf16 in, f32 accumulate in TMEM),
 //     M = 128 per instruction, N = batch tile.
+//   * The contraction is split in two: the input part W_ih . x_t is issued as
+//     soon as x_t (layer 0) or h_{l-1}(t) (from layer l-1) lands, into one of
+//     two TMEM accumulators, while the previous step's gates are still being
+//     processed; only the recurrent part W_hh . h_{t-1} (K = 128) sits on the
+//     step-to-step critical path.
 //   * Layers run as a wavefront: layer l works on step t while layer l+1 works
 //     on step t-1.  The new h tile (64 units x N rows, 16-bit) is written once
 //     into this CTA's next B buffer and pushed to the sibling CTA (recurrent
@@ -50,8 +55,8 @@
 namespace plstm {
 namespace tc {
 
-constexpr int kH = 128;          // hidden size served (64 units per CTA)
-constexpr int kXK = 16;        // padded layer-0 input width (one MMA K step)
+constexpr int kH = 128;  // hidden size served (64 units per CTA)
+constexpr int kXK = 16;  // padded layer-0 input width (one MMA K step)
 constexpr int kComputeWarps = 8;
 constexpr int kThreads = (kComputeWarps + 1) * 32;  // + one control warp
 constexpr int kABytes = 128 * 1024;                 // A image slot per CTA
@@ -65,6 +70,10 @@ __host__ __device__ inline size_t packed_bias_off(int L) { return packed_alin_of
 __host__ __device__ inline size_t packed_blin_off(int L) { return packed_bias_off(L) + (size_t)2 * L * 256 * 4; }
 __host__ __device__ inline size_t packed_total(int L) { return packed_blin_off(L) + 32 * 4; }
 
+__host__ __device__ constexpr int tmem_cols_for(int need) {
+  return need <= 32 ? 32 : need <= 64 ? 64 : need <= 128 ? 128 : need <= 256 ? 256 : 512;
+}
+
 // Shared memory layout (offsets from a 1024-byte aligned base).
 template <int N>
 struct Smem {
@@ -75,14 +84,19 @@ struct Smem {
   static constexpr int kB = kALin + kALinBytes;
   static constexpr int kBufBytes = 4 * kBKB;  // slots: [in0 | in1 | rec0 | rec1]
   static constexpr int kBar = kB + 2 * kBufBytes;
-  // barriers: full[2] empty[2] hready[2] mma ; then tmem base, abort flag, perm[N], lens[N]
-  static constexpr int kFull = kBar, kEmpty = kBar + 16, kHReady = kBar + 32, kMma = kBar + 48;
-  static constexpr int kTmemSlot = kBar + 64, kAbort = kBar + 68;
+  // mbarriers (8 bytes each, two per kind: one per step parity)
+  static constexpr int kFullIn = kBar, kFullRec = kBar + 16, kEmpty = kBar + 32, kHReady = kBar + 48,
+                       kMma = kBar + 64;
+  static constexpr int kTmemSlot = kBar + 96, kAbort = kBar + 100;
   static constexpr int kPerm = kBar + 128, kLens = kPerm + 4 * N;
   static constexpr int kEnd = kLens + 4 * N;
   static constexpr int kDynBytes = kEnd + 1024;  // + alignment slack
-  static constexpr int kNL = N >= 32 ? N / 2 : N;  // Linear columns per CTA
-  static constexpr int kTmemCols = (2 * N + kNL) <= 64 ? 64 : ((2 * N + kNL) <= 128 ? 128 : 256);
+  // Linear head columns per CTA: split between the two last-layer CTAs when
+  // N / 2 is a legal MMA width (multiple of 16), else CTA 0 takes all N.
+  static constexpr bool kSplitLinear = (N / 2) % 16 == 0;
+  static constexpr int kNL = kSplitLinear ? N / 2 : N;
+  // TMEM: gates D[buffer 0..1][tile 0..1] (N columns each), then the Linear tile.
+  static constexpr int kTmemCols = tmem_cols_for(4 * N + kNL);
 };
 
 struct Params {
@@ -98,17 +112,23 @@ struct Params {
   void* c_n;
   int* status;
   int B, T, L, O, flags;
+  int fast_act;  // 1: one-MUFU tanh.approx activations
   unsigned long long timeout_ns;
   int drop_rank, drop_step;  // fault injection: rank that skips one sibling hand-off (-1 = off)
+  unsigned long long* trace;  // PLSTM_FLAG_TRACE: [2L][64][8] clock64 stamps of cluster 0, or null
+  int trace_t0;
 };
+
+constexpr int kTraceSteps = 64, kTraceEvents = 8;
+
+__device__ __forceinline__ void trace_mark(const Params& p, int rank, int t, int ev) {
+  if (p.trace != nullptr && blockIdx.x < (unsigned)(2 * p.L) && t >= p.trace_t0 && t < p.trace_t0 + kTraceSteps)
+    p.trace[((size_t)rank * kTraceSteps + (t - p.trace_t0)) * kTraceEvents + ev] = clock64();
+}
 
 // 128-byte swizzled K-major offset of element (row, k) of a 64-wide K block.
 __device__ __forceinline__ uint32_t sw128_off(int row, int k) {
   return (uint32_t)(row * 128 + ((((k >> 3) ^ (row & 7)) & 7) << 4) + (k & 7) * 2);
-}
-// No-swizzle K-major offset (core matrices 8 rows x 16 bytes, LBO 128, SBO 256) for K = 16.
-__device__ __forceinline__ uint32_t none16_off(int row, int k) {
-  return (uint32_t)((row >> 3) * 256 + (k >> 3) * 128 + (row & 7) * 16 + (k & 7) * 2);
 }
 
 template <bool BF16>
@@ -130,14 +150,16 @@ __device__ __forceinline__ float from_bits(uint16_t b) {
   }
 }
 
-// sigmoid(x) = 1 / (1 + e^-x) and tanh(x) = 2 sigmoid(2x) - 1, from the
-// exponential intrinsic and the fast reciprocal-divide; the argument is
-// clamped so that e^-x stays finite.
-__device__ __forceinline__ float gate_sigmoid(float x) {
+// Accurate activations: sigmoid(x) = 1 / (1 + e^-x) and tanh(x) = 2 sigmoid(2x) - 1
+// from the exponential intrinsic and the fast reciprocal-divide (two MUFU
+// operations each); the argument is clamped so that e^-x stays finite.
+__device__ __forceinline__ float sigmoid_mufu2(float x) {
   x = fminf(fmaxf(x, -80.0f), 80.0f);
   return __fdividef(1.0f, 1.0f + __expf(-x));
 }
-__device__ __forceinline__ float gate_tanh(float x) { return 2.0f * gate_sigmoid(2.0f * x) - 1.0f; }
+__device__ __forceinline__ float tanh_mufu2(float x) { return 2.0f * sigmoid_mufu2(2.0f * x) - 1.0f; }
+// Fast activations: one hardware tanh.approx each; sigmoid(x) = (1 + tanh(x/2)) / 2.
+__device__ __forceinline__ float sigmoid_mufu1(float x) { return fmaf(0.5f, ptx::tanh_approx(0.5f * x), 0.5f); }
 
 // Bounded wait on an mbarrier phase; false = gave up (timeout or cluster abort).
 __device__ __forceinline__ bool wait_phase(uint32_t bar, uint32_t parity, volatile int* abort_flag,
@@ -153,11 +175,40 @@ __device__ __forceinline__ bool wait_phase(uint32_t bar, uint32_t parity, volati
   }
 }
 
+// Warp-uniform versions: lane 0 polls, the result is broadcast.
+__device__ __forceinline__ bool warp_wait_phase(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                                unsigned long long timeout_ns) {
+  int ok = 0;
+  if ((threadIdx.x & 31) == 0) ok = wait_phase(bar, parity, abort_flag, timeout_ns) ? 1 : 0;
+  return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+__device__ __forceinline__ bool warp_try_wait(uint32_t bar, uint32_t parity) {
+  int ok = 0;
+  if ((threadIdx.x & 31) == 0) ok = ptx::mbar_try_wait(bar, parity) ? 1 : 0;
+  return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+
 // Raises the abort flag in every CTA of the cluster and records the failure.
 __device__ __forceinline__ void raise_abort(const Params& p, uint8_t* sm_abort, int ncta, int step) {
   const uint32_t local = ptx::smem_u32(sm_abort);
   for (int r = 0; r < ncta; ++r) ptx::st_cluster_u32(ptx::mapa(local, (uint32_t)r), 1u);
   report_status(p.status, PLSTM_ETIMEOUT, (int)((blockIdx.x & 0x7fff) << 16) | (step & 0xffff));
+}
+
+// Loads CPW 256-bit column chunks of 16 lanes starting at `taddr` into r[0 .. 4*CPW).
+template <int CPW>
+__device__ __forceinline__ void tmem_ld_chunks(uint32_t taddr, uint32_t (&r)[4 * CPW]) {
+  if constexpr (CPW == 1) {
+    ptx::tmem_ld_16x256b_x1(taddr, *reinterpret_cast<uint32_t(*)[4]>(&r[0]));
+  } else if constexpr (CPW == 2) {
+    ptx::tmem_ld_16x256b_x2(taddr, *reinterpret_cast<uint32_t(*)[8]>(&r[0]));
+  } else if constexpr (CPW == 3) {
+    ptx::tmem_ld_16x256b_x2(taddr, *reinterpret_cast<uint32_t(*)[8]>(&r[0]));
+    ptx::tmem_ld_16x256b_x1(taddr + 16, *reinterpret_cast<uint32_t(*)[4]>(&r[8]));
+  } else {
+    static_assert(CPW == 4, "CPW must be 1..4");
+    ptx::tmem_ld_16x256b_x4(taddr, *reinterpret_cast<uint32_t(*)[16]>(&r[0]));
+  }
 }
 
 template <int N, bool BF16, bool VARLEN, int MODE>
@@ -177,25 +228,26 @@ __global__ void __launch_bounds__(kThreads, 1) wavefront_kernel(const Params p) 
   const int tile = blockIdx.x / ncta;
   const bool last_layer = l == p.L - 1;
   const bool drain = kHasLinear && last_layer;
-  const bool does_linear = drain && (N >= 32 || s == 0);
+  const bool does_linear = drain && (S::kSplitLinear || s == 0);
+  const bool sibling_linear = drain && (S::kSplitLinear || s == 1);
   const int Tt = p.tile_len[tile];
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + S::kAbort);
   int32_t* perm_s = reinterpret_cast<int32_t*>(sm + S::kPerm);
   int32_t* lens_s = reinterpret_cast<int32_t*>(sm + S::kLens);
 
-  const uint32_t bar_full = sbase + S::kFull, bar_empty = sbase + S::kEmpty;
+  const uint32_t bar_in = sbase + S::kFullIn, bar_rec = sbase + S::kFullRec, bar_empty = sbase + S::kEmpty;
   const uint32_t bar_hready = sbase + S::kHReady, bar_mma = sbase + S::kMma;
   auto bbuf = [&](int b) -> uint32_t { return sbase + S::kB + b * S::kBufBytes; };
 
   // ---- set-up ------------------------------------------------------------------
   if (tid == 0) {
-    ptx::mbar_init(bar_full + 0, 1);
-    ptx::mbar_init(bar_full + 8, 1);
-    ptx::mbar_init(bar_empty + 0, 2);
-    ptx::mbar_init(bar_empty + 8, 2);
-    ptx::mbar_init(bar_hready + 0, kComputeWarps);
-    ptx::mbar_init(bar_hready + 8, kComputeWarps);
-    ptx::mbar_init(bar_mma, 1);
+    for (int b = 0; b < 2; ++b) {
+      ptx::mbar_init(bar_in + 8 * b, 1);
+      ptx::mbar_init(bar_rec + 8 * b, 1);
+      ptx::mbar_init(bar_empty + 8 * b, 2);
+      ptx::mbar_init(bar_hready + 8 * b, kComputeWarps);
+      ptx::mbar_init(bar_mma + 8 * b, 1);
+    }
     *abort_flag = 0;
     ptx::fence_mbar_init_cluster();
   }
@@ -243,118 +295,183 @@ __global__ void __launch_bounds__(kThreads, 1) wavefront_kernel(const Params p) 
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(sm + S::kTmemSlot);
   ptx::cluster_sync();  // every CTA's barriers are initialised before any remote operation
 
-  const int steps = Tt + (drain ? 1 : 0);
-  uint32_t n_commits = 0;
+  auto dcol = [&](int buf, int tau) -> uint32_t { return tmem + (uint32_t)((2 * buf + tau) * N); };
 
   if (warp == kComputeWarps) {
     // =========================== control warp ===========================
-    if (lane == 0) {
-      const uint32_t xbytes = S::kXBytes, bkb = S::kBKB;
-      auto in_bytes = [&](int t) -> uint32_t {
-        uint32_t nb = 0;
-        if (t < Tt) nb += (l == 0) ? xbytes : 2 * bkb;
-        if (t >= 1 && t <= Tt && (t < Tt || drain)) nb += bkb;  // sibling's h_{t-1}
-        return nb;
-      };
-      constexpr uint32_t idesc_g = ptx::idesc_f16(128, N, BF16);
-      constexpr uint32_t idesc_l = ptx::idesc_f16(128, NL, BF16);
-      const uint16_t up_mask = l > 0 ? (uint16_t)(3u << (2 * (l - 1))) : 0;
-      if (steps > 0) {
-        ptx::mbar_arrive_expect_tx(bar_full, in_bytes(0));
-        if (l == 0 && Tt > 0)
-          ptx::bulk_g2s(bbuf(0), p.xp + ((size_t)tile * p.T) * xbytes, xbytes, bar_full);
-      }
-      for (int t = 0; t < steps; ++t) {
-        const int b = t & 1;
-        if (*abort_flag) break;
-        if (!wait_phase(bar_full + 8 * b, (t >> 1) & 1, abort_flag, p.timeout_ns)) {
-          raise_abort(p, sm + S::kAbort, ncta, t);
-          break;
-        }
+    const uint32_t xbytes = S::kXBytes, bkb = S::kBKB;
+    const uint32_t in_bytes = (l == 0) ? xbytes : 2 * bkb;
+    constexpr uint32_t idesc_g = ptx::idesc_f16(128, N, BF16);
+    constexpr uint32_t idesc_l = ptx::idesc_f16(128, NL, BF16);
+    const uint16_t up_mask = l > 0 ? (uint16_t)(3u << (2 * (l - 1))) : 0;
+    // Descriptors advance by (byte offset >> 4) in the start-address field.
+    const uint64_t dA = ptx::desc_k_sw128(sbase + S::kA);
+    const uint64_t dAx = ptx::desc_k_none(sbase + S::kA + 64 * 1024, 128, 256);
+    const uint64_t dAl = ptx::desc_k_sw128(sbase + S::kALin);
+    const uint64_t dB0 = ptx::desc_k_sw128(bbuf(0));
+    const uint64_t dBx0 = ptx::desc_k_none(bbuf(0), 128, 256);
+    constexpr uint64_t kBufStep = (uint64_t)(S::kBufBytes >> 4);
+    const uint32_t lin_row_off = S::kSplitLinear ? (uint32_t)(s * NL) * 128u : 0u;
+    const int steps = Tt + (does_linear ? 1 : 0);
+    int last_commit = -1;
+
+    auto x_src = [&](int t) { return p.xp + ((size_t)tile * p.T + t) * xbytes; };
+    // Input part of step t (W_ih . x_t) into D[t & 1]; it initialises the accumulator.
+    auto issue_in = [&](int t) {
+      const int b = t & 1;
+      if (ptx::elect_one()) {
         ptx::tc_fence_after();
-        const bool gates = t < Tt;
-        const uint32_t B0 = bbuf(b);
-        if (gates) {
+        const uint64_t dB = dB0 + kBufStep * b;
 #pragma unroll
-          for (int tau = 0; tau < 2; ++tau) {
-            const uint32_t d = tmem + (uint32_t)(tau * N);
-            if (l == 0) {
-              const uint32_t a_x = sbase + S::kA + 64 * 1024 + tau * 4096;
-              ptx::mma_f16_ss(d, ptx::desc_k_none(a_x, 128, 256), ptx::desc_k_none(B0, 128, 256), idesc_g, 0u);
+        for (int tau = 0; tau < 2; ++tau) {
+          if (l == 0) {
+            ptx::mma_f16_ss(dcol(b, tau), dAx + (uint64_t)((tau * 4096) >> 4), dBx0 + kBufStep * b, idesc_g, 0u);
+          } else {
 #pragma unroll
-              for (int kb = 0; kb < 2; ++kb)
+            for (int kb = 0; kb < 2; ++kb)
 #pragma unroll
-                for (int kk = 0; kk < 4; ++kk) {
-                  const uint32_t a = sbase + S::kA + tau * 2 * kATileKB + kb * kATileKB + kk * 32;
-                  const uint32_t bb = B0 + (2 + kb) * bkb + kk * 32;
-                  ptx::mma_f16_ss(d, ptx::desc_k_sw128(a), ptx::desc_k_sw128(bb), idesc_g, 1u);
-                }
-            } else {
-#pragma unroll
-              for (int kb = 0; kb < 4; ++kb)
-#pragma unroll
-                for (int kk = 0; kk < 4; ++kk) {
-                  const uint32_t a = sbase + S::kA + tau * 4 * kATileKB + kb * kATileKB + kk * 32;
-                  const uint32_t bb = B0 + kb * bkb + kk * 32;
-                  ptx::mma_f16_ss(d, ptx::desc_k_sw128(a), ptx::desc_k_sw128(bb), idesc_g,
-                                  (kb | kk) != 0 ? 1u : 0u);
-                }
-            }
+              for (int kk = 0; kk < 4; ++kk)
+                ptx::mma_f16_ss(dcol(b, tau), dA + (uint64_t)((tau * 4 * kATileKB + kb * kATileKB + kk * 32) >> 4),
+                                dB + (uint64_t)((kb * S::kBKB + kk * 32) >> 4), idesc_g, (kb | kk) != 0 ? 1u : 0u);
           }
         }
-        const bool lin = does_linear && (t == Tt || (MODE == kModeSeq && t >= 1));
+        // Layer l-1 may overwrite this input slot once these MMAs are done.
+        if (l > 0 && t + 2 < Tt) ptx::mma_commit_mc(bar_empty + 8 * b, up_mask);
+      }
+      __syncwarp();
+    };
+    // Recurrent part of step t (W_hh . h_{t-1}) and/or the Linear head on h_{t-1}; commit -> mma[t & 1].
+    auto issue_rec = [&](int t, bool gates, bool lin) {
+      const int b = t & 1;
+      if (ptx::elect_one()) {
+        ptx::tc_fence_after();
+        const uint64_t dB = dB0 + kBufStep * b;
+        if (gates) {
+#pragma unroll
+          for (int tau = 0; tau < 2; ++tau)
+#pragma unroll
+            for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+              for (int kk = 0; kk < 4; ++kk) {
+                const int a_off = (l == 0) ? (tau * 2 * kATileKB + kb * kATileKB + kk * 32)
+                                           : (tau * 4 * kATileKB + (2 + kb) * kATileKB + kk * 32);
+                ptx::mma_f16_ss(dcol(b, tau), dA + (uint64_t)(a_off >> 4),
+                                dB + (uint64_t)(((2 + kb) * S::kBKB + kk * 32) >> 4), idesc_g, 1u);
+              }
+        }
         if (lin) {
-          const uint32_t d = tmem + (uint32_t)(2 * N);
-          const uint32_t row_off = (N >= 32 ? (uint32_t)(s * NL) : 0u) * 128u;
 #pragma unroll
           for (int kb = 0; kb < 2; ++kb)
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-              const uint32_t a = sbase + S::kALin + kb * kATileKB + kk * 32;
-              const uint32_t bb = B0 + (2 + kb) * bkb + row_off + kk * 32;
-              ptx::mma_f16_ss(d, ptx::desc_k_sw128(a), ptx::desc_k_sw128(bb), idesc_l,
+            for (int kk = 0; kk < 4; ++kk)
+              ptx::mma_f16_ss(tmem + (uint32_t)(4 * N), dAl + (uint64_t)((kb * kATileKB + kk * 32) >> 4),
+                              dB + (uint64_t)(((2 + kb) * S::kBKB + lin_row_off + kk * 32) >> 4), idesc_l,
                               (kb | kk) != 0 ? 1u : 0u);
+        }
+        ptx::mma_commit(bar_mma + 8 * b);
+      }
+      __syncwarp();
+    };
+    bool ok = true;
+    auto fail = [&](int t) {
+      if (ptx::elect_one()) raise_abort(p, sm + S::kAbort, ncta, t);
+      __syncwarp();
+      ok = false;
+    };
+
+    // Prologue: expected bytes of steps 0 / 1 (inputs) and 1 / 2 (sibling h), x of steps 0 / 1.
+    if (ptx::elect_one()) {
+      for (int t = 0; t < 2 && t < Tt; ++t) {
+        ptx::mbar_arrive_expect_tx(bar_in + 8 * t, in_bytes);
+        if (l == 0) ptx::bulk_g2s(bbuf(t), x_src(t), xbytes, bar_in + 8 * t);
+      }
+      for (int t = 1; t <= 2; ++t)
+        if (t < Tt || (does_linear && t == Tt))
+          ptx::mbar_arrive_expect_tx(bar_rec + 8 * (t & 1), bkb);
+    }
+    __syncwarp();
+    if (Tt > 0) {
+      if (!warp_wait_phase(bar_in, 0, abort_flag, p.timeout_ns)) {
+        fail(0);
+      } else {
+        issue_in(0);
+        if (2 < Tt && ptx::elect_one()) ptx::mbar_arrive_expect_tx(bar_in, in_bytes);
+        __syncwarp();
+      }
+    }
+    for (int t = 0; ok && t < steps; ++t) {
+      const int b = t & 1;
+      const bool gates = t < Tt;
+      const bool lin = does_linear && (t == Tt || (MODE == kModeSeq && t >= 1));
+      if (t >= 1) {
+        if (!warp_wait_phase(bar_rec + 8 * b, ((t - 1) >> 1) & 1, abort_flag, p.timeout_ns)) {
+          fail(t);
+          break;
+        }
+        if ((t + 2 < Tt || (does_linear && t + 2 == Tt)) && ptx::elect_one())
+          ptx::mbar_arrive_expect_tx(bar_rec + 8 * b, bkb);
+        __syncwarp();
+      }
+      if (lane == 0) trace_mark(p, rank, t, 0);
+      issue_rec(t, gates, lin);
+      last_commit = t;
+      if (lane == 0) trace_mark(p, rank, t, 1);
+      if (!gates) break;  // drain step issued
+      // Next step's input MMAs and this step's h hand-off, whichever is ready first.
+      bool in_pending = t + 1 < Tt, copy_pending = true;
+      const unsigned long long t0 = ptx::globaltimer();
+      while (in_pending || copy_pending) {
+        if (in_pending && warp_try_wait(bar_in + 8 * (b ^ 1), ((t + 1) >> 1) & 1)) {
+          issue_in(t + 1);
+          if (t + 3 < Tt && ptx::elect_one()) ptx::mbar_arrive_expect_tx(bar_in + 8 * (b ^ 1), in_bytes);
+          __syncwarp();
+          in_pending = false;
+        }
+        if (copy_pending && warp_try_wait(bar_hready + 8 * b, (t >> 1) & 1)) {
+          if (lane == 0) trace_mark(p, rank, t, 2);
+          if (ptx::elect_one()) {
+            const uint32_t src = bbuf(b ^ 1) + (2 + s) * bkb;
+            const bool to_sibling = (t + 1 < Tt) || (sibling_linear && t + 1 == Tt);
+            const bool dropped = rank == p.drop_rank && t == p.drop_step;
+            if (to_sibling && !dropped) {
+              const uint32_t peer = (uint32_t)(rank ^ 1);
+              ptx::bulk_s2c(ptx::mapa(src, peer), src, bkb, ptx::mapa(bar_rec + 8 * (b ^ 1), peer));
             }
-        }
-        ptx::mma_commit(bar_mma);
-        ++n_commits;
-        if (l > 0 && gates && t + 2 < Tt) ptx::mma_commit_mc(bar_empty + 8 * b, up_mask);
-        if (t + 1 < steps) {
-          ptx::mbar_arrive_expect_tx(bar_full + 8 * (b ^ 1), in_bytes(t + 1));
-          if (l == 0 && t + 1 < Tt)
-            ptx::bulk_g2s(bbuf(b ^ 1), p.xp + ((size_t)tile * p.T + t + 1) * xbytes, xbytes,
-                          bar_full + 8 * (b ^ 1));
-        }
-        if (gates) {
-          if (!wait_phase(bar_hready + 8 * b, (t >> 1) & 1, abort_flag, p.timeout_ns)) {
-            raise_abort(p, sm + S::kAbort, ncta, t);
-            break;
-          }
-          const uint32_t src = bbuf(b ^ 1) + (2 + s) * bkb;
-          const bool to_sibling = (t + 1 < Tt) || (drain && t + 1 == Tt);
-          const bool dropped = rank == p.drop_rank && t == p.drop_step;
-          if (to_sibling && !dropped) {
-            const uint32_t peer = (uint32_t)(rank ^ 1);
-            ptx::bulk_s2c(ptx::mapa(src, peer), src, bkb, ptx::mapa(bar_full + 8 * (b ^ 1), peer));
-          }
-          if (l + 1 < p.L) {
-            const uint32_t dst_local = bbuf(b) + s * bkb;
+            if (l + 1 < p.L) {
+              const uint32_t dst_local = bbuf(b) + s * bkb;
 #pragma unroll
-            for (int j = 0; j < 2; ++j) {
-              const uint32_t peer = (uint32_t)(2 * (l + 1) + j);
-              ptx::bulk_s2c(ptx::mapa(dst_local, peer), src, bkb, ptx::mapa(bar_full + 8 * b, peer));
+              for (int j = 0; j < 2; ++j) {
+                const uint32_t peer = (uint32_t)(2 * (l + 1) + j);
+                ptx::bulk_s2c(ptx::mapa(dst_local, peer), src, bkb, ptx::mapa(bar_in + 8 * b, peer));
+              }
             }
+            // x of step t+2 into the input slot step t's MMAs have finished reading.
+            if (l == 0 && t + 2 < Tt) ptx::bulk_g2s(bbuf(b), x_src(t + 2), xbytes, bar_in + 8 * b);
+          }
+          __syncwarp();
+          if (lane == 0) trace_mark(p, rank, t, 3);
+          copy_pending = false;
+        }
+        if (in_pending || copy_pending) {
+          int bad = 0;
+          if (lane == 0) bad = (*abort_flag != 0) || (ptx::globaltimer() - t0 > p.timeout_ns);
+          if (__shfl_sync(0xffffffffu, bad, 0)) {
+            fail(t);
+            break;
           }
         }
       }
-      // All MMAs must have completed before TMEM is released.
-      if (n_commits > 0) wait_phase(bar_mma, (n_commits - 1) & 1, abort_flag, p.timeout_ns);
     }
+    // All MMAs must have completed before TMEM is released.
+    if (last_commit >= 0 && lane == 0)
+      wait_phase(bar_mma + 8 * (last_commit & 1), (last_commit >> 1) & 1, abort_flag, p.timeout_ns);
+    __syncwarp();
   } else {
     // =========================== compute warps ===========================
     const int q = warp & 3, half = warp >> 2;
-    const int j8 = lane >> 2;        // unit within the quadrant's group of 8
+    const int j8 = lane >> 2;          // unit within the quadrant's group of 8
     const int cpair = (lane & 3) * 2;  // first of the two batch columns in a chunk
+    const bool fast = p.fast_act != 0;
     const float* bias_img = reinterpret_cast<const float*>(p.packed + packed_bias_off(p.L)) + rank * 256;
     float bi[2], bf[2], bg[2], bo[2];
 #pragma unroll
@@ -399,25 +516,28 @@ __global__ void __launch_bounds__(kThreads, 1) wavefront_kernel(const Params p) 
     const int o = lane;  // Linear output row handled by this lane (lin_warp only)
     const float blin_o = (lin_warp && o < p.O) ? blin[o] : 0.0f;
     uint16_t* out16 = static_cast<uint16_t*>(p.out);
+    const int lin_n0 = (S::kSplitLinear ? s * NL : 0) + half * (NL / 2);  // first batch column of this warp
 
-    // Stores Linear outputs of step `ts` from D_lin (lanes 0..31 = output rows).
+    // Stores the Linear outputs of step `ts` from the Linear accumulator (lanes = output rows).
     auto store_linear = [&](int ts, bool last_mode) {
-      uint32_t r[8];
-      const uint32_t taddr = tmem + (uint32_t)(2 * N + half * (NL / 2));
-      ptx::tmem_ld_32x32b_x8(taddr, r);
-      ptx::tmem_wait_ld();
-      if (o < p.O) {
 #pragma unroll
-        for (int i = 0; i < NL / 2; ++i) {
-          const int n = (N >= 32 ? s * NL : 0) + half * (NL / 2) + i;
-          const int b = perm_s[n];
-          if (b < 0) continue;
-          const float v = __uint_as_float(r[i]) + blin_o;
-          if (last_mode) {
-            out16[(size_t)b * p.O + o] = to_bits<BF16>(v);
-          } else {
-            const bool live = ts < lens_s[n];
-            out16[((size_t)b * p.T + ts) * p.O + o] = to_bits<BF16>(live ? v : 0.0f);
+      for (int c0 = 0; c0 < NL / 2; c0 += 8) {
+        uint32_t r[8];
+        ptx::tmem_ld_32x32b_x8(tmem + (uint32_t)(4 * N + half * (NL / 2) + c0), r);
+        ptx::tmem_wait_ld();
+        if (o < p.O) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int n = lin_n0 + c0 + i;
+            const int b = perm_s[n];
+            if (b < 0) continue;
+            const float v = __uint_as_float(r[i]) + blin_o;
+            if (last_mode) {
+              out16[(size_t)b * p.O + o] = to_bits<BF16>(v);
+            } else {
+              const bool live = ts < lens_s[n];
+              out16[((size_t)b * p.T + ts) * p.O + o] = to_bits<BF16>(live ? v : 0.0f);
+            }
           }
         }
       }
@@ -426,30 +546,21 @@ __global__ void __launch_bounds__(kThreads, 1) wavefront_kernel(const Params p) 
     for (int t = 0; t < Tt; ++t) {
       const int b = t & 1;
       if (*abort_flag) break;
-      if (!wait_phase(bar_mma, t & 1, abort_flag, p.timeout_ns)) {
+      if (!wait_phase(bar_mma + 8 * b, (t >> 1) & 1, abort_flag, p.timeout_ns)) {
         if (lane == 0) raise_abort(p, sm + S::kAbort, ncta, t);
         break;
       }
       ptx::tc_fence_after();
+      if (tid == 0) trace_mark(p, rank, t, 4);
       uint32_t rif[2][4 * CPW], rgo[2][4 * CPW];
 #pragma unroll
       for (int tau = 0; tau < 2; ++tau) {
-        const uint32_t col = (uint32_t)(tau * N + half * CPW * 8);
-        const uint32_t a0 = tmem + ((uint32_t)(32 * q) << 16) + col;
-        const uint32_t a1 = tmem + ((uint32_t)(32 * q + 16) << 16) + col;
-        if constexpr (CPW == 1) {
-          uint32_t(&x0)[4] = *reinterpret_cast<uint32_t(*)[4]>(rif[tau]);
-          uint32_t(&x1)[4] = *reinterpret_cast<uint32_t(*)[4]>(rgo[tau]);
-          ptx::tmem_ld_16x256b_x1(a0, x0);
-          ptx::tmem_ld_16x256b_x1(a1, x1);
-        } else {
-          uint32_t(&x0)[8] = *reinterpret_cast<uint32_t(*)[8]>(rif[tau]);
-          uint32_t(&x1)[8] = *reinterpret_cast<uint32_t(*)[8]>(rgo[tau]);
-          ptx::tmem_ld_16x256b_x2(a0, x0);
-          ptx::tmem_ld_16x256b_x2(a1, x1);
-        }
+        const uint32_t col = dcol(b, tau) + (uint32_t)(half * CPW * 8);
+        tmem_ld_chunks<CPW>(col + ((uint32_t)(32 * q) << 16), rif[tau]);
+        tmem_ld_chunks<CPW>(col + ((uint32_t)(32 * q + 16) << 16), rgo[tau]);
       }
       ptx::tmem_wait_ld();
+      if (tid == 0) trace_mark(p, rank, t, 5);
       if (MODE == kModeSeq && lin_warp && t >= 1) store_linear(t - 1, false);
       ptx::tc_fence_before();
 
@@ -472,8 +583,14 @@ __global__ void __launch_bounds__(kThreads, 1) wavefront_kernel(const Params p) 
             const float gf = __uint_as_float(rif[tau][4 * jc + 2 + e]) + bf[tau];
             const float gg = __uint_as_float(rgo[tau][4 * jc + e]) + bg[tau];
             const float go = __uint_as_float(rgo[tau][4 * jc + 2 + e]) + bo[tau];
-            const float c_new = gate_sigmoid(gf) * c_st[tau][jc][e] + gate_sigmoid(gi) * gate_tanh(gg);
-            const float h_new = gate_sigmoid(go) * gate_tanh(c_new);
+            float c_new, h_new;
+            if (fast) {
+              c_new = sigmoid_mufu1(gf) * c_st[tau][jc][e] + sigmoid_mufu1(gi) * ptx::tanh_approx(gg);
+              h_new = sigmoid_mufu1(go) * ptx::tanh_approx(c_new);
+            } else {
+              c_new = sigmoid_mufu2(gf) * c_st[tau][jc][e] + sigmoid_mufu2(gi) * tanh_mufu2(gg);
+              h_new = sigmoid_mufu2(go) * tanh_mufu2(c_new);
+            }
             const uint16_t hb = to_bits<BF16>(h_new);
             bool live = true;
             if (VARLEN) live = t < len_c[jc][e];
@@ -492,12 +609,13 @@ __global__ void __launch_bounds__(kThreads, 1) wavefront_kernel(const Params p) 
           }
       }
       ptx::fence_proxy_async_smem();
+      if (tid == 0) trace_mark(p, rank, t, 6);
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(bar_hready + 8 * b);
     }
     // Drain: Linear of the last step's h.
-    if (drain && lin_warp && !*abort_flag) {
-      if (wait_phase(bar_mma, Tt & 1, abort_flag, p.timeout_ns)) {
+    if (lin_warp && !*abort_flag) {
+      if (wait_phase(bar_mma + 8 * (Tt & 1), (Tt >> 1) & 1, abort_flag, p.timeout_ns)) {
         ptx::tc_fence_after();
         if (MODE == kModeSeq) {
           if (Tt >= 1) store_linear(Tt - 1, false);
@@ -512,7 +630,7 @@ __global__ void __launch_bounds__(kThreads, 1) wavefront_kernel(const Params p) 
     // Outputs past the tile's last step are zero.
     if (MODE == kModeSeq && lin_warp && o < p.O) {
       for (int i = 0; i < NL / 2; ++i) {
-        const int n = (N >= 32 ? s * NL : 0) + half * (NL / 2) + i;
+        const int n = lin_n0 + i;
         const int b = perm_s[n];
         if (b < 0) continue;
         for (int ts = Tt; ts < p.T; ++ts) out16[((size_t)b * p.T + ts) * p.O + o] = 0;
@@ -744,12 +862,30 @@ int mode_of(const Problem& p) {
   return p.out_seq() ? kModeSeq : kModeLast;
 }
 
-int smem_bytes_for(int N) { return N == 16 ? Smem<16>::kDynBytes : Smem<32>::kDynBytes; }
+int smem_bytes_for(int N) {
+  switch (N) {
+    case 16: return Smem<16>::kDynBytes;
+    case 32: return Smem<32>::kDynBytes;
+    case 48: return Smem<48>::kDynBytes;
+    default: return Smem<64>::kDynBytes;
+  }
+}
+
+void* pick_kernel_n(int N, bool bf16, bool varlen, int mode) {
+  switch (N) {
+    case 16: return pick_kernel<16>(bf16, varlen, mode);
+    case 32: return pick_kernel<32>(bf16, varlen, mode);
+    case 48: return pick_kernel<48>(bf16, varlen, mode);
+    default: return pick_kernel<64>(bf16, varlen, mode);
+  }
+}
+
+constexpr int kTileNs[4] = {16, 32, 48, 64};
 
 // Max clusters of 2L CTAs (one per SM) co-resident on `device`; cached.
 int max_active_clusters(int device, int L, int N) {
   static std::mutex mu;
-  static int cache[64][5][2];
+  static int cache[64][5][4];
   static bool init = false;
   std::lock_guard<std::mutex> g(mu);
   if (!init) {
@@ -758,11 +894,11 @@ int max_active_clusters(int device, int L, int N) {
         for (auto& c : b) c = -1;
     init = true;
   }
-  const int ni = N == 16 ? 0 : 1;
+  const int ni = N / 16 - 1;
   if (device < 0 || device >= 64 || L < 1 || L > 4) return 1;
   int& slot = cache[device][L][ni];
   if (slot >= 0) return slot;
-  void* k = N == 16 ? pick_kernel<16>(false, false, kModeLast) : pick_kernel<32>(false, false, kModeLast);
+  void* k = pick_kernel_n(N, false, false, kModeLast);
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes_for(N));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * L * 64, 1, 1);
@@ -786,13 +922,18 @@ int max_active_clusters(int device, int L, int N) {
 
 Plan make_plan(const Problem& p) {
   Plan pl;
-  int N = 32;
+  // The smallest tile whose clusters all fit on the GPU at once (one wave);
+  // beyond that the widest tile (fewest waves).
+  int N = 64;
+  for (int n : kTileNs) {
+    if ((p.B + n - 1) / n <= max_active_clusters(p.device, p.L, n)) {
+      N = n;
+      break;
+    }
+  }
   if (const char* e = std::getenv("PLSTM_TC_NTILE")) {
     const int v = std::atoi(e);
-    if (v == 16 || v == 32) N = v;
-  } else {
-    const int clusters = max_active_clusters(p.device, p.L, 16);
-    if ((p.B + 15) / 16 <= clusters) N = 16;
+    if (v == 16 || v == 32 || v == 48 || v == 64) N = v;
   }
   pl.N = N;
   pl.tiles = (p.B + N - 1) / N;
@@ -800,7 +941,7 @@ Plan make_plan(const Problem& p) {
 }
 
 struct TcWs {
-  size_t xp, perm, tile_len, hist, sorted, total;
+  size_t xp, perm, tile_len, hist, sorted, trace, total;
 };
 
 TcWs tc_ws(const Problem& p, const Plan& pl) {
@@ -816,6 +957,8 @@ TcWs tc_ws(const Problem& p, const Plan& pl) {
   off = align_up(off + (size_t)(p.T + 1) * 4, 256);
   w.sorted = off;
   off = align_up(off + (size_t)std::max(p.B, 1) * 4, 256);
+  w.trace = off;
+  if (p.flags & PLSTM_FLAG_TRACE) off += (size_t)2 * p.L * kTraceSteps * kTraceEvents * 8;
   w.total = off;
   return w;
 }
@@ -924,16 +1067,23 @@ int32_t tc_forward(const Problem& p, const void* packed, const void* x, const in
   kp.O = p.O;
   kp.flags = p.flags;
   kp.timeout_ns = (unsigned long long)p.timeout_ms * 1000000ull;
+  kp.fast_act = 0;
+  if (const char* e = std::getenv("PLSTM_TC_ACT")) kp.fast_act = std::string(e) == "fast" ? 1 : 0;
   kp.drop_rank = -1;
   kp.drop_step = -1;
+  kp.trace = nullptr;
+  kp.trace_t0 = p.T / 2;
+  if (p.flags & PLSTM_FLAG_TRACE) {
+    kp.trace = reinterpret_cast<unsigned long long*>(wsb + w.trace);
+    PLSTM_TRY_CUDA(cudaMemsetAsync(kp.trace, 0, (size_t)2 * p.L * kTraceSteps * kTraceEvents * 8, s));
+  }
   if (p.flags & PLSTM_FLAG_TEST_DROP) {
     kp.drop_rank = p.L >= 2 ? 2 : 0;
     kp.drop_step = 0;
   }
   const bool bf16 = p.dtype == PLSTM_BF16;
   const int mode = mode_of(p);
-  void* k = pl.N == 16 ? pick_kernel<16>(bf16, lengths != nullptr, mode)
-                       : pick_kernel<32>(bf16, lengths != nullptr, mode);
+  void* k = pick_kernel_n(pl.N, bf16, lengths != nullptr, mode);
   const int smem = smem_bytes_for(pl.N);
   PLSTM_TRY_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
   cudaLaunchConfig_t cfg = {};

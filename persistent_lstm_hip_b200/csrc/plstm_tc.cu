@@ -11,8 +11,9 @@
 //     r = 2l + s owns layer l, hidden units [64 s, 64 s + 64): 256 gate rows.
 //   * Its slice of [W_ih | W_hh] (256 rows x K, K = 256 for l >= 1,
 //     16 + 128 for l = 0 with x zero-padded to 16 columns) stays resident in
-//     shared memory for the whole sequence as the A operand (K-major, 128-byte
-//     swizzle).  The per-step contraction gates^T[256 x N] = W . [x_t | h_{t-1}]^T
+//     tensor memory for the whole sequence as the A operand (256 of the SM's
+//     512 TMEM columns), so each MMA streams only the small h operand from
+//     shared memory.  The per-step contraction gates^T[256 x N] = W . [x_t | h_{t-1}]^T
 //     runs as tcgen05.mma kind::f16 (f16/bf16 in, f32 accumulate in TMEM),
 //     M = 128 per instruction, N = batch tile.
 //   * The contraction is split in two: the input part W_ih . x_t is issued as
@@ -57,9 +58,10 @@ namespace tc {
 
 constexpr int kH = 128;  // hidden size served (64 units per CTA)
 constexpr int kXK = 16;  // padded layer-0 input width (one MMA K step)
-constexpr int kComputeWarps = 8;
-constexpr int kThreads = (kComputeWarps + 1) * 32;  // + one control warp
-constexpr int kABytes = 128 * 1024;                 // A image slot per CTA
+constexpr int kABytes = 128 * 1024;                 // A image slot per CTA: [tile 2][row 128][K 256] 16-bit
+constexpr int kAK = 256;                            // K extent of an A image row
+constexpr int kTmemBias = 256;                      // TMEM columns [256, 272): bias K block of each tile
+constexpr int kTmemACols = 272;                     // TMEM columns holding A: 2 tiles x 128 + 2 x 8 bias
 constexpr int kALinBytes = 32 * 1024;               // Linear head A image (2 K blocks)
 constexpr int kATileKB = 128 * 128;                 // one (M tile, 64-wide K block): 16 KB
 constexpr int kModeSeq = 0, kModeLast = 1, kModeHSeq = 2;
@@ -79,11 +81,11 @@ template <int N>
 struct Smem {
   static constexpr int kBKB = N * 128;  // one 64-wide K block of the B operand
   static constexpr int kXBytes = N * 32;
-  static constexpr int kA = 0;
-  static constexpr int kALin = kABytes;
-  static constexpr int kB = kALin + kALinBytes;
+  static constexpr int kB = 0;
   static constexpr int kBufBytes = 4 * kBKB;  // slots: [in0 | in1 | rec0 | rec1]
-  static constexpr int kBar = kB + 2 * kBufBytes;
+  static constexpr int kALin = kB + 2 * kBufBytes;
+  static constexpr int kOnes = kALin + kALinBytes;  // constant B block: columns 0, 1 = 1 (bias K block)
+  static constexpr int kBar = kOnes + ((kXBytes + 1023) / 1024) * 1024;
   // mbarriers (8 bytes each, two per kind: one per step parity)
   static constexpr int kFullIn = kBar, kFullRec = kBar + 16, kEmpty = kBar + 32, kHReady = kBar + 48,
                        kMma = kBar + 64;
@@ -94,9 +96,16 @@ struct Smem {
   // Linear head columns per CTA: split between the two last-layer CTAs when
   // N / 2 is a legal MMA width (multiple of 16), else CTA 0 takes all N.
   static constexpr bool kSplitLinear = (N / 2) % 16 == 0;
+  // N / 16 compute warps per TMEM lane quadrant, two 256-bit column chunks each.
+  static constexpr int kG = N / 16;
+  static constexpr int kComputeWarps = 4 * kG;
+  static constexpr int kThreads = (kComputeWarps + 1) * 32;  // + one control warp (MMA issue, h hand-off)
   static constexpr int kNL = kSplitLinear ? N / 2 : N;
-  // TMEM: gates D[buffer 0..1][tile 0..1] (N columns each), then the Linear tile.
-  static constexpr int kTmemCols = tmem_cols_for(4 * N + kNL);
+  // TMEM: A (256 columns), gates D[buffer 0..1][tile 0..1] (N columns each), the Linear tile.
+  static constexpr int kD = kTmemACols;
+  static constexpr int kDLin = kD + 4 * N;
+  static constexpr int kTmemCols = tmem_cols_for(kDLin + kNL);
+  static_assert(kDLin + kNL <= 512, "tile too wide for tensor memory");
 };
 
 struct Params {
@@ -112,7 +121,7 @@ struct Params {
   void* c_n;
   int* status;
   int B, T, L, O, flags;
-  int fast_act;  // 1: one-MUFU tanh.approx activations
+  int fast_act;  // activations: 0 = expf / fast divide, 1 = f32 tanh.approx, 2 = f16x2 tanh.approx
   unsigned long long timeout_ns;
   int drop_rank, drop_step;  // fault injection: rank that skips one sibling hand-off (-1 = off)
   unsigned long long* trace;  // PLSTM_FLAG_TRACE: [2L][64][8] clock64 stamps of cluster 0, or null
@@ -126,6 +135,10 @@ __device__ __forceinline__ void trace_mark(const Params& p, int rank, int t, int
     p.trace[((size_t)rank * kTraceSteps + (t - p.trace_t0)) * kTraceEvents + ev] = clock64();
 }
 
+// No-swizzle K-major offset (core matrices 8 rows x 16 bytes, LBO 128, SBO 256) for K = 16.
+__device__ __forceinline__ uint32_t none16_off(int row, int k) {
+  return (uint32_t)((row >> 3) * 256 + (k >> 3) * 128 + (row & 7) * 16 + (k & 7) * 2);
+}
 // 128-byte swizzled K-major offset of element (row, k) of a 64-wide K block.
 __device__ __forceinline__ uint32_t sw128_off(int row, int k) {
   return (uint32_t)(row * 128 + ((((k >> 3) ^ (row & 7)) & 7) << 4) + (k & 7) * 2);
@@ -212,9 +225,12 @@ __device__ __forceinline__ void tmem_ld_chunks(uint32_t taddr, uint32_t (&r)[4 *
 }
 
 template <int N, bool BF16, bool VARLEN, int MODE>
-__global__ void __launch_bounds__(kThreads, 1) wavefront_kernel(const Params p) {
+__global__ void __launch_bounds__(Smem<N>::kThreads, 1) wavefront_kernel(const Params p) {
   using S = Smem<N>;
-  constexpr int CPW = N / 16;  // 256-bit column chunks per compute warp
+  constexpr int G = S::kG;
+  constexpr int kThreads = S::kThreads;
+  constexpr int kComputeWarps = S::kComputeWarps;
+  constexpr int CPW = 2;  // 256-bit column chunks per compute warp
   constexpr int NL = S::kNL;
   constexpr bool kHasLinear = MODE != kModeHSeq;
   extern __shared__ uint8_t smem_raw[];
@@ -263,10 +279,6 @@ __global__ void __launch_bounds__(kThreads, 1) wavefront_kernel(const Params p) 
     lens_s[i] = len;
   }
   {
-    const uint4* src = reinterpret_cast<const uint4*>(p.packed + (size_t)rank * kABytes);
-    uint4* dst = reinterpret_cast<uint4*>(sm + S::kA);
-    const int n16 = (l == 0 ? (64 + 8) * 1024 : kABytes) / 16;
-    for (int i = tid; i < n16; i += kThreads) dst[i] = src[i];
     if (does_linear) {
       const uint4* srcl = reinterpret_cast<const uint4*>(p.packed + packed_alin_off(p.L));
       uint4* dstl = reinterpret_cast<uint4*>(sm + S::kALin);
@@ -288,26 +300,65 @@ __global__ void __launch_bounds__(kThreads, 1) wavefront_kernel(const Params p) 
       *reinterpret_cast<uint16_t*>(b0 + (2 + (k >> 6)) * S::kBKB + sw128_off(n, k & 63)) = to_bits<BF16>(v);
     }
   }
+  for (int i = tid; i < N * kXK; i += kThreads) {
+    const int n = i / kXK, k = i % kXK;
+    *reinterpret_cast<uint16_t*>(sm + S::kOnes + none16_off(n, k)) = to_bits<BF16>(k < 2 ? 1.0f : 0.0f);
+  }
   ptx::fence_proxy_async_smem();
+  ptx::tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(sm + S::kTmemSlot);
+  // This CTA's weight slice -> TMEM columns [0, 256), one A row per lane, K
+  // packed two 16-bit values per column; the bias of each row -> the tile's bias
+  // K block at [256 + 8 tile, +8): b = hi + lo split over K = 0, 1 (the B side
+  // holds 1 in both), so the MMA adds the f32-accurate bias.
+  if (warp < kComputeWarps) {
+    const int row = 32 * (warp & 3) + lane;
+    const uint32_t lane_off = (uint32_t)(32 * (warp & 3)) << 16;
+    const float* bias_img = reinterpret_cast<const float*>(p.packed + packed_bias_off(p.L)) + rank * 256;
+    for (int tau = warp >> 2; tau < 2; tau += G) {
+      const uint4* src = reinterpret_cast<const uint4*>(p.packed + (size_t)rank * kABytes +
+                                                        ((size_t)tau * 128 + row) * kAK * 2);
+#pragma unroll 1
+      for (int c = 0; c < kAK / 2; c += 32) {
+        uint32_t r[32];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const uint4 v = src[c / 4 + i];
+          r[4 * i + 0] = v.x;
+          r[4 * i + 1] = v.y;
+          r[4 * i + 2] = v.z;
+          r[4 * i + 3] = v.w;
+        }
+        ptx::tmem_st_32x32b_x32(tmem + lane_off + (uint32_t)(tau * 128 + c), r);
+      }
+      const float bv = bias_img[tau * 128 + row];
+      const uint16_t hi = to_bits<BF16>(bv);
+      const uint16_t lo = to_bits<BF16>(bv - from_bits<BF16>(hi));
+      uint32_t rb[8] = {(uint32_t)hi | ((uint32_t)lo << 16), 0, 0, 0, 0, 0, 0, 0};
+      ptx::tmem_st_32x32b_x8(tmem + lane_off + (uint32_t)(kTmemBias + 8 * tau), rb);
+    }
+    ptx::tmem_wait_st();
+  }
   ptx::tc_fence_before();
   __syncthreads();
   ptx::tc_fence_after();
-  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(sm + S::kTmemSlot);
   ptx::cluster_sync();  // every CTA's barriers are initialised before any remote operation
 
-  auto dcol = [&](int buf, int tau) -> uint32_t { return tmem + (uint32_t)((2 * buf + tau) * N); };
+  auto dcol = [&](int buf, int tau) -> uint32_t { return tmem + (uint32_t)(S::kD + (2 * buf + tau) * N); };
 
   if (warp == kComputeWarps) {
-    // =========================== control warp ===========================
+    // ============================ control warp ==========================
     const uint32_t xbytes = S::kXBytes, bkb = S::kBKB;
     const uint32_t in_bytes = (l == 0) ? xbytes : 2 * bkb;
     constexpr uint32_t idesc_g = ptx::idesc_f16(128, N, BF16);
     constexpr uint32_t idesc_l = ptx::idesc_f16(128, NL, BF16);
     const uint16_t up_mask = l > 0 ? (uint16_t)(3u << (2 * (l - 1))) : 0;
-    // Descriptors advance by (byte offset >> 4) in the start-address field.
-    const uint64_t dA = ptx::desc_k_sw128(sbase + S::kA);
-    const uint64_t dAx = ptx::desc_k_none(sbase + S::kA + 64 * 1024, 128, 256);
+    // Descriptors advance by (byte offset >> 4) in the start-address field; A
+    // K-steps advance by 8 TMEM columns.  A columns: layer 0: x at [0, 8),
+    // W_hh at [8, 72); layers >= 1: W_ih at [0, 64), W_hh at [64, 128) (+128 per tile).
+    const uint32_t a_rec0 = l == 0 ? 8u : 64u;
     const uint64_t dAl = ptx::desc_k_sw128(sbase + S::kALin);
+    const uint64_t dOnes = ptx::desc_k_none(sbase + S::kOnes, 128, 256);
     const uint64_t dB0 = ptx::desc_k_sw128(bbuf(0));
     const uint64_t dBx0 = ptx::desc_k_none(bbuf(0), 128, 256);
     constexpr uint64_t kBufStep = (uint64_t)(S::kBufBytes >> 4);
@@ -315,7 +366,7 @@ __global__ void __launch_bounds__(kThreads, 1) wavefront_kernel(const Params p) 
     const int steps = Tt + (does_linear ? 1 : 0);
     int last_commit = -1;
 
-    auto x_src = [&](int t) { return p.xp + ((size_t)tile * p.T + t) * xbytes; };
+    auto x_src = [&](int t) { return p.xp + ((size_t)tile * p.T + t) * xbytes; };  // layer 0 only
     // Input part of step t (W_ih . x_t) into D[t & 1]; it initialises the accumulator.
     auto issue_in = [&](int t) {
       const int b = t & 1;
@@ -324,16 +375,18 @@ __global__ void __launch_bounds__(kThreads, 1) wavefront_kernel(const Params p) 
         const uint64_t dB = dB0 + kBufStep * b;
 #pragma unroll
         for (int tau = 0; tau < 2; ++tau) {
+          const uint32_t a = tmem + (uint32_t)(tau * 128);
           if (l == 0) {
-            ptx::mma_f16_ss(dcol(b, tau), dAx + (uint64_t)((tau * 4096) >> 4), dBx0 + kBufStep * b, idesc_g, 0u);
+            ptx::mma_f16_ts(dcol(b, tau), a, dBx0 + kBufStep * b, idesc_g, 0u);
           } else {
 #pragma unroll
             for (int kb = 0; kb < 2; ++kb)
 #pragma unroll
               for (int kk = 0; kk < 4; ++kk)
-                ptx::mma_f16_ss(dcol(b, tau), dA + (uint64_t)((tau * 4 * kATileKB + kb * kATileKB + kk * 32) >> 4),
+                ptx::mma_f16_ts(dcol(b, tau), a + (uint32_t)(32 * kb + 8 * kk),
                                 dB + (uint64_t)((kb * S::kBKB + kk * 32) >> 4), idesc_g, (kb | kk) != 0 ? 1u : 0u);
           }
+          ptx::mma_f16_ts(dcol(b, tau), tmem + (uint32_t)(kTmemBias + 8 * tau), dOnes, idesc_g, 1u);
         }
         // Layer l-1 may overwrite this input slot once these MMAs are done.
         if (l > 0 && t + 2 < Tt) ptx::mma_commit_mc(bar_empty + 8 * b, up_mask);
@@ -352,19 +405,16 @@ __global__ void __launch_bounds__(kThreads, 1) wavefront_kernel(const Params p) 
 #pragma unroll
             for (int kb = 0; kb < 2; ++kb)
 #pragma unroll
-              for (int kk = 0; kk < 4; ++kk) {
-                const int a_off = (l == 0) ? (tau * 2 * kATileKB + kb * kATileKB + kk * 32)
-                                           : (tau * 4 * kATileKB + (2 + kb) * kATileKB + kk * 32);
-                ptx::mma_f16_ss(dcol(b, tau), dA + (uint64_t)(a_off >> 4),
+              for (int kk = 0; kk < 4; ++kk)
+                ptx::mma_f16_ts(dcol(b, tau), tmem + (uint32_t)(tau * 128) + a_rec0 + (uint32_t)(32 * kb + 8 * kk),
                                 dB + (uint64_t)(((2 + kb) * S::kBKB + kk * 32) >> 4), idesc_g, 1u);
-              }
         }
         if (lin) {
 #pragma unroll
           for (int kb = 0; kb < 2; ++kb)
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk)
-              ptx::mma_f16_ss(tmem + (uint32_t)(4 * N), dAl + (uint64_t)((kb * kATileKB + kk * 32) >> 4),
+              ptx::mma_f16_ss(tmem + (uint32_t)S::kDLin, dAl + (uint64_t)((kb * kATileKB + kk * 32) >> 4),
                               dB + (uint64_t)(((2 + kb) * S::kBKB + lin_row_off + kk * 32) >> 4), idesc_l,
                               (kb | kk) != 0 ? 1u : 0u);
         }
@@ -399,6 +449,30 @@ __global__ void __launch_bounds__(kThreads, 1) wavefront_kernel(const Params p) 
         __syncwarp();
       }
     }
+    // Pushes h(t) to the sibling CTA and to layer l+1, and (layer 0) streams x of
+    // step t+2 into the input slot step t has finished with.
+    auto hand_off = [&](int t) {
+      const int b = t & 1;
+      if (ptx::elect_one()) {
+        const uint32_t src = bbuf(b ^ 1) + (2 + s) * bkb;
+        const bool to_sibling = (t + 1 < Tt) || (sibling_linear && t + 1 == Tt);
+        const bool dropped = rank == p.drop_rank && t == p.drop_step;
+        if (to_sibling && !dropped) {
+          const uint32_t peer = (uint32_t)(rank ^ 1);
+          ptx::bulk_s2c(ptx::mapa(src, peer), src, bkb, ptx::mapa(bar_rec + 8 * (b ^ 1), peer));
+        }
+        if (l + 1 < p.L) {
+          const uint32_t dst_local = bbuf(b) + s * bkb;
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const uint32_t peer = (uint32_t)(2 * (l + 1) + j);
+            ptx::bulk_s2c(ptx::mapa(dst_local, peer), src, bkb, ptx::mapa(bar_in + 8 * b, peer));
+          }
+        }
+        if (l == 0 && t + 2 < Tt) ptx::bulk_g2s(bbuf(b), x_src(t + 2), xbytes, bar_in + 8 * b);
+      }
+      __syncwarp();
+    };
     for (int t = 0; ok && t < steps; ++t) {
       const int b = t & 1;
       const bool gates = t < Tt;
@@ -417,48 +491,30 @@ __global__ void __launch_bounds__(kThreads, 1) wavefront_kernel(const Params p) 
       last_commit = t;
       if (lane == 0) trace_mark(p, rank, t, 1);
       if (!gates) break;  // drain step issued
-      // Next step's input MMAs and this step's h hand-off, whichever is ready first.
+      // This step's h hand-off and the next step's input MMAs, whichever is ready first
+      // (the hand-off first when both are).
       bool in_pending = t + 1 < Tt, copy_pending = true;
       const unsigned long long t0 = ptx::globaltimer();
       while (in_pending || copy_pending) {
+        if (copy_pending && warp_try_wait(bar_hready + 8 * b, (t >> 1) & 1)) {
+          if (lane == 0) trace_mark(p, rank, t, 2);
+          hand_off(t);
+          if (lane == 0) trace_mark(p, rank, t, 3);
+          copy_pending = false;
+          continue;
+        }
         if (in_pending && warp_try_wait(bar_in + 8 * (b ^ 1), ((t + 1) >> 1) & 1)) {
           issue_in(t + 1);
           if (t + 3 < Tt && ptx::elect_one()) ptx::mbar_arrive_expect_tx(bar_in + 8 * (b ^ 1), in_bytes);
           __syncwarp();
           in_pending = false;
+          continue;
         }
-        if (copy_pending && warp_try_wait(bar_hready + 8 * b, (t >> 1) & 1)) {
-          if (lane == 0) trace_mark(p, rank, t, 2);
-          if (ptx::elect_one()) {
-            const uint32_t src = bbuf(b ^ 1) + (2 + s) * bkb;
-            const bool to_sibling = (t + 1 < Tt) || (sibling_linear && t + 1 == Tt);
-            const bool dropped = rank == p.drop_rank && t == p.drop_step;
-            if (to_sibling && !dropped) {
-              const uint32_t peer = (uint32_t)(rank ^ 1);
-              ptx::bulk_s2c(ptx::mapa(src, peer), src, bkb, ptx::mapa(bar_rec + 8 * (b ^ 1), peer));
-            }
-            if (l + 1 < p.L) {
-              const uint32_t dst_local = bbuf(b) + s * bkb;
-#pragma unroll
-              for (int j = 0; j < 2; ++j) {
-                const uint32_t peer = (uint32_t)(2 * (l + 1) + j);
-                ptx::bulk_s2c(ptx::mapa(dst_local, peer), src, bkb, ptx::mapa(bar_in + 8 * b, peer));
-              }
-            }
-            // x of step t+2 into the input slot step t's MMAs have finished reading.
-            if (l == 0 && t + 2 < Tt) ptx::bulk_g2s(bbuf(b), x_src(t + 2), xbytes, bar_in + 8 * b);
-          }
-          __syncwarp();
-          if (lane == 0) trace_mark(p, rank, t, 3);
-          copy_pending = false;
-        }
-        if (in_pending || copy_pending) {
-          int bad = 0;
-          if (lane == 0) bad = (*abort_flag != 0) || (ptx::globaltimer() - t0 > p.timeout_ns);
-          if (__shfl_sync(0xffffffffu, bad, 0)) {
-            fail(t);
-            break;
-          }
+        int bad = 0;
+        if (lane == 0) bad = (*abort_flag != 0) || (ptx::globaltimer() - t0 > p.timeout_ns);
+        if (__shfl_sync(0xffffffffu, bad, 0)) {
+          fail(t);
+          break;
         }
       }
     }
@@ -468,28 +524,19 @@ __global__ void __launch_bounds__(kThreads, 1) wavefront_kernel(const Params p) 
     __syncwarp();
   } else {
     // =========================== compute warps ===========================
-    const int q = warp & 3, half = warp >> 2;
+    const int q = warp & 3, grp = warp >> 2;
     const int j8 = lane >> 2;          // unit within the quadrant's group of 8
     const int cpair = (lane & 3) * 2;  // first of the two batch columns in a chunk
-    const bool fast = p.fast_act != 0;
-    const float* bias_img = reinterpret_cast<const float*>(p.packed + packed_bias_off(p.L)) + rank * 256;
-    float bi[2], bf[2], bg[2], bo[2];
-#pragma unroll
-    for (int tau = 0; tau < 2; ++tau) {
-      const int r = tau * 128 + 32 * q + j8;
-      bi[tau] = bias_img[r];
-      bf[tau] = bias_img[r + 8];
-      bg[tau] = bias_img[r + 16];
-      bo[tau] = bias_img[r + 24];
-    }
+    const int act = p.fast_act;
     // cells: [tau][chunk j][e]
-    float c_st[2][CPW][2], h_st[2][CPW][2];
+    float c_st[2][CPW][2];
+    uint16_t h_st[2][CPW][2];  // h bits (the frozen value of finished rows)
     int ncol[CPW][2], len_c[CPW][2], bidx[CPW][2];
 #pragma unroll
     for (int jc = 0; jc < CPW; ++jc)
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
-        const int n = 8 * (half * CPW + jc) + cpair + e;
+        const int n = 8 * (grp * CPW + jc) + cpair + e;
         ncol[jc][e] = n;
         len_c[jc][e] = lens_s[n];
         bidx[jc][e] = perm_s[n];
@@ -502,9 +549,10 @@ __global__ void __launch_bounds__(kThreads, 1) wavefront_kernel(const Params p) 
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
           const int b = bidx[jc][e];
-          float hv = 0.0f, cv = 0.0f;
+          uint16_t hv = 0;
+          float cv = 0.0f;
           if (b >= 0 && p.h0 != nullptr) {
-            hv = from_bits<BF16>(static_cast<const uint16_t*>(p.h0)[((size_t)l * p.B + b) * kH + u]);
+            hv = static_cast<const uint16_t*>(p.h0)[((size_t)l * p.B + b) * kH + u];
             cv = from_bits<BF16>(static_cast<const uint16_t*>(p.c0)[((size_t)l * p.B + b) * kH + u]);
           }
           h_st[tau][jc][e] = hv;
@@ -516,14 +564,14 @@ __global__ void __launch_bounds__(kThreads, 1) wavefront_kernel(const Params p) 
     const int o = lane;  // Linear output row handled by this lane (lin_warp only)
     const float blin_o = (lin_warp && o < p.O) ? blin[o] : 0.0f;
     uint16_t* out16 = static_cast<uint16_t*>(p.out);
-    const int lin_n0 = (S::kSplitLinear ? s * NL : 0) + half * (NL / 2);  // first batch column of this warp
+    const int lin_n0 = (S::kSplitLinear ? s * NL : 0) + grp * (NL / G);  // first batch column of this warp
 
     // Stores the Linear outputs of step `ts` from the Linear accumulator (lanes = output rows).
     auto store_linear = [&](int ts, bool last_mode) {
 #pragma unroll
-      for (int c0 = 0; c0 < NL / 2; c0 += 8) {
+      for (int c0 = 0; c0 < NL / G; c0 += 8) {
         uint32_t r[8];
-        ptx::tmem_ld_32x32b_x8(tmem + (uint32_t)(4 * N + half * (NL / 2) + c0), r);
+        ptx::tmem_ld_32x32b_x8(tmem + (uint32_t)(S::kDLin + grp * (NL / G) + c0), r);
         ptx::tmem_wait_ld();
         if (o < p.O) {
 #pragma unroll
@@ -555,7 +603,7 @@ __global__ void __launch_bounds__(kThreads, 1) wavefront_kernel(const Params p) 
       uint32_t rif[2][4 * CPW], rgo[2][4 * CPW];
 #pragma unroll
       for (int tau = 0; tau < 2; ++tau) {
-        const uint32_t col = dcol(b, tau) + (uint32_t)(half * CPW * 8);
+        const uint32_t col = dcol(b, tau) + (uint32_t)(grp * CPW * 8);
         tmem_ld_chunks<CPW>(col + ((uint32_t)(32 * q) << 16), rif[tau]);
         tmem_ld_chunks<CPW>(col + ((uint32_t)(32 * q + 16) << 16), rgo[tau]);
       }
@@ -576,37 +624,73 @@ __global__ void __launch_bounds__(kThreads, 1) wavefront_kernel(const Params p) 
       for (int tau = 0; tau < 2; ++tau) {
         const int ul = 8 * (4 * tau + q) + j8;  // unit within this CTA's 64
 #pragma unroll
-        for (int jc = 0; jc < CPW; ++jc)
+        for (int jc = 0; jc < CPW; ++jc) {
+          // Pre-activations of the cell pair (columns e = 0, 1).  Gate rows i, f, o
+          // are packed pre-scaled by 1/2, so sigmoid(z) = (1 + tanh(a)) / 2 with a = z / 2.
+          float ai[2], af[2], ag[2], ao[2], c_new[2];
+          uint16_t hb[2];
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
-            const float gi = __uint_as_float(rif[tau][4 * jc + e]) + bi[tau];
-            const float gf = __uint_as_float(rif[tau][4 * jc + 2 + e]) + bf[tau];
-            const float gg = __uint_as_float(rgo[tau][4 * jc + e]) + bg[tau];
-            const float go = __uint_as_float(rgo[tau][4 * jc + 2 + e]) + bo[tau];
-            float c_new, h_new;
-            if (fast) {
-              c_new = sigmoid_mufu1(gf) * c_st[tau][jc][e] + sigmoid_mufu1(gi) * ptx::tanh_approx(gg);
-              h_new = sigmoid_mufu1(go) * ptx::tanh_approx(c_new);
+            ai[e] = __uint_as_float(rif[tau][4 * jc + e]);
+            af[e] = __uint_as_float(rif[tau][4 * jc + 2 + e]);
+            ag[e] = __uint_as_float(rgo[tau][4 * jc + e]);
+            ao[e] = __uint_as_float(rgo[tau][4 * jc + 2 + e]);
+          }
+          if (act == 2) {
+            // f16x2 hardware tanh: one MUFU operation per two cells and activation.
+            const __half2 half2c = __float2half2_rn(0.5f);
+            const __half2 si = __hfma2(ptx::tanh_approx_h2(__floats2half2_rn(ai[0], ai[1])), half2c, half2c);
+            const __half2 sf = __hfma2(ptx::tanh_approx_h2(__floats2half2_rn(af[0], af[1])), half2c, half2c);
+            const __half2 so = __hfma2(ptx::tanh_approx_h2(__floats2half2_rn(ao[0], ao[1])), half2c, half2c);
+            const __half2 tg = ptx::tanh_approx_h2(__floats2half2_rn(ag[0], ag[1]));
+            const float2 ig = __half22float2(__hmul2(si, tg));
+            const float2 f2 = __half22float2(sf);
+            c_new[0] = fmaf(f2.x, c_st[tau][jc][0], ig.x);
+            c_new[1] = fmaf(f2.y, c_st[tau][jc][1], ig.y);
+            const __half2 h2 = __hmul2(so, ptx::tanh_approx_h2(__floats2half2_rn(c_new[0], c_new[1])));
+            if (BF16) {
+              const float2 hf = __half22float2(h2);
+              hb[0] = to_bits<true>(hf.x);
+              hb[1] = to_bits<true>(hf.y);
             } else {
-              c_new = sigmoid_mufu2(gf) * c_st[tau][jc][e] + sigmoid_mufu2(gi) * tanh_mufu2(gg);
-              h_new = sigmoid_mufu2(go) * tanh_mufu2(c_new);
+              const uint32_t bits = *reinterpret_cast<const uint32_t*>(&h2);
+              hb[0] = (uint16_t)(bits & 0xffffu);
+              hb[1] = (uint16_t)(bits >> 16);
             }
-            const uint16_t hb = to_bits<BF16>(h_new);
+          } else {
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              float h_new;
+              if (act == 1) {
+                c_new[e] = fmaf(fmaf(0.5f, ptx::tanh_approx(af[e]), 0.5f), c_st[tau][jc][e],
+                                fmaf(0.5f, ptx::tanh_approx(ai[e]), 0.5f) * ptx::tanh_approx(ag[e]));
+                h_new = fmaf(0.5f, ptx::tanh_approx(ao[e]), 0.5f) * ptx::tanh_approx(c_new[e]);
+              } else {
+                c_new[e] = sigmoid_mufu2(2.0f * af[e]) * c_st[tau][jc][e] +
+                           sigmoid_mufu2(2.0f * ai[e]) * tanh_mufu2(ag[e]);
+                h_new = sigmoid_mufu2(2.0f * ao[e]) * tanh_mufu2(c_new[e]);
+              }
+              hb[e] = to_bits<BF16>(h_new);
+            }
+          }
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
             bool live = true;
             if (VARLEN) live = t < len_c[jc][e];
             uint16_t wb;
             if (live) {
-              c_st[tau][jc][e] = c_new;
-              h_st[tau][jc][e] = from_bits<BF16>(hb);
-              wb = hb;
+              c_st[tau][jc][e] = c_new[e];
+              h_st[tau][jc][e] = hb[e];
+              wb = hb[e];
             } else {
-              wb = to_bits<BF16>(h_st[tau][jc][e]);
+              wb = h_st[tau][jc][e];
             }
             const int n = ncol[jc][e];
             *reinterpret_cast<uint16_t*>(dst + sw128_off(n, ul)) = wb;
             if (MODE == kModeHSeq && last_layer && bidx[jc][e] >= 0)
-              out16[((size_t)bidx[jc][e] * p.T + t) * kH + 64 * s + ul] = live ? hb : (uint16_t)0;
+              out16[((size_t)bidx[jc][e] * p.T + t) * kH + 64 * s + ul] = live ? hb[e] : (uint16_t)0;
           }
+        }
       }
       ptx::fence_proxy_async_smem();
       if (tid == 0) trace_mark(p, rank, t, 6);
@@ -629,7 +713,7 @@ __global__ void __launch_bounds__(kThreads, 1) wavefront_kernel(const Params p) 
     }
     // Outputs past the tile's last step are zero.
     if (MODE == kModeSeq && lin_warp && o < p.O) {
-      for (int i = 0; i < NL / 2; ++i) {
+      for (int i = 0; i < NL / G; ++i) {
         const int n = lin_n0 + i;
         const int b = perm_s[n];
         if (b < 0) continue;
@@ -661,7 +745,7 @@ __global__ void __launch_bounds__(kThreads, 1) wavefront_kernel(const Params p) 
           const int bb = bidx[jc][e];
           if (bb < 0) continue;
           const size_t idx = ((size_t)l * p.B + bb) * kH + u;
-          if (p.h_n != nullptr) static_cast<uint16_t*>(p.h_n)[idx] = to_bits<BF16>(h_st[tau][jc][e]);
+          if (p.h_n != nullptr) static_cast<uint16_t*>(p.h_n)[idx] = h_st[tau][jc][e];
           if (p.c_n != nullptr) {
             if (p.flags & PLSTM_FLAG_CN_F32)
               static_cast<float*>(p.c_n)[idx] = c_st[tau][jc][e];
@@ -700,6 +784,10 @@ struct PackArgs {
   int ih_layout, hh_layout, dtype, L, I, O;
 };
 
+// Gate rows i, f, o are stored pre-scaled by 1/2 (exact in f16 / bf16 up to
+// subnormals) so that the kernel's sigmoid(z) = (1 + tanh(z / 2)) / 2 needs no multiply.
+__device__ __forceinline__ float gate_scale(int r) { return ((r & 31) >> 3) == 2 ? 1.0f : 0.5f; }
+
 __device__ __forceinline__ int gate_row(int s, int tau, int r) {
   const int q = r >> 5, rr = r & 31, gate = rr >> 3, j = rr & 7;
   return gate * kH + 64 * s + 8 * (4 * tau + q) + j;
@@ -715,34 +803,25 @@ __global__ void tc_pack_kernel(const PackArgs a, uint8_t* packed) {
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
     if (i < n_a) {
+      // A image: [tile][row][K] 16-bit, K-major rows of 256 (see the TMEM column map).
       const int rank = (int)(i / (kABytes / 2));
-      const int off = (int)(i % (kABytes / 2)) * 2;  // byte offset within slot
+      const int within = (int)(i % (kABytes / 2));
+      const int tau = within / (128 * kAK), r = (within / kAK) % 128, k = within % kAK;
       const int l = rank >> 1, s = rank & 1;
+      const int row = gate_row(s, tau, r);
       float v = 0.0f;
       if (l == 0) {
-        if (off < 64 * 1024) {  // W_hh part: [tau][kb][128 rows x 128 B]
-          const int tau = off / (2 * kATileKB), kb = (off / kATileKB) & 1, within = off % kATileKB;
-          const int r = within / 128, chunk = (within % 128) >> 4, e = (within & 15) >> 1;
-          const int kk = ((chunk ^ (r & 7)) << 3) + e;
-          v = load_any(a.w_hh[0], a.dtype, weight_src_index(a.hh_layout, 4 * kH, kH, gate_row(s, tau, r), kb * 64 + kk));
-        } else if (off < 72 * 1024) {  // x part: [tau][128 rows x 16 k], no swizzle
-          const int o2 = off - 64 * 1024;
-          const int tau = o2 / 4096, w = o2 % 4096;
-          const int r = (w / 256) * 8 + (w % 128) / 16;
-          const int k = ((w % 256) / 128) * 8 + (w % 16) / 2;
-          if (k < a.I) v = load_any(a.w_ih[0], a.dtype, weight_src_index(a.ih_layout, 4 * kH, a.I, gate_row(s, tau, r), k));
+        if (k < kXK) {
+          if (k < a.I) v = load_any(a.w_ih[0], a.dtype, weight_src_index(a.ih_layout, 4 * kH, a.I, row, k));
+        } else if (k < kXK + kH) {
+          v = load_any(a.w_hh[0], a.dtype, weight_src_index(a.hh_layout, 4 * kH, kH, row, k - kXK));
         }
-      } else {  // [tau][kb 0..3][128 rows x 128 B]; kb 0,1 = W_ih, kb 2,3 = W_hh
-        const int tau = off / (4 * kATileKB), kb = (off / kATileKB) & 3, within = off % kATileKB;
-        const int r = within / 128, chunk = (within % 128) >> 4, e = (within & 15) >> 1;
-        const int kk = ((chunk ^ (r & 7)) << 3) + e;
-        const int k = (kb & 1) * 64 + kk;
-        const int row = gate_row(s, tau, r);
-        v = kb < 2 ? load_any(a.w_ih[l], a.dtype, weight_src_index(a.ih_layout, 4 * kH, kH, row, k))
-                   : load_any(a.w_hh[l], a.dtype, weight_src_index(a.hh_layout, 4 * kH, kH, row, k));
+      } else {
+        v = k < kH ? load_any(a.w_ih[l], a.dtype, weight_src_index(a.ih_layout, 4 * kH, kH, row, k))
+                   : load_any(a.w_hh[l], a.dtype, weight_src_index(a.hh_layout, 4 * kH, kH, row, k - kH));
       }
-      const uint16_t bits = a.dtype == PLSTM_BF16 ? to_bits<true>(v) : to_bits<false>(v);
-      img[i] = bits;
+      v *= gate_scale(r);
+      img[i] = a.dtype == PLSTM_BF16 ? to_bits<true>(v) : to_bits<false>(v);
     } else if (i < n_a + n_lin) {
       const int off = (int)(i - n_a) * 2;
       const int kb = off / kATileKB, within = off % kATileKB;
@@ -759,7 +838,7 @@ __global__ void tc_pack_kernel(const PackArgs a, uint8_t* packed) {
       float v = 0.0f;
       if (a.b_ih[l] != nullptr) v += load_any(a.b_ih[l], a.dtype, row);
       if (a.b_hh[l] != nullptr) v += load_any(a.b_hh[l], a.dtype, row);
-      reinterpret_cast<float*>(packed + packed_bias_off(a.L))[j] = v;
+      reinterpret_cast<float*>(packed + packed_bias_off(a.L))[j] = v * gate_scale(rr & 127);
     } else {
       const int o = (int)(i - n_a - n_lin - n_bias);
       float v = 0.0f;
@@ -866,8 +945,7 @@ int smem_bytes_for(int N) {
   switch (N) {
     case 16: return Smem<16>::kDynBytes;
     case 32: return Smem<32>::kDynBytes;
-    case 48: return Smem<48>::kDynBytes;
-    default: return Smem<64>::kDynBytes;
+    default: return Smem<48>::kDynBytes;
   }
 }
 
@@ -875,17 +953,24 @@ void* pick_kernel_n(int N, bool bf16, bool varlen, int mode) {
   switch (N) {
     case 16: return pick_kernel<16>(bf16, varlen, mode);
     case 32: return pick_kernel<32>(bf16, varlen, mode);
-    case 48: return pick_kernel<48>(bf16, varlen, mode);
-    default: return pick_kernel<64>(bf16, varlen, mode);
+    default: return pick_kernel<48>(bf16, varlen, mode);
   }
 }
 
-constexpr int kTileNs[4] = {16, 32, 48, 64};
+constexpr int kTileNs[3] = {16, 32, 48};
+
+int threads_for(int N) {
+  switch (N) {
+    case 16: return Smem<16>::kThreads;
+    case 32: return Smem<32>::kThreads;
+    default: return Smem<48>::kThreads;
+  }
+}
 
 // Max clusters of 2L CTAs (one per SM) co-resident on `device`; cached.
 int max_active_clusters(int device, int L, int N) {
   static std::mutex mu;
-  static int cache[64][5][4];
+  static int cache[64][5][3];
   static bool init = false;
   std::lock_guard<std::mutex> g(mu);
   if (!init) {
@@ -902,7 +987,7 @@ int max_active_clusters(int device, int L, int N) {
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes_for(N));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * L * 64, 1, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.blockDim = dim3((unsigned)threads_for(N), 1, 1);
   cfg.dynamicSmemBytes = smem_bytes_for(N);
   cudaLaunchAttribute attr;
   attr.id = cudaLaunchAttributeClusterDimension;
@@ -924,7 +1009,7 @@ Plan make_plan(const Problem& p) {
   Plan pl;
   // The smallest tile whose clusters all fit on the GPU at once (one wave);
   // beyond that the widest tile (fewest waves).
-  int N = 64;
+  int N = 48;
   for (int n : kTileNs) {
     if ((p.B + n - 1) / n <= max_active_clusters(p.device, p.L, n)) {
       N = n;
@@ -933,7 +1018,7 @@ Plan make_plan(const Problem& p) {
   }
   if (const char* e = std::getenv("PLSTM_TC_NTILE")) {
     const int v = std::atoi(e);
-    if (v == 16 || v == 32 || v == 48 || v == 64) N = v;
+    if (v == 16 || v == 32 || v == 48) N = v;
   }
   pl.N = N;
   pl.tiles = (p.B + N - 1) / N;
@@ -1067,8 +1152,13 @@ int32_t tc_forward(const Problem& p, const void* packed, const void* x, const in
   kp.O = p.O;
   kp.flags = p.flags;
   kp.timeout_ns = (unsigned long long)p.timeout_ms * 1000000ull;
-  kp.fast_act = 0;
-  if (const char* e = std::getenv("PLSTM_TC_ACT")) kp.fast_act = std::string(e) == "fast" ? 1 : 0;
+  // Activations: f32 hardware tanh (one MUFU operation each) by default; the
+  // expf-based form and the f16x2 form stay selectable for accuracy studies.
+  kp.fast_act = 1;
+  if (const char* e = std::getenv("PLSTM_TC_ACT")) {
+    const std::string v(e);
+    kp.fast_act = v == "accurate" ? 0 : v == "fast2" ? 2 : 1;
+  }
   kp.drop_rank = -1;
   kp.drop_step = -1;
   kp.trace = nullptr;
@@ -1088,7 +1178,7 @@ int32_t tc_forward(const Problem& p, const void* packed, const void* x, const in
   PLSTM_TRY_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(pl.tiles * 2 * p.L), 1, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.blockDim = dim3((unsigned)threads_for(pl.N), 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   cudaLaunchAttribute attr;

@@ -1,0 +1,95 @@
+"""Microbenchmarks of the library's kernels (CUDA-event timed, one JSON line each).
+
+    python -m persistent_lstm_hip_b200.microbench gemm [--m 512000 --k 5 --n 512]
+        The input-projection GEMM (plstm_input_gemm) at the layer-0 shape of
+        config 2 (x[B*T, I] . W_ih^T for B=512, T=1000, I=5, 4H=512): achieved HBM
+        GB/s over its algorithmic bytes (read M*K + K*N, write M*N 16-bit values)
+        and TFLOP/s over 2*M*N*K.
+    python -m persistent_lstm_hip_b200.microbench step [--batch 16 --seq 1000]
+        The recurrent wavefront kernel on one cluster: per-step latency floor.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+
+import torch
+
+
+def _time(fn, iters: int, warmup: int) -> float:
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters)]
+    for a, b in ev:
+        a.record()
+        fn()
+        b.record()
+    torch.cuda.synchronize()
+    return sorted(a.elapsed_time(b) for a, b in ev)[iters // 2]
+
+
+def gemm(args) -> dict:
+    from .adaptive_ext import adaptive_lstm_input_gemm_forward_workspace
+
+    dev = torch.device("cuda:0")
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(args.m, args.k, generator=g).to(dev, torch.float16)
+    w = (torch.rand(args.k, args.n, generator=g) * 0.2 - 0.1).to(dev, torch.float16)
+    gate = torch.empty(args.m, args.n, device=dev, dtype=torch.float16)
+    ms = _time(lambda: adaptive_lstm_input_gemm_forward_workspace(x, w, gate), args.iters, 3)
+    nbytes = 2 * (args.m * args.k + args.k * args.n + args.m * args.n)
+    flops = 2.0 * args.m * args.n * args.k
+    return {"kernel": "plstm::gemm::input_gemm_kernel", "m": args.m, "k": args.k, "n": args.n, "ms": ms,
+            "algorithmic_bytes": nbytes, "gbs": nbytes / ms / 1e6, "tflops": flops / ms / 1e9}
+
+
+def step(args) -> dict:
+    from . import _lib, core
+
+    dev = torch.device("cuda:0")
+    torch.manual_seed(0)
+    lstm = torch.nn.LSTM(5, 128, 4, batch_first=True)
+    lin = torch.nn.Linear(128, 24)
+    h = lambda t: t.detach().to(dev, torch.float16).contiguous()
+    pw = core.PackedWeights([h(getattr(lstm, f"weight_ih_l{l}")) for l in range(4)],
+                            [h(getattr(lstm, f"weight_hh_l{l}")) for l in range(4)],
+                            [h(getattr(lstm, f"bias_ih_l{l}")) for l in range(4)],
+                            [h(getattr(lstm, f"bias_hh_l{l}")) for l in range(4)], h(lin.weight), h(lin.bias),
+                            out_mode="last")
+    x = torch.randn(args.batch, args.seq, 5, device=dev).half()
+    lib = _lib.load()
+    for _ in range(3):
+        pw.forward(x, need_state=False)
+    lib.plstm_profile(1)
+    ms, n = ctypes.c_float(0), ctypes.c_int32(0)
+    lib.plstm_profile_read(ctypes.byref(ms), ctypes.byref(n))
+    for _ in range(args.iters):
+        pw.forward(x, need_state=False)
+    torch.cuda.synchronize()
+    lib.plstm_profile_read(ctypes.byref(ms), ctypes.byref(n))
+    lib.plstm_profile(0)
+    k_ms = ms.value / max(n.value, 1)
+    return {"kernel": "plstm::tc::wavefront_kernel", "batch": args.batch, "seq": args.seq, "ms": k_ms,
+            "us_per_step": k_ms * 1e3 / (args.seq + 4)}
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    sub = ap.add_subparsers(dest="cmd", required=True)
+    g = sub.add_parser("gemm")
+    g.add_argument("--m", type=int, default=512 * 1000)
+    g.add_argument("--k", type=int, default=5)
+    g.add_argument("--n", type=int, default=512)
+    g.add_argument("--iters", type=int, default=20)
+    s = sub.add_parser("step")
+    s.add_argument("--batch", type=int, default=16)
+    s.add_argument("--seq", type=int, default=1000)
+    s.add_argument("--iters", type=int, default=10)
+    args = ap.parse_args()
+    print(json.dumps(gemm(args) if args.cmd == "gemm" else step(args)))
+
+
+if __name__ == "__main__":
+    main()

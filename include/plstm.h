@@ -136,6 +136,20 @@ PLSTM_API int32_t plstm_forward(const plstm_desc* d, const void* x, const void* 
                       const void* c0, void* out, void* h_n, void* c_n, void* workspace,
                       size_t workspace_bytes, void* stream);
 
+/* The forward for callers that cannot hand the library a device workspace
+ * (no counterpart in the reference): plugin hosts whose execute hook must not
+ * allocate device memory, and programs on a fixed device-memory budget after
+ * start-up.  Same contract as plstm_forward_packed for the f16 / bf16
+ * tensor-core path, but the scratch comes from a 24 MiB array the library
+ * keeps on every device it is loaded on; it allocates nothing.  Problems that
+ * need more scratch (plstm_workspace_size) are rejected with PLSTM_EINVAL.
+ * The first call on a device looks up that array's device address (make it
+ * before any stream capture).  All calls share the array: calls whose GPU work
+ * overlaps race and must be serialised by the caller. */
+PLSTM_API int32_t plstm_forward_packed_noalloc(const plstm_desc* d, const void* packed, const void* x,
+                                               const int32_t* lengths, const void* h0, const void* c0,
+                                               void* out, void* h_n, void* c_n, void* stream);
+
 /* Reads (and clears) the device status word the kernels of the last forward
  * using `workspace` left, synchronising `stream`.  *status receives PLSTM_OK
  * or PLSTM_ETIMEOUT; *detail the first failing (cta << 16 | step & 0xffff). */

@@ -52,6 +52,7 @@ PROTOTYPES = {
     "plstm_forward_packed": (_I32, [_DP, _P, _P, _P, _P, _P, _P, _P, _P, _P, _SZ, _P]),
     "plstm_forward": (_I32, [_DP, _P, _PP, _PP, _PP, _PP, _P, _P, _P, _P, _P, _P, _P, _P, _P, _SZ, _P]),
     "plstm_read_status": (_I32, [_P, _P, ctypes.POINTER(_I32), ctypes.POINTER(_I32)]),
+    "plstm_forward_packed_noalloc": (_I32, [_DP, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
     "plstm_ref4_workspace_size": (_I32, [_I32, _I32, _I32, _I32, _I32, ctypes.POINTER(_SZ)]),
     "plstm_persistent_lstm4_forward": (_I32, [_P, _I32, _I32, _I32, _I32, _I32, _PP, _PP, _PP, _P, _P, _P, _P, _SZ, _P]),
     "plstm_persistent_lstm4_forward_packed": (_I32, [_P, _I32, _I32, _I32, _I32, _I32, _PP, _PP, _PP, _P, _P, _P, _P, _SZ, _P]),

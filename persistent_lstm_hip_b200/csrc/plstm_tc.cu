@@ -16,11 +16,13 @@
 //     shared memory.  The per-step contraction gates^T[256 x N] = W . [x_t | h_{t-1}]^T
 //     runs as tcgen05.mma kind::f16 (f16/bf16 in, f32 accumulate in TMEM),
 //     M = 128 per instruction, N = batch tile.
-//   * The contraction is split in two: the input part W_ih . x_t is issued as
-//     soon as x_t (layer 0) or h_{l-1}(t) (from layer l-1) lands, into one of
-//     two TMEM accumulators, while the previous step's gates are still being
-//     processed; only the recurrent part W_hh . h_{t-1} (K = 128) sits on the
-//     step-to-step critical path.
+//   * The contraction is split in three: the input part W_ih . x_t (+ bias) is
+//     issued as soon as x_t (layer 0) or h_{l-1}(t) (from layer l-1) lands, into
+//     one of two TMEM accumulators, while the previous step's gates are still
+//     being processed; the recurrent part over this CTA's own 64 units of
+//     h_{t-1} is issued as soon as this CTA has written them; only the
+//     recurrent part over the sibling CTA's 64 units (K = 64, 8 MMAs) waits for
+//     the cross-CTA hand-off.
 //   * Layers run as a wavefront: layer l works on step t while layer l+1 works
 //     on step t-1.  The new h tile (64 units x N rows, 16-bit) is written once
 //     into this CTA's next B buffer and pushed to the sibling CTA (recurrent
@@ -393,22 +395,25 @@ __global__ void __launch_bounds__(Smem<N>::kThreads, 1) wavefront_kernel(const P
       }
       __syncwarp();
     };
-    // Recurrent part of step t (W_hh . h_{t-1}) and/or the Linear head on h_{t-1}; commit -> mma[t & 1].
-    auto issue_rec = [&](int t, bool gates, bool lin) {
+    auto issue_rec_half = [&](int t, int kb) {
       const int b = t & 1;
       if (ptx::elect_one()) {
         ptx::tc_fence_after();
         const uint64_t dB = dB0 + kBufStep * b;
-        if (gates) {
 #pragma unroll
-          for (int tau = 0; tau < 2; ++tau)
+        for (int tau = 0; tau < 2; ++tau)
 #pragma unroll
-            for (int kb = 0; kb < 2; ++kb)
-#pragma unroll
-              for (int kk = 0; kk < 4; ++kk)
-                ptx::mma_f16_ts(dcol(b, tau), tmem + (uint32_t)(tau * 128) + a_rec0 + (uint32_t)(32 * kb + 8 * kk),
-                                dB + (uint64_t)(((2 + kb) * S::kBKB + kk * 32) >> 4), idesc_g, 1u);
-        }
+          for (int kk = 0; kk < 4; ++kk)
+            ptx::mma_f16_ts(dcol(b, tau), tmem + (uint32_t)(tau * 128) + a_rec0 + (uint32_t)(32 * kb + 8 * kk),
+                            dB + (uint64_t)(((2 + kb) * S::kBKB + kk * 32) >> 4), idesc_g, 1u);
+      }
+      __syncwarp();
+    };
+    auto issue_lin_commit = [&](int t, bool lin) {
+      const int b = t & 1;
+      if (ptx::elect_one()) {
+        ptx::tc_fence_after();
+        const uint64_t dB = dB0 + kBufStep * b;
         if (lin) {
 #pragma unroll
           for (int kb = 0; kb < 2; ++kb)
@@ -477,6 +482,7 @@ __global__ void __launch_bounds__(Smem<N>::kThreads, 1) wavefront_kernel(const P
       const int b = t & 1;
       const bool gates = t < Tt;
       const bool lin = does_linear && (t == Tt || (MODE == kModeSeq && t >= 1));
+      if (gates) issue_rec_half(t, s);  // own half of h_{t-1}: written before the previous step ended
       if (t >= 1) {
         if (!warp_wait_phase(bar_rec + 8 * b, ((t - 1) >> 1) & 1, abort_flag, p.timeout_ns)) {
           fail(t);
@@ -487,7 +493,8 @@ __global__ void __launch_bounds__(Smem<N>::kThreads, 1) wavefront_kernel(const P
         __syncwarp();
       }
       if (lane == 0) trace_mark(p, rank, t, 0);
-      issue_rec(t, gates, lin);
+      if (gates) issue_rec_half(t, 1 - s);
+      issue_lin_commit(t, lin);
       last_commit = t;
       if (lane == 0) trace_mark(p, rank, t, 1);
       if (!gates) break;  // drain step issued

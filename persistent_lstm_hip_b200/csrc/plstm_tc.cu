@@ -16,7 +16,7 @@
 //     shared memory.  The per-step contraction gates^T[256 x N] = W . [x_t | h_{t-1}]^T
 //     runs as tcgen05.mma kind::f16 (f16/bf16 in, f32 accumulate in TMEM),
 //     M = 128 per instruction, N = batch tile.
-//   * The contraction is split in three: the input part W_ih . x_t (+ bias) is
+//   * The contraction is split in three: the input part W_ih . x_t is
 //     issued as soon as x_t (layer 0) or h_{l-1}(t) (from layer l-1) lands, into
 //     one of two TMEM accumulators, while the previous step's gates are still
 //     being processed; the recurrent part over this CTA's own 64 units of
@@ -62,8 +62,7 @@ constexpr int kH = 128;  // hidden size served (64 units per CTA)
 constexpr int kXK = 16;  // padded layer-0 input width (one MMA K step)
 constexpr int kABytes = 128 * 1024;                 // A image slot per CTA: [tile 2][row 128][K 256] 16-bit
 constexpr int kAK = 256;                            // K extent of an A image row
-constexpr int kTmemBias = 256;                      // TMEM columns [256, 272): bias K block of each tile
-constexpr int kTmemACols = 272;                     // TMEM columns holding A: 2 tiles x 128 + 2 x 8 bias
+constexpr int kTmemACols = 256;                     // TMEM columns holding A: 2 tiles x 128
 constexpr int kALinBytes = 32 * 1024;               // Linear head A image (2 K blocks)
 constexpr int kATileKB = 128 * 128;                 // one (M tile, 64-wide K block): 16 KB
 constexpr int kModeSeq = 0, kModeLast = 1, kModeHSeq = 2;
@@ -86,8 +85,7 @@ struct Smem {
   static constexpr int kB = 0;
   static constexpr int kBufBytes = 4 * kBKB;  // slots: [in0 | in1 | rec0 | rec1]
   static constexpr int kALin = kB + 2 * kBufBytes;
-  static constexpr int kOnes = kALin + kALinBytes;  // constant B block: columns 0, 1 = 1 (bias K block)
-  static constexpr int kBar = kOnes + ((kXBytes + 1023) / 1024) * 1024;
+  static constexpr int kBar = kALin + kALinBytes;
   // mbarriers (8 bytes each, two per kind: one per step parity)
   static constexpr int kFullIn = kBar, kFullRec = kBar + 16, kEmpty = kBar + 32, kHReady = kBar + 48,
                        kMma = kBar + 64;
@@ -130,6 +128,9 @@ struct Params {
   int trace_t0;
 };
 
+// Trace events: control warp 0 sibling h landed, 1 recurrent MMAs + commit issued,
+// 2 hready seen (copies follow), 3 own-half MMAs issued (loop top); compute warp 0:
+// 4 accumulators ready, 5 loaded, 6 h written; 7 h written by the last compute warp.
 constexpr int kTraceSteps = 64, kTraceEvents = 8;
 
 __device__ __forceinline__ void trace_mark(const Params& p, int rank, int t, int ev) {
@@ -137,10 +138,6 @@ __device__ __forceinline__ void trace_mark(const Params& p, int rank, int t, int
     p.trace[((size_t)rank * kTraceSteps + (t - p.trace_t0)) * kTraceEvents + ev] = clock64();
 }
 
-// No-swizzle K-major offset (core matrices 8 rows x 16 bytes, LBO 128, SBO 256) for K = 16.
-__device__ __forceinline__ uint32_t none16_off(int row, int k) {
-  return (uint32_t)((row >> 3) * 256 + (k >> 3) * 128 + (row & 7) * 16 + (k & 7) * 2);
-}
 // 128-byte swizzled K-major offset of element (row, k) of a 64-wide K block.
 __device__ __forceinline__ uint32_t sw128_off(int row, int k) {
   return (uint32_t)(row * 128 + ((((k >> 3) ^ (row & 7)) & 7) << 4) + (k & 7) * 2);
@@ -197,9 +194,10 @@ __device__ __forceinline__ bool warp_wait_phase(uint32_t bar, uint32_t parity, v
   if ((threadIdx.x & 31) == 0) ok = wait_phase(bar, parity, abort_flag, timeout_ns) ? 1 : 0;
   return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
-__device__ __forceinline__ bool warp_try_wait(uint32_t bar, uint32_t parity) {
+// Non-blocking: a warp that polls two barriers in turn must not sleep on one of them.
+__device__ __forceinline__ bool warp_test_wait(uint32_t bar, uint32_t parity) {
   int ok = 0;
-  if ((threadIdx.x & 31) == 0) ok = ptx::mbar_try_wait(bar, parity) ? 1 : 0;
+  if ((threadIdx.x & 31) == 0) ok = ptx::mbar_test_wait(bar, parity) ? 1 : 0;
   return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
 
@@ -302,21 +300,14 @@ __global__ void __launch_bounds__(Smem<N>::kThreads, 1) wavefront_kernel(const P
       *reinterpret_cast<uint16_t*>(b0 + (2 + (k >> 6)) * S::kBKB + sw128_off(n, k & 63)) = to_bits<BF16>(v);
     }
   }
-  for (int i = tid; i < N * kXK; i += kThreads) {
-    const int n = i / kXK, k = i % kXK;
-    *reinterpret_cast<uint16_t*>(sm + S::kOnes + none16_off(n, k)) = to_bits<BF16>(k < 2 ? 1.0f : 0.0f);
-  }
   ptx::fence_proxy_async_smem();
   ptx::tc_fence_after();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(sm + S::kTmemSlot);
   // This CTA's weight slice -> TMEM columns [0, 256), one A row per lane, K
-  // packed two 16-bit values per column; the bias of each row -> the tile's bias
-  // K block at [256 + 8 tile, +8): b = hi + lo split over K = 0, 1 (the B side
-  // holds 1 in both), so the MMA adds the f32-accurate bias.
+  // packed two 16-bit values per column.
   if (warp < kComputeWarps) {
     const int row = 32 * (warp & 3) + lane;
     const uint32_t lane_off = (uint32_t)(32 * (warp & 3)) << 16;
-    const float* bias_img = reinterpret_cast<const float*>(p.packed + packed_bias_off(p.L)) + rank * 256;
     for (int tau = warp >> 2; tau < 2; tau += G) {
       const uint4* src = reinterpret_cast<const uint4*>(p.packed + (size_t)rank * kABytes +
                                                         ((size_t)tau * 128 + row) * kAK * 2);
@@ -333,11 +324,6 @@ __global__ void __launch_bounds__(Smem<N>::kThreads, 1) wavefront_kernel(const P
         }
         ptx::tmem_st_32x32b_x32(tmem + lane_off + (uint32_t)(tau * 128 + c), r);
       }
-      const float bv = bias_img[tau * 128 + row];
-      const uint16_t hi = to_bits<BF16>(bv);
-      const uint16_t lo = to_bits<BF16>(bv - from_bits<BF16>(hi));
-      uint32_t rb[8] = {(uint32_t)hi | ((uint32_t)lo << 16), 0, 0, 0, 0, 0, 0, 0};
-      ptx::tmem_st_32x32b_x8(tmem + lane_off + (uint32_t)(kTmemBias + 8 * tau), rb);
     }
     ptx::tmem_wait_st();
   }
@@ -360,7 +346,6 @@ __global__ void __launch_bounds__(Smem<N>::kThreads, 1) wavefront_kernel(const P
     // W_hh at [8, 72); layers >= 1: W_ih at [0, 64), W_hh at [64, 128) (+128 per tile).
     const uint32_t a_rec0 = l == 0 ? 8u : 64u;
     const uint64_t dAl = ptx::desc_k_sw128(sbase + S::kALin);
-    const uint64_t dOnes = ptx::desc_k_none(sbase + S::kOnes, 128, 256);
     const uint64_t dB0 = ptx::desc_k_sw128(bbuf(0));
     const uint64_t dBx0 = ptx::desc_k_none(bbuf(0), 128, 256);
     constexpr uint64_t kBufStep = (uint64_t)(S::kBufBytes >> 4);
@@ -388,7 +373,6 @@ __global__ void __launch_bounds__(Smem<N>::kThreads, 1) wavefront_kernel(const P
                 ptx::mma_f16_ts(dcol(b, tau), a + (uint32_t)(32 * kb + 8 * kk),
                                 dB + (uint64_t)((kb * S::kBKB + kk * 32) >> 4), idesc_g, (kb | kk) != 0 ? 1u : 0u);
           }
-          ptx::mma_f16_ts(dcol(b, tau), tmem + (uint32_t)(kTmemBias + 8 * tau), dOnes, idesc_g, 1u);
         }
         // Layer l-1 may overwrite this input slot once these MMAs are done.
         if (l > 0 && t + 2 < Tt) ptx::mma_commit_mc(bar_empty + 8 * b, up_mask);
@@ -483,6 +467,7 @@ __global__ void __launch_bounds__(Smem<N>::kThreads, 1) wavefront_kernel(const P
       const bool gates = t < Tt;
       const bool lin = does_linear && (t == Tt || (MODE == kModeSeq && t >= 1));
       if (gates) issue_rec_half(t, s);  // own half of h_{t-1}: written before the previous step ended
+      if (lane == 0) trace_mark(p, rank, t, 3);
       if (t >= 1) {
         if (!warp_wait_phase(bar_rec + 8 * b, ((t - 1) >> 1) & 1, abort_flag, p.timeout_ns)) {
           fail(t);
@@ -503,14 +488,13 @@ __global__ void __launch_bounds__(Smem<N>::kThreads, 1) wavefront_kernel(const P
       bool in_pending = t + 1 < Tt, copy_pending = true;
       const unsigned long long t0 = ptx::globaltimer();
       while (in_pending || copy_pending) {
-        if (copy_pending && warp_try_wait(bar_hready + 8 * b, (t >> 1) & 1)) {
+        if (copy_pending && warp_test_wait(bar_hready + 8 * b, (t >> 1) & 1)) {
           if (lane == 0) trace_mark(p, rank, t, 2);
           hand_off(t);
-          if (lane == 0) trace_mark(p, rank, t, 3);
           copy_pending = false;
           continue;
         }
-        if (in_pending && warp_try_wait(bar_in + 8 * (b ^ 1), ((t + 1) >> 1) & 1)) {
+        if (in_pending && warp_test_wait(bar_in + 8 * (b ^ 1), ((t + 1) >> 1) & 1)) {
           issue_in(t + 1);
           if (t + 3 < Tt && ptx::elect_one()) ptx::mbar_arrive_expect_tx(bar_in + 8 * (b ^ 1), in_bytes);
           __syncwarp();
@@ -565,6 +549,16 @@ __global__ void __launch_bounds__(Smem<N>::kThreads, 1) wavefront_kernel(const P
           h_st[tau][jc][e] = hv;
           c_st[tau][jc][e] = cv;
         }
+    }
+    // f32 gate bias of this thread's two units (i, f, o rows pre-scaled by 1/2 like the
+    // weights), added to the accumulators in registers (the pointwise stage has spare issue slots).
+    float bz[2][4];
+    {
+      const float* bias_img = reinterpret_cast<const float*>(p.packed + packed_bias_off(p.L)) + rank * 256;
+#pragma unroll
+      for (int tau = 0; tau < 2; ++tau)
+#pragma unroll
+        for (int g = 0; g < 4; ++g) bz[tau][g] = bias_img[tau * 128 + 32 * q + 8 * g + j8];
     }
     const float* blin = reinterpret_cast<const float*>(p.packed + packed_blin_off(p.L));
     const bool lin_warp = does_linear && q == 0;
@@ -638,10 +632,10 @@ __global__ void __launch_bounds__(Smem<N>::kThreads, 1) wavefront_kernel(const P
           uint16_t hb[2];
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
-            ai[e] = __uint_as_float(rif[tau][4 * jc + e]);
-            af[e] = __uint_as_float(rif[tau][4 * jc + 2 + e]);
-            ag[e] = __uint_as_float(rgo[tau][4 * jc + e]);
-            ao[e] = __uint_as_float(rgo[tau][4 * jc + 2 + e]);
+            ai[e] = __uint_as_float(rif[tau][4 * jc + e]) + bz[tau][0];
+            af[e] = __uint_as_float(rif[tau][4 * jc + 2 + e]) + bz[tau][1];
+            ag[e] = __uint_as_float(rgo[tau][4 * jc + e]) + bz[tau][2];
+            ao[e] = __uint_as_float(rgo[tau][4 * jc + 2 + e]) + bz[tau][3];
           }
           if (act == 2) {
             // f16x2 hardware tanh: one MUFU operation per two cells and activation.
@@ -701,6 +695,7 @@ __global__ void __launch_bounds__(Smem<N>::kThreads, 1) wavefront_kernel(const P
       }
       ptx::fence_proxy_async_smem();
       if (tid == 0) trace_mark(p, rank, t, 6);
+      if (tid == 32 * (kComputeWarps - 1)) trace_mark(p, rank, t, 7);
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(bar_hready + 8 * b);
     }

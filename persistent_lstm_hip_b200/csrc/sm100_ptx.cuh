@@ -42,13 +42,27 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t byt
                "r"(bytes)
                : "memory");
 }
-// Returns true once the phase with parity `parity` has completed (acquire at
-// cluster scope: data delivered by remote CTAs' bulk copies is visible).
+// Returns true once the phase with parity `parity` has completed.  CTA-scope
+// acquire: bytes that bulk copies (from this or a peer CTA) delivered with
+// complete_tx on this barrier are visible once the phase completes.
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Non-blocking test of the same phase (try_wait may suspend the thread for a
+// while, which delays a warp that polls several barriers in turn).
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
       "selp.b32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
       : "r"(bar), "r"(parity)
@@ -86,6 +100,14 @@ __device__ __forceinline__ void bulk_s2c(uint32_t dst, uint32_t src, uint32_t by
       "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
       "r"(src), "r"(bytes), "r"(bar)
       : "memory");
+}
+// 16-byte store into a cluster peer's shared memory that completes as 16
+// transaction bytes on the peer's mbarrier (both shared::cluster addresses).
+__device__ __forceinline__ void st_async_v4(uint32_t dst, const uint4& v, uint32_t bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
+                   dst),
+               "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w), "r"(bar)
+               : "memory");
 }
 // Orders this thread's generic-proxy shared-memory writes before later
 // async-proxy (bulk copy, tensor core) reads of them.

@@ -121,11 +121,11 @@ struct Params {
   void* c_n;
   int* status;
   int B, T, L, O, flags;
-  int fast_act;  // activations: 0 = expf / fast divide, 1 = f32 tanh.approx, 2 = f16x2 tanh.approx
   unsigned long long timeout_ns;
   int drop_rank, drop_step;  // fault injection: rank that skips one sibling hand-off (-1 = off)
   unsigned long long* trace;  // PLSTM_FLAG_TRACE: [2L][64][8] clock64 stamps of cluster 0, or null
   int trace_t0;
+  int trace_slot;  // two-slot kernel: the slot whose events are recorded
 };
 
 // Trace events: control warp 0 sibling h landed, 1 recurrent MMAs + commit issued,
@@ -153,6 +153,17 @@ __device__ __forceinline__ uint16_t to_bits(float v) {
     return *reinterpret_cast<uint16_t*>(&h);
   }
 }
+// Two values rounded to 16 bits in one instruction: lo -> bits [0, 16), hi -> [16, 32).
+template <bool BF16>
+__device__ __forceinline__ uint32_t pack2_bits(float lo, float hi) {
+  if (BF16) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+  } else {
+    __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+  }
+}
 template <bool BF16>
 __device__ __forceinline__ float from_bits(uint16_t b) {
   if (BF16) {
@@ -162,16 +173,58 @@ __device__ __forceinline__ float from_bits(uint16_t b) {
   }
 }
 
-// Accurate activations: sigmoid(x) = 1 / (1 + e^-x) and tanh(x) = 2 sigmoid(2x) - 1
-// from the exponential intrinsic and the fast reciprocal-divide (two MUFU
-// operations each); the argument is clamped so that e^-x stays finite.
-__device__ __forceinline__ float sigmoid_mufu2(float x) {
-  x = fminf(fmaxf(x, -80.0f), 80.0f);
-  return __fdividef(1.0f, 1.0f + __expf(-x));
+// Gate math of one step for this thread's cells [tau][jc][e] (its two units x CPW
+// 8-column chunks x two columns).  rif / rgo hold the raw i, f / g, o accumulators
+// (gate rows i, f, o pre-scaled by 1/2), bz the f32 bias per unit and gate.  Every
+// activation is one hardware tanh: sigmoid(z) = (1 + tanh(z / 2)) / 2.  The four gate
+// activations of all cells are issued back to back (independent MUFU operations),
+// then the cell update, then tanh(c).  c stays f32; h is rounded to 16 bits in pairs.
+// Rows past their length keep c and h; hw receives the h bits to write.
+template <int CPW, bool BF16, bool VARLEN>
+__device__ __forceinline__ void lstm_cells(const uint32_t (&rif)[2][4 * CPW], const uint32_t (&rgo)[2][4 * CPW],
+                                           const float (&bz)[2][4], float (&c_st)[2][CPW][2],
+                                           uint16_t (&h_st)[2][CPW][2], const int (&len_c)[CPW][2], int t,
+                                           uint16_t (&hw)[2][CPW][2]) {
+  float ti[2][CPW][2], tf[2][CPW][2], tg[2][CPW][2], to[2][CPW][2];
+#pragma unroll
+  for (int tau = 0; tau < 2; ++tau)
+#pragma unroll
+    for (int jc = 0; jc < CPW; ++jc)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        ti[tau][jc][e] = ptx::tanh_approx(__uint_as_float(rif[tau][4 * jc + e]) + bz[tau][0]);
+        tf[tau][jc][e] = ptx::tanh_approx(__uint_as_float(rif[tau][4 * jc + 2 + e]) + bz[tau][1]);
+        tg[tau][jc][e] = ptx::tanh_approx(__uint_as_float(rgo[tau][4 * jc + e]) + bz[tau][2]);
+        to[tau][jc][e] = ptx::tanh_approx(__uint_as_float(rgo[tau][4 * jc + 2 + e]) + bz[tau][3]);
+      }
+  float c_new[2][CPW][2];
+#pragma unroll
+  for (int tau = 0; tau < 2; ++tau)
+#pragma unroll
+    for (int jc = 0; jc < CPW; ++jc)
+#pragma unroll
+      for (int e = 0; e < 2; ++e)
+        c_new[tau][jc][e] = fmaf(fmaf(0.5f, tf[tau][jc][e], 0.5f), c_st[tau][jc][e],
+                                 fmaf(0.5f, ti[tau][jc][e], 0.5f) * tg[tau][jc][e]);
+#pragma unroll
+  for (int tau = 0; tau < 2; ++tau)
+#pragma unroll
+    for (int jc = 0; jc < CPW; ++jc) {
+      float h[2];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) h[e] = fmaf(0.5f, to[tau][jc][e], 0.5f) * ptx::tanh_approx(c_new[tau][jc][e]);
+      const uint32_t bits = pack2_bits<BF16>(h[0], h[1]);
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const uint16_t hb = (uint16_t)(e == 0 ? bits & 0xffffu : bits >> 16);
+        if (!VARLEN || t < len_c[jc][e]) {
+          c_st[tau][jc][e] = c_new[tau][jc][e];
+          h_st[tau][jc][e] = hb;
+        }
+        hw[tau][jc][e] = h_st[tau][jc][e];
+      }
+    }
 }
-__device__ __forceinline__ float tanh_mufu2(float x) { return 2.0f * sigmoid_mufu2(2.0f * x) - 1.0f; }
-// Fast activations: one hardware tanh.approx each; sigmoid(x) = (1 + tanh(x/2)) / 2.
-__device__ __forceinline__ float sigmoid_mufu1(float x) { return fmaf(0.5f, ptx::tanh_approx(0.5f * x), 0.5f); }
 
 // Bounded wait on an mbarrier phase; false = gave up (timeout or cluster abort).
 __device__ __forceinline__ bool wait_phase(uint32_t bar, uint32_t parity, volatile int* abort_flag,
@@ -487,6 +540,7 @@ __global__ void __launch_bounds__(Smem<N>::kThreads, 1) wavefront_kernel(const P
       // (the hand-off first when both are).
       bool in_pending = t + 1 < Tt, copy_pending = true;
       const unsigned long long t0 = ptx::globaltimer();
+      unsigned spins = 0;
       while (in_pending || copy_pending) {
         if (copy_pending && warp_test_wait(bar_hready + 8 * b, (t >> 1) & 1)) {
           if (lane == 0) trace_mark(p, rank, t, 2);
@@ -501,11 +555,13 @@ __global__ void __launch_bounds__(Smem<N>::kThreads, 1) wavefront_kernel(const P
           in_pending = false;
           continue;
         }
-        int bad = 0;
-        if (lane == 0) bad = (*abort_flag != 0) || (ptx::globaltimer() - t0 > p.timeout_ns);
-        if (__shfl_sync(0xffffffffu, bad, 0)) {
-          fail(t);
-          break;
+        if ((++spins & 31) == 0) {  // abort / timeout checks are slow: every 32 polls
+          int bad = 0;
+          if (lane == 0) bad = (*abort_flag != 0) || (ptx::globaltimer() - t0 > p.timeout_ns);
+          if (__shfl_sync(0xffffffffu, bad, 0)) {
+            fail(t);
+            break;
+          }
         }
       }
     }
@@ -518,7 +574,6 @@ __global__ void __launch_bounds__(Smem<N>::kThreads, 1) wavefront_kernel(const P
     const int q = warp & 3, grp = warp >> 2;
     const int j8 = lane >> 2;          // unit within the quadrant's group of 8
     const int cpair = (lane & 3) * 2;  // first of the two batch columns in a chunk
-    const int act = p.fast_act;
     // cells: [tau][chunk j][e]
     float c_st[2][CPW][2];
     uint16_t h_st[2][CPW][2];  // h bits (the frozen value of finished rows)
@@ -620,78 +675,21 @@ __global__ void __launch_bounds__(Smem<N>::kThreads, 1) wavefront_kernel(const P
           break;
         }
       }
+      uint16_t hw[2][CPW][2];
+      lstm_cells<CPW, BF16, VARLEN>(rif, rgo, bz, c_st, h_st, len_c, t, hw);
       uint8_t* dst = sm + S::kB + (b ^ 1) * S::kBufBytes + (2 + s) * S::kBKB;
 #pragma unroll
       for (int tau = 0; tau < 2; ++tau) {
         const int ul = 8 * (4 * tau + q) + j8;  // unit within this CTA's 64
 #pragma unroll
-        for (int jc = 0; jc < CPW; ++jc) {
-          // Pre-activations of the cell pair (columns e = 0, 1).  Gate rows i, f, o
-          // are packed pre-scaled by 1/2, so sigmoid(z) = (1 + tanh(a)) / 2 with a = z / 2.
-          float ai[2], af[2], ag[2], ao[2], c_new[2];
-          uint16_t hb[2];
+        for (int jc = 0; jc < CPW; ++jc)
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
-            ai[e] = __uint_as_float(rif[tau][4 * jc + e]) + bz[tau][0];
-            af[e] = __uint_as_float(rif[tau][4 * jc + 2 + e]) + bz[tau][1];
-            ag[e] = __uint_as_float(rgo[tau][4 * jc + e]) + bz[tau][2];
-            ao[e] = __uint_as_float(rgo[tau][4 * jc + 2 + e]) + bz[tau][3];
-          }
-          if (act == 2) {
-            // f16x2 hardware tanh: one MUFU operation per two cells and activation.
-            const __half2 half2c = __float2half2_rn(0.5f);
-            const __half2 si = __hfma2(ptx::tanh_approx_h2(__floats2half2_rn(ai[0], ai[1])), half2c, half2c);
-            const __half2 sf = __hfma2(ptx::tanh_approx_h2(__floats2half2_rn(af[0], af[1])), half2c, half2c);
-            const __half2 so = __hfma2(ptx::tanh_approx_h2(__floats2half2_rn(ao[0], ao[1])), half2c, half2c);
-            const __half2 tg = ptx::tanh_approx_h2(__floats2half2_rn(ag[0], ag[1]));
-            const float2 ig = __half22float2(__hmul2(si, tg));
-            const float2 f2 = __half22float2(sf);
-            c_new[0] = fmaf(f2.x, c_st[tau][jc][0], ig.x);
-            c_new[1] = fmaf(f2.y, c_st[tau][jc][1], ig.y);
-            const __half2 h2 = __hmul2(so, ptx::tanh_approx_h2(__floats2half2_rn(c_new[0], c_new[1])));
-            if (BF16) {
-              const float2 hf = __half22float2(h2);
-              hb[0] = to_bits<true>(hf.x);
-              hb[1] = to_bits<true>(hf.y);
-            } else {
-              const uint32_t bits = *reinterpret_cast<const uint32_t*>(&h2);
-              hb[0] = (uint16_t)(bits & 0xffffu);
-              hb[1] = (uint16_t)(bits >> 16);
-            }
-          } else {
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              float h_new;
-              if (act == 1) {
-                c_new[e] = fmaf(fmaf(0.5f, ptx::tanh_approx(af[e]), 0.5f), c_st[tau][jc][e],
-                                fmaf(0.5f, ptx::tanh_approx(ai[e]), 0.5f) * ptx::tanh_approx(ag[e]));
-                h_new = fmaf(0.5f, ptx::tanh_approx(ao[e]), 0.5f) * ptx::tanh_approx(c_new[e]);
-              } else {
-                c_new[e] = sigmoid_mufu2(2.0f * af[e]) * c_st[tau][jc][e] +
-                           sigmoid_mufu2(2.0f * ai[e]) * tanh_mufu2(ag[e]);
-                h_new = sigmoid_mufu2(2.0f * ao[e]) * tanh_mufu2(c_new[e]);
-              }
-              hb[e] = to_bits<BF16>(h_new);
-            }
-          }
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            bool live = true;
-            if (VARLEN) live = t < len_c[jc][e];
-            uint16_t wb;
-            if (live) {
-              c_st[tau][jc][e] = c_new[e];
-              h_st[tau][jc][e] = hb[e];
-              wb = hb[e];
-            } else {
-              wb = h_st[tau][jc][e];
-            }
-            const int n = ncol[jc][e];
-            *reinterpret_cast<uint16_t*>(dst + sw128_off(n, ul)) = wb;
+            *reinterpret_cast<uint16_t*>(dst + sw128_off(ncol[jc][e], ul)) = hw[tau][jc][e];
             if (MODE == kModeHSeq && last_layer && bidx[jc][e] >= 0)
-              out16[((size_t)bidx[jc][e] * p.T + t) * kH + 64 * s + ul] = live ? hb[e] : (uint16_t)0;
+              out16[((size_t)bidx[jc][e] * p.T + t) * kH + 64 * s + ul] =
+                  (!VARLEN || t < len_c[jc][e]) ? hw[tau][jc][e] : (uint16_t)0;
           }
-        }
       }
       ptx::fence_proxy_async_smem();
       if (tid == 0) trace_mark(p, rank, t, 6);
@@ -755,6 +753,578 @@ __global__ void __launch_bounds__(Smem<N>::kThreads, 1) wavefront_kernel(const P
               static_cast<uint16_t*>(p.c_n)[idx] = to_bits<BF16>(c_st[tau][jc][e]);
           }
         }
+    }
+  }
+
+  // ---- teardown -----------------------------------------------------------------
+  if (*abort_flag) {
+    // Let bulk copies already in flight toward peers land before any CTA leaves.
+    const unsigned long long t0 = ptx::globaltimer();
+    while (ptx::globaltimer() - t0 < 50000ull) {
+    }
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem, S::kTmemCols);
+  }
+  ptx::cluster_sync();
+}
+
+// ---- two-slot wavefront kernel -------------------------------------------------------
+// Same cluster layout, weight residency and per-step protocol as wavefront_kernel, but
+// each cluster tile of N = 2 NH batch rows runs as two independent slots of NH rows.
+// The two recurrences have no data dependence on each other, so while one slot waits
+// on its MMA pipeline, its TMEM loads or the DSMEM hand-off to the sibling CTA, the
+// other slot's compute warps run their gate math: the latency of one slot's step is
+// hidden behind the other's MUFU work.  Each slot has its own compute warps (one per
+// TMEM lane quadrant), its own control warp, B buffers and barriers; the slots share
+// the CTA's resident weights (TMEM columns [0, 256)) and the Linear head's A image.
+// Each slot's gate accumulator is single-buffered (TMEM holds A + 2 slots x 2 tiles x
+// NH columns + the Linear tiles): the next step's input MMAs wait until the compute
+// warps have loaded the current accumulator ("dfree").
+template <int NH>
+struct Smem2 {
+  static constexpr int kBKB = NH * 128;             // one 64-wide K block of a slot's B operand
+  static constexpr int kXBytes = NH * 32;           // a slot's layer-0 x tile (K = 16, no swizzle)
+  static constexpr int kBufBytes = 4 * kBKB;        // [in0 | in1 | rec0 | rec1]
+  static constexpr int kSlotBytes = 2 * kBufBytes;  // step-parity double buffer
+  static constexpr int kB = 0;
+  static constexpr int kALin = kB + 2 * kSlotBytes;
+  static constexpr int kBar = kALin + kALinBytes;
+  // Per slot: six barrier kinds, one per step parity (8 bytes each).
+  static constexpr int kFullIn = 0, kFullRec = 16, kEmpty = 32, kHReady = 48, kMma = 64, kDFree = 80;
+  static constexpr int kBarSlot = 96;
+  static constexpr int kTmemSlot = kBar + 2 * kBarSlot, kAbort = kTmemSlot + 4, kDone = kTmemSlot + 8;
+  static constexpr int kPerm = kTmemSlot + 64, kLens = kPerm + 4 * 2 * NH;
+  static constexpr int kEnd = kLens + 4 * 2 * NH;
+  static constexpr int kDynBytes = kEnd + 1024;  // + alignment slack
+  static constexpr int CPW = NH / 8;               // 8-column chunks per compute warp (all NH columns)
+  static constexpr int kSlotWarps = 4;             // compute warps per slot: one per TMEM lane quadrant
+  static constexpr int kComputeWarps = 2 * kSlotWarps;
+  static constexpr int kThreads = (kComputeWarps + 2) * 32;  // + one control warp per slot
+  static constexpr bool kSplitLinear = (NH / 2) % 16 == 0;
+  static constexpr int kNL = kSplitLinear ? NH / 2 : NH;
+  static constexpr int kD = kTmemACols;            // D[slot][tau] at kD + (2 slot + tau) NH
+  static constexpr int kDLin = kD + 4 * NH;        // D_lin[slot] at kDLin + slot NL
+  static constexpr int kTmemCols = tmem_cols_for(kDLin + 2 * kNL);
+  static_assert(kDLin + 2 * kNL <= 512, "tile too wide for tensor memory");
+  static_assert(NH % 16 == 0 && CPW >= 2 && CPW <= 4, "slot width must be 16 or 32");
+};
+
+template <int NH, bool BF16, bool VARLEN, int MODE>
+__global__ void __launch_bounds__(Smem2<NH>::kThreads, 1) wavefront2_kernel(const Params p) {
+  using S = Smem2<NH>;
+  constexpr int N = 2 * NH;
+  constexpr int CPW = S::CPW;
+  constexpr int NL = S::kNL;
+  constexpr int kComputeWarps = S::kComputeWarps;
+  constexpr bool kHasLinear = MODE != kModeHSeq;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = ptx::smem_u32(sm);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int ncta = 2 * p.L;
+  const int rank = (int)ptx::cluster_ctarank();
+  const int l = rank >> 1, s = rank & 1;
+  const int tile = blockIdx.x / ncta;
+  const bool last_layer = l == p.L - 1;
+  const bool drain = kHasLinear && last_layer;
+  const bool does_linear = drain && (S::kSplitLinear || s == 0);
+  const bool sibling_linear = drain && (S::kSplitLinear || s == 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + S::kAbort);
+  int32_t* perm_s = reinterpret_cast<int32_t*>(sm + S::kPerm);
+  int32_t* lens_s = reinterpret_cast<int32_t*>(sm + S::kLens);
+  auto bar = [&](int sl, int kind, int par) -> uint32_t {
+    return sbase + (uint32_t)(S::kBar + sl * S::kBarSlot + kind + 8 * par);
+  };
+  auto bbuf = [&](int sl, int b) -> uint32_t {
+    return sbase + (uint32_t)(S::kB + sl * S::kSlotBytes + b * S::kBufBytes);
+  };
+
+  // ---- set-up ------------------------------------------------------------------
+  if (tid == 0) {
+    for (int sl = 0; sl < 2; ++sl)
+      for (int b = 0; b < 2; ++b) {
+        ptx::mbar_init(bar(sl, S::kFullIn, b), 1);
+        ptx::mbar_init(bar(sl, S::kFullRec, b), 1);
+        ptx::mbar_init(bar(sl, S::kEmpty, b), 2);
+        ptx::mbar_init(bar(sl, S::kHReady, b), S::kSlotWarps);
+        ptx::mbar_init(bar(sl, S::kMma, b), 1);
+        ptx::mbar_init(bar(sl, S::kDFree, b), S::kSlotWarps);
+      }
+    *abort_flag = 0;
+    reinterpret_cast<uint32_t*>(sm + S::kDone)[0] = 0;
+    reinterpret_cast<uint32_t*>(sm + S::kDone)[1] = 0;
+    ptx::fence_mbar_init_cluster();
+  }
+  if (warp == 0) {
+    ptx::tmem_alloc(sbase + S::kTmemSlot, S::kTmemCols);
+    ptx::tmem_relinquish();
+  }
+  for (int i = tid; i < N; i += S::kThreads) {
+    const int b = p.perm[tile * N + i];
+    perm_s[i] = b;
+    int len = 0;
+    if (b >= 0) len = VARLEN ? min(max(p.lengths[b], 0), p.T) : p.T;
+    lens_s[i] = len;
+  }
+  if (does_linear) {
+    const uint4* srcl = reinterpret_cast<const uint4*>(p.packed + packed_alin_off(p.L));
+    uint4* dstl = reinterpret_cast<uint4*>(sm + S::kALin);
+    for (int i = tid; i < kALinBytes / 16; i += S::kThreads) dstl[i] = srcl[i];
+  }
+  __syncthreads();  // perm_s / lens_s / tmem slot visible
+  // Initial recurrent state h0 -> both recurrent K blocks of each slot's B buffer 0.
+  for (int i = tid; i < N * kH; i += S::kThreads) {
+    const int n = i / kH, k = i % kH;
+    const int sl = n / NH, nn = n % NH;
+    float v = 0.0f;
+    const int b = perm_s[n];
+    if (p.h0 != nullptr && b >= 0) {
+      const uint16_t* h0 = static_cast<const uint16_t*>(p.h0);
+      v = from_bits<BF16>(h0[((size_t)l * p.B + b) * kH + k]);
+    }
+    *reinterpret_cast<uint16_t*>(sm + S::kB + sl * S::kSlotBytes + (2 + (k >> 6)) * S::kBKB +
+                                 sw128_off(nn, k & 63)) = to_bits<BF16>(v);
+  }
+  ptx::fence_proxy_async_smem();
+  ptx::tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(sm + S::kTmemSlot);
+  // This CTA's weight slice -> TMEM columns [0, 256): warps 0-3 store tile 0, warps
+  // 4-7 tile 1, each its lane quadrant's 32 rows.
+  if (warp < kComputeWarps) {
+    const int row = 32 * (warp & 3) + lane;
+    const uint32_t lane_off = (uint32_t)(32 * (warp & 3)) << 16;
+    const int tau = warp >> 2;
+    const uint4* src =
+        reinterpret_cast<const uint4*>(p.packed + (size_t)rank * kABytes + ((size_t)tau * 128 + row) * kAK * 2);
+#pragma unroll 1
+    for (int c = 0; c < kAK / 2; c += 32) {
+      uint32_t r[32];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const uint4 v = src[c / 4 + i];
+        r[4 * i + 0] = v.x;
+        r[4 * i + 1] = v.y;
+        r[4 * i + 2] = v.z;
+        r[4 * i + 3] = v.w;
+      }
+      ptx::tmem_st_32x32b_x32(tmem + lane_off + (uint32_t)(tau * 128 + c), r);
+    }
+    ptx::tmem_wait_st();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  ptx::cluster_sync();  // every CTA's barriers are initialised before any remote operation
+
+  // Each slot runs as many steps as its longest row (rows are sorted by length for
+  // variable lengths); a slot without rows does nothing.
+  auto slot_len = [&](int sl, bool* any) -> int {
+    int m = 0;
+    bool a = false;
+    for (int i = 0; i < NH; ++i) {
+      a |= perm_s[sl * NH + i] >= 0;
+      m = max(m, lens_s[sl * NH + i]);
+    }
+    *any = a;
+    return m;
+  };
+  auto dcol = [&](int sl, int tau) -> uint32_t { return tmem + (uint32_t)(S::kD + (2 * sl + tau) * NH); };
+
+  if (warp >= kComputeWarps) {
+    // ============================ control warps ==========================
+    const int sl = warp - kComputeWarps;
+    bool active = false;
+    const int Tt = slot_len(sl, &active);
+    const uint32_t xbytes = S::kXBytes, bkb = S::kBKB;
+    const uint32_t in_bytes = (l == 0) ? xbytes : 2 * bkb;
+    constexpr uint32_t idesc_g = ptx::idesc_f16(128, NH, BF16);
+    constexpr uint32_t idesc_l = ptx::idesc_f16(128, NL, BF16);
+    const uint16_t up_mask = l > 0 ? (uint16_t)(3u << (2 * (l - 1))) : 0;
+    const uint32_t a_rec0 = l == 0 ? 8u : 64u;  // A columns of W_hh within a tile
+    const uint64_t dAl = ptx::desc_k_sw128(sbase + S::kALin);
+    const uint64_t dB0 = ptx::desc_k_sw128(bbuf(sl, 0));
+    const uint64_t dBx0 = ptx::desc_k_none(bbuf(sl, 0), 128, 256);
+    constexpr uint64_t kBufStep = (uint64_t)(S::kBufBytes >> 4);
+    const uint32_t lin_row_off = S::kSplitLinear ? (uint32_t)(s * NL) * 128u : 0u;
+    const uint32_t dlin = tmem + (uint32_t)(S::kDLin + sl * NL);
+    const int steps = Tt + (does_linear ? 1 : 0);
+    int last_commit = -1;
+    bool ok = true;
+    const bool tracer = sl == p.trace_slot;
+
+    auto x_src = [&](int t) { return p.xp + (((size_t)tile * p.T + t) * N + (size_t)sl * NH) * 32; };
+    auto issue_in = [&](int t) {
+      const int b = t & 1;
+      if (ptx::elect_one()) {
+        ptx::tc_fence_after();
+        const uint64_t dB = dB0 + kBufStep * b;
+#pragma unroll
+        for (int tau = 0; tau < 2; ++tau) {
+          const uint32_t a = tmem + (uint32_t)(tau * 128);
+          if (l == 0) {
+            ptx::mma_f16_ts(dcol(sl, tau), a, dBx0 + kBufStep * b, idesc_g, 0u);
+          } else {
+#pragma unroll
+            for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+              for (int kk = 0; kk < 4; ++kk)
+                ptx::mma_f16_ts(dcol(sl, tau), a + (uint32_t)(32 * kb + 8 * kk),
+                                dB + (uint64_t)((kb * S::kBKB + kk * 32) >> 4), idesc_g, (kb | kk) != 0 ? 1u : 0u);
+          }
+        }
+        // Layer l-1 may overwrite this input slot once these MMAs are done.
+        if (l > 0 && t + 2 < Tt) ptx::mma_commit_mc(bar(sl, S::kEmpty, b), up_mask);
+      }
+      __syncwarp();
+    };
+    auto issue_rec_half = [&](int t, int kb) {
+      const int b = t & 1;
+      if (ptx::elect_one()) {
+        ptx::tc_fence_after();
+        const uint64_t dB = dB0 + kBufStep * b;
+#pragma unroll
+        for (int tau = 0; tau < 2; ++tau)
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            ptx::mma_f16_ts(dcol(sl, tau), tmem + (uint32_t)(tau * 128) + a_rec0 + (uint32_t)(32 * kb + 8 * kk),
+                            dB + (uint64_t)(((2 + kb) * S::kBKB + kk * 32) >> 4), idesc_g, 1u);
+      }
+      __syncwarp();
+    };
+    auto issue_lin_commit = [&](int t, bool lin) {
+      const int b = t & 1;
+      if (ptx::elect_one()) {
+        ptx::tc_fence_after();
+        const uint64_t dB = dB0 + kBufStep * b;
+        if (lin) {
+#pragma unroll
+          for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              ptx::mma_f16_ss(dlin, dAl + (uint64_t)((kb * kATileKB + kk * 32) >> 4),
+                              dB + (uint64_t)(((2 + kb) * S::kBKB + lin_row_off + kk * 32) >> 4), idesc_l,
+                              (kb | kk) != 0 ? 1u : 0u);
+        }
+        ptx::mma_commit(bar(sl, S::kMma, b));
+      }
+      __syncwarp();
+    };
+    auto fail = [&](int t) {
+      if (ptx::elect_one()) raise_abort(p, sm + S::kAbort, ncta, t);
+      __syncwarp();
+      ok = false;
+    };
+    // Pushes h(t) to the sibling CTA and to layer l+1, and (layer 0) streams x of
+    // step t+2 into the input slot step t has finished with.
+    auto hand_off = [&](int t) {
+      const int b = t & 1;
+      if (ptx::elect_one()) {
+        const uint32_t src = bbuf(sl, b ^ 1) + (2 + s) * bkb;
+        const bool to_sibling = (t + 1 < Tt) || (sibling_linear && t + 1 == Tt);
+        const bool dropped = sl == 0 && rank == p.drop_rank && t == p.drop_step;
+        if (to_sibling && !dropped) {
+          const uint32_t peer = (uint32_t)(rank ^ 1);
+          ptx::bulk_s2c(ptx::mapa(src, peer), src, bkb, ptx::mapa(bar(sl, S::kFullRec, b ^ 1), peer));
+        }
+        if (l + 1 < p.L) {
+          const uint32_t dst_local = bbuf(sl, b) + s * bkb;
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const uint32_t peer = (uint32_t)(2 * (l + 1) + j);
+            ptx::bulk_s2c(ptx::mapa(dst_local, peer), src, bkb, ptx::mapa(bar(sl, S::kFullIn, b), peer));
+          }
+        }
+        if (l == 0 && t + 2 < Tt) ptx::bulk_g2s(bbuf(sl, b), x_src(t + 2), xbytes, bar(sl, S::kFullIn, b));
+      }
+      __syncwarp();
+    };
+
+    if (active) {
+      // Prologue: expected bytes of steps 0 / 1 (inputs) and 1 / 2 (sibling h), x of steps 0 / 1.
+      if (ptx::elect_one()) {
+        for (int t = 0; t < 2 && t < Tt; ++t) {
+          ptx::mbar_arrive_expect_tx(bar(sl, S::kFullIn, t), in_bytes);
+          if (l == 0) ptx::bulk_g2s(bbuf(sl, t), x_src(t), xbytes, bar(sl, S::kFullIn, t));
+        }
+        for (int t = 1; t <= 2; ++t)
+          if (t < Tt || (does_linear && t == Tt)) ptx::mbar_arrive_expect_tx(bar(sl, S::kFullRec, t & 1), bkb);
+      }
+      __syncwarp();
+      if (Tt > 0) {
+        if (!warp_wait_phase(bar(sl, S::kFullIn, 0), 0, abort_flag, p.timeout_ns)) {
+          fail(0);
+        } else {
+          issue_in(0);
+          if (2 < Tt && ptx::elect_one()) ptx::mbar_arrive_expect_tx(bar(sl, S::kFullIn, 0), in_bytes);
+          __syncwarp();
+        }
+      }
+      for (int t = 0; ok && t < steps; ++t) {
+        const int b = t & 1;
+        const bool gates = t < Tt;
+        const bool lin = does_linear && (t == Tt || (MODE == kModeSeq && t >= 1));
+        if (gates) issue_rec_half(t, s);  // own half of h_{t-1}: written before the previous step ended
+        if (tracer && lane == 0) trace_mark(p, rank, t, 3);
+        if (t >= 1) {
+          if (!warp_wait_phase(bar(sl, S::kFullRec, b), ((t - 1) >> 1) & 1, abort_flag, p.timeout_ns)) {
+            fail(t);
+            break;
+          }
+          if ((t + 2 < Tt || (does_linear && t + 2 == Tt)) && ptx::elect_one())
+            ptx::mbar_arrive_expect_tx(bar(sl, S::kFullRec, b), bkb);
+          __syncwarp();
+        }
+        if (tracer && lane == 0) trace_mark(p, rank, t, 0);
+        if (gates) issue_rec_half(t, 1 - s);
+        issue_lin_commit(t, lin);
+        last_commit = t;
+        if (tracer && lane == 0) trace_mark(p, rank, t, 1);
+        if (!gates) break;  // drain step issued
+        // This step's h hand-off, and the next step's input MMAs once the compute
+        // warps have loaded this step's accumulator and the input has landed (the
+        // hand-off first when both are ready).
+        bool in_pending = t + 1 < Tt, copy_pending = true;
+        const unsigned long long t0 = ptx::globaltimer();
+        unsigned spins = 0;
+        while (in_pending || copy_pending) {
+          if (copy_pending && warp_test_wait(bar(sl, S::kHReady, b), (t >> 1) & 1)) {
+            if (tracer && lane == 0) trace_mark(p, rank, t, 2);
+            hand_off(t);
+            copy_pending = false;
+            continue;
+          }
+          if (in_pending && warp_test_wait(bar(sl, S::kDFree, b), (t >> 1) & 1) &&
+              warp_test_wait(bar(sl, S::kFullIn, b ^ 1), ((t + 1) >> 1) & 1)) {
+            issue_in(t + 1);
+            if (t + 3 < Tt && ptx::elect_one()) ptx::mbar_arrive_expect_tx(bar(sl, S::kFullIn, b ^ 1), in_bytes);
+            __syncwarp();
+            in_pending = false;
+            continue;
+          }
+          if ((++spins & 31) == 0) {  // abort / timeout checks are slow: every 32 polls
+            int bad = 0;
+            if (lane == 0) bad = (*abort_flag != 0) || (ptx::globaltimer() - t0 > p.timeout_ns);
+            if (__shfl_sync(0xffffffffu, bad, 0)) {
+              fail(t);
+              break;
+            }
+          }
+        }
+      }
+      // All MMAs must have completed before TMEM is released.
+      if (last_commit >= 0 && lane == 0)
+        wait_phase(bar(sl, S::kMma, last_commit & 1), (last_commit >> 1) & 1, abort_flag, p.timeout_ns);
+      __syncwarp();
+    }
+  } else {
+    // =========================== compute warps ===========================
+    const int sl = warp >> 2, q = warp & 3;
+    bool active = false, other_active = false;
+    const int Tt = slot_len(sl, &active);
+    const int T_other = slot_len(sl ^ 1, &other_active);
+    const int j8 = lane >> 2;          // unit within the quadrant's group of 8
+    const int cpair = (lane & 3) * 2;  // first of the two batch columns in a chunk
+    const bool tracer = sl == p.trace_slot;
+    // cells: [tau][chunk jc][e]; column within the slot nn = 8 jc + cpair + e
+    float c_st[2][CPW][2];
+    uint16_t h_st[2][CPW][2];  // h bits (the frozen value of finished rows)
+    int len_c[CPW][2], bidx[CPW][2];
+#pragma unroll
+    for (int jc = 0; jc < CPW; ++jc)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int n = sl * NH + 8 * jc + cpair + e;
+        len_c[jc][e] = lens_s[n];
+        bidx[jc][e] = perm_s[n];
+      }
+#pragma unroll
+    for (int tau = 0; tau < 2; ++tau) {
+      const int u = 64 * s + 8 * (4 * tau + q) + j8;
+#pragma unroll
+      for (int jc = 0; jc < CPW; ++jc)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int b = bidx[jc][e];
+          uint16_t hv = 0;
+          float cv = 0.0f;
+          if (b >= 0 && p.h0 != nullptr) {
+            hv = static_cast<const uint16_t*>(p.h0)[((size_t)l * p.B + b) * kH + u];
+            cv = from_bits<BF16>(static_cast<const uint16_t*>(p.c0)[((size_t)l * p.B + b) * kH + u]);
+          }
+          h_st[tau][jc][e] = hv;
+          c_st[tau][jc][e] = cv;
+        }
+    }
+    // f32 gate bias of this thread's two units (i, f, o rows pre-scaled by 1/2 like the
+    // weights), added to the accumulators in registers.
+    float bz[2][4];
+    {
+      const float* bias_img = reinterpret_cast<const float*>(p.packed + packed_bias_off(p.L)) + rank * 256;
+#pragma unroll
+      for (int tau = 0; tau < 2; ++tau)
+#pragma unroll
+        for (int g = 0; g < 4; ++g) bz[tau][g] = bias_img[tau * 128 + 32 * q + 8 * g + j8];
+    }
+    const float* blin = reinterpret_cast<const float*>(p.packed + packed_blin_off(p.L));
+    const bool lin_warp = does_linear && q == 0;
+    const int o = lane;  // Linear output row handled by this lane (lin_warp only)
+    const float blin_o = (lin_warp && o < p.O) ? blin[o] : 0.0f;
+    uint16_t* out16 = static_cast<uint16_t*>(p.out);
+    const int lin_n0 = sl * NH + (S::kSplitLinear ? s * NL : 0);  // first tile row of this CTA's Linear columns
+    const uint32_t dlin = tmem + (uint32_t)(S::kDLin + sl * NL);
+
+    // Stores the Linear outputs of step `ts` from the slot's Linear accumulator (lanes = output rows).
+    auto store_linear = [&](int ts, bool last_mode) {
+#pragma unroll
+      for (int c0 = 0; c0 < NL; c0 += 8) {
+        uint32_t r[8];
+        ptx::tmem_ld_32x32b_x8(dlin + (uint32_t)c0, r);
+        ptx::tmem_wait_ld();
+        if (o < p.O) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int n = lin_n0 + c0 + i;
+            const int b = perm_s[n];
+            if (b < 0) continue;
+            const float v = __uint_as_float(r[i]) + blin_o;
+            if (last_mode) {
+              out16[(size_t)b * p.O + o] = to_bits<BF16>(v);
+            } else {
+              const bool live = ts < lens_s[n];
+              out16[((size_t)b * p.T + ts) * p.O + o] = to_bits<BF16>(live ? v : 0.0f);
+            }
+          }
+        }
+      }
+    };
+
+    if (active) {
+      for (int t = 0; t < Tt; ++t) {
+        const int b = t & 1;
+        if (*abort_flag) break;
+        if (!wait_phase(bar(sl, S::kMma, b), (t >> 1) & 1, abort_flag, p.timeout_ns)) {
+          if (lane == 0) raise_abort(p, sm + S::kAbort, ncta, t);
+          break;
+        }
+        ptx::tc_fence_after();
+        if (tracer && q == 0 && lane == 0) trace_mark(p, rank, t, 4);
+        uint32_t rif[2][4 * CPW], rgo[2][4 * CPW];
+#pragma unroll
+        for (int tau = 0; tau < 2; ++tau) {
+          const uint32_t col = dcol(sl, tau);
+          tmem_ld_chunks<CPW>(col + ((uint32_t)(32 * q) << 16), rif[tau]);
+          tmem_ld_chunks<CPW>(col + ((uint32_t)(32 * q + 16) << 16), rgo[tau]);
+        }
+        ptx::tmem_wait_ld();
+        if (MODE == kModeSeq && lin_warp && t >= 1) store_linear(t - 1, false);
+        ptx::tc_fence_before();
+        // The accumulator may now be re-initialised by the next step's input MMAs.
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(bar(sl, S::kDFree, b));
+        if (tracer && q == 0 && lane == 0) trace_mark(p, rank, t, 5);
+
+        // Layer l+1 must have consumed h_{t-2} (same buffer and copy source) before it is overwritten.
+        if (l + 1 < p.L && t >= 2) {
+          if (!wait_phase(bar(sl, S::kEmpty, b), ((t - 2) >> 1) & 1, abort_flag, p.timeout_ns)) {
+            if (lane == 0) raise_abort(p, sm + S::kAbort, ncta, t);
+            break;
+          }
+        }
+        // The slots take turns on the MUFU pipes: slot 1 runs its gate math after
+        // slot 0's of the same step, slot 0 after slot 1's previous step, so that one
+        // slot's MMA / hand-off latency overlaps the other's gate math.
+        {
+          const int tt = sl == 1 ? t : t - 1;
+          if (other_active && tt >= 0 && tt < T_other &&
+              !wait_phase(bar(sl ^ 1, S::kHReady, tt & 1), (tt >> 1) & 1, abort_flag, p.timeout_ns)) {
+            if (lane == 0) raise_abort(p, sm + S::kAbort, ncta, t);
+            break;
+          }
+        }
+        uint16_t hw[2][CPW][2];
+        lstm_cells<CPW, BF16, VARLEN>(rif, rgo, bz, c_st, h_st, len_c, t, hw);
+        uint8_t* dst = sm + S::kB + sl * S::kSlotBytes + (b ^ 1) * S::kBufBytes + (2 + s) * S::kBKB;
+#pragma unroll
+        for (int tau = 0; tau < 2; ++tau) {
+          const int ul = 8 * (4 * tau + q) + j8;  // unit within this CTA's 64
+#pragma unroll
+          for (int jc = 0; jc < CPW; ++jc)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              *reinterpret_cast<uint16_t*>(dst + sw128_off(8 * jc + cpair + e, ul)) = hw[tau][jc][e];
+              if (MODE == kModeHSeq && last_layer && bidx[jc][e] >= 0)
+                out16[((size_t)bidx[jc][e] * p.T + t) * kH + 64 * s + ul] =
+                    (!VARLEN || t < len_c[jc][e]) ? hw[tau][jc][e] : (uint16_t)0;
+            }
+        }
+        ptx::fence_proxy_async_smem();
+        if (tracer && q == 0 && lane == 0) trace_mark(p, rank, t, 6);
+        if (tracer && q == 3 && lane == 0) trace_mark(p, rank, t, 7);
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(bar(sl, S::kHReady, b));
+      }
+      // Drain: Linear of the last step's h.
+      if (lin_warp && !*abort_flag) {
+        if (wait_phase(bar(sl, S::kMma, Tt & 1), (Tt >> 1) & 1, abort_flag, p.timeout_ns)) {
+          ptx::tc_fence_after();
+          if (MODE == kModeSeq) {
+            if (Tt >= 1) store_linear(Tt - 1, false);
+          } else {
+            store_linear(0, true);
+          }
+          ptx::tc_fence_before();
+        } else if (lane == 0) {
+          raise_abort(p, sm + S::kAbort, ncta, Tt);
+        }
+      }
+      // Outputs past the slot's last step are zero.
+      if (MODE == kModeSeq && lin_warp && o < p.O) {
+        for (int i = 0; i < NL; ++i) {
+          const int n = lin_n0 + i;
+          const int b = perm_s[n];
+          if (b < 0) continue;
+          for (int ts = Tt; ts < p.T; ++ts) out16[((size_t)b * p.T + ts) * p.O + o] = 0;
+        }
+      }
+      if (MODE == kModeHSeq && last_layer) {
+#pragma unroll
+        for (int tau = 0; tau < 2; ++tau) {
+          const int u = 64 * s + 8 * (4 * tau + q) + j8;
+#pragma unroll
+          for (int jc = 0; jc < CPW; ++jc)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const int bb = bidx[jc][e];
+              if (bb < 0) continue;
+              for (int ts = Tt; ts < p.T; ++ts) out16[((size_t)bb * p.T + ts) * kH + u] = 0;
+            }
+        }
+      }
+      // Final state.
+#pragma unroll
+      for (int tau = 0; tau < 2; ++tau) {
+        const int u = 64 * s + 8 * (4 * tau + q) + j8;
+#pragma unroll
+        for (int jc = 0; jc < CPW; ++jc)
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int bb = bidx[jc][e];
+            if (bb < 0) continue;
+            const size_t idx = ((size_t)l * p.B + bb) * kH + u;
+            if (p.h_n != nullptr) static_cast<uint16_t*>(p.h_n)[idx] = h_st[tau][jc][e];
+            if (p.c_n != nullptr) {
+              if (p.flags & PLSTM_FLAG_CN_F32)
+                static_cast<float*>(p.c_n)[idx] = c_st[tau][jc][e];
+              else
+                static_cast<uint16_t*>(p.c_n)[idx] = to_bits<BF16>(c_st[tau][jc][e]);
+            }
+          }
+      }
     }
   }
 
@@ -917,8 +1487,10 @@ __global__ void tc_xpack_kernel(const T16* __restrict__ x, const int32_t* __rest
 }
 
 // ---- host side ----------------------------------------------------------------------
+// slots = 1: wavefront_kernel with N-row tiles; slots = 2: wavefront2_kernel with
+// two slots of N / 2 rows per tile.
 struct Plan {
-  int N, tiles;
+  int N, tiles, slots;
 };
 
 template <int N, bool BF16, bool VARLEN, int MODE>
@@ -969,28 +1541,58 @@ int threads_for(int N) {
   }
 }
 
-// Max clusters of 2L CTAs (one per SM) co-resident on `device`; cached.
-int max_active_clusters(int device, int L, int N) {
+template <int NH, bool BF16, bool VARLEN, int MODE>
+void* kernel2_ptr() {
+  return reinterpret_cast<void*>(&wavefront2_kernel<NH, BF16, VARLEN, MODE>);
+}
+template <int NH>
+void* pick_kernel2(bool bf16, bool varlen, int mode) {
+#define PLSTM_TC_K(B, V, M) \
+  if (bf16 == B && varlen == V && mode == M) return kernel2_ptr<NH, B, V, M>();
+  PLSTM_TC_K(false, false, kModeSeq) PLSTM_TC_K(false, false, kModeLast) PLSTM_TC_K(false, false, kModeHSeq)
+  PLSTM_TC_K(false, true, kModeSeq) PLSTM_TC_K(false, true, kModeLast) PLSTM_TC_K(false, true, kModeHSeq)
+  PLSTM_TC_K(true, false, kModeSeq) PLSTM_TC_K(true, false, kModeLast) PLSTM_TC_K(true, false, kModeHSeq)
+  PLSTM_TC_K(true, true, kModeSeq) PLSTM_TC_K(true, true, kModeLast) PLSTM_TC_K(true, true, kModeHSeq)
+#undef PLSTM_TC_K
+  return nullptr;
+}
+// Kernel, dynamic shared memory and block size of a plan's launch.
+void* plan_kernel(const Plan& pl, bool bf16, bool varlen, int mode) {
+  if (pl.slots == 2) return pl.N == 32 ? pick_kernel2<16>(bf16, varlen, mode) : pick_kernel2<32>(bf16, varlen, mode);
+  return pick_kernel_n(pl.N, bf16, varlen, mode);
+}
+int plan_smem(const Plan& pl) {
+  if (pl.slots == 2) return pl.N == 32 ? Smem2<16>::kDynBytes : Smem2<32>::kDynBytes;
+  return smem_bytes_for(pl.N);
+}
+int plan_threads(const Plan& pl) {
+  if (pl.slots == 2) return pl.N == 32 ? Smem2<16>::kThreads : Smem2<32>::kThreads;
+  return threads_for(pl.N);
+}
+
+// Max clusters of 2L CTAs (one per SM) of a plan's kernel co-resident on `device`; cached.
+int max_active_clusters(int device, int L, const Plan& pl) {
   static std::mutex mu;
-  static int cache[64][5][3];
+  static int cache[64][5][4][2];
   static bool init = false;
   std::lock_guard<std::mutex> g(mu);
   if (!init) {
     for (auto& a : cache)
       for (auto& b : a)
-        for (auto& c : b) c = -1;
+        for (auto& c : b)
+          for (auto& d : c) d = -1;
     init = true;
   }
-  const int ni = N / 16 - 1;
+  const int ni = std::min(pl.N / 16, 4) - 1;
   if (device < 0 || device >= 64 || L < 1 || L > 4) return 1;
-  int& slot = cache[device][L][ni];
+  int& slot = cache[device][L][ni][pl.slots - 1];
   if (slot >= 0) return slot;
-  void* k = pick_kernel_n(N, false, false, kModeLast);
-  cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes_for(N));
+  void* k = plan_kernel(pl, false, false, kModeLast);
+  cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, plan_smem(pl));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * L * 64, 1, 1);
-  cfg.blockDim = dim3((unsigned)threads_for(N), 1, 1);
-  cfg.dynamicSmemBytes = smem_bytes_for(N);
+  cfg.blockDim = dim3((unsigned)plan_threads(pl), 1, 1);
+  cfg.dynamicSmemBytes = plan_smem(pl);
   cudaLaunchAttribute attr;
   attr.id = cudaLaunchAttributeClusterDimension;
   attr.val.clusterDim.x = 2 * L;
@@ -1009,18 +1611,28 @@ int max_active_clusters(int device, int L, int N) {
 
 Plan make_plan(const Problem& p) {
   Plan pl;
-  // The smallest tile whose clusters all fit on the GPU at once (one wave);
-  // beyond that the widest tile (fewest waves).
-  int N = 48;
-  for (int n : kTileNs) {
-    if ((p.B + n - 1) / n <= max_active_clusters(p.device, p.L, n)) {
-      N = n;
+  // Two-slot tiles of 32 or 64 rows by default (PLSTM_TC_KERNEL=1 selects the
+  // single-slot kernel with 16 / 32 / 48-row tiles).  The smallest tile whose
+  // clusters all fit on the GPU at once (one wave); beyond that the widest tile.
+  pl.slots = 2;
+  if (const char* e = std::getenv("PLSTM_TC_KERNEL"))
+    if (std::atoi(e) == 1) pl.slots = 1;
+  static constexpr int kTile2Ns[2] = {32, 64};
+  const int* ns = pl.slots == 2 ? kTile2Ns : kTileNs;
+  const int nn = pl.slots == 2 ? 2 : 3;
+  int N = ns[nn - 1];
+  for (int i = 0; i < nn; ++i) {
+    Plan c = pl;
+    c.N = ns[i];
+    if ((p.B + ns[i] - 1) / ns[i] <= max_active_clusters(p.device, p.L, c)) {
+      N = ns[i];
       break;
     }
   }
   if (const char* e = std::getenv("PLSTM_TC_NTILE")) {
     const int v = std::atoi(e);
-    if (v == 16 || v == 32 || v == 48) N = v;
+    for (int i = 0; i < nn; ++i)
+      if (v == ns[i]) N = v;
   }
   pl.N = N;
   pl.tiles = (p.B + N - 1) / N;
@@ -1154,17 +1766,12 @@ int32_t tc_forward(const Problem& p, const void* packed, const void* x, const in
   kp.O = p.O;
   kp.flags = p.flags;
   kp.timeout_ns = (unsigned long long)p.timeout_ms * 1000000ull;
-  // Activations: f32 hardware tanh (one MUFU operation each) by default; the
-  // expf-based form and the f16x2 form stay selectable for accuracy studies.
-  kp.fast_act = 1;
-  if (const char* e = std::getenv("PLSTM_TC_ACT")) {
-    const std::string v(e);
-    kp.fast_act = v == "accurate" ? 0 : v == "fast2" ? 2 : 1;
-  }
   kp.drop_rank = -1;
   kp.drop_step = -1;
   kp.trace = nullptr;
   kp.trace_t0 = p.T / 2;
+  kp.trace_slot = 0;
+  if (const char* e = std::getenv("PLSTM_TC_TRACE_SLOT")) kp.trace_slot = std::atoi(e) == 1 ? 1 : 0;
   if (p.flags & PLSTM_FLAG_TRACE) {
     kp.trace = reinterpret_cast<unsigned long long*>(wsb + w.trace);
     PLSTM_TRY_CUDA(cudaMemsetAsync(kp.trace, 0, (size_t)2 * p.L * kTraceSteps * kTraceEvents * 8, s));
@@ -1175,12 +1782,12 @@ int32_t tc_forward(const Problem& p, const void* packed, const void* x, const in
   }
   const bool bf16 = p.dtype == PLSTM_BF16;
   const int mode = mode_of(p);
-  void* k = pick_kernel_n(pl.N, bf16, lengths != nullptr, mode);
-  const int smem = smem_bytes_for(pl.N);
+  void* k = plan_kernel(pl, bf16, lengths != nullptr, mode);
+  const int smem = plan_smem(pl);
   PLSTM_TRY_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(pl.tiles * 2 * p.L), 1, 1);
-  cfg.blockDim = dim3((unsigned)threads_for(pl.N), 1, 1);
+  cfg.blockDim = dim3((unsigned)plan_threads(pl), 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   cudaLaunchAttribute attr;

@@ -89,7 +89,7 @@ struct Smem {
   // mbarriers (8 bytes each, two per kind: one per step parity)
   static constexpr int kFullIn = kBar, kFullRec = kBar + 16, kEmpty = kBar + 32, kHReady = kBar + 48,
                        kMma = kBar + 64;
-  static constexpr int kTmemSlot = kBar + 96, kAbort = kBar + 100;
+  static constexpr int kTmemSlot = kBar + 96, kAbort = kBar + 100, kDone = kBar + 104;
   static constexpr int kPerm = kBar + 128, kLens = kPerm + 4 * N;
   static constexpr int kEnd = kLens + 4 * N;
   static constexpr int kDynBytes = kEnd + 1024;  // + alignment slack
@@ -254,6 +254,25 @@ __device__ __forceinline__ bool warp_test_wait(uint32_t bar, uint32_t parity) {
   return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
 
+// Pushes this CTA's half of h(t) (`bytes` at shared address `src`) to the sibling
+// CTA (recurrent half of its next step: same local offset, barrier `sib_bar`) and to
+// both CTAs of layer l+1 (input slot `in_dst`, barrier `in_bar`).  Issued by the last
+// compute warp to finish the step, right after its writes.
+__device__ __forceinline__ void push_h(uint32_t src, uint32_t bytes, int rank, bool to_sibling, uint32_t sib_bar,
+                                       bool downstream, int next_layer_rank0, uint32_t in_dst, uint32_t in_bar) {
+  if (to_sibling) {
+    const uint32_t peer = (uint32_t)(rank ^ 1);
+    ptx::bulk_s2c(ptx::mapa(src, peer), src, bytes, ptx::mapa(sib_bar, peer));
+  }
+  if (downstream) {
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const uint32_t peer = (uint32_t)(next_layer_rank0 + j);
+      ptx::bulk_s2c(ptx::mapa(in_dst, peer), src, bytes, ptx::mapa(in_bar, peer));
+    }
+  }
+}
+
 // Raises the abort flag in every CTA of the cluster and records the failure.
 __device__ __forceinline__ void raise_abort(const Params& p, uint8_t* sm_abort, int ncta, int step) {
   const uint32_t local = ptx::smem_u32(sm_abort);
@@ -318,6 +337,7 @@ __global__ void __launch_bounds__(Smem<N>::kThreads, 1) wavefront_kernel(const P
       ptx::mbar_init(bar_mma + 8 * b, 1);
     }
     *abort_flag = 0;
+    *reinterpret_cast<uint32_t*>(sm + S::kDone) = 0;
     ptx::fence_mbar_init_cluster();
   }
   if (warp == 0) {
@@ -491,28 +511,11 @@ __global__ void __launch_bounds__(Smem<N>::kThreads, 1) wavefront_kernel(const P
         __syncwarp();
       }
     }
-    // Pushes h(t) to the sibling CTA and to layer l+1, and (layer 0) streams x of
-    // step t+2 into the input slot step t has finished with.
+    // Layer 0: streams x of step t+2 into the input slot step t has finished with
+    // (h(t) itself is pushed by the last compute warp to finish the step).
     auto hand_off = [&](int t) {
       const int b = t & 1;
-      if (ptx::elect_one()) {
-        const uint32_t src = bbuf(b ^ 1) + (2 + s) * bkb;
-        const bool to_sibling = (t + 1 < Tt) || (sibling_linear && t + 1 == Tt);
-        const bool dropped = rank == p.drop_rank && t == p.drop_step;
-        if (to_sibling && !dropped) {
-          const uint32_t peer = (uint32_t)(rank ^ 1);
-          ptx::bulk_s2c(ptx::mapa(src, peer), src, bkb, ptx::mapa(bar_rec + 8 * (b ^ 1), peer));
-        }
-        if (l + 1 < p.L) {
-          const uint32_t dst_local = bbuf(b) + s * bkb;
-#pragma unroll
-          for (int j = 0; j < 2; ++j) {
-            const uint32_t peer = (uint32_t)(2 * (l + 1) + j);
-            ptx::bulk_s2c(ptx::mapa(dst_local, peer), src, bkb, ptx::mapa(bar_in + 8 * b, peer));
-          }
-        }
-        if (l == 0 && t + 2 < Tt) ptx::bulk_g2s(bbuf(b), x_src(t + 2), xbytes, bar_in + 8 * b);
-      }
+      if (l == 0 && t + 2 < Tt && ptx::elect_one()) ptx::bulk_g2s(bbuf(b), x_src(t + 2), xbytes, bar_in + 8 * b);
       __syncwarp();
     };
     for (int t = 0; ok && t < steps; ++t) {
@@ -695,7 +698,18 @@ __global__ void __launch_bounds__(Smem<N>::kThreads, 1) wavefront_kernel(const P
       if (tid == 0) trace_mark(p, rank, t, 6);
       if (tid == 32 * (kComputeWarps - 1)) trace_mark(p, rank, t, 7);
       __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(bar_hready + 8 * b);
+      if (lane == 0) {
+        ptx::mbar_arrive(bar_hready + 8 * b);  // the control warp: own half of the next step's MMAs
+        // The last warp to finish pushes the tile (acquire-release counter: the other
+        // warps' writes, fenced for the async proxy, are ordered before its copies).
+        if (ptx::atom_add_acq_rel_smem(sbase + S::kDone, 1u) % (uint32_t)kComputeWarps == kComputeWarps - 1u) {
+          const bool to_sibling = ((t + 1 < Tt) || (sibling_linear && t + 1 == Tt)) &&
+                                  !(rank == p.drop_rank && t == p.drop_step);
+          push_h(sbase + (uint32_t)(S::kB + (b ^ 1) * S::kBufBytes + (2 + s) * S::kBKB), S::kBKB, rank, to_sibling,
+                 bar_rec + 8 * (b ^ 1), l + 1 < p.L, 2 * (l + 1),
+                 sbase + (uint32_t)(S::kB + b * S::kBufBytes + s * S::kBKB), bar_in + 8 * b);
+        }
+      }
     }
     // Drain: Linear of the last step's h.
     if (lin_warp && !*abort_flag) {
@@ -1019,28 +1033,12 @@ __global__ void __launch_bounds__(Smem2<NH>::kThreads, 1) wavefront2_kernel(cons
       __syncwarp();
       ok = false;
     };
-    // Pushes h(t) to the sibling CTA and to layer l+1, and (layer 0) streams x of
-    // step t+2 into the input slot step t has finished with.
+    // Layer 0: streams x of step t+2 into the input slot step t has finished with
+    // (h(t) itself is pushed by the slot's last compute warp to finish the step).
     auto hand_off = [&](int t) {
       const int b = t & 1;
-      if (ptx::elect_one()) {
-        const uint32_t src = bbuf(sl, b ^ 1) + (2 + s) * bkb;
-        const bool to_sibling = (t + 1 < Tt) || (sibling_linear && t + 1 == Tt);
-        const bool dropped = sl == 0 && rank == p.drop_rank && t == p.drop_step;
-        if (to_sibling && !dropped) {
-          const uint32_t peer = (uint32_t)(rank ^ 1);
-          ptx::bulk_s2c(ptx::mapa(src, peer), src, bkb, ptx::mapa(bar(sl, S::kFullRec, b ^ 1), peer));
-        }
-        if (l + 1 < p.L) {
-          const uint32_t dst_local = bbuf(sl, b) + s * bkb;
-#pragma unroll
-          for (int j = 0; j < 2; ++j) {
-            const uint32_t peer = (uint32_t)(2 * (l + 1) + j);
-            ptx::bulk_s2c(ptx::mapa(dst_local, peer), src, bkb, ptx::mapa(bar(sl, S::kFullIn, b), peer));
-          }
-        }
-        if (l == 0 && t + 2 < Tt) ptx::bulk_g2s(bbuf(sl, b), x_src(t + 2), xbytes, bar(sl, S::kFullIn, b));
-      }
+      if (l == 0 && t + 2 < Tt && ptx::elect_one())
+        ptx::bulk_g2s(bbuf(sl, b), x_src(t + 2), xbytes, bar(sl, S::kFullIn, b));
       __syncwarp();
     };
 
@@ -1266,7 +1264,18 @@ __global__ void __launch_bounds__(Smem2<NH>::kThreads, 1) wavefront2_kernel(cons
         if (tracer && q == 0 && lane == 0) trace_mark(p, rank, t, 6);
         if (tracer && q == 3 && lane == 0) trace_mark(p, rank, t, 7);
         __syncwarp();
-        if (lane == 0) ptx::mbar_arrive(bar(sl, S::kHReady, b));
+        if (lane == 0) {
+          ptx::mbar_arrive(bar(sl, S::kHReady, b));  // the control warp: own half of the next step's MMAs
+          // The slot's last warp to finish pushes the tile (acquire-release counter: the
+          // other warps' writes, fenced for the async proxy, are ordered before its copies).
+          if (ptx::atom_add_acq_rel_smem(sbase + S::kDone + 4 * sl, 1u) % 4u == 3u) {
+            const bool to_sibling = ((t + 1 < Tt) || (sibling_linear && t + 1 == Tt)) &&
+                                    !(sl == 0 && rank == p.drop_rank && t == p.drop_step);
+            push_h(bbuf(sl, b ^ 1) + (uint32_t)((2 + s) * S::kBKB), S::kBKB, rank, to_sibling,
+                   bar(sl, S::kFullRec, b ^ 1), l + 1 < p.L, 2 * (l + 1), bbuf(sl, b) + (uint32_t)(s * S::kBKB),
+                   bar(sl, S::kFullIn, b));
+          }
+        }
       }
       // Drain: Linear of the last step's h.
       if (lin_warp && !*abort_flag) {

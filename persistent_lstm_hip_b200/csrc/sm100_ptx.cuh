@@ -70,6 +70,14 @@ __device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Atomic add on a shared-memory word with acquire-release semantics at CTA
+// scope; returns the previous value.
+__device__ __forceinline__ uint32_t atom_add_acq_rel_smem(uint32_t addr, uint32_t v) {
+  uint32_t old;
+  asm volatile("atom.acq_rel.cta.shared::cta.add.u32 %0, [%1], %2;" : "=r"(old) : "r"(addr), "r"(v) : "memory");
+  return old;
+}
+
 // ---- cluster -------------------------------------------------------------------
 __device__ __forceinline__ uint32_t mapa(uint32_t local_addr, uint32_t rank) {
   uint32_t r;

@@ -138,7 +138,7 @@ def measured_peak():
 
 def profiled_traffic():
     """Per-launch DRAM bytes of the recurrent kernel from the committed ncu summary, if any."""
-    path = os.path.join(ROOT, "profiles", "wavefront_kernel_cfg2.md")
+    path = os.path.join(ROOT, "profiles", "wavefront2_kernel_cfg2.md")
     try:
         for line in open(path):
             if line.startswith("traffic_bytes_per_launch:"):
@@ -326,7 +326,8 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         t_step_us = k16 * 1e3 / (T + L)
         bound_ms = t_step_us * (T + L) / 1e3
         lat = {"t_step_us": t_step_us, "steps": T + L,
-               "method": "same kernel, B=16 (one 8-CTA cluster, N=16 tile), T=1000, CUDA events, 10 runs",
+               "method": "same kernel, B=16 (one 8-CTA cluster, one active 16-row slot), T=1000, "
+                         "CUDA events, 10 runs",
                "bound_ms": bound_ms, "frac": bound_ms / kernel_ms}
 
     if rank != 0:
@@ -339,7 +340,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     flops = flops_per_forward(B_PER_GPU, T, "last")
     achieved = flops / (kernel_ms / 1e3) / 1e12
     roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-            "traffic": profiled_traffic(), "kernel": "plstm::tc::wavefront_kernel", "kernel_ms": kernel_ms,
+            "traffic": profiled_traffic(), "kernel": "plstm::tc::wavefront2_kernel", "kernel_ms": kernel_ms,
             "peak_note": peak_note,
             "algorithmic_flops_per_launch": flops,
             "latency": lat}

@@ -119,6 +119,25 @@ int32_t tc_forward(const Problem& p, const void* packed, const void* x, const in
                    const void* h0, const void* c0, void* out, void* h_n, void* c_n, void* ws,
                    cudaStream_t s);
 
+// Tile row order shared by the tensor-core backends: perm[tiles * N] = batch row of
+// each tile row (-1 = padding), tile_len[tiles] = steps of each tile.  Uniform
+// lengths keep batch order; variable lengths sort rows by length, longest first
+// (hist / sorted: (T + 1) and B int32 scratch words).
+int32_t tc_make_perm(const Problem& p, int N, int tiles, const int32_t* lengths, int32_t* perm, int32_t* tile_len,
+                     int32_t* hist, int32_t* sorted, cudaStream_t s);
+
+// tcgen05 layer-sequential backend for H = 256 / 512 (plstm_tcl.cu): per layer a
+// projection GEMM and a cluster-wide recurrence; the H128 entry points above
+// forward these sizes to it.
+bool tcl_supported(const Problem& p, std::string* why);
+size_t tcl_packed_size(const Problem& p);
+size_t tcl_workspace_size(const Problem& p);
+int32_t tcl_pack(const Problem& p, int ih_layout, int hh_layout, const void* const* w_ih, const void* const* w_hh,
+                 const void* const* b_ih, const void* const* b_hh, const void* w_lin, const void* b_lin,
+                 void* packed, cudaStream_t s);
+int32_t tcl_forward(const Problem& p, const void* packed, const void* x, const int32_t* lengths, const void* h0,
+                    const void* c0, void* out, void* h_n, void* c_n, void* ws, cudaStream_t s);
+
 // Reads element (r, k) of a [4H or O][K] weight given in any PLSTM_W_* layout.
 __device__ __forceinline__ int64_t weight_src_index(int layout, int rows, int K, int r, int k) {
   if (layout == PLSTM_W_TRANSPOSED) return (int64_t)k * rows + r;

@@ -1675,7 +1675,28 @@ TcWs tc_ws(const Problem& p, const Plan& pl) {
 
 using namespace tc;
 
+int32_t tc_make_perm(const Problem& p, int N, int tiles, const int32_t* lengths, int32_t* perm, int32_t* tile_len,
+                     int32_t* hist, int32_t* sorted, cudaStream_t s) {
+  const int nthr = 256;
+  const int nperm = tiles * N;
+  if (lengths == nullptr) {
+    tc_perm_uniform_kernel<<<(nperm + nthr - 1) / nthr, nthr, 0, s>>>(perm, tile_len, p.B, p.T, N, tiles);
+    note_launches(1);
+  } else {
+    PLSTM_TRY_CUDA(cudaMemsetAsync(hist, 0, (size_t)(p.T + 1) * 4, s));
+    tc_len_hist_kernel<<<(p.B + nthr - 1) / nthr, nthr, 0, s>>>(lengths, p.B, p.T, hist);
+    tc_len_scan_kernel<<<1, 32, 0, s>>>(hist, p.T + 1);
+    tc_len_scatter_kernel<<<(p.B + nthr - 1) / nthr, nthr, 0, s>>>(lengths, p.B, p.T, hist, sorted);
+    tc_perm_varlen_kernel<<<(nperm + nthr - 1) / nthr, nthr, 0, s>>>(sorted, lengths, perm, tile_len, p.B, p.T, N,
+                                                                      tiles);
+    note_launches(4);
+  }
+  PLSTM_TRY_CUDA(cudaGetLastError());
+  return PLSTM_OK;
+}
+
 bool tc_supported(const Problem& p, std::string* why) {
+  if (p.H == 256 || p.H == 512) return tcl_supported(p, why);
   auto no = [&](const char* m) {
     if (why) *why = m;
     return false;
@@ -1696,13 +1717,14 @@ bool tc_supported(const Problem& p, std::string* why) {
   return true;
 }
 
-size_t tc_packed_size(const Problem& p) { return packed_total(p.L); }
+size_t tc_packed_size(const Problem& p) { return p.H == kH ? packed_total(p.L) : tcl_packed_size(p); }
 
-size_t tc_workspace_size(const Problem& p) { return tc_ws(p, make_plan(p)).total; }
+size_t tc_workspace_size(const Problem& p) { return p.H == kH ? tc_ws(p, make_plan(p)).total : tcl_workspace_size(p); }
 
 int32_t tc_pack(const Problem& p, int ih_layout, int hh_layout, const void* const* w_ih,
                 const void* const* w_hh, const void* const* b_ih, const void* const* b_hh,
                 const void* w_lin, const void* b_lin, void* packed, cudaStream_t s) {
+  if (p.H != kH) return tcl_pack(p, ih_layout, hh_layout, w_ih, w_hh, b_ih, b_hh, w_lin, b_lin, packed, s);
   PackArgs a = {};
   for (int l = 0; l < p.L; ++l) {
     a.w_ih[l] = w_ih[l];
@@ -1727,28 +1749,18 @@ int32_t tc_pack(const Problem& p, int ih_layout, int hh_layout, const void* cons
 int32_t tc_forward(const Problem& p, const void* packed, const void* x, const int32_t* lengths,
                    const void* h0, const void* c0, void* out, void* h_n, void* c_n, void* ws,
                    cudaStream_t s) {
+  if (p.H != kH) return tcl_forward(p, packed, x, lengths, h0, c0, out, h_n, c_n, ws, s);
   const Plan pl = make_plan(p);
   const TcWs w = tc_ws(p, pl);
   uint8_t* wsb = static_cast<uint8_t*>(ws);
   int32_t* perm = reinterpret_cast<int32_t*>(wsb + w.perm);
   int32_t* tile_len = reinterpret_cast<int32_t*>(wsb + w.tile_len);
   const int nthr = 256;
-  const int nperm = pl.tiles * pl.N;
-  if (lengths == nullptr) {
-    tc_perm_uniform_kernel<<<(nperm + nthr - 1) / nthr, nthr, 0, s>>>(perm, tile_len, p.B, p.T, pl.N, pl.tiles);
-    note_launches(1);
-  } else {
-    int32_t* hist = reinterpret_cast<int32_t*>(wsb + w.hist);
-    int32_t* sorted = reinterpret_cast<int32_t*>(wsb + w.sorted);
-    PLSTM_TRY_CUDA(cudaMemsetAsync(hist, 0, (size_t)(p.T + 1) * 4, s));
-    tc_len_hist_kernel<<<(p.B + nthr - 1) / nthr, nthr, 0, s>>>(lengths, p.B, p.T, hist);
-    tc_len_scan_kernel<<<1, 32, 0, s>>>(hist, p.T + 1);
-    tc_len_scatter_kernel<<<(p.B + nthr - 1) / nthr, nthr, 0, s>>>(lengths, p.B, p.T, hist, sorted);
-    tc_perm_varlen_kernel<<<(nperm + nthr - 1) / nthr, nthr, 0, s>>>(sorted, lengths, perm, tile_len, p.B, p.T,
-                                                                      pl.N, pl.tiles);
-    note_launches(4);
+  {
+    const int32_t rc = tc_make_perm(p, pl.N, pl.tiles, lengths, perm, tile_len,
+                                    reinterpret_cast<int32_t*>(wsb + w.hist), reinterpret_cast<int32_t*>(wsb + w.sorted), s);
+    if (rc != PLSTM_OK) return rc;
   }
-  PLSTM_TRY_CUDA(cudaGetLastError());
   if (p.T > 0) {
     const int64_t total = (int64_t)pl.tiles * p.T * pl.N;
     const int grid = (int)std::min<int64_t>((total + nthr - 1) / nthr, 148 * 32);

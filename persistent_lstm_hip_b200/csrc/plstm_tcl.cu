@@ -1,0 +1,1105 @@
+// plstm_tcl.cu — tcgen05 layer-sequential backend for H = 256 and H = 512.
+//
+// What it replaces.  The reference runs these sizes through its adaptive path:
+// per layer an input-projection GEMM (adaptive_lstm_input_gemm_forward_workspace,
+// miopen_adaptive_lstm_hip/csrc/adaptive_lstm_hip.cu:389-433) and then either a
+// packed-MMAC persistent recurrence (adaptive_lstm_mmac_packed_kernel, :3461-3667)
+// or, per timestep, a library GEMM [B,H]x[H,4H] plus a pointwise launch
+// (:2388-2678); the generic path does the same with ATen matmuls
+// (persistent_lstm_hip.cu:2923-3181).
+//
+// Design (B200-first), per layer l:
+//   1. proj_kernel: gates_l = in_l . W_ih_l^T + b_ih_l + b_hh_l on tcgen05 (M = 128
+//      batch rows of one timestep, N = 128 gate rows, f32 accumulation in TMEM).
+//      in_0 is x (K = I padded to 16); in_l (l >= 1) is layer l-1's h sequence.
+//      The W_ih slice of the CTA's 128 gate rows stays resident in shared memory;
+//      the epilogue writes one 128-row x 64-column block per (step, batch tile,
+//      recurrent CTA), already in the order the recurrence reads it.
+//   2. rec_kernel: one cluster of C = H / 32 CTAs per 64-row batch tile; CTA r owns
+//      hidden units [32 r, 32 r + 32), i.e. 128 gate rows = one M = 128 MMA tile.
+//      Its W_hh slice [128 x H] stays resident in tensor memory (H / 2 columns) for
+//      the whole sequence.  Per step: D[128 x 64] = W_hh . h_{t-1}^T as H / 16
+//      tcgen05.mma (A from TMEM, B = h_{t-1} from shared memory), the MMAs over the
+//      CTA's own 32 units issued as soon as it has written them, the rest once the
+//      other C - 1 pieces have landed; the compute warps add the projected gate
+//      block (prefetched three steps ahead by bulk copy), apply the gate math in
+//      registers (c in f32), write their h piece and the last one to finish pushes
+//      it to the C - 1 peers with shared -> distributed shared bulk copies that
+//      complete on the peers' barriers.  The control warp stores the piece to the
+//      h sequence in global memory for the next layer's projection.
+//   3. the Linear head (or the h sequence output) from the last layer's h.
+// Layers run one after the other; every wait in the kernels is bounded.
+#include <algorithm>
+#include <cstdlib>
+#include <mutex>
+#include <string>
+
+#include "plstm_common.cuh"
+#include "sm100_ptx.cuh"
+
+namespace plstm {
+namespace tcl {
+
+constexpr int kU = 32;      // hidden units per recurrent CTA (4 x 32 = 128 gate rows)
+constexpr int kRows = 128;  // gate rows per CTA
+constexpr int kXK = 16;     // padded layer-0 input width
+constexpr int kNT = 64;     // batch rows per cluster tile (N of the recurrent MMAs)
+constexpr int kGRow = kNT + 8;              // gate block row stride in elements (+16 bytes: no bank conflicts)
+constexpr int kGBlock = kRows * kGRow * 2;  // bytes of one (step, tile, CTA) gate block
+constexpr int kPiece = kNT * kU * 2;        // bytes of one CTA's h piece (32 units x 64 rows)
+constexpr int kKG = (kNT / 8) * 128;        // bytes of one 8-unit K group of a piece (8 row groups x 128 B)
+constexpr int kMaxL = 16;
+
+__host__ __device__ inline int ctas_of(int H) { return H / kU; }
+__host__ __device__ inline int kin_of(int l, int H) { return l == 0 ? kXK : H; }
+
+// Packed image: [W_hh images L x 4H x H][W_ih images per layer 4H x Kin][bias f32 L x 4H]
+// [W_lin 16-bit O x H][b_lin f32 O]; gate rows in the recurrent CTA order below.
+__host__ __device__ inline size_t off_whh(int l, int H) { return (size_t)l * 4 * H * H * 2; }
+__host__ __device__ inline size_t off_wih(int l, int H, int L) {
+  return off_whh(L, H) + (l == 0 ? 0 : (size_t)4 * H * kXK * 2 + (size_t)(l - 1) * 4 * H * H * 2);
+}
+__host__ __device__ inline size_t off_bias(int H, int L) { return off_wih(L, H, L); }
+__host__ __device__ inline size_t off_wlin(int H, int L) { return off_bias(H, L) + (size_t)L * 4 * H * 4; }
+__host__ __device__ inline size_t off_blin(int H, int L, int O) {
+  return off_wlin(H, L) + (((size_t)O * H * 2 + 15) / 16) * 16;
+}
+__host__ __device__ inline size_t packed_total(int H, int L, int O) { return off_blin(H, L, O) + (size_t)O * 4 + 16; }
+
+// Permuted gate row rho of CTA r: quadrant q = rho / 32 holds units 32 r + 8 q + [0, 8)
+// as [i x 8 | f x 8 | g x 8 | o x 8]; returns the nn.LSTM row (gate * H + unit).
+__host__ __device__ inline int src_row(int H, int r, int rho) {
+  const int q = rho >> 5, gate = (rho >> 3) & 3, j = rho & 7;
+  return gate * H + kU * r + 8 * q + j;
+}
+// Gate rows i, f, o are stored pre-scaled by 1/2: sigmoid(z) = (1 + tanh(z / 2)) / 2.
+__host__ __device__ inline float row_scale(int rho) { return ((rho >> 3) & 3) == 2 ? 1.0f : 0.5f; }
+
+template <bool BF16>
+__device__ __forceinline__ uint16_t to_bits(float v) {
+  if (BF16) {
+    __nv_bfloat16 h = __float2bfloat16_rn(v);
+    return *reinterpret_cast<uint16_t*>(&h);
+  }
+  __half h = __float2half_rn(v);
+  return *reinterpret_cast<uint16_t*>(&h);
+}
+template <bool BF16>
+__device__ __forceinline__ float from_bits(uint16_t b) {
+  if (BF16) return __bfloat162float(*reinterpret_cast<__nv_bfloat16*>(&b));
+  return __half2float(*reinterpret_cast<__half*>(&b));
+}
+template <bool BF16>
+__device__ __forceinline__ float2 from_bits2(uint32_t b) {
+  if (BF16) return __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&b));
+  return __half22float2(*reinterpret_cast<__half2*>(&b));
+}
+template <bool BF16>
+__device__ __forceinline__ uint32_t pack2_bits(float lo, float hi) {
+  if (BF16) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+  }
+  __half2 v = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+__device__ __forceinline__ uint32_t sw128_off(int row, int k) {
+  return (uint32_t)(row * 128 + ((((k >> 3) ^ (row & 7)) & 7) << 4) + (k & 7) * 2);
+}
+__device__ __forceinline__ uint32_t none16_off(int row, int k) {
+  return (uint32_t)((row >> 3) * 256 + (k >> 3) * 128 + (row & 7) * 16 + (k & 7) * 2);
+}
+// Byte offset of (unit k, tile row n) in an h tile of H units: pieces of 32 units,
+// each [4 K groups][8 row groups][8 rows][8 units] (K-major, no swizzle: the K
+// groups of the whole tile are kKG bytes apart, row groups 128 bytes apart).
+__device__ __forceinline__ uint32_t hoff(int k, int n) {
+  return (uint32_t)((k >> 3) * kKG + (n >> 3) * 128 + (n & 7) * 16 + (k & 7) * 2);
+}
+
+// Bounded mbarrier wait; false = gave up (timeout or abort).
+__device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                         unsigned long long timeout_ns) {
+  if (ptx::mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = ptx::globaltimer();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 32; ++i)
+      if (ptx::mbar_try_wait(bar, parity)) return true;
+    if (abort_flag != nullptr && *abort_flag) return false;
+    if (ptx::globaltimer() - t0 > timeout_ns) return false;
+  }
+}
+
+// Warp-uniform version: lane 0 waits, the result is broadcast.
+__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                          unsigned long long timeout_ns) {
+  int ok = 0;
+  if ((threadIdx.x & 31) == 0) ok = wait_bar(bar, parity, abort_flag, timeout_ns) ? 1 : 0;
+  return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+
+__device__ __forceinline__ void bulk_s2g(void* gdst, uint32_t ssrc, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gdst), "r"(ssrc), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// ---- packing ------------------------------------------------------------------------
+struct PackArgs {
+  const void* w_ih[kMaxL];
+  const void* w_hh[kMaxL];
+  const void* b_ih[kMaxL];
+  const void* b_hh[kMaxL];
+  const void* w_lin;
+  const void* b_lin;
+  int ih_layout, hh_layout, dtype, L, I, H, O;
+};
+
+__global__ void pack_kernel(const PackArgs a, uint8_t* packed) {
+  const int H = a.H, L = a.L, G = 4 * H;
+  const int64_t n_hh = (int64_t)L * G * H;
+  const int64_t n_ih = (int64_t)G * kXK + (int64_t)(L - 1) * G * H;
+  const int64_t n_b = (int64_t)L * G;
+  const int64_t n_wl = (int64_t)a.O * H;
+  const int64_t total = n_hh + n_ih + n_b + n_wl + a.O;
+  const bool bf16 = a.dtype == PLSTM_BF16;
+  auto put16 = [&](size_t off_bytes, int64_t idx, float v) {
+    __half hv = __float2half_rn(v);
+    __nv_bfloat16 bv = __float2bfloat16_rn(v);
+    reinterpret_cast<uint16_t*>(packed + off_bytes)[idx] =
+        bf16 ? *reinterpret_cast<uint16_t*>(&bv) : *reinterpret_cast<uint16_t*>(&hv);
+  };
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    if (i < n_hh) {
+      const int l = (int)(i / ((int64_t)G * H));
+      const int64_t rem = i % ((int64_t)G * H);
+      const int rp = (int)(rem / H), k = (int)(rem % H);
+      const int r = rp / kRows, rho = rp % kRows;
+      const float v = load_any(a.w_hh[l], a.dtype, weight_src_index(a.hh_layout, G, H, src_row(H, r, rho), k));
+      put16(off_whh(l, H), rem, v * row_scale(rho));
+    } else if (i < n_hh + n_ih) {
+      int64_t j = i - n_hh;
+      int l = 0, kin = kXK;
+      if (j >= (int64_t)G * kXK) {
+        j -= (int64_t)G * kXK;
+        l = 1 + (int)(j / ((int64_t)G * H));
+        j %= (int64_t)G * H;
+        kin = H;
+      }
+      const int rp = (int)(j / kin), k = (int)(j % kin);
+      const int r = rp / kRows, rho = rp % kRows;
+      const int kreal = l == 0 ? a.I : H;
+      float v = 0.0f;
+      if (k < kreal) v = load_any(a.w_ih[l], a.dtype, weight_src_index(a.ih_layout, G, kreal, src_row(H, r, rho), k));
+      put16(off_wih(l, H, L), j, v * row_scale(rho));
+    } else if (i < n_hh + n_ih + n_b) {
+      const int64_t j = i - n_hh - n_ih;
+      const int l = (int)(j / G), rp = (int)(j % G);
+      const int r = rp / kRows, rho = rp % kRows;
+      const int sr = src_row(H, r, rho);
+      float v = 0.0f;
+      if (a.b_ih[l] != nullptr) v += load_any(a.b_ih[l], a.dtype, sr);
+      if (a.b_hh[l] != nullptr) v += load_any(a.b_hh[l], a.dtype, sr);
+      reinterpret_cast<float*>(packed + off_bias(H, L))[j] = v * row_scale(rho);
+    } else if (i < n_hh + n_ih + n_b + n_wl) {
+      const int64_t j = i - n_hh - n_ih - n_b;
+      const int o = (int)(j / H), k = (int)(j % H);
+      float v = 0.0f;
+      if (a.w_lin != nullptr) v = load_any(a.w_lin, a.dtype, weight_src_index(PLSTM_W_NATIVE, a.O, H, o, k));
+      put16(off_wlin(H, L), j, v);
+    } else {
+      const int o = (int)(i - n_hh - n_ih - n_b - n_wl);
+      float v = 0.0f;
+      if (a.b_lin != nullptr) v = load_any(a.b_lin, a.dtype, o);
+      reinterpret_cast<float*>(packed + off_blin(H, L, a.O))[o] = v;
+    }
+  }
+}
+
+// ---- projection GEMM ----------------------------------------------------------------
+constexpr int kGemmThreads = 9 * 32;  // warps 0-3 producers, 4 MMA issue, 5-8 epilogue
+constexpr int kAStages = 4;
+
+template <int KP>
+struct GemmSmem {
+  static constexpr int kChunks = KP <= kXK ? 1 : KP / 64;
+  static constexpr int kChunkBytes = KP <= kXK ? kRows * 32 : kRows * 128;  // 128 rows of one K chunk
+  static constexpr int kB = 0;                                            // resident W_ih slice
+  static constexpr int kA = kB + kChunks * kChunkBytes;                   // A stages
+  static constexpr int kBias = kA + kAStages * kChunkBytes;
+  static constexpr int kBar = kBias + kRows * 4;
+  static constexpr int kTmemSlot = kBar + 96;
+  static constexpr int kEnd = kBar + 128;
+  static constexpr int kDyn = kEnd + 1024;
+};
+
+struct GemmArgs {
+  const uint16_t* x;      // layer 0: [B][T][I]
+  const int32_t* perm;    // [tiles * kNT]: batch row of each tile row (-1 = padding)
+  const uint8_t* hseq;    // layers >= 1: [T][tiles][C] h pieces of layer l-1
+  const uint16_t* wih;    // [4H][KP] this layer's permuted W_ih
+  const float* bias;      // [4H] this layer's permuted, pre-scaled bias
+  uint16_t* gates;        // [T][tiles][C][128][kGRow]
+  int* status;
+  int B, T, I, H, tiles;
+};
+
+template <int KP, bool BF16>
+__global__ void __launch_bounds__(kGemmThreads, 1) proj_kernel(const GemmArgs a) {
+  using S = GemmSmem<KP>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = ptx::smem_u32(sm);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int C = ctas_of(a.H);
+  const int Bp = a.tiles * kNT;
+  const int mt_per_t = (Bp + kRows - 1) / kRows;
+  const int total_m = a.T * mt_per_t;
+  const int r = blockIdx.x % C;  // gate-row tile = recurrent CTA rank
+  const int cpr = (int)(gridDim.x - r + C - 1) / C;
+  const int first = blockIdx.x / C;
+  const int my = first < total_m ? (total_m - first + cpr - 1) / cpr : 0;
+  const unsigned long long kTimeout = 2000000000ull;
+
+  const uint32_t bar = sbase + S::kBar;
+  const uint32_t a_full = bar, a_empty = bar + 32, d_full = bar + 64, d_empty = bar + 80;
+  float* bias_s = reinterpret_cast<float*>(sm + S::kBias);
+  if (tid == 0) {
+    for (int s = 0; s < kAStages; ++s) {
+      ptx::mbar_init(a_full + 8 * s, 4);
+      ptx::mbar_init(a_empty + 8 * s, 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      ptx::mbar_init(d_full + 8 * s, 1);
+      ptx::mbar_init(d_empty + 8 * s, 4);
+    }
+    ptx::fence_mbar_init_cluster();
+  }
+  if (warp == 4) {
+    ptx::tmem_alloc(sbase + S::kTmemSlot, 256);
+    ptx::tmem_relinquish();
+  }
+  // Resident B operand: this CTA's 128 gate rows of W_ih, K-major.
+  for (int i = tid; i < kRows * KP / 8; i += kGemmThreads) {
+    const int row = i / (KP / 8), k = (i % (KP / 8)) * 8;
+    const uint4 v = *reinterpret_cast<const uint4*>(a.wih + ((size_t)r * kRows + row) * KP + k);
+    uint32_t off;
+    if (KP <= kXK)
+      off = none16_off(row, k);
+    else
+      off = (uint32_t)((k >> 6) * S::kChunkBytes) + sw128_off(row, k & 63);
+    *reinterpret_cast<uint4*>(sm + S::kB + off) = v;
+  }
+  for (int i = tid; i < kRows; i += kGemmThreads) bias_s[i] = a.bias[r * kRows + i];
+  ptx::fence_proxy_async_smem();
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(sm + S::kTmemSlot);
+
+  if (warp < 4) {
+    // ---------------- producers: thread = one row of the A tile ----------------
+    const int row = tid;
+    int cnt = 0;
+    bool ok = true;
+    for (int it = 0; it < my && ok; ++it) {
+      const int mt = first + it * cpr;
+      const int t = mt / mt_per_t;
+      const int p = (mt % mt_per_t) * kRows + row;
+      for (int c = 0; c < S::kChunks; ++c, ++cnt) {
+        const int s = cnt % kAStages;
+        if (cnt >= kAStages && !wait_bar(a_empty + 8 * s, ((cnt / kAStages) - 1) & 1, nullptr, kTimeout)) {
+          if (lane == 0) report_status(a.status, PLSTM_ETIMEOUT, 0x7fff0000);
+          ok = false;
+          break;
+        }
+        uint8_t* A = sm + S::kA + s * S::kChunkBytes;
+        if (KP <= kXK) {
+          uint16_t v[16];
+#pragma unroll
+          for (int k = 0; k < 16; ++k) v[k] = 0;
+          if (p < Bp) {
+            const int b = a.perm[p];
+            if (b >= 0) {
+              const uint16_t* src = a.x + ((size_t)b * a.T + t) * a.I;
+              for (int k = 0; k < a.I && k < 16; ++k) v[k] = src[k];
+            }
+          }
+          uint4 lo, hi;
+          lo.x = v[0] | (v[1] << 16); lo.y = v[2] | (v[3] << 16); lo.z = v[4] | (v[5] << 16); lo.w = v[6] | (v[7] << 16);
+          hi.x = v[8] | (v[9] << 16); hi.y = v[10] | (v[11] << 16); hi.z = v[12] | (v[13] << 16); hi.w = v[14] | (v[15] << 16);
+          *reinterpret_cast<uint4*>(A + none16_off(row, 0)) = lo;
+          *reinterpret_cast<uint4*>(A + none16_off(row, 8)) = hi;
+        } else {
+          uint4 v[8];
+          if (p < Bp) {
+            const int tile = p / kNT, n = p % kNT;
+            const uint8_t* tbase = a.hseq + ((size_t)t * a.tiles + tile) * (size_t)C * kPiece;
+#pragma unroll
+            for (int g = 0; g < 8; ++g) {
+              const int kg = c * 8 + g;  // 8-unit K group of the previous layer's h
+              v[g] = *reinterpret_cast<const uint4*>(tbase + (size_t)kg * kKG + (n >> 3) * 128 + (n & 7) * 16);
+            }
+          } else {
+#pragma unroll
+            for (int g = 0; g < 8; ++g) v[g] = make_uint4(0, 0, 0, 0);
+          }
+#pragma unroll
+          for (int g = 0; g < 8; ++g) *reinterpret_cast<uint4*>(A + sw128_off(row, 8 * g)) = v[g];
+        }
+        ptx::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(a_full + 8 * s);
+      }
+    }
+  } else if (warp == 4) {
+    // ---------------- MMA issue ----------------
+    constexpr uint32_t idesc = ptx::idesc_f16(128, 128, BF16);
+    int cnt = 0;
+    bool ok = true;
+    for (int it = 0; it < my && ok; ++it) {
+      const int db = it & 1;
+      if (it >= 2) {
+        int w = 1;
+        if (lane == 0) w = wait_bar(d_empty + 8 * db, ((it - 2) >> 1) & 1, nullptr, kTimeout) ? 1 : 0;
+        if (!__shfl_sync(0xffffffffu, w, 0)) break;
+      }
+      const uint32_t d = tmem + (uint32_t)(db * 128);
+      for (int c = 0; c < S::kChunks; ++c, ++cnt) {
+        const int s = cnt % kAStages;
+        int w = 1;
+        if (lane == 0) w = wait_bar(a_full + 8 * s, (cnt / kAStages) & 1, nullptr, kTimeout) ? 1 : 0;
+        if (!__shfl_sync(0xffffffffu, w, 0)) {
+          ok = false;
+          break;
+        }
+        if (ptx::elect_one()) {
+          ptx::tc_fence_after();
+          const uint32_t a0 = sbase + S::kA + s * S::kChunkBytes;
+          const uint32_t b0 = sbase + S::kB + c * S::kChunkBytes;
+          if (KP <= kXK) {
+            ptx::mma_f16_ss(d, ptx::desc_k_none(a0, 128, 256), ptx::desc_k_none(b0, 128, 256), idesc, 0u);
+          } else {
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              ptx::mma_f16_ss(d, ptx::desc_k_sw128(a0 + kk * 32), ptx::desc_k_sw128(b0 + kk * 32), idesc,
+                              (c | kk) != 0 ? 1u : 0u);
+          }
+          ptx::mma_commit(a_empty + 8 * s);
+        }
+        __syncwarp();
+      }
+      if (ok && ptx::elect_one()) ptx::mma_commit(d_full + 8 * db);
+      __syncwarp();
+    }
+  } else {
+    // ---------------- epilogue: lane = batch row, columns = gate rows ----------------
+    const int q = warp & 3;
+    const int row = 32 * q + lane;
+    for (int it = 0; it < my; ++it) {
+      const int db = it & 1;
+      if (!wait_bar(d_full + 8 * db, (it >> 1) & 1, nullptr, kTimeout)) break;
+      ptx::tc_fence_after();
+      const int mt = first + it * cpr;
+      const int t = mt / mt_per_t;
+      const int p = (mt % mt_per_t) * kRows + row;
+      const bool valid = p < Bp;
+      uint16_t* dst = a.gates;
+      if (valid) {
+        const int tile = p / kNT, n = p % kNT;
+        dst += (((size_t)t * a.tiles + tile) * C + r) * (size_t)kRows * kGRow + n;
+      }
+#pragma unroll 1
+      for (int cb = 0; cb < 4; ++cb) {
+        uint32_t v[32];
+        const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(db * 128 + cb * 32);
+        ptx::tmem_ld_32x32b_x16(taddr, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
+        ptx::tmem_ld_32x32b_x16(taddr + 16, *reinterpret_cast<uint32_t(*)[16]>(&v[16]));
+        ptx::tmem_wait_ld();
+        if (valid) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int col = cb * 32 + j;
+            dst[(size_t)col * kGRow] = to_bits<BF16>(__uint_as_float(v[j]) + bias_s[col]);
+          }
+        }
+      }
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(d_empty + 8 * db);
+    }
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 4) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem, 256);
+  }
+}
+
+// ---- recurrence -----------------------------------------------------------------------
+template <int H>
+struct RecSmem {
+  static constexpr int C = H / kU;
+  static constexpr int kTile = H * kNT * 2;  // one h tile (all units x 64 rows)
+  static constexpr int kB = 0;               // h tiles, double-buffered by step parity
+  static constexpr int kG = kB + 2 * kTile;  // gate blocks, ring of 3
+  static constexpr int kBar = kG + 3 * kGBlock;
+  // barriers: full_rec[2] @0, mma[2] @16, hready[2] @32, gfull[3] @48
+  static constexpr int kTmemSlot = kBar + 80, kAbort = kBar + 84, kDone = kBar + 88;
+  static constexpr int kPerm = kBar + 128, kLens = kPerm + 4 * kNT;
+  static constexpr int kEnd = kLens + 4 * kNT;
+  static constexpr int kDyn = kEnd + 1024;
+  static constexpr int kComputeWarps = 4;  // one per TMEM lane quadrant, 64 columns each
+  static constexpr int kThreads = (kComputeWarps + 1) * 32;
+  static constexpr int kACols = H / 2;  // W_hh slice: 128 lanes x H 16-bit values
+  static constexpr int kD = kACols;     // gate accumulator [128 x 64] (single buffer)
+  static constexpr int kTmemCols = kACols + kNT <= 256 ? 256 : 512;
+  static_assert(kDyn <= 232448, "shared memory");
+};
+
+struct RecArgs {
+  const uint8_t* whh;      // this layer's W_hh images [C][128][H]
+  const uint16_t* gates;   // [T][tiles][C][128][kGRow]
+  const int32_t* perm;     // [tiles * kNT]
+  const int32_t* lengths;  // [B] or null
+  const int32_t* tile_len; // [tiles]
+  const void* h0;          // [L][B][H] or null
+  const void* c0;
+  uint8_t* hseq;           // [T][tiles][C] pieces, or null
+  void* h_n;               // [L][B][H] or null
+  void* c_n;
+  uint16_t* hlast;         // [B][H] (last layer, Linear input) or null
+  int* status;
+  int B, T, layer, flags;
+  unsigned long long timeout_ns;
+};
+
+__device__ __forceinline__ void rec_abort(const RecArgs& a, uint8_t* sm_abort, int ncta, int step) {
+  const uint32_t local = ptx::smem_u32(sm_abort);
+  for (int r = 0; r < ncta; ++r) ptx::st_cluster_u32(ptx::mapa(local, (uint32_t)r), 1u);
+  report_status(a.status, PLSTM_ETIMEOUT, (int)((blockIdx.x & 0x7fff) << 16) | (step & 0xffff));
+}
+
+template <int H, bool BF16, bool VARLEN>
+__global__ void __launch_bounds__(RecSmem<H>::kThreads, 1) rec_kernel(const RecArgs a) {
+  using S = RecSmem<H>;
+  constexpr int C = S::C;
+  constexpr int CPW = kNT / 8;  // 8-column chunks per compute warp
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = ptx::smem_u32(sm);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int r = (int)ptx::cluster_ctarank();
+  const int tile = blockIdx.x / C;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + S::kAbort);
+  int32_t* perm_s = reinterpret_cast<int32_t*>(sm + S::kPerm);
+  int32_t* lens_s = reinterpret_cast<int32_t*>(sm + S::kLens);
+  const uint32_t bar_rec = sbase + S::kBar, bar_mma = bar_rec + 16, bar_hready = bar_rec + 32,
+                 bar_g = bar_rec + 48;
+  auto bbuf = [&](int b) -> uint32_t { return sbase + (uint32_t)(S::kB + b * S::kTile); };
+  auto gslot = [&](int s) -> uint32_t { return sbase + (uint32_t)(S::kG + s * kGBlock); };
+  const int l = a.layer;
+
+  if (tid == 0) {
+    for (int b = 0; b < 2; ++b) {
+      ptx::mbar_init(bar_rec + 8 * b, 1);
+      ptx::mbar_init(bar_mma + 8 * b, 1);
+      ptx::mbar_init(bar_hready + 8 * b, S::kComputeWarps);
+    }
+    for (int s = 0; s < 3; ++s) ptx::mbar_init(bar_g + 8 * s, 1);
+    *abort_flag = 0;
+    *reinterpret_cast<uint32_t*>(sm + S::kDone) = 0;
+    ptx::fence_mbar_init_cluster();
+  }
+  if (warp == 0) {
+    ptx::tmem_alloc(sbase + S::kTmemSlot, S::kTmemCols);
+    ptx::tmem_relinquish();
+  }
+  for (int i = tid; i < kNT; i += S::kThreads) {
+    const int b = a.perm[tile * kNT + i];
+    perm_s[i] = b;
+    int len = 0;
+    if (b >= 0) len = VARLEN ? min(max(a.lengths[b], 0), a.T) : a.T;
+    lens_s[i] = len;
+  }
+  __syncthreads();
+  // h_{-1} = h0 (all units of the tile's rows) -> h tile buffer 0.
+  for (int i = tid; i < kNT * H; i += S::kThreads) {
+    const int n = i / H, k = i % H;
+    uint16_t v = 0;
+    const int b = perm_s[n];
+    if (a.h0 != nullptr && b >= 0) v = static_cast<const uint16_t*>(a.h0)[((size_t)l * a.B + b) * H + k];
+    *reinterpret_cast<uint16_t*>(sm + S::kB + hoff(k, n)) = v;
+  }
+  ptx::fence_proxy_async_smem();
+  ptx::tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(sm + S::kTmemSlot);
+  // W_hh slice -> TMEM columns [0, H / 2): compute warp q stores its quadrant's 32 rows.
+  if (warp < S::kComputeWarps) {
+    const int row = 32 * warp + lane;
+    const uint32_t lane_off = (uint32_t)(32 * warp) << 16;
+    const uint4* src = reinterpret_cast<const uint4*>(a.whh + ((size_t)r * kRows + row) * H * 2);
+#pragma unroll 1
+    for (int c = 0; c < H / 2; c += 32) {
+      uint32_t v[32];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const uint4 u = src[c / 4 + i];
+        v[4 * i + 0] = u.x;
+        v[4 * i + 1] = u.y;
+        v[4 * i + 2] = u.z;
+        v[4 * i + 3] = u.w;
+      }
+      ptx::tmem_st_32x32b_x32(tmem + lane_off + (uint32_t)c, v);
+    }
+    ptx::tmem_wait_st();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  ptx::cluster_sync();  // every CTA's barriers are initialised before any remote copy
+
+  const int Tt = a.tile_len[tile];
+  const uint32_t dcol = tmem + (uint32_t)S::kD;
+  auto gates_src = [&](int t) {
+    return reinterpret_cast<const uint8_t*>(a.gates) + (((size_t)t * gridDim.x / C + tile) * C + r) * (size_t)kGBlock;
+  };
+
+  if (warp == S::kComputeWarps) {
+    // ============================ control warp ============================
+    constexpr uint32_t idesc = ptx::idesc_f16(128, kNT, BF16);
+    const uint32_t rec_bytes = (uint32_t)(C - 1) * kPiece;
+    // One MMA covers K = 16 units = two 8-unit K groups (kKG bytes apart).
+    auto issue = [&](int t, int j0, int j1, bool init) {
+      const int b = t & 1;
+      if (ptx::elect_one()) {
+        ptx::tc_fence_after();
+        for (int j = j0; j < j1; ++j) {
+          const uint64_t dB = ptx::desc_k_none(bbuf(b) + (uint32_t)(2 * j * kKG), kKG, 128);
+          ptx::mma_f16_ts(dcol, tmem + (uint32_t)(8 * j), dB, idesc, (init && j == j0) ? 0u : 1u);
+        }
+      }
+      __syncwarp();
+    };
+    auto issue_others = [&](int t, bool init) {
+      // every K step but this CTA's own two (units [32 r, 32 r + 32))
+      bool first = init;
+      if (2 * r > 0) {
+        issue(t, 0, 2 * r, first);
+        first = false;
+      }
+      if (2 * r + 2 < H / 16) issue(t, 2 * r + 2, H / 16, first);
+    };
+    auto commit = [&](int t) {
+      if (ptx::elect_one()) ptx::mma_commit(bar_mma + 8 * (t & 1));
+      __syncwarp();
+    };
+    auto load_gates = [&](int t) {
+      if (ptx::elect_one()) {
+        const int s = t % 3;
+        ptx::mbar_arrive_expect_tx(bar_g + 8 * s, kGBlock);
+        ptx::bulk_g2s(gslot(s), gates_src(t), kGBlock, bar_g + 8 * s);
+      }
+      __syncwarp();
+    };
+    bool ok = true;
+    auto fail = [&](int t) {
+      if (ptx::elect_one()) rec_abort(a, sm + S::kAbort, C, t);
+      __syncwarp();
+      ok = false;
+    };
+    if (Tt > 0) {
+      for (int t = 0; t < 3 && t < Tt; ++t) load_gates(t);
+      if (ptx::elect_one())
+        for (int t = 1; t <= 2 && t < Tt; ++t) ptx::mbar_arrive_expect_tx(bar_rec + 8 * (t & 1), rec_bytes);
+      __syncwarp();
+      // Step 0 runs on h0, already complete in buffer 0.
+      issue(0, 2 * r, 2 * r + 2, true);
+      issue_others(0, false);
+      commit(0);
+    }
+    for (int t = 0; ok && t < Tt; ++t) {
+      const int b = t & 1;
+      if (t >= 1) {
+        if (!warp_wait(bar_rec + 8 * b, ((t - 1) >> 1) & 1, abort_flag, a.timeout_ns)) {
+          fail(t);
+          break;
+        }
+        if (t + 2 < Tt && ptx::elect_one()) ptx::mbar_arrive_expect_tx(bar_rec + 8 * b, rec_bytes);
+        __syncwarp();
+        issue_others(t, false);
+        commit(t);
+      }
+      // Compute warps done with step t: its gate block slot and accumulator are free,
+      // h(t)'s own piece is written (buffer b ^ 1).
+      if (!warp_wait(bar_hready + 8 * b, (t >> 1) & 1, abort_flag, a.timeout_ns)) {
+        fail(t);
+        break;
+      }
+      if (t + 3 < Tt) load_gates(t + 3);
+      if (t + 1 < Tt) {
+        // Step t + 1 writes h(t + 1) into buffer b, the source of the h-sequence
+        // store issued at step t - 1: that store must have read it first.
+        if (a.hseq != nullptr && lane == 0) bulk_wait_read0();
+        __syncwarp();
+        issue(t + 1, 2 * r, 2 * r + 2, true);
+      }
+      if (a.hseq != nullptr) {
+        if (lane == 0) {
+          const uint32_t piece = bbuf(b ^ 1) + (uint32_t)(r * kPiece);
+          bulk_s2g(a.hseq + (((size_t)t * gridDim.x / C + tile) * C + r) * (size_t)kPiece, piece, kPiece);
+          bulk_commit();
+        }
+        __syncwarp();
+      }
+    }
+    if (a.hseq != nullptr && lane == 0) bulk_wait0();
+    __syncwarp();
+  } else {
+    // ============================ compute warps ============================
+    const int q = warp;
+    const int j8 = lane >> 2, cpair = (lane & 3) * 2;
+    const int ul = 8 * q + j8;  // unit within this CTA's 32
+    const int u = kU * r + ul;  // unit within the layer
+    float c_st[CPW][2];
+    uint16_t h_st[CPW][2];
+    int len_c[CPW][2], bidx[CPW][2];
+#pragma unroll
+    for (int jc = 0; jc < CPW; ++jc)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int n = 8 * jc + cpair + e;
+        const int bb = perm_s[n];
+        bidx[jc][e] = bb;
+        len_c[jc][e] = lens_s[n];
+        uint16_t hv = 0;
+        float cv = 0.0f;
+        if (bb >= 0 && a.h0 != nullptr) {
+          hv = static_cast<const uint16_t*>(a.h0)[((size_t)l * a.B + bb) * H + u];
+          cv = from_bits<BF16>(static_cast<const uint16_t*>(a.c0)[((size_t)l * a.B + bb) * H + u]);
+        }
+        h_st[jc][e] = hv;
+        c_st[jc][e] = cv;
+      }
+    for (int t = 0; t < Tt; ++t) {
+      const int b = t & 1, gs = t % 3;
+      if (*abort_flag) break;
+      if (!wait_bar(bar_g + 8 * gs, (t / 3) & 1, abort_flag, a.timeout_ns) ||
+          !wait_bar(bar_mma + 8 * b, (t >> 1) & 1, abort_flag, a.timeout_ns)) {
+        if (lane == 0) rec_abort(a, sm + S::kAbort, C, t);
+        break;
+      }
+      ptx::tc_fence_after();
+      uint32_t rif[4 * CPW], rgo[4 * CPW];
+      const uint32_t lo = (uint32_t)(32 * q) << 16, hi = (uint32_t)(32 * q + 16) << 16;
+      ptx::tmem_ld_16x256b_x4(dcol + lo, *reinterpret_cast<uint32_t(*)[16]>(&rif[0]));
+      ptx::tmem_ld_16x256b_x4(dcol + lo + 32, *reinterpret_cast<uint32_t(*)[16]>(&rif[16]));
+      ptx::tmem_ld_16x256b_x4(dcol + hi, *reinterpret_cast<uint32_t(*)[16]>(&rgo[0]));
+      ptx::tmem_ld_16x256b_x4(dcol + hi + 32, *reinterpret_cast<uint32_t(*)[16]>(&rgo[16]));
+      ptx::tmem_wait_ld();
+      ptx::tc_fence_before();
+      // Projected input + bias of the four gates of this thread's cells.
+      const uint8_t* gsl = sm + S::kG + gs * kGBlock;
+      float pre[4][CPW][2];
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        const uint8_t* grow = gsl + (size_t)(32 * q + 8 * g + j8) * kGRow * 2;
+#pragma unroll
+        for (int jc = 0; jc < CPW; ++jc) {
+          const float2 gv = from_bits2<BF16>(*reinterpret_cast<const uint32_t*>(grow + (8 * jc + cpair) * 2));
+          const uint32_t* acc = g < 2 ? rif : rgo;
+          const int base = 4 * jc + (g & 1) * 2;
+          pre[g][jc][0] = __uint_as_float(acc[base]) + gv.x;
+          pre[g][jc][1] = __uint_as_float(acc[base + 1]) + gv.y;
+        }
+      }
+      uint8_t* dst = sm + S::kB + (b ^ 1) * S::kTile;
+#pragma unroll
+      for (int jc = 0; jc < CPW; ++jc) {
+        float h[2], cn[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const float ti = ptx::tanh_approx(pre[0][jc][e]), tf = ptx::tanh_approx(pre[1][jc][e]);
+          const float tg = ptx::tanh_approx(pre[2][jc][e]), to = ptx::tanh_approx(pre[3][jc][e]);
+          cn[e] = fmaf(fmaf(0.5f, tf, 0.5f), c_st[jc][e], fmaf(0.5f, ti, 0.5f) * tg);
+          h[e] = fmaf(0.5f, to, 0.5f) * ptx::tanh_approx(cn[e]);
+        }
+        const uint32_t bits = pack2_bits<BF16>(h[0], h[1]);
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          if (!VARLEN || t < len_c[jc][e]) {
+            c_st[jc][e] = cn[e];
+            h_st[jc][e] = (uint16_t)(e == 0 ? bits & 0xffffu : bits >> 16);
+          }
+          *reinterpret_cast<uint16_t*>(dst + hoff(u, 8 * jc + cpair + e)) = h_st[jc][e];
+        }
+      }
+      ptx::fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        ptx::mbar_arrive(bar_hready + 8 * b);
+        // The last warp to finish pushes the piece to the peers (acquire-release
+        // counter: the other warps' writes, fenced for the async proxy, come first).
+        if (t + 1 < Tt && ptx::atom_add_acq_rel_smem(sbase + S::kDone, 1u) % 4u == 3u) {
+          const uint32_t piece = bbuf(b ^ 1) + (uint32_t)(r * kPiece);
+          for (int pr = 0; pr < C; ++pr) {
+            if (pr == r) continue;
+            ptx::bulk_s2c(ptx::mapa(piece, (uint32_t)pr), piece, kPiece,
+                          ptx::mapa(bar_rec + 8 * (b ^ 1), (uint32_t)pr));
+          }
+        }
+      }
+    }
+    // Final state of this CTA's units.
+#pragma unroll
+    for (int jc = 0; jc < CPW; ++jc)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int bb = bidx[jc][e];
+        if (bb < 0) continue;
+        const size_t idx = ((size_t)l * a.B + bb) * H + u;
+        if (a.h_n != nullptr) static_cast<uint16_t*>(a.h_n)[idx] = h_st[jc][e];
+        if (a.c_n != nullptr) {
+          if (a.flags & PLSTM_FLAG_CN_F32)
+            static_cast<float*>(a.c_n)[idx] = c_st[jc][e];
+          else
+            static_cast<uint16_t*>(a.c_n)[idx] = to_bits<BF16>(c_st[jc][e]);
+        }
+        if (a.hlast != nullptr) a.hlast[(size_t)bb * H + u] = h_st[jc][e];
+      }
+  }
+
+  if (*abort_flag) {
+    const unsigned long long t0 = ptx::globaltimer();
+    while (ptx::globaltimer() - t0 < 50000ull) {
+    }
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem, S::kTmemCols);
+  }
+  ptx::cluster_sync();
+}
+
+// ---- outputs -------------------------------------------------------------------------
+// out[b][o] = b_lin[o] + W_lin[o] . h_last[b]
+template <bool BF16>
+__global__ void linear_last_kernel(const uint16_t* __restrict__ hlast, const uint16_t* __restrict__ wlin,
+                                   const float* __restrict__ blin, uint16_t* __restrict__ out, int B, int H, int O) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < B * O; i += gridDim.x * blockDim.x) {
+    const int b = i / O, o = i % O;
+    float acc = 0.0f;
+    for (int k = 0; k < H; k += 2) {
+      const float2 hv = from_bits2<BF16>(*reinterpret_cast<const uint32_t*>(hlast + (size_t)b * H + k));
+      const float2 wv = from_bits2<BF16>(*reinterpret_cast<const uint32_t*>(wlin + (size_t)o * H + k));
+      acc = fmaf(hv.x, wv.x, acc);
+      acc = fmaf(hv.y, wv.y, acc);
+    }
+    out[i] = to_bits<BF16>(acc + blin[o]);
+  }
+}
+
+// One block per (step, tile): the tile's h from its C pieces, then either the Linear
+// head (out[b][t][o]) or the h sequence itself (out[b][t][u]); zero past each length.
+template <bool BF16, bool LINEAR>
+__global__ void seq_out_kernel(const uint8_t* __restrict__ hseq, const int32_t* __restrict__ perm,
+                               const int32_t* __restrict__ lengths, const uint16_t* __restrict__ wlin,
+                               const float* __restrict__ blin, uint16_t* __restrict__ out, int B, int T, int H,
+                               int O, int tiles) {
+  extern __shared__ uint8_t smem_o[];
+  float* hs = reinterpret_cast<float*>(smem_o);  // [kNT][H + 1]
+  const int C = ctas_of(H);
+  const int t = blockIdx.x / tiles, tile = blockIdx.x % tiles;
+  const uint8_t* base = hseq + ((size_t)t * tiles + tile) * (size_t)C * kPiece;
+  for (int i = threadIdx.x; i < kNT * H; i += blockDim.x) {
+    const int n = i / H, k = i % H;
+    hs[n * (H + 1) + k] = from_bits<BF16>(*reinterpret_cast<const uint16_t*>(
+        base + (size_t)(k >> 3) * kKG + (n >> 3) * 128 + (n & 7) * 16 + (k & 7) * 2));
+  }
+  __syncthreads();
+  const int W = LINEAR ? O : H;
+  for (int i = threadIdx.x; i < kNT * W; i += blockDim.x) {
+    const int n = i / W, w = i % W;
+    const int b = perm[tile * kNT + n];
+    if (b < 0) continue;
+    const int len = lengths != nullptr ? min(max(lengths[b], 0), T) : T;
+    float v = 0.0f;
+    if (t < len) {
+      if (LINEAR) {
+        float acc = blin[w];
+        for (int k = 0; k < H; ++k) acc = fmaf(hs[n * (H + 1) + k], from_bits<BF16>(wlin[(size_t)w * H + k]), acc);
+        v = acc;
+      } else {
+        v = hs[n * (H + 1) + w];
+      }
+    }
+    out[((size_t)b * T + t) * W + w] = to_bits<BF16>(v);
+  }
+}
+
+// ---- host side -------------------------------------------------------------------------
+struct Ws {
+  size_t perm, tile_len, hist, sorted, gates, hseq, hlast, total;
+};
+
+Ws ws_layout(const Problem& p) {
+  Ws w;
+  const int tiles = (p.B + kNT - 1) / kNT;
+  const int C = ctas_of(p.H);
+  size_t off = kStatusBytes;
+  w.perm = off;
+  off = align_up(off + (size_t)tiles * kNT * 4, 256);
+  w.tile_len = off;
+  off = align_up(off + (size_t)tiles * 4, 256);
+  w.hist = off;
+  off = align_up(off + (size_t)(p.T + 1) * 4, 256);
+  w.sorted = off;
+  off = align_up(off + (size_t)std::max(p.B, 1) * 4, 256);
+  w.gates = off;
+  off = align_up(off + (size_t)p.T * tiles * C * kGBlock, 256);
+  w.hseq = off;
+  off = align_up(off + (size_t)p.T * tiles * C * kPiece, 256);
+  w.hlast = off;
+  off = align_up(off + (size_t)std::max(p.B, 1) * p.H * 2, 256);
+  w.total = off;
+  return w;
+}
+
+template <int H, bool BF16, bool VARLEN>
+void* rec_ptr() {
+  return reinterpret_cast<void*>(&rec_kernel<H, BF16, VARLEN>);
+}
+void* pick_rec(int H, bool bf16, bool varlen) {
+  if (H == 256) {
+    if (bf16) return varlen ? rec_ptr<256, true, true>() : rec_ptr<256, true, false>();
+    return varlen ? rec_ptr<256, false, true>() : rec_ptr<256, false, false>();
+  }
+  if (bf16) return varlen ? rec_ptr<512, true, true>() : rec_ptr<512, true, false>();
+  return varlen ? rec_ptr<512, false, true>() : rec_ptr<512, false, false>();
+}
+int rec_smem(int H) { return H == 256 ? RecSmem<256>::kDyn : RecSmem<512>::kDyn; }
+int rec_threads(int H) { return H == 256 ? RecSmem<256>::kThreads : RecSmem<512>::kThreads; }
+
+cudaError_t config_rec(void* k, int H) {
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, rec_smem(H));
+  if (e == cudaSuccess && ctas_of(H) > 8) e = cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  return e;
+}
+
+// Clusters of C CTAs of the recurrence that fit on `device` at once (0 = none); cached.
+int rec_max_clusters(int device, int H) {
+  static std::mutex mu;
+  static int cache[64][2];
+  static bool init = false;
+  std::lock_guard<std::mutex> g(mu);
+  if (!init) {
+    for (auto& a : cache) a[0] = a[1] = -1;
+    init = true;
+  }
+  if (device < 0 || device >= 64) return 0;
+  int& slot = cache[device][H == 512 ? 1 : 0];
+  if (slot >= 0) return slot;
+  void* k = pick_rec(H, false, false);
+  int n = 0;
+  if (config_rec(k, H) == cudaSuccess) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(ctas_of(H) * 16), 1, 1);
+    cfg.blockDim = dim3((unsigned)rec_threads(H), 1, 1);
+    cfg.dynamicSmemBytes = rec_smem(H);
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = ctas_of(H);
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    if (cudaOccupancyMaxActiveClusters(&n, k, &cfg) != cudaSuccess) n = 0;
+  }
+  cudaGetLastError();
+  slot = n;
+  return n;
+}
+
+template <int KP, bool BF16>
+int32_t launch_proj(const GemmArgs& ga, int sms, cudaStream_t s) {
+  auto k = proj_kernel<KP, BF16>;
+  PLSTM_TRY_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmSmem<KP>::kDyn));
+  const int C = ctas_of(ga.H);
+  const int grid = std::max(C, (sms / C) * C);
+  k<<<grid, kGemmThreads, GemmSmem<KP>::kDyn, s>>>(ga);
+  PLSTM_TRY_CUDA(cudaGetLastError());
+  note_launches(1);
+  return PLSTM_OK;
+}
+
+}  // namespace tcl
+
+using namespace tcl;
+
+bool tcl_supported(const Problem& p, std::string* why) {
+  auto no = [&](const char* m) {
+    if (why) *why = m;
+    return false;
+  };
+  if (p.dtype != PLSTM_F16 && p.dtype != PLSTM_BF16) return no("activation type must be f16 or bf16");
+  if (p.H != 256 && p.H != 512) return no("hidden_size must be 256 or 512");
+  if (p.L < 1 || p.L > kMaxL) return no("num_layers must be 1..16");
+  if (p.I > kXK) return no("input_size must be <= 16");
+  if (p.T < 1 || p.T > 65535) return no("seq_len must be 1..65535");
+  int dev = p.device, major = 0, minor = 0;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess) {
+    cudaGetLastError();
+    return no("no CUDA device");
+  }
+  if (major != 10 || minor != 0) return no("device is not sm_100 (B200)");
+  if (rec_max_clusters(dev, p.H) < 1) return no("the recurrence's CTA cluster does not fit on this device");
+  return true;
+}
+
+size_t tcl_packed_size(const Problem& p) { return packed_total(p.H, p.L, p.has_linear() ? p.O : 0); }
+
+size_t tcl_workspace_size(const Problem& p) { return ws_layout(p).total; }
+
+int32_t tcl_pack(const Problem& p, int ih_layout, int hh_layout, const void* const* w_ih, const void* const* w_hh,
+                 const void* const* b_ih, const void* const* b_hh, const void* w_lin, const void* b_lin,
+                 void* packed, cudaStream_t s) {
+  PackArgs a = {};
+  for (int l = 0; l < p.L; ++l) {
+    a.w_ih[l] = w_ih[l];
+    a.w_hh[l] = w_hh[l];
+    a.b_ih[l] = b_ih ? b_ih[l] : nullptr;
+    a.b_hh[l] = b_hh ? b_hh[l] : nullptr;
+  }
+  a.w_lin = p.has_linear() ? w_lin : nullptr;
+  a.b_lin = p.has_linear() ? b_lin : nullptr;
+  a.ih_layout = ih_layout;
+  a.hh_layout = hh_layout;
+  a.dtype = p.dtype;
+  a.L = p.L;
+  a.I = p.I;
+  a.H = p.H;
+  a.O = p.has_linear() ? p.O : 0;
+  pack_kernel<<<148 * 4, 256, 0, s>>>(a, static_cast<uint8_t*>(packed));
+  PLSTM_TRY_CUDA(cudaGetLastError());
+  note_launches(1);
+  return PLSTM_OK;
+}
+
+int32_t tcl_forward(const Problem& p, const void* packed, const void* x, const int32_t* lengths, const void* h0,
+                    const void* c0, void* out, void* h_n, void* c_n, void* ws, cudaStream_t s) {
+  const int H = p.H, L = p.L, C = ctas_of(H);
+  const int tiles = (p.B + kNT - 1) / kNT;
+  const Ws w = ws_layout(p);
+  uint8_t* wsb = static_cast<uint8_t*>(ws);
+  const uint8_t* pk = static_cast<const uint8_t*>(packed);
+  int32_t* perm = reinterpret_cast<int32_t*>(wsb + w.perm);
+  int32_t* tile_len = reinterpret_cast<int32_t*>(wsb + w.tile_len);
+  const bool bf16 = p.dtype == PLSTM_BF16;
+  const bool varlen = lengths != nullptr;
+  const int O = p.has_linear() ? p.O : 0;
+  {
+    const int32_t rc = tc_make_perm(p, kNT, tiles, lengths, perm, tile_len, reinterpret_cast<int32_t*>(wsb + w.hist),
+                                    reinterpret_cast<int32_t*>(wsb + w.sorted), s);
+    if (rc != PLSTM_OK) return rc;
+  }
+  int sms = 148;
+  PLSTM_TRY_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, p.device));
+  void* rk = pick_rec(H, bf16, varlen);
+  PLSTM_TRY_CUDA(config_rec(rk, H));
+  const bool seq_out = !p.has_linear() || p.out_seq();
+  for (int l = 0; l < L; ++l) {
+    GemmArgs ga = {};
+    ga.x = static_cast<const uint16_t*>(x);
+    ga.perm = perm;
+    ga.hseq = wsb + w.hseq;
+    ga.wih = reinterpret_cast<const uint16_t*>(pk + off_wih(l, H, L));
+    ga.bias = reinterpret_cast<const float*>(pk + off_bias(H, L)) + (size_t)l * 4 * H;
+    ga.gates = reinterpret_cast<uint16_t*>(wsb + w.gates);
+    ga.status = reinterpret_cast<int*>(wsb);
+    ga.B = p.B;
+    ga.T = p.T;
+    ga.I = p.I;
+    ga.H = H;
+    ga.tiles = tiles;
+    int32_t rc;
+    if (l == 0)
+      rc = bf16 ? launch_proj<kXK, true>(ga, sms, s) : launch_proj<kXK, false>(ga, sms, s);
+    else if (H == 256)
+      rc = bf16 ? launch_proj<256, true>(ga, sms, s) : launch_proj<256, false>(ga, sms, s);
+    else
+      rc = bf16 ? launch_proj<512, true>(ga, sms, s) : launch_proj<512, false>(ga, sms, s);
+    if (rc != PLSTM_OK) return rc;
+
+    RecArgs ra = {};
+    ra.whh = pk + off_whh(l, H);
+    ra.gates = reinterpret_cast<const uint16_t*>(wsb + w.gates);
+    ra.perm = perm;
+    ra.lengths = lengths;
+    ra.tile_len = tile_len;
+    ra.h0 = h0;
+    ra.c0 = c0;
+    ra.hseq = (l + 1 < L || seq_out) ? wsb + w.hseq : nullptr;
+    ra.h_n = h_n;
+    ra.c_n = c_n;
+    ra.hlast = l + 1 == L ? reinterpret_cast<uint16_t*>(wsb + w.hlast) : nullptr;
+    ra.status = reinterpret_cast<int*>(wsb);
+    ra.B = p.B;
+    ra.T = p.T;
+    ra.layer = l;
+    ra.flags = p.flags;
+    ra.timeout_ns = (unsigned long long)p.timeout_ms * 1000000ull;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(tiles * C), 1, 1);
+    cfg.blockDim = dim3((unsigned)rec_threads(H), 1, 1);
+    cfg.dynamicSmemBytes = rec_smem(H);
+    cfg.stream = s;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = C;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    void* args[] = {&ra};
+    if (l == 0) profile_begin(s);
+    PLSTM_TRY_CUDA(cudaLaunchKernelExC(&cfg, rk, args));
+    if (l + 1 == L) profile_end(s);
+    note_launches(1);
+  }
+  const uint16_t* wlin = reinterpret_cast<const uint16_t*>(pk + off_wlin(H, L));
+  const float* blin = reinterpret_cast<const float*>(pk + off_blin(H, L, O));
+  uint16_t* o16 = static_cast<uint16_t*>(out);
+  if (p.has_linear() && !p.out_seq()) {
+    const int n = p.B * O;
+    if (bf16)
+      linear_last_kernel<true><<<(n + 255) / 256, 256, 0, s>>>(reinterpret_cast<const uint16_t*>(wsb + w.hlast), wlin,
+                                                               blin, o16, p.B, H, O);
+    else
+      linear_last_kernel<false><<<(n + 255) / 256, 256, 0, s>>>(reinterpret_cast<const uint16_t*>(wsb + w.hlast), wlin,
+                                                                blin, o16, p.B, H, O);
+  } else {
+    const int smem = kNT * (H + 1) * 4;
+    const int grid = p.T * tiles;
+    if (p.has_linear()) {
+      auto k = bf16 ? seq_out_kernel<true, true> : seq_out_kernel<false, true>;
+      PLSTM_TRY_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+      k<<<grid, 256, smem, s>>>(wsb + w.hseq, perm, lengths, wlin, blin, o16, p.B, p.T, H, O, tiles);
+    } else {
+      auto k = bf16 ? seq_out_kernel<true, false> : seq_out_kernel<false, false>;
+      PLSTM_TRY_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+      k<<<grid, 256, smem, s>>>(wsb + w.hseq, perm, lengths, wlin, blin, o16, p.B, p.T, H, 0, tiles);
+    }
+  }
+  PLSTM_TRY_CUDA(cudaGetLastError());
+  note_launches(1);
+  return PLSTM_OK;
+}
+
+}  // namespace plstm

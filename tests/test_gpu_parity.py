@@ -88,7 +88,7 @@ def test_simt_16bit_other_hidden_sizes(cuda_device, H, L):
     for dt in (torch.float16, torch.bfloat16):
         w = weights_of(m, L, dt, cuda_device)
         x = _rand_x(B, T, I, dt, cuda_device)
-        out, h_n, c_n = plstm.lstm_linear_forward(x, *w, out_mode="seq", check=True)
+        out, h_n, c_n = plstm.lstm_linear_forward(x, *w, out_mode="seq", backend="simt", check=True)
         r_out, r_h, r_c = oracle_of(x, *w, out_mode="seq")
         assert_close16(out, r_out, f"{dt} out")
         assert_close16(h_n, r_h, f"{dt} h_n")

@@ -1,0 +1,73 @@
+"""GPU parity of the tensor-core path for hidden sizes 256 and 512 (per layer a
+tcgen05 projection GEMM and a cluster recurrence with W_hh resident in tensor
+memory) against the f64 oracle, with the north star's 16-bit tolerances."""
+from __future__ import annotations
+
+import pytest
+import torch
+
+from helpers import assert_close16, make_model, oracle_of, weights_of
+import persistent_lstm_hip_b200 as plstm
+from persistent_lstm_hip_b200 import core
+
+pytestmark = pytest.mark.gpu
+
+
+def _x(B, T, I, dtype, dev, seed=1):
+    g = torch.Generator().manual_seed(seed)
+    return torch.randn(B, T, I, generator=g).to(device=dev, dtype=dtype)
+
+
+@pytest.mark.parametrize("H", [256, 512])
+@pytest.mark.parametrize("B, T, L", [(1, 1, 1), (5, 7, 2), (70, 12, 3)])
+@pytest.mark.parametrize("mode", ["seq", "last", "hseq"])
+def test_tcl_matches_oracle(cuda_device, H, B, T, L, mode):
+    I, O = 5, 24
+    dtype = torch.float16 if H == 256 else torch.bfloat16
+    m = make_model(I, H, L, O, seed=H + L)
+    w = weights_of(m, L, dtype, cuda_device)
+    x = _x(B, T, I, dtype, cuda_device, seed=B + T)
+    pw = core.PackedWeights(*w, out_mode=mode, backend="tc")
+    assert pw.backend == "tc"
+    out, h_n, c_n = pw.forward(x, check=True)
+    r_out, r_h, r_c = oracle_of(x, *w, out_mode=mode)
+    assert_close16(out, r_out, "out")
+    assert_close16(h_n, r_h, "h_n")
+    assert_close16(c_n, r_c, "c_n")
+
+
+@pytest.mark.parametrize("H, dtype", [(256, torch.bfloat16), (512, torch.float16)])
+@pytest.mark.parametrize("mode", ["seq", "last"])
+def test_tcl_varlen_and_state(cuda_device, H, dtype, mode):
+    B, T, I, L, O = 67, 16, 5, 2, 24
+    m = make_model(I, H, L, O, seed=11)
+    w = weights_of(m, L, dtype, cuda_device)
+    x = _x(B, T, I, dtype, cuda_device)
+    g = torch.Generator().manual_seed(3)
+    lens = torch.randint(0, T + 1, (B,), generator=g, dtype=torch.int32)
+    lens[0] = T
+    hx = ((0.5 * torch.randn(L, B, H, generator=g)).to(cuda_device, dtype),
+          (0.5 * torch.randn(L, B, H, generator=g)).to(cuda_device, dtype))
+    pw = core.PackedWeights(*w, out_mode=mode, backend="tc")
+    out, h_n, c_n = pw.forward(x, lengths=lens.to(cuda_device), hx=hx, check=True)
+    r_out, r_h, r_c = oracle_of(x, *w, lengths=lens, hx=hx, out_mode=mode)
+    assert_close16(out, r_out, "out")
+    assert_close16(h_n, r_h, "h_n")
+    assert_close16(c_n, r_c, "c_n")
+    if mode == "seq":
+        o = out.cpu()
+        for b in range(B):
+            assert torch.all(o[b, int(lens[b]):] == 0)
+
+
+def test_tcl_is_the_auto_backend_and_matches_simt(cuda_device):
+    """The default backend for H = 256 is the tensor-core path; it agrees with the
+    FFMA backend on the same 16-bit weights."""
+    B, T, I, H, L, O = 9, 20, 5, 256, 2, 24
+    m = make_model(I, H, L, O, seed=2)
+    w = weights_of(m, L, torch.float16, cuda_device)
+    x = _x(B, T, I, torch.float16, cuda_device)
+    assert core.PackedWeights(*w, out_mode="last").backend == "tc"
+    a, _, _ = plstm.lstm_linear_forward(x, *w, out_mode="last", check=True)
+    b, _, _ = plstm.lstm_linear_forward(x, *w, out_mode="last", backend="simt", check=True)
+    assert (a.float() - b.float()).abs().max().item() <= 2e-2

@@ -126,6 +126,12 @@ int32_t tc_forward(const Problem& p, const void* packed, const void* x, const in
 int32_t tc_make_perm(const Problem& p, int N, int tiles, const int32_t* lengths, int32_t* perm, int32_t* tile_len,
                      int32_t* hist, int32_t* sorted, cudaStream_t s);
 
+// x[B][T][I] (I <= 16) -> xp[tiles][T][N rows x 16] 16-bit K-major core matrices
+// (8 rows x 16 bytes; K groups 128 bytes apart, row groups 256 bytes apart), rows in
+// tile order, zero for padding rows.
+int32_t tc_xpack(const Problem& p, int N, int tiles, const void* x, const int32_t* perm, uint8_t* xp,
+                 cudaStream_t s);
+
 // tcgen05 layer-sequential backend for H = 256 / 512 (plstm_tcl.cu): per layer a
 // projection GEMM and a cluster-wide recurrence; the H128 entry points above
 // forward these sizes to it.

@@ -1695,6 +1695,18 @@ int32_t tc_make_perm(const Problem& p, int N, int tiles, const int32_t* lengths,
   return PLSTM_OK;
 }
 
+int32_t tc_xpack(const Problem& p, int N, int tiles, const void* x, const int32_t* perm, uint8_t* xp,
+                 cudaStream_t s) {
+  if (p.T <= 0) return PLSTM_OK;
+  const int nthr = 256;
+  const int64_t total = (int64_t)tiles * p.T * N;
+  const int grid = (int)std::min<int64_t>((total + nthr - 1) / nthr, 148 * 32);
+  tc_xpack_kernel<uint16_t><<<grid, nthr, 0, s>>>(static_cast<const uint16_t*>(x), perm, xp, p.B, p.T, p.I, N, tiles);
+  PLSTM_TRY_CUDA(cudaGetLastError());
+  note_launches(1);
+  return PLSTM_OK;
+}
+
 bool tc_supported(const Problem& p, std::string* why) {
   if (p.H == 256 || p.H == 512) return tcl_supported(p, why);
   auto no = [&](const char* m) {
@@ -1755,19 +1767,14 @@ int32_t tc_forward(const Problem& p, const void* packed, const void* x, const in
   uint8_t* wsb = static_cast<uint8_t*>(ws);
   int32_t* perm = reinterpret_cast<int32_t*>(wsb + w.perm);
   int32_t* tile_len = reinterpret_cast<int32_t*>(wsb + w.tile_len);
-  const int nthr = 256;
   {
     const int32_t rc = tc_make_perm(p, pl.N, pl.tiles, lengths, perm, tile_len,
                                     reinterpret_cast<int32_t*>(wsb + w.hist), reinterpret_cast<int32_t*>(wsb + w.sorted), s);
     if (rc != PLSTM_OK) return rc;
   }
-  if (p.T > 0) {
-    const int64_t total = (int64_t)pl.tiles * p.T * pl.N;
-    const int grid = (int)std::min<int64_t>((total + nthr - 1) / nthr, 148 * 32);
-    tc_xpack_kernel<uint16_t><<<grid, nthr, 0, s>>>(static_cast<const uint16_t*>(x), perm, wsb + w.xp, p.B,
-                                                    p.T, p.I, pl.N, pl.tiles);
-    PLSTM_TRY_CUDA(cudaGetLastError());
-    note_launches(1);
+  {
+    const int32_t rc = tc_xpack(p, pl.N, pl.tiles, x, perm, wsb + w.xp, s);
+    if (rc != PLSTM_OK) return rc;
   }
   Params kp = {};
   kp.packed = static_cast<const uint8_t*>(packed);

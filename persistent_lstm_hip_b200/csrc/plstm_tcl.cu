@@ -23,10 +23,11 @@
 //      CTA's own 32 units issued as soon as it has written them, the rest once the
 //      other C - 1 pieces have landed; the compute warps add the projected gate
 //      block (prefetched three steps ahead by bulk copy), apply the gate math in
-//      registers (c in f32), write their h piece and the last one to finish pushes
-//      it to the C - 1 peers with shared -> distributed shared bulk copies that
-//      complete on the peers' barriers.  The control warp stores the piece to the
-//      h sequence in global memory for the next layer's projection.
+//      registers (c in f32), write their h piece (and store it to the layer's h
+//      sequence in global memory, the next layer's projection input); the last
+//      one to finish pushes the piece to the C - 1 peers with shared -> distributed
+//      shared bulk copies that complete on the peers' barriers, then prefetches the
+//      gate block of step t + 3.
 //   3. the Linear head (or the h sequence output) from the last layer's h.
 // Layers run one after the other; every wait in the kernels is bounded.
 #include <algorithm>
@@ -139,13 +140,6 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatil
   return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
 
-__device__ __forceinline__ void bulk_s2g(void* gdst, uint32_t ssrc, uint32_t bytes) {
-  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gdst), "r"(ssrc), "r"(bytes)
-               : "memory");
-}
-__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
-__device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 // ---- packing ------------------------------------------------------------------------
 struct PackArgs {
@@ -220,31 +214,40 @@ __global__ void pack_kernel(const PackArgs a, uint8_t* packed) {
 }
 
 // ---- projection GEMM ----------------------------------------------------------------
-constexpr int kGemmThreads = 9 * 32;  // warps 0-3 producers, 4 MMA issue, 5-8 epilogue
-constexpr int kAStages = 4;
+// One job = (step t, batch tile, recurrent CTA r): D[128 gate rows x 64 batch rows] =
+// W_ih[r's rows] . in(t, tile)^T.  W_ih's slice stays resident in tensor memory (A
+// operand); the input tile (all K of one step and batch tile: layer l-1's h pieces,
+// or the packed x tile for layer 0) arrives with one bulk copy into a 3-stage ring;
+// two TMEM accumulators let the epilogue of one job overlap the MMAs of the next.
+// The epilogue (lane = gate row) adds the bias and writes the gate block row of the
+// recurrence directly: 64 contiguous 16-bit values.  The CTAs sharing a step / tile
+// (one per r) run together, so each input tile is read from HBM once and from L2
+// C times.
+constexpr int kGemmThreads = 6 * 32;  // warp 0 loads, warp 1 issues MMAs, warps 2-5 epilogue
+constexpr int kBStages = 3;
 
 template <int KP>
 struct GemmSmem {
-  static constexpr int kChunks = KP <= kXK ? 1 : KP / 64;
-  static constexpr int kChunkBytes = KP <= kXK ? kRows * 32 : kRows * 128;  // 128 rows of one K chunk
-  static constexpr int kB = 0;                                            // resident W_ih slice
-  static constexpr int kA = kB + kChunks * kChunkBytes;                   // A stages
-  static constexpr int kBias = kA + kAStages * kChunkBytes;
+  static constexpr int kStage = KP <= kXK ? kNT * 32 : KP * kNT * 2;  // one step's input tile
+  static constexpr int kB = 0;
+  static constexpr int kBias = kB + kBStages * kStage;
   static constexpr int kBar = kBias + kRows * 4;
   static constexpr int kTmemSlot = kBar + 96;
   static constexpr int kEnd = kBar + 128;
   static constexpr int kDyn = kEnd + 1024;
+  static constexpr int kACols = KP <= kXK ? 8 : KP / 2;  // W_ih slice: 128 lanes x KP 16-bit values
+  static constexpr int kTmemCols = kACols + 2 * kNT <= 256 ? 256 : 512;
+  static_assert(kDyn <= 232448, "shared memory");
 };
 
 struct GemmArgs {
-  const uint16_t* x;      // layer 0: [B][T][I]
-  const int32_t* perm;    // [tiles * kNT]: batch row of each tile row (-1 = padding)
-  const uint8_t* hseq;    // layers >= 1: [T][tiles][C] h pieces of layer l-1
-  const uint16_t* wih;    // [4H][KP] this layer's permuted W_ih
-  const float* bias;      // [4H] this layer's permuted, pre-scaled bias
-  uint16_t* gates;        // [T][tiles][C][128][kGRow]
+  const uint8_t* xp;    // layer 0: [tiles][T] packed x tiles (64 rows x 16, core matrices)
+  const uint8_t* hseq;  // layers >= 1: [T][tiles][C] h pieces of layer l-1
+  const uint16_t* wih;  // [4H][KP] this layer's permuted, pre-scaled W_ih
+  const float* bias;    // [4H] this layer's permuted, pre-scaled bias
+  uint16_t* gates;      // [T][tiles][C][128][kGRow]
   int* status;
-  int B, T, I, H, tiles;
+  int T, H, tiles;
 };
 
 template <int KP, bool BF16>
@@ -255,22 +258,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1) proj_kernel(const GemmArgs a)
   const uint32_t sbase = ptx::smem_u32(sm);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int C = ctas_of(a.H);
-  const int Bp = a.tiles * kNT;
-  const int mt_per_t = (Bp + kRows - 1) / kRows;
-  const int total_m = a.T * mt_per_t;
-  const int r = blockIdx.x % C;  // gate-row tile = recurrent CTA rank
-  const int cpr = (int)(gridDim.x - r + C - 1) / C;
-  const int first = blockIdx.x / C;
-  const int my = first < total_m ? (total_m - first + cpr - 1) / cpr : 0;
+  const long long jobs = (long long)a.T * a.tiles * C;
+  const int r = blockIdx.x % C;  // gridDim.x is a multiple of C: every job of this CTA has the same r
+  const int my = blockIdx.x < jobs ? (int)((jobs - blockIdx.x + gridDim.x - 1) / gridDim.x) : 0;
   const unsigned long long kTimeout = 2000000000ull;
-
   const uint32_t bar = sbase + S::kBar;
-  const uint32_t a_full = bar, a_empty = bar + 32, d_full = bar + 64, d_empty = bar + 80;
+  const uint32_t b_full = bar, b_empty = bar + 24, d_full = bar + 48, d_empty = bar + 64;
   float* bias_s = reinterpret_cast<float*>(sm + S::kBias);
   if (tid == 0) {
-    for (int s = 0; s < kAStages; ++s) {
-      ptx::mbar_init(a_full + 8 * s, 4);
-      ptx::mbar_init(a_empty + 8 * s, 1);
+    for (int s = 0; s < kBStages; ++s) {
+      ptx::mbar_init(b_full + 8 * s, 1);
+      ptx::mbar_init(b_empty + 8 * s, 1);
     }
     for (int s = 0; s < 2; ++s) {
       ptx::mbar_init(d_full + 8 * s, 1);
@@ -278,170 +276,140 @@ __global__ void __launch_bounds__(kGemmThreads, 1) proj_kernel(const GemmArgs a)
     }
     ptx::fence_mbar_init_cluster();
   }
-  if (warp == 4) {
-    ptx::tmem_alloc(sbase + S::kTmemSlot, 256);
+  if (warp == 1) {
+    ptx::tmem_alloc(sbase + S::kTmemSlot, S::kTmemCols);
     ptx::tmem_relinquish();
   }
-  // Resident B operand: this CTA's 128 gate rows of W_ih, K-major.
-  for (int i = tid; i < kRows * KP / 8; i += kGemmThreads) {
-    const int row = i / (KP / 8), k = (i % (KP / 8)) * 8;
-    const uint4 v = *reinterpret_cast<const uint4*>(a.wih + ((size_t)r * kRows + row) * KP + k);
-    uint32_t off;
-    if (KP <= kXK)
-      off = none16_off(row, k);
-    else
-      off = (uint32_t)((k >> 6) * S::kChunkBytes) + sw128_off(row, k & 63);
-    *reinterpret_cast<uint4*>(sm + S::kB + off) = v;
-  }
   for (int i = tid; i < kRows; i += kGemmThreads) bias_s[i] = a.bias[r * kRows + i];
-  ptx::fence_proxy_async_smem();
+  __syncthreads();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(sm + S::kTmemSlot);
+  // W_ih slice -> TMEM columns [0, KP / 2): epilogue warp (quadrant q) stores rows 32 q + lane.
+  if (warp >= 2) {
+    const int q = warp & 3;
+    const int row = 32 * q + lane;
+    const uint32_t* src = reinterpret_cast<const uint32_t*>(a.wih + ((size_t)r * kRows + row) * KP);
+    const uint32_t lane_off = (uint32_t)(32 * q) << 16;
+    if (KP <= kXK) {
+      uint32_t v[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = src[i];
+      ptx::tmem_st_32x32b_x8(tmem + lane_off, v);
+    } else {
+#pragma unroll 1
+      for (int c = 0; c < S::kACols; c += 32) {
+        uint32_t v[32];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const uint4 u = reinterpret_cast<const uint4*>(src + c)[i];
+          v[4 * i + 0] = u.x;
+          v[4 * i + 1] = u.y;
+          v[4 * i + 2] = u.z;
+          v[4 * i + 3] = u.w;
+        }
+        ptx::tmem_st_32x32b_x32(tmem + lane_off + (uint32_t)c, v);
+      }
+    }
+    ptx::tmem_wait_st();
+  }
   ptx::tc_fence_before();
   __syncthreads();
   ptx::tc_fence_after();
-  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(sm + S::kTmemSlot);
 
-  if (warp < 4) {
-    // ---------------- producers: thread = one row of the A tile ----------------
-    const int row = tid;
-    int cnt = 0;
-    bool ok = true;
-    for (int it = 0; it < my && ok; ++it) {
-      const int mt = first + it * cpr;
-      const int t = mt / mt_per_t;
-      const int p = (mt % mt_per_t) * kRows + row;
-      for (int c = 0; c < S::kChunks; ++c, ++cnt) {
-        const int s = cnt % kAStages;
-        if (cnt >= kAStages && !wait_bar(a_empty + 8 * s, ((cnt / kAStages) - 1) & 1, nullptr, kTimeout)) {
-          if (lane == 0) report_status(a.status, PLSTM_ETIMEOUT, 0x7fff0000);
-          ok = false;
+  auto job_src = [&](int k, int* t_out, int* tile_out) -> const uint8_t* {
+    const long long j = blockIdx.x + (long long)k * gridDim.x;
+    const long long ts = j / C;
+    const int t = (int)(ts / a.tiles), tile = (int)(ts % a.tiles);
+    *t_out = t;
+    *tile_out = tile;
+    if (KP <= kXK) return a.xp + ((size_t)tile * a.T + t) * (size_t)(kNT * 32);
+    return a.hseq + ((size_t)t * a.tiles + tile) * (size_t)C * kPiece;
+  };
+
+  if (warp == 0) {
+    // ---------------- loads ----------------
+    if (lane == 0) {
+      for (int k = 0; k < my; ++k) {
+        const int s = k % kBStages;
+        if (k >= kBStages && !wait_bar(b_empty + 8 * s, ((k / kBStages) - 1) & 1, nullptr, kTimeout)) {
+          report_status(a.status, PLSTM_ETIMEOUT, 0x7ffe0000);
           break;
         }
-        uint8_t* A = sm + S::kA + s * S::kChunkBytes;
-        if (KP <= kXK) {
-          uint16_t v[16];
-#pragma unroll
-          for (int k = 0; k < 16; ++k) v[k] = 0;
-          if (p < Bp) {
-            const int b = a.perm[p];
-            if (b >= 0) {
-              const uint16_t* src = a.x + ((size_t)b * a.T + t) * a.I;
-              for (int k = 0; k < a.I && k < 16; ++k) v[k] = src[k];
-            }
-          }
-          uint4 lo, hi;
-          lo.x = v[0] | (v[1] << 16); lo.y = v[2] | (v[3] << 16); lo.z = v[4] | (v[5] << 16); lo.w = v[6] | (v[7] << 16);
-          hi.x = v[8] | (v[9] << 16); hi.y = v[10] | (v[11] << 16); hi.z = v[12] | (v[13] << 16); hi.w = v[14] | (v[15] << 16);
-          *reinterpret_cast<uint4*>(A + none16_off(row, 0)) = lo;
-          *reinterpret_cast<uint4*>(A + none16_off(row, 8)) = hi;
-        } else {
-          uint4 v[8];
-          if (p < Bp) {
-            const int tile = p / kNT, n = p % kNT;
-            const uint8_t* tbase = a.hseq + ((size_t)t * a.tiles + tile) * (size_t)C * kPiece;
-#pragma unroll
-            for (int g = 0; g < 8; ++g) {
-              const int kg = c * 8 + g;  // 8-unit K group of the previous layer's h
-              v[g] = *reinterpret_cast<const uint4*>(tbase + (size_t)kg * kKG + (n >> 3) * 128 + (n & 7) * 16);
-            }
-          } else {
-#pragma unroll
-            for (int g = 0; g < 8; ++g) v[g] = make_uint4(0, 0, 0, 0);
-          }
-#pragma unroll
-          for (int g = 0; g < 8; ++g) *reinterpret_cast<uint4*>(A + sw128_off(row, 8 * g)) = v[g];
-        }
-        ptx::fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) ptx::mbar_arrive(a_full + 8 * s);
+        int t, tile;
+        const uint8_t* src = job_src(k, &t, &tile);
+        ptx::mbar_arrive_expect_tx(b_full + 8 * s, S::kStage);
+        ptx::bulk_g2s(sbase + S::kB + s * S::kStage, src, S::kStage, b_full + 8 * s);
       }
     }
-  } else if (warp == 4) {
+    __syncwarp();
+  } else if (warp == 1) {
     // ---------------- MMA issue ----------------
-    constexpr uint32_t idesc = ptx::idesc_f16(128, 128, BF16);
-    int cnt = 0;
-    bool ok = true;
-    for (int it = 0; it < my && ok; ++it) {
-      const int db = it & 1;
-      if (it >= 2) {
-        int w = 1;
-        if (lane == 0) w = wait_bar(d_empty + 8 * db, ((it - 2) >> 1) & 1, nullptr, kTimeout) ? 1 : 0;
-        if (!__shfl_sync(0xffffffffu, w, 0)) break;
+    constexpr uint32_t idesc = ptx::idesc_f16(128, kNT, BF16);
+    for (int k = 0; k < my; ++k) {
+      const int s = k % kBStages, db = k & 1;
+      int w = 1;
+      if (lane == 0) {
+        if (k >= 2) w = wait_bar(d_empty + 8 * db, ((k - 2) >> 1) & 1, nullptr, kTimeout) ? 1 : 0;
+        if (w) w = wait_bar(b_full + 8 * s, (k / kBStages) & 1, nullptr, kTimeout) ? 1 : 0;
       }
-      const uint32_t d = tmem + (uint32_t)(db * 128);
-      for (int c = 0; c < S::kChunks; ++c, ++cnt) {
-        const int s = cnt % kAStages;
-        int w = 1;
-        if (lane == 0) w = wait_bar(a_full + 8 * s, (cnt / kAStages) & 1, nullptr, kTimeout) ? 1 : 0;
-        if (!__shfl_sync(0xffffffffu, w, 0)) {
-          ok = false;
-          break;
+      if (!__shfl_sync(0xffffffffu, w, 0)) break;
+      if (ptx::elect_one()) {
+        ptx::tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(S::kACols + db * kNT);
+        const uint32_t b0 = sbase + S::kB + s * S::kStage;
+        if (KP <= kXK) {
+          ptx::mma_f16_ts(d, tmem, ptx::desc_k_none(b0, 128, 256), idesc, 0u);
+        } else {
+#pragma unroll 4
+          for (int i = 0; i < KP / 16; ++i)
+            ptx::mma_f16_ts(d, tmem + (uint32_t)(8 * i), ptx::desc_k_none(b0 + (uint32_t)(2 * i * kKG), kKG, 128),
+                            idesc, i != 0 ? 1u : 0u);
         }
-        if (ptx::elect_one()) {
-          ptx::tc_fence_after();
-          const uint32_t a0 = sbase + S::kA + s * S::kChunkBytes;
-          const uint32_t b0 = sbase + S::kB + c * S::kChunkBytes;
-          if (KP <= kXK) {
-            ptx::mma_f16_ss(d, ptx::desc_k_none(a0, 128, 256), ptx::desc_k_none(b0, 128, 256), idesc, 0u);
-          } else {
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-              ptx::mma_f16_ss(d, ptx::desc_k_sw128(a0 + kk * 32), ptx::desc_k_sw128(b0 + kk * 32), idesc,
-                              (c | kk) != 0 ? 1u : 0u);
-          }
-          ptx::mma_commit(a_empty + 8 * s);
-        }
-        __syncwarp();
+        ptx::mma_commit(b_empty + 8 * s);
+        ptx::mma_commit(d_full + 8 * db);
       }
-      if (ok && ptx::elect_one()) ptx::mma_commit(d_full + 8 * db);
       __syncwarp();
     }
   } else {
-    // ---------------- epilogue: lane = batch row, columns = gate rows ----------------
+    // ---------------- epilogue: lane = gate row, columns = the tile's 64 batch rows ----------------
     const int q = warp & 3;
     const int row = 32 * q + lane;
-    for (int it = 0; it < my; ++it) {
-      const int db = it & 1;
-      if (!wait_bar(d_full + 8 * db, (it >> 1) & 1, nullptr, kTimeout)) break;
+    const float bv = bias_s[row];
+    for (int k = 0; k < my; ++k) {
+      const int db = k & 1;
+      if (!wait_bar(d_full + 8 * db, (k >> 1) & 1, nullptr, kTimeout)) break;
       ptx::tc_fence_after();
-      const int mt = first + it * cpr;
-      const int t = mt / mt_per_t;
-      const int p = (mt % mt_per_t) * kRows + row;
-      const bool valid = p < Bp;
-      uint16_t* dst = a.gates;
-      if (valid) {
-        const int tile = p / kNT, n = p % kNT;
-        dst += (((size_t)t * a.tiles + tile) * C + r) * (size_t)kRows * kGRow + n;
-      }
-#pragma unroll 1
-      for (int cb = 0; cb < 4; ++cb) {
-        uint32_t v[32];
-        const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(db * 128 + cb * 32);
-        ptx::tmem_ld_32x32b_x16(taddr, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
-        ptx::tmem_ld_32x32b_x16(taddr + 16, *reinterpret_cast<uint32_t(*)[16]>(&v[16]));
-        ptx::tmem_wait_ld();
-        if (valid) {
+      uint32_t v[kNT];
+      const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(S::kACols + db * kNT);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int col = cb * 32 + j;
-            dst[(size_t)col * kGRow] = to_bits<BF16>(__uint_as_float(v[j]) + bias_s[col]);
-          }
-        }
-      }
+      for (int c = 0; c < kNT; c += 16) ptx::tmem_ld_32x32b_x16(taddr + c, *reinterpret_cast<uint32_t(*)[16]>(&v[c]));
+      ptx::tmem_wait_ld();
       ptx::tc_fence_before();
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(d_empty + 8 * db);
+      int t, tile;
+      job_src(k, &t, &tile);
+      uint4* dst = reinterpret_cast<uint4*>(a.gates + ((((size_t)t * a.tiles + tile) * C + r) * kRows + row) * kGRow);
+#pragma unroll
+      for (int c = 0; c < kNT / 8; ++c) {
+        uint4 o;
+        o.x = pack2_bits<BF16>(__uint_as_float(v[8 * c + 0]) + bv, __uint_as_float(v[8 * c + 1]) + bv);
+        o.y = pack2_bits<BF16>(__uint_as_float(v[8 * c + 2]) + bv, __uint_as_float(v[8 * c + 3]) + bv);
+        o.z = pack2_bits<BF16>(__uint_as_float(v[8 * c + 4]) + bv, __uint_as_float(v[8 * c + 5]) + bv);
+        o.w = pack2_bits<BF16>(__uint_as_float(v[8 * c + 6]) + bv, __uint_as_float(v[8 * c + 7]) + bv);
+        dst[c] = o;
+      }
     }
   }
   ptx::tc_fence_before();
   __syncthreads();
-  if (warp == 4) {
+  if (warp == 1) {
     ptx::tc_fence_after();
-    ptx::tmem_dealloc(tmem, 256);
+    ptx::tmem_dealloc(tmem, S::kTmemCols);
   }
 }
 
 // ---- recurrence -----------------------------------------------------------------------
-template <int H>
+template <int H, int NCW>
 struct RecSmem {
   static constexpr int C = H / kU;
   static constexpr int kTile = H * kNT * 2;  // one h tile (all units x 64 rows)
@@ -453,7 +421,7 @@ struct RecSmem {
   static constexpr int kPerm = kBar + 128, kLens = kPerm + 4 * kNT;
   static constexpr int kEnd = kLens + 4 * kNT;
   static constexpr int kDyn = kEnd + 1024;
-  static constexpr int kComputeWarps = 4;  // one per TMEM lane quadrant, 64 columns each
+  static constexpr int kComputeWarps = NCW;  // NCW / 4 per TMEM lane quadrant, 256 / NCW columns each
   static constexpr int kThreads = (kComputeWarps + 1) * 32;
   static constexpr int kACols = H / 2;  // W_hh slice: 128 lanes x H 16-bit values
   static constexpr int kD = kACols;     // gate accumulator [128 x 64] (single buffer)
@@ -476,7 +444,19 @@ struct RecArgs {
   int* status;
   int B, T, layer, flags;
   unsigned long long timeout_ns;
+  unsigned long long* trace;  // PLSTM_FLAG_TRACE: [C][64][8] clock64 stamps of cluster 0, or null
+  int trace_t0;
 };
+
+// Trace events (steps trace_t0 .. +63 of cluster 0): control warp 0 peer pieces of
+// h_{t-1} landed, 1 peer MMAs + commit issued, 2 compute warps done with step t,
+// 3 own-piece MMAs of step t+1 issued; compute warp 0: 4 accumulator ready,
+// 5 loaded, 6 h written; 7 the step's pusher issued its copies.
+constexpr int kTraceSteps = 64, kTraceEvents = 8;
+__device__ __forceinline__ void trace_mark(const RecArgs& a, int tile, int r, int t, int ev) {
+  if (a.trace != nullptr && tile == 0 && t >= a.trace_t0 && t < a.trace_t0 + kTraceSteps)
+    a.trace[((size_t)r * kTraceSteps + (t - a.trace_t0)) * kTraceEvents + ev] = clock64();
+}
 
 __device__ __forceinline__ void rec_abort(const RecArgs& a, uint8_t* sm_abort, int ncta, int step) {
   const uint32_t local = ptx::smem_u32(sm_abort);
@@ -484,11 +464,11 @@ __device__ __forceinline__ void rec_abort(const RecArgs& a, uint8_t* sm_abort, i
   report_status(a.status, PLSTM_ETIMEOUT, (int)((blockIdx.x & 0x7fff) << 16) | (step & 0xffff));
 }
 
-template <int H, bool BF16, bool VARLEN>
-__global__ void __launch_bounds__(RecSmem<H>::kThreads, 1) rec_kernel(const RecArgs a) {
-  using S = RecSmem<H>;
+template <int H, int NCW, bool BF16, bool VARLEN>
+__global__ void __launch_bounds__(RecSmem<H, NCW>::kThreads, 1) rec_kernel(const RecArgs a) {
+  using S = RecSmem<H, NCW>;
   constexpr int C = S::C;
-  constexpr int CPW = kNT / 8;  // 8-column chunks per compute warp
+  constexpr int CPW = kNT * 4 / (NCW * 8);  // 8-column chunks per compute warp
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = ptx::smem_u32(sm);
@@ -538,8 +518,8 @@ __global__ void __launch_bounds__(RecSmem<H>::kThreads, 1) rec_kernel(const RecA
   ptx::fence_proxy_async_smem();
   ptx::tc_fence_after();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(sm + S::kTmemSlot);
-  // W_hh slice -> TMEM columns [0, H / 2): compute warp q stores its quadrant's 32 rows.
-  if (warp < S::kComputeWarps) {
+  // W_hh slice -> TMEM columns [0, H / 2): warp q < 4 stores its quadrant's 32 rows.
+  if (warp < 4) {
     const int row = 32 * warp + lane;
     const uint32_t lane_off = (uint32_t)(32 * warp) << 16;
     const uint4* src = reinterpret_cast<const uint4*>(a.whh + ((size_t)r * kRows + row) * H * 2);
@@ -629,10 +609,12 @@ __global__ void __launch_bounds__(RecSmem<H>::kThreads, 1) rec_kernel(const RecA
           fail(t);
           break;
         }
+        if (lane == 0) trace_mark(a, tile, r, t, 0);
         if (t + 2 < Tt && ptx::elect_one()) ptx::mbar_arrive_expect_tx(bar_rec + 8 * b, rec_bytes);
         __syncwarp();
         issue_others(t, false);
         commit(t);
+        if (lane == 0) trace_mark(a, tile, r, t, 1);
       }
       // Compute warps done with step t: its gate block slot and accumulator are free,
       // h(t)'s own piece is written (buffer b ^ 1).
@@ -640,29 +622,17 @@ __global__ void __launch_bounds__(RecSmem<H>::kThreads, 1) rec_kernel(const RecA
         fail(t);
         break;
       }
-      if (t + 3 < Tt) load_gates(t + 3);
+      if (lane == 0) trace_mark(a, tile, r, t, 2);
       if (t + 1 < Tt) {
-        // Step t + 1 writes h(t + 1) into buffer b, the source of the h-sequence
-        // store issued at step t - 1: that store must have read it first.
-        if (a.hseq != nullptr && lane == 0) bulk_wait_read0();
-        __syncwarp();
         issue(t + 1, 2 * r, 2 * r + 2, true);
-      }
-      if (a.hseq != nullptr) {
-        if (lane == 0) {
-          const uint32_t piece = bbuf(b ^ 1) + (uint32_t)(r * kPiece);
-          bulk_s2g(a.hseq + (((size_t)t * gridDim.x / C + tile) * C + r) * (size_t)kPiece, piece, kPiece);
-          bulk_commit();
-        }
-        __syncwarp();
+        if (lane == 0) trace_mark(a, tile, r, t, 3);
       }
     }
-    if (a.hseq != nullptr && lane == 0) bulk_wait0();
-    __syncwarp();
   } else {
     // ============================ compute warps ============================
-    const int q = warp;
+    const int q = warp & 3, cg = warp >> 2;  // TMEM lane quadrant, column group
     const int j8 = lane >> 2, cpair = (lane & 3) * 2;
+    const int n0 = 8 * CPW * cg;
     const int ul = 8 * q + j8;  // unit within this CTA's 32
     const int u = kU * r + ul;  // unit within the layer
     float c_st[CPW][2];
@@ -672,7 +642,7 @@ __global__ void __launch_bounds__(RecSmem<H>::kThreads, 1) rec_kernel(const RecA
     for (int jc = 0; jc < CPW; ++jc)
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
-        const int n = 8 * jc + cpair + e;
+        const int n = n0 + 8 * jc + cpair + e;
         const int bb = perm_s[n];
         bidx[jc][e] = bb;
         len_c[jc][e] = lens_s[n];
@@ -694,14 +664,17 @@ __global__ void __launch_bounds__(RecSmem<H>::kThreads, 1) rec_kernel(const RecA
         break;
       }
       ptx::tc_fence_after();
+      if (warp == 0 && lane == 0) trace_mark(a, tile, r, t, 4);
       uint32_t rif[4 * CPW], rgo[4 * CPW];
       const uint32_t lo = (uint32_t)(32 * q) << 16, hi = (uint32_t)(32 * q + 16) << 16;
-      ptx::tmem_ld_16x256b_x4(dcol + lo, *reinterpret_cast<uint32_t(*)[16]>(&rif[0]));
-      ptx::tmem_ld_16x256b_x4(dcol + lo + 32, *reinterpret_cast<uint32_t(*)[16]>(&rif[16]));
-      ptx::tmem_ld_16x256b_x4(dcol + hi, *reinterpret_cast<uint32_t(*)[16]>(&rgo[0]));
-      ptx::tmem_ld_16x256b_x4(dcol + hi + 32, *reinterpret_cast<uint32_t(*)[16]>(&rgo[16]));
+#pragma unroll
+      for (int i = 0; i < CPW / 4; ++i) {
+        ptx::tmem_ld_16x256b_x4(dcol + lo + (uint32_t)(n0 + 32 * i), *reinterpret_cast<uint32_t(*)[16]>(&rif[16 * i]));
+        ptx::tmem_ld_16x256b_x4(dcol + hi + (uint32_t)(n0 + 32 * i), *reinterpret_cast<uint32_t(*)[16]>(&rgo[16 * i]));
+      }
       ptx::tmem_wait_ld();
       ptx::tc_fence_before();
+      if (warp == 0 && lane == 0) trace_mark(a, tile, r, t, 5);
       // Projected input + bias of the four gates of this thread's cells.
       const uint8_t* gsl = sm + S::kG + gs * kGBlock;
       float pre[4][CPW][2];
@@ -710,7 +683,7 @@ __global__ void __launch_bounds__(RecSmem<H>::kThreads, 1) rec_kernel(const RecA
         const uint8_t* grow = gsl + (size_t)(32 * q + 8 * g + j8) * kGRow * 2;
 #pragma unroll
         for (int jc = 0; jc < CPW; ++jc) {
-          const float2 gv = from_bits2<BF16>(*reinterpret_cast<const uint32_t*>(grow + (8 * jc + cpair) * 2));
+          const float2 gv = from_bits2<BF16>(*reinterpret_cast<const uint32_t*>(grow + (n0 + 8 * jc + cpair) * 2));
           const uint32_t* acc = g < 2 ? rif : rgo;
           const int base = 4 * jc + (g & 1) * 2;
           pre[g][jc][0] = __uint_as_float(acc[base]) + gv.x;
@@ -718,6 +691,8 @@ __global__ void __launch_bounds__(RecSmem<H>::kThreads, 1) rec_kernel(const RecA
         }
       }
       uint8_t* dst = sm + S::kB + (b ^ 1) * S::kTile;
+      // The layer's h sequence (the next layer's projection input, or the output).
+      uint8_t* gdst = a.hseq != nullptr ? a.hseq + ((size_t)t * (gridDim.x / C) + tile) * (size_t)C * kPiece : nullptr;
 #pragma unroll
       for (int jc = 0; jc < CPW; ++jc) {
         float h[2], cn[2];
@@ -735,22 +710,33 @@ __global__ void __launch_bounds__(RecSmem<H>::kThreads, 1) rec_kernel(const RecA
             c_st[jc][e] = cn[e];
             h_st[jc][e] = (uint16_t)(e == 0 ? bits & 0xffffu : bits >> 16);
           }
-          *reinterpret_cast<uint16_t*>(dst + hoff(u, 8 * jc + cpair + e)) = h_st[jc][e];
+          const uint32_t off = hoff(u, n0 + 8 * jc + cpair + e);
+          *reinterpret_cast<uint16_t*>(dst + off) = h_st[jc][e];
+          if (gdst != nullptr) *reinterpret_cast<uint16_t*>(gdst + off) = h_st[jc][e];
         }
       }
       ptx::fence_proxy_async_smem();
+      if (warp == 0 && lane == 0) trace_mark(a, tile, r, t, 6);
       __syncwarp();
       if (lane == 0) {
         ptx::mbar_arrive(bar_hready + 8 * b);
         // The last warp to finish pushes the piece to the peers (acquire-release
         // counter: the other warps' writes, fenced for the async proxy, come first).
-        if (t + 1 < Tt && ptx::atom_add_acq_rel_smem(sbase + S::kDone, 1u) % 4u == 3u) {
+        // It then prefetches the gate block of step t + 3 into this step's slot
+        // (after the pushes: they are on the critical path).
+        if (t + 1 < Tt && ptx::atom_add_acq_rel_smem(sbase + S::kDone, 1u) % (uint32_t)S::kComputeWarps ==
+                              (uint32_t)S::kComputeWarps - 1u) {
           const uint32_t piece = bbuf(b ^ 1) + (uint32_t)(r * kPiece);
           for (int pr = 0; pr < C; ++pr) {
             if (pr == r) continue;
             ptx::bulk_s2c(ptx::mapa(piece, (uint32_t)pr), piece, kPiece,
                           ptx::mapa(bar_rec + 8 * (b ^ 1), (uint32_t)pr));
           }
+          if (t + 3 < Tt) {
+            ptx::mbar_arrive_expect_tx(bar_g + 8 * gs, kGBlock);
+            ptx::bulk_g2s(gslot(gs), gates_src(t + 3), kGBlock, bar_g + 8 * gs);
+          }
+          trace_mark(a, tile, r, t, 7);
         }
       }
     }
@@ -845,7 +831,7 @@ __global__ void seq_out_kernel(const uint8_t* __restrict__ hseq, const int32_t* 
 
 // ---- host side -------------------------------------------------------------------------
 struct Ws {
-  size_t perm, tile_len, hist, sorted, gates, hseq, hlast, total;
+  size_t perm, tile_len, hist, sorted, xp, gates, hseq, hlast, trace, total;
 };
 
 Ws ws_layout(const Problem& p) {
@@ -861,30 +847,42 @@ Ws ws_layout(const Problem& p) {
   off = align_up(off + (size_t)(p.T + 1) * 4, 256);
   w.sorted = off;
   off = align_up(off + (size_t)std::max(p.B, 1) * 4, 256);
+  w.xp = off;
+  off = align_up(off + (size_t)tiles * p.T * kNT * 32, 256);
   w.gates = off;
   off = align_up(off + (size_t)p.T * tiles * C * kGBlock, 256);
   w.hseq = off;
   off = align_up(off + (size_t)p.T * tiles * C * kPiece, 256);
   w.hlast = off;
   off = align_up(off + (size_t)std::max(p.B, 1) * p.H * 2, 256);
+  w.trace = off;
+  if (p.flags & PLSTM_FLAG_TRACE) off += (size_t)C * kTraceSteps * kTraceEvents * 8;
   w.total = off;
   return w;
 }
 
-template <int H, bool BF16, bool VARLEN>
-void* rec_ptr() {
-  return reinterpret_cast<void*>(&rec_kernel<H, BF16, VARLEN>);
+// Compute warps of the recurrence: 8 (two per TMEM lane quadrant, 8 cells per
+// thread; measured faster) unless PLSTM_TCL_WARPS=4 (one per quadrant, 16 cells).
+int rec_warps() {
+  static const int w = [] {
+    const char* e = std::getenv("PLSTM_TCL_WARPS");
+    return (e != nullptr && std::atoi(e) == 4) ? 4 : 8;
+  }();
+  return w;
+}
+template <int H, int NCW>
+void* rec_ptr(bool bf16, bool varlen) {
+  if (bf16) return varlen ? reinterpret_cast<void*>(&rec_kernel<H, NCW, true, true>)
+                          : reinterpret_cast<void*>(&rec_kernel<H, NCW, true, false>);
+  return varlen ? reinterpret_cast<void*>(&rec_kernel<H, NCW, false, true>)
+                : reinterpret_cast<void*>(&rec_kernel<H, NCW, false, false>);
 }
 void* pick_rec(int H, bool bf16, bool varlen) {
-  if (H == 256) {
-    if (bf16) return varlen ? rec_ptr<256, true, true>() : rec_ptr<256, true, false>();
-    return varlen ? rec_ptr<256, false, true>() : rec_ptr<256, false, false>();
-  }
-  if (bf16) return varlen ? rec_ptr<512, true, true>() : rec_ptr<512, true, false>();
-  return varlen ? rec_ptr<512, false, true>() : rec_ptr<512, false, false>();
+  if (rec_warps() == 8) return H == 256 ? rec_ptr<256, 8>(bf16, varlen) : rec_ptr<512, 8>(bf16, varlen);
+  return H == 256 ? rec_ptr<256, 4>(bf16, varlen) : rec_ptr<512, 4>(bf16, varlen);
 }
-int rec_smem(int H) { return H == 256 ? RecSmem<256>::kDyn : RecSmem<512>::kDyn; }
-int rec_threads(int H) { return H == 256 ? RecSmem<256>::kThreads : RecSmem<512>::kThreads; }
+int rec_smem(int H) { return H == 256 ? RecSmem<256, 4>::kDyn : RecSmem<512, 4>::kDyn; }
+int rec_threads(int H) { return (rec_warps() + 1) * 32; }
 
 cudaError_t config_rec(void* k, int H) {
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, rec_smem(H));
@@ -931,7 +929,8 @@ int32_t launch_proj(const GemmArgs& ga, int sms, cudaStream_t s) {
   auto k = proj_kernel<KP, BF16>;
   PLSTM_TRY_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmSmem<KP>::kDyn));
   const int C = ctas_of(ga.H);
-  const int grid = std::max(C, (sms / C) * C);
+  const long long jobs = (long long)ga.T * ga.tiles * C;
+  const int grid = (int)std::max<long long>(C, std::min<long long>((sms / C) * C, jobs));
   k<<<grid, kGemmThreads, GemmSmem<KP>::kDyn, s>>>(ga);
   PLSTM_TRY_CUDA(cudaGetLastError());
   note_launches(1);
@@ -1009,6 +1008,10 @@ int32_t tcl_forward(const Problem& p, const void* packed, const void* x, const i
                                     reinterpret_cast<int32_t*>(wsb + w.sorted), s);
     if (rc != PLSTM_OK) return rc;
   }
+  {
+    const int32_t rc = tc_xpack(p, kNT, tiles, x, perm, wsb + w.xp, s);
+    if (rc != PLSTM_OK) return rc;
+  }
   int sms = 148;
   PLSTM_TRY_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, p.device));
   void* rk = pick_rec(H, bf16, varlen);
@@ -1016,16 +1019,13 @@ int32_t tcl_forward(const Problem& p, const void* packed, const void* x, const i
   const bool seq_out = !p.has_linear() || p.out_seq();
   for (int l = 0; l < L; ++l) {
     GemmArgs ga = {};
-    ga.x = static_cast<const uint16_t*>(x);
-    ga.perm = perm;
+    ga.xp = wsb + w.xp;
     ga.hseq = wsb + w.hseq;
     ga.wih = reinterpret_cast<const uint16_t*>(pk + off_wih(l, H, L));
     ga.bias = reinterpret_cast<const float*>(pk + off_bias(H, L)) + (size_t)l * 4 * H;
     ga.gates = reinterpret_cast<uint16_t*>(wsb + w.gates);
     ga.status = reinterpret_cast<int*>(wsb);
-    ga.B = p.B;
     ga.T = p.T;
-    ga.I = p.I;
     ga.H = H;
     ga.tiles = tiles;
     int32_t rc;
@@ -1055,6 +1055,12 @@ int32_t tcl_forward(const Problem& p, const void* packed, const void* x, const i
     ra.layer = l;
     ra.flags = p.flags;
     ra.timeout_ns = (unsigned long long)p.timeout_ms * 1000000ull;
+    ra.trace = nullptr;
+    ra.trace_t0 = p.T / 2;
+    if ((p.flags & PLSTM_FLAG_TRACE) && l == 0) {  // the first layer's recurrence
+      ra.trace = reinterpret_cast<unsigned long long*>(wsb + w.trace);
+      PLSTM_TRY_CUDA(cudaMemsetAsync(ra.trace, 0, (size_t)C * kTraceSteps * kTraceEvents * 8, s));
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(tiles * C), 1, 1);
     cfg.blockDim = dim3((unsigned)rec_threads(H), 1, 1);

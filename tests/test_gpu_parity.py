@@ -258,3 +258,21 @@ def test_timeout_is_reported_not_hung(cuda_device):
     out, _, _ = pw.forward(x, check=True)
     r_out, _, _ = oracle_of(x, *w, out_mode="last")
     assert_close16(out, r_out, "after timeout")
+
+
+@pytest.mark.parametrize("mode", ["seq", "last", "hseq"])
+@pytest.mark.parametrize("varlen", [False, True])
+def test_single_slot_wavefront_kernel(cuda_device, monkeypatch, mode, varlen):
+    """The single-slot wavefront kernel (PLSTM_TC_KERNEL=1) stays selectable and exact."""
+    monkeypatch.setenv("PLSTM_TC_KERNEL", "1")
+    B, T, I, H, L, O = 50, 21, 5, 128, 3, 24
+    m = make_model(I, H, L, O, seed=13)
+    w = weights_of(m, L, torch.float16, cuda_device)
+    x = _rand_x(B, T, I, torch.float16, cuda_device, seed=3)
+    lens = _rand_lengths(B, T, lo=1) if varlen else None
+    pw = core.PackedWeights(*w, out_mode=mode, backend="tc")
+    out, h_n, c_n = pw.forward(x, lengths=None if lens is None else lens.to(cuda_device), check=True)
+    r_out, r_h, r_c = oracle_of(x, *w, lengths=lens, out_mode=mode)
+    assert_close16(out, r_out, "out")
+    assert_close16(h_n, r_h, "h_n")
+    assert_close16(c_n, r_c, "c_n")

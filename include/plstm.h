@@ -58,6 +58,10 @@ extern "C" {
 /* k-pair interleaved: [ceil(K/2)][4H][2], odd K zero-padded
  * (`_pack_recurrent_weight_kpairs`, persistent_lstm_hip/model.py:20-27). */
 #define PLSTM_W_KPAIR 2
+/* MMAC-packed recurrent weight (plstm_hidden_update only, K = H): flat
+ * [H/16 unit tiles][H/16 k tiles][16 k][4 unit groups][4 gates][4 units]
+ * (`_pack_mmac_weight`, miopen_adaptive_lstm_hip/model.py:259-286). */
+#define PLSTM_W_MMAC 3
 
 /* ---- backends ----------------------------------------------------------- */
 #define PLSTM_BACKEND_AUTO 0 /* tensor-core wavefront kernel when it applies, else SIMT */
@@ -225,6 +229,32 @@ PLSTM_API int32_t plstm_repeat_first_row(const void* input, int32_t cols, int32_
  * (no bias), f16 or bf16 in and out, f32 accumulation, on tcgen05 tensor cores. */
 PLSTM_API int32_t plstm_input_gemm(const void* x, int32_t m, int32_t k, const void* w_t, int32_t n,
                          int32_t dtype, void* gate, void* stream);
+
+/* Hidden update: the LSTM recurrence over precomputed input projections, from
+ * h = c = 0.  For every row b and step t:
+ *   gates = gate_proj[b, t] + bias + W_hh . h_{t-1}   (gate order i, f, g, o)
+ *   c_t = sigmoid(f) c_{t-1} + sigmoid(i) tanh(g),  h_t = sigmoid(o) tanh(c_t)
+ * Replaces every hidden-update function of `miopen_adaptive_lstm_hip._C`
+ * (bindings.cpp:6-36, 42-78; adaptive_lstm_hip.h:5-170: the generic, partitioned,
+ * cached, GEMM-scan, gate-accumulate, seq-major, persistent and MMAC-packed
+ * variants all compute this).
+ *   gate_proj [B][T][4H] (or [T][B][4H] with PLSTM_HU_SEQ_MAJOR), activation type
+ *   w_hh      [4H][H] (PLSTM_W_NATIVE), [H][4H] (PLSTM_W_TRANSPOSED) or PLSTM_W_MMAC
+ *   bias      [4H] activation type, or NULL
+ *   h_state   [B][H] activation type, c_state [B][H] f32: the final state
+ *   out       h sequence [B][T][H] ([T][B][H] with PLSTM_HU_SEQ_MAJOR) with
+ *             PLSTM_HU_WRITE_SEQUENCE, else the final h [B][H]
+ * f16 / bf16 with H = 128, 256 or 512 run the tcgen05 cluster recurrence; other
+ * sizes and f32 run the FFMA kernel.  The workspace is caller-owned
+ * (plstm_hidden_update_workspace_size). */
+#define PLSTM_HU_SEQ_MAJOR 0x1
+#define PLSTM_HU_WRITE_SEQUENCE 0x2
+PLSTM_API int32_t plstm_hidden_update_workspace_size(int32_t batch, int32_t seq_len, int32_t hidden, int32_t dtype,
+                                           int32_t flags, int32_t device, size_t* bytes);
+PLSTM_API int32_t plstm_hidden_update(const void* gate_proj, int32_t batch, int32_t seq_len, int32_t hidden,
+                            const void* w_hh, int32_t w_layout, const void* bias, int32_t dtype, int32_t flags,
+                            void* h_state, float* c_state, void* out, void* workspace, size_t workspace_bytes,
+                            void* stream);
 
 /* ---- instrumentation (no counterpart in the reference beyond its
  * MIOPEN_ADAPTIVE_LSTM_PROFILE per-layer CUDA-event timings,

@@ -8,13 +8,14 @@ torch-free CUDA library with a C ABI (include/plstm.h, lib/libplstm.so).
 
 ``install_aliases()`` registers this package under the reference's import
 names so unmodified reference-style code (``from persistent_lstm_hip import
-convert_regressor_module``) runs on it.
+convert_regressor_module``, ``from miopen_adaptive_lstm_hip import
+AdaptiveLSTMRegressor``, ``miopen_adaptive_lstm_hip._C``) runs on it.
 """
 from __future__ import annotations
 
 import sys
 
-from . import ext
+from . import adaptive, adaptive_ext, ext
 from ._lib import PlstmError, PlstmUnavailable
 from .api import convert_lstm_module, convert_model_copy, convert_regressor_module, replace_lstm_inplace
 from .core import PackedWeights, lstm_linear_forward, select_backend
@@ -37,6 +38,8 @@ __all__ = [
     "PlstmError",
     "PlstmUnavailable",
     "ext",
+    "adaptive",
+    "adaptive_ext",
     "install_aliases",
 ]
 
@@ -52,3 +55,6 @@ def install_aliases() -> None:
     sys.modules.setdefault("persistent_lstm_hip.model", model)
     sys.modules.setdefault("persistent_lstm_hip.packing", packing)
     sys.modules.setdefault("persistent_lstm_hip_ext", ext)
+    sys.modules.setdefault("miopen_adaptive_lstm_hip", adaptive)
+    sys.modules.setdefault("miopen_adaptive_lstm_hip.api", adaptive)
+    sys.modules.setdefault("miopen_adaptive_lstm_hip._C", adaptive_ext)

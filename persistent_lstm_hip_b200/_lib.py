@@ -14,7 +14,8 @@ LIB_PATH = os.environ.get("PLSTM_LIB", os.path.join(HERE, "lib", "libplstm.so"))
 
 OK, EINVAL, ENOTSUP, ETIMEOUT, ECUDA, EWORKSPACE = 0, 1, 2, 3, 4, 5
 F32, F16, BF16 = 0, 1, 2
-W_NATIVE, W_TRANSPOSED, W_KPAIR = 0, 1, 2
+W_NATIVE, W_TRANSPOSED, W_KPAIR, W_MMAC = 0, 1, 2, 3
+HU_SEQ_MAJOR, HU_WRITE_SEQUENCE = 0x1, 0x2
 BACKEND_AUTO, BACKEND_SIMT, BACKEND_TC = 0, 1, 2
 FLAG_OUT_SEQ = 0x1
 FLAG_OUT_LAST = 0x2
@@ -62,6 +63,8 @@ PROTOTYPES = {
     "plstm_regressor_forward_generic": (_I32, [_P, _I32, _I32, _I32, _I32, _I32, _I32, _PP, _PP, _PP, _P, _P, _P, _P, _SZ, _P]),
     "plstm_repeat_first_row": (_I32, [_P, _I32, _I32, _I32, _P, _P]),
     "plstm_input_gemm": (_I32, [_P, _I32, _I32, _P, _I32, _I32, _P, _P]),
+    "plstm_hidden_update_workspace_size": (_I32, [_I32, _I32, _I32, _I32, _I32, _I32, ctypes.POINTER(_SZ)]),
+    "plstm_hidden_update": (_I32, [_P, _I32, _I32, _I32, _P, _I32, _P, _I32, _I32, _P, _P, _P, _P, _SZ, _P]),
     "plstm_diag_tmem_layout": (_I32, [_P, _P]),
     "plstm_launch_count": (ctypes.c_int64, []),
     "plstm_profile": (_I32, [_I32]),

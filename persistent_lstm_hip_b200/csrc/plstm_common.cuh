@@ -144,10 +144,28 @@ int32_t tcl_pack(const Problem& p, int ih_layout, int hh_layout, const void* con
 int32_t tcl_forward(const Problem& p, const void* packed, const void* x, const int32_t* lengths, const void* h0,
                     const void* c0, void* out, void* h_n, void* c_n, void* ws, cudaStream_t s);
 
+// Hidden update (plstm_hidden_update): recurrence over precomputed input projections.
+struct HuProblem {
+  int B, T, H, dtype, flags, w_layout, device;
+  bool seq_major() const { return (flags & PLSTM_HU_SEQ_MAJOR) != 0; }
+  bool write_seq() const { return (flags & PLSTM_HU_WRITE_SEQUENCE) != 0; }
+};
+bool tcl_hu_supported(const HuProblem& p);
+size_t tcl_hu_workspace_size(const HuProblem& p);
+int32_t tcl_hidden_update(const HuProblem& p, const void* gate_proj, const void* w_hh, const void* bias, void* h_state,
+                          float* c_state, void* out, void* ws, cudaStream_t s);
+size_t simt_hu_workspace_size(const HuProblem& p);
+int32_t simt_hidden_update(const HuProblem& p, const void* gate_proj, const void* w_hh, const void* bias,
+                           void* h_state, float* c_state, void* out, void* ws, cudaStream_t s);
+
 // Reads element (r, k) of a [4H or O][K] weight given in any PLSTM_W_* layout.
 __device__ __forceinline__ int64_t weight_src_index(int layout, int rows, int K, int r, int k) {
   if (layout == PLSTM_W_TRANSPOSED) return (int64_t)k * rows + r;
   if (layout == PLSTM_W_KPAIR) return ((int64_t)(k >> 1) * rows + r) * 2 + (k & 1);
+  if (layout == PLSTM_W_MMAC) {  // rows = 4K: row = gate * K + unit
+    const int gate = r / K, u = r % K, nt = K / 16;
+    return (((((int64_t)(u >> 4) * nt + (k >> 4)) * 16 + (k & 15)) * 4 + ((u & 15) >> 2)) * 4 + gate) * 4 + (u & 3);
+  }
   return (int64_t)r * K + k;
 }
 

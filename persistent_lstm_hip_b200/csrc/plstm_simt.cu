@@ -107,7 +107,9 @@ __global__ void pack_bias_kernel(const void* a, const void* b, int dtype, int n,
 constexpr int kSimtThreads = 256;
 
 // One layer, whole sequence, NB batch rows per CTA.
-// xin: layer input [B][T][K] (activation type T).  seq_out: [B][T][H].
+// xin: layer input [B][T][K] (activation type T).  seq_out[b * out_sb + t * out_st + u].
+// gin: optional precomputed input projection added to the gates, gin[b * gin_sb + t * gin_st + r]
+// (the hidden-update entry point runs with K = 0 and gin set).
 // hfin/cfin: final state of this layer [B][H] (T / f32).
 template <typename T, int NB>
 __global__ void __launch_bounds__(kSimtThreads)
@@ -115,7 +117,8 @@ __global__ void __launch_bounds__(kSimtThreads)
                       const T* __restrict__ whh_t, const float* __restrict__ bias,
                       const int32_t* __restrict__ lengths, const T* __restrict__ h0,
                       const T* __restrict__ c0, T* __restrict__ seq_out, T* __restrict__ hfin,
-                      float* __restrict__ cfin, int B, int Tn, int H) {
+                      float* __restrict__ cfin, int B, int Tn, int H, const T* __restrict__ gin,
+                      int64_t gin_sb, int64_t gin_st, int64_t out_sb, int64_t out_st) {
   extern __shared__ float smem[];
   const int G = 4 * H;
   const int KH = K + H;
@@ -157,7 +160,10 @@ __global__ void __launch_bounds__(kSimtThreads)
       float acc[NB];
       const float bv = bias != nullptr ? bias[r] : 0.0f;
 #pragma unroll
-      for (int n = 0; n < NB; ++n) acc[n] = bv;
+      for (int n = 0; n < NB; ++n) {
+        acc[n] = bv;
+        if (gin != nullptr && b0 + n < B) acc[n] += to_f32(gin[(int64_t)(b0 + n) * gin_sb + (int64_t)t * gin_st + r]);
+      }
       int k = 0;
       for (; k + 4 <= K; k += 4) {
         const float w0 = to_f32(wih_t[(int64_t)(k + 0) * G + r]);
@@ -214,9 +220,9 @@ __global__ void __launch_bounds__(kSimtThreads)
         cst[i] = c;
         const T hq = from_f32<T>(og * tanh_acc(c));  // h is kept in the activation type
         xh[n * KH + K + u] = to_f32(hq);
-        seq_out[((int64_t)b * Tn + t) * H + u] = hq;
+        seq_out[(int64_t)b * out_sb + (int64_t)t * out_st + u] = hq;
       } else if (b < B) {
-        seq_out[((int64_t)b * Tn + t) * H + u] = from_f32<T>(0.0f);
+        seq_out[(int64_t)b * out_sb + (int64_t)t * out_st + u] = from_f32<T>(0.0f);
       }
     }
     __syncthreads();
@@ -225,9 +231,9 @@ __global__ void __launch_bounds__(kSimtThreads)
   for (int n = 0; n < NB; ++n) {
     const int b = b0 + n;
     if (b >= B) break;
-    T* dst = seq_out + ((int64_t)b * Tn + tmax) * H;
     const int64_t cnt = (int64_t)(Tn - tmax) * H;
-    for (int64_t i = tid; i < cnt; i += blockDim.x) dst[i] = from_f32<T>(0.0f);
+    for (int64_t i = tid; i < cnt; i += blockDim.x)
+      seq_out[(int64_t)b * out_sb + (int64_t)(tmax + i / H) * out_st + i % H] = from_f32<T>(0.0f);
   }
   for (int i = tid; i < NB * H; i += blockDim.x) {
     const int n = i / H, u = i % H, b = b0 + n;
@@ -312,7 +318,7 @@ int32_t simt_forward_t(const Problem& p, const void* packed, const void* x, cons
         layer_in, K, reinterpret_cast<const T*>(pk + lo.wih[l]),
         reinterpret_cast<const T*>(pk + lo.whh[l]), reinterpret_cast<const float*>(pk + lo.bias[l]),
         lengths, h0l, c0l, dst, hfin + (size_t)l * p.B * p.H, cfin + (size_t)l * p.B * p.H, p.B,
-        p.T, p.H);
+        p.T, p.H, nullptr, 0, 0, (int64_t)p.T * p.H, p.H);
     PLSTM_TRY_CUDA(cudaGetLastError());
     note_launches(1);
     if (l == p.L - 1) profile_end(s);
@@ -339,7 +345,73 @@ int32_t simt_forward_t(const Problem& p, const void* packed, const void* x, cons
   return PLSTM_OK;
 }
 
+// ---- hidden update (plstm_hidden_update) --------------------------------------------
+struct HuWs {
+  size_t whh, bias, seq, total;
+};
+HuWs hu_ws(const HuProblem& p) {
+  HuWs w;
+  const size_t es = dtype_size(p.dtype);
+  size_t off = kStatusBytes;
+  w.whh = off;
+  off = align_up(off + (size_t)p.H * 4 * p.H * es, 256);
+  w.bias = off;
+  off = align_up(off + (size_t)4 * p.H * 4, 256);
+  w.seq = off;
+  if (!p.write_seq()) off = align_up(off + (size_t)p.B * p.T * p.H * es, 256);
+  w.total = off;
+  return w;
+}
+
+template <typename T>
+int32_t simt_hu_t(const HuProblem& p, const void* gate_proj, const void* w_hh, const void* bias, void* h_state,
+                  float* c_state, void* out, void* ws, cudaStream_t s) {
+  const HuWs w = hu_ws(p);
+  char* wsb = static_cast<char*>(ws);
+  const int G = 4 * p.H;
+  pack_transposed_kernel<<<grid_for((int64_t)G * p.H, 256), 256, 0, s>>>(w_hh, p.dtype, p.w_layout, G, p.H,
+                                                                          wsb + w.whh, p.dtype);
+  pack_bias_kernel<<<grid_for(G, 256), 256, 0, s>>>(bias, nullptr, p.dtype, G, reinterpret_cast<float*>(wsb + w.bias));
+  PLSTM_TRY_CUDA(cudaGetLastError());
+  note_launches(2);
+  const bool sm = p.seq_major();
+  T* seq = p.write_seq() ? static_cast<T*>(out) : reinterpret_cast<T*>(wsb + w.seq);
+  const int64_t out_sb = (p.write_seq() && sm) ? p.H : (int64_t)p.T * p.H;
+  const int64_t out_st = (p.write_seq() && sm) ? (int64_t)p.B * p.H : p.H;
+  const int64_t gin_sb = sm ? G : (int64_t)p.T * G;
+  const int64_t gin_st = sm ? (int64_t)p.B * G : G;
+  constexpr int NB = 4;
+  const size_t smem = sizeof(float) * NB * ((size_t)p.H + 4 * (size_t)p.H + p.H);
+  auto kern = simt_layer_kernel<T, NB>;
+  PLSTM_TRY_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  profile_begin(s);
+  kern<<<(p.B + NB - 1) / NB, kSimtThreads, smem, s>>>(
+      nullptr, 0, nullptr, reinterpret_cast<const T*>(wsb + w.whh), reinterpret_cast<const float*>(wsb + w.bias),
+      nullptr, nullptr, nullptr, seq, static_cast<T*>(h_state), c_state, p.B, p.T, p.H,
+      static_cast<const T*>(gate_proj), gin_sb, gin_st, out_sb, out_st);
+  PLSTM_TRY_CUDA(cudaGetLastError());
+  profile_end(s);
+  note_launches(1);
+  if (!p.write_seq())
+    PLSTM_TRY_CUDA(cudaMemcpyAsync(out, h_state, (size_t)p.B * p.H * sizeof(T), cudaMemcpyDeviceToDevice, s));
+  return PLSTM_OK;
+}
+
 }  // namespace
+
+size_t simt_hu_workspace_size(const HuProblem& p) { return hu_ws(p).total; }
+
+int32_t simt_hidden_update(const HuProblem& p, const void* gate_proj, const void* w_hh, const void* bias,
+                           void* h_state, float* c_state, void* out, void* ws, cudaStream_t s) {
+  switch (p.dtype) {
+    case PLSTM_F32:
+      return simt_hu_t<float>(p, gate_proj, w_hh, bias, h_state, c_state, out, ws, s);
+    case PLSTM_F16:
+      return simt_hu_t<__half>(p, gate_proj, w_hh, bias, h_state, c_state, out, ws, s);
+    default:
+      return simt_hu_t<__nv_bfloat16>(p, gate_proj, w_hh, bias, h_state, c_state, out, ws, s);
+  }
+}
 
 size_t simt_packed_size(const Problem& p) { return simt_layout(p).total; }
 size_t simt_workspace_size(const Problem& p) { return simt_ws(p).total; }

@@ -797,7 +797,7 @@ template <bool BF16, bool LINEAR>
 __global__ void seq_out_kernel(const uint8_t* __restrict__ hseq, const int32_t* __restrict__ perm,
                                const int32_t* __restrict__ lengths, const uint16_t* __restrict__ wlin,
                                const float* __restrict__ blin, uint16_t* __restrict__ out, int B, int T, int H,
-                               int O, int tiles) {
+                               int O, int tiles, int out_seq_major) {
   extern __shared__ uint8_t smem_o[];
   float* hs = reinterpret_cast<float*>(smem_o);  // [kNT][H + 1]
   const int C = ctas_of(H);
@@ -825,8 +825,81 @@ __global__ void seq_out_kernel(const uint8_t* __restrict__ hseq, const int32_t* 
         v = hs[n * (H + 1) + w];
       }
     }
-    out[((size_t)b * T + t) * W + w] = to_bits<BF16>(v);
+    const size_t row = out_seq_major ? (size_t)t * B + b : (size_t)b * T + t;
+    out[row * W + w] = to_bits<BF16>(v);
   }
+}
+
+// ---- hidden update (plstm_hidden_update) ------------------------------------------------
+// W_hh [4H][H] in any PLSTM_W_* layout -> the recurrence's TMEM images [C][128][H]
+// (rows permuted per CTA, i / f / o pre-scaled by 1/2).
+__global__ void hu_pack_whh_kernel(const void* w_hh, int dtype, int layout, int H, uint16_t* img) {
+  const int G = 4 * H;
+  const bool bf16 = dtype == PLSTM_BF16;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < (int64_t)G * H;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int rp = (int)(i / H), k = (int)(i % H);
+    const int r = rp / kRows, rho = rp % kRows;
+    const float v = load_any(w_hh, dtype, weight_src_index(layout, G, H, src_row(H, r, rho), k)) * row_scale(rho);
+    __half hv = __float2half_rn(v);
+    __nv_bfloat16 bv = __float2bfloat16_rn(v);
+    img[i] = bf16 ? *reinterpret_cast<uint16_t*>(&bv) : *reinterpret_cast<uint16_t*>(&hv);
+  }
+}
+
+// gate_proj [B][T][4H] (or [T][B][4H]) + bias -> gate blocks [T][tiles][C][128][kGRow]
+// (rows permuted per CTA and pre-scaled like the weights; padding rows zero).  One
+// block per (step, tile, CTA): reads 64 rows x 4 runs of 32 gate values, writes the
+// 128 x 64 block row by row.
+template <bool BF16>
+__global__ void hu_gates_kernel(const uint16_t* __restrict__ gp, const uint16_t* __restrict__ bias, int B, int T,
+                                int H, int tiles, int seq_major, uint16_t* __restrict__ gates) {
+  __shared__ float blk[kRows][kNT + 1];
+  const int C = ctas_of(H);
+  const int r = blockIdx.x % C;
+  const int ts = blockIdx.x / C;
+  const int t = ts / tiles, tile = ts % tiles;
+  for (int i = threadIdx.x; i < kNT * kRows; i += blockDim.x) {
+    const int n = i / kRows, rho = i % kRows;  // rho fastest: 32-value runs are contiguous in gate_proj
+    const int b = tile * kNT + n;
+    const int sr = src_row(H, r, rho);
+    float v = 0.0f;
+    if (b < B) {
+      const size_t row = seq_major ? (size_t)t * B + b : (size_t)b * T + t;
+      v = from_bits<BF16>(gp[row * 4 * H + sr]);
+      if (bias != nullptr) v += from_bits<BF16>(bias[sr]);
+      v *= row_scale(rho);
+    }
+    blk[rho][n] = v;
+  }
+  __syncthreads();
+  uint16_t* dst = gates + (((size_t)ts * C + r) * kRows) * kGRow;
+  for (int i = threadIdx.x; i < kRows * kNT / 2; i += blockDim.x) {
+    const int rho = i / (kNT / 2), n = (i % (kNT / 2)) * 2;
+    *reinterpret_cast<uint32_t*>(dst + (size_t)rho * kGRow + n) = pack2_bits<BF16>(blk[rho][n], blk[rho][n + 1]);
+  }
+}
+
+struct HuWs {
+  size_t perm, tile_len, whh, gates, hseq, total;
+};
+HuWs hu_ws(const HuProblem& p) {
+  HuWs w;
+  const int tiles = (p.B + kNT - 1) / kNT;
+  const int C = ctas_of(p.H);
+  size_t off = kStatusBytes;
+  w.perm = off;
+  off = align_up(off + (size_t)tiles * kNT * 4, 256);
+  w.tile_len = off;
+  off = align_up(off + (size_t)tiles * 4, 256);
+  w.whh = off;
+  off = align_up(off + (size_t)4 * p.H * p.H * 2, 256);
+  w.gates = off;
+  off = align_up(off + (size_t)p.T * tiles * C * kGBlock, 256);
+  w.hseq = off;
+  if (p.write_seq()) off = align_up(off + (size_t)p.T * tiles * C * kPiece, 256);
+  w.total = off;
+  return w;
 }
 
 // ---- host side -------------------------------------------------------------------------
@@ -878,10 +951,16 @@ void* rec_ptr(bool bf16, bool varlen) {
                 : reinterpret_cast<void*>(&rec_kernel<H, NCW, false, false>);
 }
 void* pick_rec(int H, bool bf16, bool varlen) {
-  if (rec_warps() == 8) return H == 256 ? rec_ptr<256, 8>(bf16, varlen) : rec_ptr<512, 8>(bf16, varlen);
+  if (rec_warps() == 8) {
+    if (H == 128) return rec_ptr<128, 8>(bf16, varlen);
+    return H == 256 ? rec_ptr<256, 8>(bf16, varlen) : rec_ptr<512, 8>(bf16, varlen);
+  }
+  if (H == 128) return rec_ptr<128, 4>(bf16, varlen);
   return H == 256 ? rec_ptr<256, 4>(bf16, varlen) : rec_ptr<512, 4>(bf16, varlen);
 }
-int rec_smem(int H) { return H == 256 ? RecSmem<256, 4>::kDyn : RecSmem<512, 4>::kDyn; }
+int rec_smem(int H) {
+  return H == 128 ? RecSmem<128, 4>::kDyn : H == 256 ? RecSmem<256, 4>::kDyn : RecSmem<512, 4>::kDyn;
+}
 int rec_threads(int H) { return (rec_warps() + 1) * 32; }
 
 cudaError_t config_rec(void* k, int H) {
@@ -893,15 +972,15 @@ cudaError_t config_rec(void* k, int H) {
 // Clusters of C CTAs of the recurrence that fit on `device` at once (0 = none); cached.
 int rec_max_clusters(int device, int H) {
   static std::mutex mu;
-  static int cache[64][2];
+  static int cache[64][3];
   static bool init = false;
   std::lock_guard<std::mutex> g(mu);
   if (!init) {
-    for (auto& a : cache) a[0] = a[1] = -1;
+    for (auto& a : cache) a[0] = a[1] = a[2] = -1;
     init = true;
   }
   if (device < 0 || device >= 64) return 0;
-  int& slot = cache[device][H == 512 ? 1 : 0];
+  int& slot = cache[device][H == 512 ? 2 : H == 256 ? 1 : 0];
   if (slot >= 0) return slot;
   void* k = pick_rec(H, false, false);
   int n = 0;
@@ -988,6 +1067,107 @@ int32_t tcl_pack(const Problem& p, int ih_layout, int hh_layout, const void* con
   pack_kernel<<<148 * 4, 256, 0, s>>>(a, static_cast<uint8_t*>(packed));
   PLSTM_TRY_CUDA(cudaGetLastError());
   note_launches(1);
+  return PLSTM_OK;
+}
+
+bool tcl_hu_supported(const HuProblem& p) {
+  if (p.dtype != PLSTM_F16 && p.dtype != PLSTM_BF16) return false;
+  if (p.H != 128 && p.H != 256 && p.H != 512) return false;
+  if (p.T < 1 || p.T > 65535 || p.B < 1) return false;
+  int major = 0, minor = 0;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, p.device) != cudaSuccess ||
+      cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, p.device) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return major == 10 && minor == 0 && rec_max_clusters(p.device, p.H) >= 1;
+}
+
+size_t tcl_hu_workspace_size(const HuProblem& p) { return hu_ws(p).total; }
+
+int32_t tcl_hidden_update(const HuProblem& p, const void* gate_proj, const void* w_hh, const void* bias, void* h_state,
+                          float* c_state, void* out, void* ws, cudaStream_t s) {
+  const int H = p.H, C = ctas_of(H);
+  const int tiles = (p.B + kNT - 1) / kNT;
+  const HuWs w = hu_ws(p);
+  uint8_t* wsb = static_cast<uint8_t*>(ws);
+  const bool bf16 = p.dtype == PLSTM_BF16;
+  int32_t* perm = reinterpret_cast<int32_t*>(wsb + w.perm);
+  int32_t* tile_len = reinterpret_cast<int32_t*>(wsb + w.tile_len);
+  Problem pp = {};
+  pp.B = p.B;
+  pp.T = p.T;
+  pp.H = H;
+  pp.L = 1;
+  pp.dtype = p.dtype;
+  pp.device = p.device;
+  {
+    const int32_t rc = tc_make_perm(pp, kNT, tiles, nullptr, perm, tile_len, nullptr, nullptr, s);
+    if (rc != PLSTM_OK) return rc;
+  }
+  uint16_t* img = reinterpret_cast<uint16_t*>(wsb + w.whh);
+  hu_pack_whh_kernel<<<148 * 4, 256, 0, s>>>(w_hh, p.dtype, p.w_layout, H, img);
+  const int gblocks = p.T * tiles * C;
+  const uint16_t* gp = static_cast<const uint16_t*>(gate_proj);
+  const uint16_t* bp = static_cast<const uint16_t*>(bias);
+  uint16_t* gates = reinterpret_cast<uint16_t*>(wsb + w.gates);
+  if (bf16)
+    hu_gates_kernel<true><<<gblocks, 256, 0, s>>>(gp, bp, p.B, p.T, H, tiles, p.seq_major() ? 1 : 0, gates);
+  else
+    hu_gates_kernel<false><<<gblocks, 256, 0, s>>>(gp, bp, p.B, p.T, H, tiles, p.seq_major() ? 1 : 0, gates);
+  PLSTM_TRY_CUDA(cudaGetLastError());
+  note_launches(2);
+
+  void* rk = pick_rec(H, bf16, false);
+  PLSTM_TRY_CUDA(config_rec(rk, H));
+  RecArgs ra = {};
+  ra.whh = reinterpret_cast<const uint8_t*>(img);
+  ra.gates = gates;
+  ra.perm = perm;
+  ra.lengths = nullptr;
+  ra.tile_len = tile_len;
+  ra.h0 = nullptr;
+  ra.c0 = nullptr;
+  ra.hseq = p.write_seq() ? wsb + w.hseq : nullptr;
+  ra.h_n = h_state;
+  ra.c_n = c_state;
+  ra.hlast = nullptr;
+  ra.status = reinterpret_cast<int*>(wsb);
+  ra.B = p.B;
+  ra.T = p.T;
+  ra.layer = 0;
+  ra.flags = PLSTM_FLAG_CN_F32;
+  ra.timeout_ns = 2000000000ull;
+  ra.trace = nullptr;
+  ra.trace_t0 = 0;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(tiles * C), 1, 1);
+  cfg.blockDim = dim3((unsigned)rec_threads(H), 1, 1);
+  cfg.dynamicSmemBytes = rec_smem(H);
+  cfg.stream = s;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeClusterDimension;
+  attr.val.clusterDim.x = C;
+  attr.val.clusterDim.y = 1;
+  attr.val.clusterDim.z = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  void* args[] = {&ra};
+  profile_begin(s);
+  PLSTM_TRY_CUDA(cudaLaunchKernelExC(&cfg, rk, args));
+  profile_end(s);
+  note_launches(1);
+  if (p.write_seq()) {
+    const int smem = kNT * (H + 1) * 4;
+    auto k = bf16 ? seq_out_kernel<true, false> : seq_out_kernel<false, false>;
+    PLSTM_TRY_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    k<<<p.T * tiles, 256, smem, s>>>(wsb + w.hseq, perm, nullptr, nullptr, nullptr, static_cast<uint16_t*>(out), p.B,
+                                     p.T, H, 0, tiles, p.seq_major() ? 1 : 0);
+    PLSTM_TRY_CUDA(cudaGetLastError());
+    note_launches(1);
+  } else {
+    PLSTM_TRY_CUDA(cudaMemcpyAsync(out, h_state, (size_t)p.B * H * 2, cudaMemcpyDeviceToDevice, s));
+  }
   return PLSTM_OK;
 }
 
@@ -1096,11 +1276,11 @@ int32_t tcl_forward(const Problem& p, const void* packed, const void* x, const i
     if (p.has_linear()) {
       auto k = bf16 ? seq_out_kernel<true, true> : seq_out_kernel<false, true>;
       PLSTM_TRY_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-      k<<<grid, 256, smem, s>>>(wsb + w.hseq, perm, lengths, wlin, blin, o16, p.B, p.T, H, O, tiles);
+      k<<<grid, 256, smem, s>>>(wsb + w.hseq, perm, lengths, wlin, blin, o16, p.B, p.T, H, O, tiles, 0);
     } else {
       auto k = bf16 ? seq_out_kernel<true, false> : seq_out_kernel<false, false>;
       PLSTM_TRY_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-      k<<<grid, 256, smem, s>>>(wsb + w.hseq, perm, lengths, wlin, blin, o16, p.B, p.T, H, 0, tiles);
+      k<<<grid, 256, smem, s>>>(wsb + w.hseq, perm, lengths, wlin, blin, o16, p.B, p.T, H, 0, tiles, 0);
     }
   }
   PLSTM_TRY_CUDA(cudaGetLastError());

@@ -10,6 +10,7 @@ imported from its sources:
   * reference_regressor_forward   persistent_lstm_hip/persistent_lstm_hip/reference.py:66-72
   * pack_lstm_module              persistent_lstm_hip/persistent_lstm_hip/packing.py:38-63
   * _pack_recurrent_weight_kpairs persistent_lstm_hip/persistent_lstm_hip/model.py:20-27
+  * _pack_mmac_weight             miopen_adaptive_lstm_hip/miopen_adaptive_lstm_hip/model.py:259-286
 The `torch_varlen` fixture (variable lengths, which the reference has no path
 for) comes from torch.nn.LSTM + pack_padded_sequence, the semantics the
 north star defines the masked path by.
@@ -100,6 +101,19 @@ def make_kpair_case(refs, name, H, K, seed):
                         packed=packed.numpy())
 
 
+def make_mmac_case(root, name, H, seed):
+    import torch
+
+    sys.dont_write_bytecode = True  # never write into the reference checkout
+    sys.path.insert(0, os.path.join(root, "miopen_adaptive_lstm_hip"))
+    from miopen_adaptive_lstm_hip import model as ada_model  # noqa: E402
+
+    g = torch.Generator().manual_seed(seed)
+    w = torch.randn(4 * H, H, generator=g, dtype=torch.float32).half()
+    packed = ada_model._pack_mmac_weight(w, H)
+    np.savez_compressed(os.path.join(HERE, name + ".npz"), weight=w.numpy(), packed=packed.numpy())
+
+
 def make_varlen_case(name, I, H, L, O, B, T, seed):
     import torch
     from torch.nn.utils.rnn import pack_padded_sequence, pad_packed_sequence
@@ -123,9 +137,12 @@ def make_varlen_case(name, I, H, L, O, B, T, seed):
     np.savez_compressed(os.path.join(HERE, name + ".npz"), **arrays)
 
 
-def main(root: str) -> None:
+def main(root: str, only: str = "") -> None:
     import torch
 
+    if only == "mmac":
+        make_mmac_case(root, "ref_mmac_h32", H=32, seed=17)
+        return
     refs = _import_reference(root)
     make_reference_case(refs, "ref_small_f64", I=5, H=16, L=2, O=4, B=3, T=7,
                         dtype=torch.float64, seed=11, with_state=False)
@@ -136,9 +153,10 @@ def main(root: str) -> None:
     make_kpair_case(refs, "ref_kpair_odd", H=8, K=5, seed=14)
     make_kpair_case(refs, "ref_kpair_even", H=8, K=8, seed=15)
     make_varlen_case("torch_varlen_f64", I=5, H=16, L=2, O=4, B=5, T=9, seed=16)
+    make_mmac_case(root, "ref_mmac_h32", H=32, seed=17)
 
 
 if __name__ == "__main__":
-    if len(sys.argv) != 2:
-        sys.exit("usage: make_golden.py <reference checkout root>")
-    main(sys.argv[1])
+    if len(sys.argv) not in (2, 3):
+        sys.exit("usage: make_golden.py <reference checkout root> [mmac]")
+    main(sys.argv[1], sys.argv[2] if len(sys.argv) == 3 else "")

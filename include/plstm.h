@@ -75,6 +75,13 @@ extern "C" {
 #define PLSTM_FLAG_BIAS_SUMMED 0x8  /* b_ih already holds b_ih + b_hh; b_hh must be NULL */
 #define PLSTM_FLAG_SYNC_CHECK 0x10  /* synchronise `stream` and turn the device status into the return code */
 #define PLSTM_FLAG_CN_F32 0x20      /* c_n is written as f32 instead of the activation type */
+/* Duplicate-row elimination: rows with the same identity (x up to the row's
+ * length, the length, the row's h0 / c0 in every layer; bit for bit) are
+ * computed once and their results copied to every duplicate.  The general
+ * form of the reference's uniform-batch shortcut (persistent_lstm_hip/model.py:
+ * 493-530).  Synchronises `stream` once to read the distinct-row count, so the
+ * call is refused under stream capture. */
+#define PLSTM_FLAG_DEDUPE 0x40
 #define PLSTM_FLAG_TEST_DROP 0x100  /* fault injection: one producer CTA skips one h hand-off (tests only) */
 /* Diagnostics: the tensor-core kernel records SM clock (clock64) timestamps of
  * 8 events for 64 steps starting at T/2, for every CTA of the first cluster,
@@ -153,6 +160,18 @@ PLSTM_API int32_t plstm_forward(const plstm_desc* d, const void* x, const void* 
 PLSTM_API int32_t plstm_forward_packed_noalloc(const plstm_desc* d, const void* packed, const void* x,
                                                const int32_t* lengths, const void* h0, const void* c0,
                                                void* out, void* h_n, void* c_n, void* stream);
+
+/* Groups identical rows as PLSTM_FLAG_DEDUPE does, without running the
+ * forward (the generalisation of the reference's uniform-batch check,
+ * persistent_lstm_hip/model.py:493-520).  row_map[B] (device) receives each
+ * row's distinct-row index in 0..count-1, unique_index[B] (device) in its
+ * first *count entries the first row of each distinct row, ascending; *count
+ * (host) the number of distinct rows.  Synchronises `stream`; refused under
+ * stream capture.  The workspace needs plstm_unique_rows_workspace_size bytes. */
+PLSTM_API int32_t plstm_unique_rows_workspace_size(const plstm_desc* d, size_t* bytes);
+PLSTM_API int32_t plstm_unique_rows(const plstm_desc* d, const void* x, const int32_t* lengths, const void* h0,
+                                    const void* c0, int32_t* row_map, int32_t* unique_index, int32_t* count,
+                                    void* workspace, size_t workspace_bytes, void* stream);
 
 /* Reads (and clears) the device status word the kernels of the last forward
  * using `workspace` left, synchronising `stream`.  *status receives PLSTM_OK

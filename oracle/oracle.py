@@ -172,3 +172,30 @@ def forward_numpy(x, w_ih, w_hh, b_ih, b_hh, w_lin, b_lin, *, lengths=None, h0=N
     out = layer_in @ w_lin.T + bl
     mask = (np.arange(T)[None, :] < lens[:, None])[:, :, None]
     return np.where(mask, out, 0.0), h_n, c_n
+
+
+def unique_rows(x, *, lengths=None, h0=None, c0=None):
+    """Groups identical batch rows: the general form of the reference's
+    all-rows-equal check (persistent_lstm_hip/persistent_lstm_hip/model.py:
+    493-520, ``torch.equal(x, x[:1].expand_as(x))``).
+
+    A row's identity is the bytes of x[b, :len_b], len_b and, when given, the
+    bytes of h0[:, b] and c0[:, b].  Returns (row_map[B], unique_index[U], U):
+    distinct rows are numbered in order of first occurrence, unique_index
+    lists each one's first row.
+    """
+    x = np.ascontiguousarray(x)
+    B, T = x.shape[0], x.shape[1]
+    lens = np.full(B, T, dtype=np.int64) if lengths is None else np.clip(np.asarray(lengths, dtype=np.int64), 0, T)
+    seen = {}
+    row_map = np.zeros(B, dtype=np.int32)
+    first = []
+    for b in range(B):
+        key = (int(lens[b]), x[b, :lens[b]].tobytes())
+        if h0 is not None:
+            key += (np.ascontiguousarray(h0[:, b]).tobytes(), np.ascontiguousarray(c0[:, b]).tobytes())
+        if key not in seen:
+            seen[key] = len(first)
+            first.append(b)
+        row_map[b] = seen[key]
+    return row_map, np.asarray(first, dtype=np.int32), len(first)

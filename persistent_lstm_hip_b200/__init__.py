@@ -18,7 +18,7 @@ import sys
 from . import adaptive, adaptive_ext, ext
 from ._lib import PlstmError, PlstmUnavailable
 from .api import convert_lstm_module, convert_model_copy, convert_regressor_module, replace_lstm_inplace
-from .core import PackedWeights, lstm_linear_forward, select_backend
+from .core import PackedWeights, lstm_linear_forward, select_backend, unique_rows
 from .model import (NativeModuleFallback, PersistentLSTM, PersistentLSTM4LayerRegressor, PersistentLSTMRegressor,
                     StandardLSTMRegressor)
 
@@ -35,6 +35,7 @@ __all__ = [
     "lstm_linear_forward",
     "PackedWeights",
     "select_backend",
+    "unique_rows",
     "PlstmError",
     "PlstmUnavailable",
     "ext",

@@ -23,6 +23,7 @@ FLAG_NO_LINEAR = 0x4
 FLAG_BIAS_SUMMED = 0x8
 FLAG_SYNC_CHECK = 0x10
 FLAG_CN_F32 = 0x20
+FLAG_DEDUPE = 0x40
 FLAG_TEST_DROP = 0x100
 
 _CODE_NAMES = {EINVAL: "PLSTM_EINVAL", ENOTSUP: "PLSTM_ENOTSUP", ETIMEOUT: "PLSTM_ETIMEOUT",
@@ -52,6 +53,8 @@ PROTOTYPES = {
     "plstm_workspace_size": (_I32, [_DP, ctypes.POINTER(_SZ)]),
     "plstm_forward_packed": (_I32, [_DP, _P, _P, _P, _P, _P, _P, _P, _P, _P, _SZ, _P]),
     "plstm_forward": (_I32, [_DP, _P, _PP, _PP, _PP, _PP, _P, _P, _P, _P, _P, _P, _P, _P, _P, _SZ, _P]),
+    "plstm_unique_rows_workspace_size": (_I32, [_DP, ctypes.POINTER(_SZ)]),
+    "plstm_unique_rows": (_I32, [_DP, _P, _P, _P, _P, _P, _P, ctypes.POINTER(_I32), _P, _SZ, _P]),
     "plstm_read_status": (_I32, [_P, _P, ctypes.POINTER(_I32), ctypes.POINTER(_I32)]),
     "plstm_forward_packed_noalloc": (_I32, [_DP, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
     "plstm_ref4_workspace_size": (_I32, [_I32, _I32, _I32, _I32, _I32, ctypes.POINTER(_SZ)]),

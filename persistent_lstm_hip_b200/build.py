@@ -19,7 +19,7 @@ LIB_DIR = os.path.join(HERE, "lib")
 OBJ_DIR = os.path.join(HERE, "lib", "obj")
 LIB = os.path.join(LIB_DIR, "libplstm.so")
 SOURCES = ["plstm_abi.cu", "plstm_simt.cu", "plstm_tc.cu", "plstm_tcl.cu", "plstm_gemm.cu", "plstm_misc.cu",
-           "plstm_noalloc.cu"]
+           "plstm_noalloc.cu", "plstm_dedupe.cu"]
 HEADERS = ["plstm_common.cuh", "sm100_ptx.cuh"]
 NVCC = os.environ.get("NVCC", "nvcc")
 FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",

@@ -168,8 +168,13 @@ class PackedWeights:
     def forward(self, x: torch.Tensor, *, lengths: Optional[torch.Tensor] = None,
                 hx: Optional[Tuple[torch.Tensor, torch.Tensor]] = None, need_state: bool = True,
                 check: Optional[bool] = None, timeout_ms: int = 0, extra_flags: int = 0,
-                c_n_f32: bool = False):
-        """Runs the LSTM + Linear forward on x[B,T,I]; returns (out, h_n, c_n)."""
+                c_n_f32: bool = False, dedupe: bool = False):
+        """Runs the LSTM + Linear forward on x[B,T,I]; returns (out, h_n, c_n).
+
+        dedupe=True computes each distinct row (x up to its length, the length,
+        its hx rows) once and copies the results to the duplicates
+        (PLSTM_FLAG_DEDUPE); it synchronises the stream once.
+        """
         lib = _lib.load()
         dev = self.device
         x = _require_cuda(x, "x", dev, self.dtype)
@@ -198,7 +203,7 @@ class PackedWeights:
         if need_state:
             h_n = torch.empty(L, B, H, dtype=self.dtype, device=dev)
             c_n = torch.empty(L, B, H, dtype=torch.float32 if c_n_f32 else self.dtype, device=dev)
-        flags = extra_flags | (_lib.FLAG_CN_F32 if c_n_f32 else 0)
+        flags = extra_flags | (_lib.FLAG_CN_F32 if c_n_f32 else 0) | (_lib.FLAG_DEDUPE if dedupe else 0)
         if check if check is not None else _env_check():
             flags |= _lib.FLAG_SYNC_CHECK
         d = self.desc(batch=B, seq_len=T, extra_flags=flags, timeout_ms=timeout_ms)
@@ -218,17 +223,65 @@ def lstm_linear_forward(x: torch.Tensor, w_ih: Sequence[torch.Tensor], w_hh: Seq
                         w_lin: Optional[torch.Tensor] = None, b_lin: Optional[torch.Tensor] = None, *,
                         lengths: Optional[torch.Tensor] = None,
                         hx: Optional[Tuple[torch.Tensor, torch.Tensor]] = None, out_mode: str = "seq",
-                        backend: str = "auto", check: Optional[bool] = None):
+                        backend: str = "auto", check: Optional[bool] = None, dedupe: bool = False):
     """x[B,T,I] with nn.LSTM(batch_first=True)-layout weights -> (out, h_n, c_n).
 
     out is [B,T,O] for out_mode="seq" (zero past each row's length), [B,O] for
     "last" (Linear on each row's last valid step) and the last layer's h
     sequence [B,T,H] for "hseq".  h_n / c_n are [L,B,H] at each row's last
-    valid step.
+    valid step.  dedupe=True computes identical rows once (PLSTM_FLAG_DEDUPE).
     """
     packed = PackedWeights(w_ih, w_hh, b_ih, b_hh, w_lin, b_lin, out_mode=out_mode, backend=backend,
                            input_size=int(x.shape[-1]))
-    return packed.forward(x, lengths=lengths, hx=hx, check=check)
+    return packed.forward(x, lengths=lengths, hx=hx, check=check, dedupe=dedupe)
+
+
+def unique_rows(x: torch.Tensor, *, lengths: Optional[torch.Tensor] = None,
+                hx: Optional[Tuple[torch.Tensor, torch.Tensor]] = None, hidden_size: Optional[int] = None,
+                num_layers: Optional[int] = None) -> Tuple[torch.Tensor, torch.Tensor, int]:
+    """Groups the identical rows of x[B,T,I] on the GPU (plstm_unique_rows).
+
+    A row's identity is x up to its length, the length and, with hx, its h0 /
+    c0 rows in every layer, compared bit for bit.  Returns (row_map[B],
+    unique_index[count], count): row_map[b] is the distinct-row index of row
+    b, unique_index the first row of each distinct row, ascending.  This is
+    the general form of the reference's all-rows-equal check
+    (persistent_lstm_hip/model.py:493-520).
+    """
+    lib = _lib.load()
+    if not isinstance(x, torch.Tensor) or x.dim() != 3:
+        raise ValueError("x must be a [B, T, I] tensor")
+    dev = x.device
+    x = _require_cuda(x, "x", dev)
+    if x.dtype not in _DTYPES:
+        raise ValueError(f"unsupported dtype {x.dtype}")
+    B, T, I = (int(v) for v in x.shape)
+    lens = None
+    if lengths is not None:
+        lens = lengths.to(device=dev, dtype=torch.int32).contiguous()
+        if lens.shape != (B,):
+            raise ValueError(f"lengths must be [{B}], got {tuple(lens.shape)}")
+    h0 = c0 = None
+    H, L = hidden_size or 1, num_layers or 1
+    if hx is not None:
+        h0 = _require_cuda(hx[0], "h0", dev, x.dtype)
+        c0 = _require_cuda(hx[1], "c0", dev, x.dtype)
+        if h0.dim() != 3 or h0.shape != c0.shape or int(h0.shape[1]) != B:
+            raise ValueError(f"hx tensors must both be [L, {B}, H]")
+        L, H = int(h0.shape[0]), int(h0.shape[2])
+    d = make_desc(batch=B, seq_len=T, input_size=I, hidden_size=H, num_layers=L, output_size=1, dtype=x.dtype,
+                  flags=_lib.FLAG_OUT_LAST, device=dev.index or 0)
+    nbytes = ctypes.c_size_t(0)
+    _lib.check(lib.plstm_unique_rows_workspace_size(ctypes.byref(d), ctypes.byref(nbytes)))
+    ws = torch.empty(max(int(nbytes.value), 256), dtype=torch.uint8, device=dev)
+    row_map = torch.empty(B, dtype=torch.int32, device=dev)
+    uniq = torch.empty(B, dtype=torch.int32, device=dev)
+    count = ctypes.c_int32(0)
+    with torch.cuda.device(dev):
+        rc = lib.plstm_unique_rows(ctypes.byref(d), _ptr(x), _ptr(lens), _ptr(h0), _ptr(c0), row_map.data_ptr(),
+                                   uniq.data_ptr(), ctypes.byref(count), ws.data_ptr(), ws.numel(), _stream(dev))
+    _lib.check(rc)
+    return row_map, uniq[:count.value], int(count.value)
 
 
 def read_status(ws: torch.Tensor) -> Tuple[int, int]:

@@ -102,6 +102,29 @@ int32_t check_device(const Problem& p) {
   return PLSTM_OK;
 }
 
+size_t backend_ws(int backend, const Problem& p) {
+  return backend == PLSTM_BACKEND_TC ? tc_workspace_size(p) : simt_workspace_size(p);
+}
+
+// Scratch plstm_forward_packed needs: the backend's, then (PLSTM_FLAG_DEDUPE)
+// the row grouping and the distinct-row copies.
+size_t forward_ws(int backend, const Problem& p) {
+  const size_t inner = backend_ws(backend, p);
+  return (p.flags & PLSTM_FLAG_DEDUPE) ? align_up(inner, 256) + dedupe_scratch_size(p) : inner;
+}
+
+struct BackendCtx {
+  int backend;
+  const void* packed;
+};
+
+int32_t run_backend(void* ctx, const Problem& q, const void* x, const int32_t* lengths, const void* h0,
+                    const void* c0, void* out, void* h_n, void* c_n, void* ws, cudaStream_t s) {
+  const BackendCtx* c = static_cast<const BackendCtx*>(ctx);
+  return c->backend == PLSTM_BACKEND_TC ? tc_forward(q, c->packed, x, lengths, h0, c0, out, h_n, c_n, ws, s)
+                                        : simt_forward(q, c->packed, x, lengths, h0, c0, out, h_n, c_n, ws, s);
+}
+
 int32_t finish(const Problem& p, void* ws, cudaStream_t s) {
   if (!(p.flags & PLSTM_FLAG_SYNC_CHECK)) return PLSTM_OK;
   int32_t st = 0, detail = 0;
@@ -190,7 +213,7 @@ int32_t plstm_workspace_size(const plstm_desc* d, size_t* bytes) {
   PLSTM_CHECK_ARG(bytes != nullptr, "bytes is NULL");
   int b = 0;
   if ((rc = pick_backend(d, p, &b)) != PLSTM_OK) return rc;
-  *bytes = b == PLSTM_BACKEND_TC ? tc_workspace_size(p) : simt_workspace_size(p);
+  *bytes = forward_ws(b, p);
   return PLSTM_OK;
 }
 
@@ -246,17 +269,22 @@ int32_t plstm_forward_packed(const plstm_desc* d, const void* packed, const void
   PLSTM_CHECK_ARG((h0 == nullptr) == (c0 == nullptr), "h0 and c0 must both be given or both be NULL");
   int b = 0;
   if ((rc = pick_backend(d, p, &b)) != PLSTM_OK) return rc;
-  const size_t need = b == PLSTM_BACKEND_TC ? tc_workspace_size(p) : simt_workspace_size(p);
+  const size_t need = forward_ws(b, p);
   if (workspace_bytes < need) {
     set_error("workspace too small: need " + std::to_string(need) + " bytes");
     return PLSTM_EWORKSPACE;
   }
   if ((rc = check_device(p)) != PLSTM_OK) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if ((p.flags & PLSTM_FLAG_DEDUPE) && (rc = dedupe_stream_ok(s)) != PLSTM_OK) return rc;
   PLSTM_TRY_CUDA(cudaMemsetAsync(workspace, 0, kStatusBytes, s));
   if (p.B == 0) return PLSTM_OK;
-  rc = b == PLSTM_BACKEND_TC ? tc_forward(p, packed, x, lengths, h0, c0, out, h_n, c_n, workspace, s)
-                             : simt_forward(p, packed, x, lengths, h0, c0, out, h_n, c_n, workspace, s);
+  BackendCtx ctx = {b, packed};
+  if ((p.flags & PLSTM_FLAG_DEDUPE) && p.B > 1 && p.T > 0)
+    rc = dedupe_forward(p, DedupeInner{run_backend, &ctx}, x, lengths, h0, c0, out, h_n, c_n, workspace,
+                        backend_ws(b, p), s);
+  else
+    rc = run_backend(&ctx, p, x, lengths, h0, c0, out, h_n, c_n, workspace, s);
   if (rc != PLSTM_OK) return rc;
   return finish(p, workspace, s);
 }
@@ -293,6 +321,39 @@ int32_t plstm_forward(const plstm_desc* d, const void* x, const void* const* w_i
   PLSTM_CHECK_ARG(d != nullptr, "descriptor is NULL");
   return forward_impl(d, d->w_layout, d->w_layout, x, w_ih, w_hh, b_ih, b_hh, w_lin, b_lin, lengths,
                       h0, c0, out, h_n, c_n, workspace, workspace_bytes, stream);
+}
+
+int32_t plstm_unique_rows_workspace_size(const plstm_desc* d, size_t* bytes) {
+  clear_error();
+  Problem p;
+  int32_t rc = make_problem(d, &p);
+  if (rc != PLSTM_OK) return rc;
+  PLSTM_CHECK_ARG(bytes != nullptr, "bytes is NULL");
+  *bytes = unique_rows_scratch_size(p);
+  return PLSTM_OK;
+}
+
+int32_t plstm_unique_rows(const plstm_desc* d, const void* x, const int32_t* lengths, const void* h0,
+                          const void* c0, int32_t* row_map, int32_t* unique_index, int32_t* count,
+                          void* workspace, size_t workspace_bytes, void* stream) {
+  clear_error();
+  Problem p;
+  int32_t rc = make_problem(d, &p);
+  if (rc != PLSTM_OK) return rc;
+  PLSTM_CHECK_ARG(count != nullptr, "count is NULL");
+  PLSTM_CHECK_ARG(p.B == 0 || (row_map != nullptr && unique_index != nullptr), "row_map / unique_index is NULL");
+  PLSTM_CHECK_ARG(p.B == 0 || p.T == 0 || x != nullptr, "x is NULL");
+  PLSTM_CHECK_ARG((h0 == nullptr) == (c0 == nullptr), "h0 and c0 must both be given or both be NULL");
+  const size_t need = unique_rows_scratch_size(p);
+  if (workspace == nullptr || workspace_bytes < need) {
+    set_error("workspace too small: need " + std::to_string(need) + " bytes");
+    return PLSTM_EWORKSPACE;
+  }
+  *count = 0;
+  if (p.B == 0) return PLSTM_OK;
+  if ((rc = check_device(p)) != PLSTM_OK) return rc;
+  return unique_rows(p, x, lengths, h0, c0, row_map, unique_index, count, workspace,
+                     static_cast<cudaStream_t>(stream));
 }
 
 int32_t plstm_read_status(const void* workspace, void* stream, int32_t* status, int32_t* detail) {

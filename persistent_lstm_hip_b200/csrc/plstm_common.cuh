@@ -144,6 +144,23 @@ int32_t tcl_pack(const Problem& p, int ih_layout, int hh_layout, const void* con
 int32_t tcl_forward(const Problem& p, const void* packed, const void* x, const int32_t* lengths, const void* h0,
                     const void* c0, void* out, void* h_n, void* c_n, void* ws, cudaStream_t s);
 
+// Duplicate-row elimination (plstm_dedupe.cu).  `inner.run` is the backend
+// forward the distinct rows go through (Problem q: batch = distinct count).
+struct DedupeInner {
+  int32_t (*run)(void* ctx, const Problem& q, const void* x, const int32_t* lengths, const void* h0,
+                 const void* c0, void* out, void* h_n, void* c_n, void* ws, cudaStream_t s);
+  void* ctx;
+};
+int32_t dedupe_stream_ok(cudaStream_t s);  // PLSTM_EINVAL (message set) while `s` is capturing
+size_t unique_rows_scratch_size(const Problem& p);
+size_t dedupe_scratch_size(const Problem& p);
+int32_t unique_rows(const Problem& p, const void* x, const int32_t* lengths, const void* h0, const void* c0,
+                    int* row_map, int* unique_index, int* count, void* scratch, cudaStream_t s);
+// ws = [inner_ws_bytes of backend scratch, 256-aligned][dedupe_scratch_size(p)].
+int32_t dedupe_forward(const Problem& p, const DedupeInner& inner, const void* x, const int32_t* lengths,
+                       const void* h0, const void* c0, void* out, void* h_n, void* c_n, void* ws,
+                       size_t inner_ws_bytes, cudaStream_t s);
+
 // Hidden update (plstm_hidden_update): recurrence over precomputed input projections.
 struct HuProblem {
   int B, T, H, dtype, flags, w_layout, device;

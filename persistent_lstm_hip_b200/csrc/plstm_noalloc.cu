@@ -76,6 +76,7 @@ extern "C" int32_t plstm_forward_packed_noalloc(const plstm_desc* d, const void*
                    ((d->flags & PLSTM_FLAG_NO_LINEAR) ? 1 : 0);
   PLSTM_CHECK_ARG(outs == 1, "exactly one of PLSTM_FLAG_OUT_SEQ, _OUT_LAST, _NO_LINEAR must be set");
   PLSTM_CHECK_ARG(!(d->flags & PLSTM_FLAG_TRACE), "PLSTM_FLAG_TRACE needs a caller workspace");
+  PLSTM_CHECK_ARG(!(d->flags & PLSTM_FLAG_DEDUPE), "PLSTM_FLAG_DEDUPE needs a caller workspace");
   if (!(d->flags & PLSTM_FLAG_NO_LINEAR)) PLSTM_CHECK_ARG(d->output_size > 0, "output_size must be > 0");
   PLSTM_CHECK_ARG(packed != nullptr, "packed is NULL");
   PLSTM_CHECK_ARG(d->batch == 0 || d->seq_len == 0 || x != nullptr, "x is NULL");

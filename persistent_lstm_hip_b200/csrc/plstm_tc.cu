@@ -625,31 +625,42 @@ __global__ void __launch_bounds__(Smem<N>::kThreads, 1) wavefront_kernel(const P
     uint16_t* out16 = static_cast<uint16_t*>(p.out);
     const int lin_n0 = (S::kSplitLinear ? s * NL : 0) + grp * (NL / G);  // first batch column of this warp
 
-    // Stores the Linear outputs of step `ts` from the Linear accumulator (lanes = output rows).
-    auto store_linear = [&](int ts, bool last_mode) {
+    // This warp's columns of the Linear accumulator (lanes = output rows).
+    constexpr int kLinChunks = NL / G / 8;
+    auto load_linear = [&](uint32_t (&r)[kLinChunks][8]) {
 #pragma unroll
-      for (int c0 = 0; c0 < NL / G; c0 += 8) {
-        uint32_t r[8];
-        ptx::tmem_ld_32x32b_x8(tmem + (uint32_t)(S::kDLin + grp * (NL / G) + c0), r);
-        ptx::tmem_wait_ld();
-        if (o < p.O) {
+      for (int c = 0; c < kLinChunks; ++c)
+        ptx::tmem_ld_32x32b_x8(tmem + (uint32_t)(S::kDLin + grp * (NL / G) + 8 * c), r[c]);
+      ptx::tmem_wait_ld();
+    };
+    // Stores the Linear outputs of step `ts` (or, last_mode, the [B][O] result).  In the
+    // step loop this runs after the step's barrier arrivals: an arrive has release
+    // semantics and would wait for global stores issued before it to complete.
+    auto write_linear = [&](int ts, const uint32_t (&r)[kLinChunks][8], bool last_mode) {
+      if (o >= p.O) return;
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const int n = lin_n0 + c0 + i;
-            const int b = perm_s[n];
-            if (b < 0) continue;
-            const float v = __uint_as_float(r[i]) + blin_o;
-            if (last_mode) {
-              out16[(size_t)b * p.O + o] = to_bits<BF16>(v);
-            } else {
-              const bool live = ts < lens_s[n];
-              out16[((size_t)b * p.T + ts) * p.O + o] = to_bits<BF16>(live ? v : 0.0f);
-            }
+      for (int c = 0; c < kLinChunks; ++c)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int n = lin_n0 + 8 * c + i;
+          const int b = perm_s[n];
+          if (b < 0) continue;
+          const float v = __uint_as_float(r[c][i]) + blin_o;
+          if (last_mode) {
+            out16[(size_t)b * p.O + o] = to_bits<BF16>(v);
+          } else {
+            const bool live = ts < lens_s[n];
+            out16[((size_t)b * p.T + ts) * p.O + o] = to_bits<BF16>(live ? v : 0.0f);
           }
         }
-      }
+    };
+    auto store_linear = [&](int ts, bool last_mode) {
+      uint32_t r[kLinChunks][8];
+      load_linear(r);
+      write_linear(ts, r, last_mode);
     };
 
+    uint32_t lin_r[kLinChunks][8];  // Linear accumulator of step t-1, stored at the end of step t
     for (int t = 0; t < Tt; ++t) {
       const int b = t & 1;
       if (*abort_flag) break;
@@ -668,7 +679,7 @@ __global__ void __launch_bounds__(Smem<N>::kThreads, 1) wavefront_kernel(const P
       }
       ptx::tmem_wait_ld();
       if (tid == 0) trace_mark(p, rank, t, 5);
-      if (MODE == kModeSeq && lin_warp && t >= 1) store_linear(t - 1, false);
+      if (MODE == kModeSeq && lin_warp && t >= 1) load_linear(lin_r);
       ptx::tc_fence_before();
 
       // Layer l+1 must have consumed h_{t-2} (same buffer and copy source) before it is overwritten.
@@ -687,12 +698,7 @@ __global__ void __launch_bounds__(Smem<N>::kThreads, 1) wavefront_kernel(const P
 #pragma unroll
         for (int jc = 0; jc < CPW; ++jc)
 #pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            *reinterpret_cast<uint16_t*>(dst + sw128_off(ncol[jc][e], ul)) = hw[tau][jc][e];
-            if (MODE == kModeHSeq && last_layer && bidx[jc][e] >= 0)
-              out16[((size_t)bidx[jc][e] * p.T + t) * kH + 64 * s + ul] =
-                  (!VARLEN || t < len_c[jc][e]) ? hw[tau][jc][e] : (uint16_t)0;
-          }
+          for (int e = 0; e < 2; ++e) *reinterpret_cast<uint16_t*>(dst + sw128_off(ncol[jc][e], ul)) = hw[tau][jc][e];
       }
       ptx::fence_proxy_async_smem();
       if (tid == 0) trace_mark(p, rank, t, 6);
@@ -708,6 +714,21 @@ __global__ void __launch_bounds__(Smem<N>::kThreads, 1) wavefront_kernel(const P
           push_h(sbase + (uint32_t)(S::kB + (b ^ 1) * S::kBufBytes + (2 + s) * S::kBKB), S::kBKB, rank, to_sibling,
                  bar_rec + 8 * (b ^ 1), l + 1 < p.L, 2 * (l + 1),
                  sbase + (uint32_t)(S::kB + b * S::kBufBytes + s * S::kBKB), bar_in + 8 * b);
+        }
+      }
+      // Global outputs of the step, after its arrivals (see write_linear).
+      if (MODE == kModeSeq && lin_warp && t >= 1) write_linear(t - 1, lin_r, false);
+      if (MODE == kModeHSeq && last_layer) {
+#pragma unroll
+        for (int tau = 0; tau < 2; ++tau) {
+          const int ul = 8 * (4 * tau + q) + j8;
+#pragma unroll
+          for (int jc = 0; jc < CPW; ++jc)
+#pragma unroll
+            for (int e = 0; e < 2; ++e)
+              if (bidx[jc][e] >= 0)
+                out16[((size_t)bidx[jc][e] * p.T + t) * kH + 64 * s + ul] =
+                    (!VARLEN || t < len_c[jc][e]) ? hw[tau][jc][e] : (uint16_t)0;
         }
       }
     }
@@ -1176,32 +1197,41 @@ __global__ void __launch_bounds__(Smem2<NH>::kThreads, 1) wavefront2_kernel(cons
     const int lin_n0 = sl * NH + (S::kSplitLinear ? s * NL : 0);  // first tile row of this CTA's Linear columns
     const uint32_t dlin = tmem + (uint32_t)(S::kDLin + sl * NL);
 
-    // Stores the Linear outputs of step `ts` from the slot's Linear accumulator (lanes = output rows).
-    auto store_linear = [&](int ts, bool last_mode) {
+    // The slot's Linear accumulator (lanes = output rows, registers = tile columns).
+    auto load_linear = [&](auto& r) {
 #pragma unroll
-      for (int c0 = 0; c0 < NL; c0 += 8) {
-        uint32_t r[8];
-        ptx::tmem_ld_32x32b_x8(dlin + (uint32_t)c0, r);
-        ptx::tmem_wait_ld();
-        if (o < p.O) {
+      for (int c = 0; c < NL / 8; ++c) ptx::tmem_ld_32x32b_x8(dlin + (uint32_t)(8 * c), r[c]);
+      ptx::tmem_wait_ld();
+    };
+    // Stores the Linear outputs of step `ts` (or, last_mode, the [B][O] result).  In the
+    // step loop this runs after the step's barrier arrivals: an arrive has release
+    // semantics and would wait for global stores issued before it to complete.
+    auto write_linear = [&](int ts, const auto& r, bool last_mode) {
+      if (o >= p.O) return;
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const int n = lin_n0 + c0 + i;
-            const int b = perm_s[n];
-            if (b < 0) continue;
-            const float v = __uint_as_float(r[i]) + blin_o;
-            if (last_mode) {
-              out16[(size_t)b * p.O + o] = to_bits<BF16>(v);
-            } else {
-              const bool live = ts < lens_s[n];
-              out16[((size_t)b * p.T + ts) * p.O + o] = to_bits<BF16>(live ? v : 0.0f);
-            }
+      for (int c = 0; c < NL / 8; ++c)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int n = lin_n0 + 8 * c + i;
+          const int b = perm_s[n];
+          if (b < 0) continue;
+          const float v = __uint_as_float(r[c][i]) + blin_o;
+          if (last_mode) {
+            out16[(size_t)b * p.O + o] = to_bits<BF16>(v);
+          } else {
+            const bool live = ts < lens_s[n];
+            out16[((size_t)b * p.T + ts) * p.O + o] = to_bits<BF16>(live ? v : 0.0f);
           }
         }
-      }
+    };
+    auto store_linear = [&](int ts, bool last_mode) {
+      uint32_t r[NL / 8][8];
+      load_linear(r);
+      write_linear(ts, r, last_mode);
     };
 
     if (active) {
+      uint32_t lin_r[MODE == kModeSeq ? NL / 8 : 1][8];  // Linear accumulator of step t-1, stored at the end of step t
       for (int t = 0; t < Tt; ++t) {
         const int b = t & 1;
         if (*abort_flag) break;
@@ -1219,7 +1249,7 @@ __global__ void __launch_bounds__(Smem2<NH>::kThreads, 1) wavefront2_kernel(cons
           tmem_ld_chunks<CPW>(col + ((uint32_t)(32 * q + 16) << 16), rgo[tau]);
         }
         ptx::tmem_wait_ld();
-        if (MODE == kModeSeq && lin_warp && t >= 1) store_linear(t - 1, false);
+        if (MODE == kModeSeq && lin_warp && t >= 1) load_linear(lin_r);
         ptx::tc_fence_before();
         // The accumulator may now be re-initialised by the next step's input MMAs.
         __syncwarp();
@@ -1253,12 +1283,8 @@ __global__ void __launch_bounds__(Smem2<NH>::kThreads, 1) wavefront2_kernel(cons
 #pragma unroll
           for (int jc = 0; jc < CPW; ++jc)
 #pragma unroll
-            for (int e = 0; e < 2; ++e) {
+            for (int e = 0; e < 2; ++e)
               *reinterpret_cast<uint16_t*>(dst + sw128_off(8 * jc + cpair + e, ul)) = hw[tau][jc][e];
-              if (MODE == kModeHSeq && last_layer && bidx[jc][e] >= 0)
-                out16[((size_t)bidx[jc][e] * p.T + t) * kH + 64 * s + ul] =
-                    (!VARLEN || t < len_c[jc][e]) ? hw[tau][jc][e] : (uint16_t)0;
-            }
         }
         ptx::fence_proxy_async_smem();
         if (tracer && q == 0 && lane == 0) trace_mark(p, rank, t, 6);
@@ -1274,6 +1300,21 @@ __global__ void __launch_bounds__(Smem2<NH>::kThreads, 1) wavefront2_kernel(cons
             push_h(bbuf(sl, b ^ 1) + (uint32_t)((2 + s) * S::kBKB), S::kBKB, rank, to_sibling,
                    bar(sl, S::kFullRec, b ^ 1), l + 1 < p.L, 2 * (l + 1), bbuf(sl, b) + (uint32_t)(s * S::kBKB),
                    bar(sl, S::kFullIn, b));
+          }
+        }
+        // Global outputs of the step, after its arrivals (see write_linear).
+        if (MODE == kModeSeq && lin_warp && t >= 1) write_linear(t - 1, lin_r, false);
+        if (MODE == kModeHSeq && last_layer) {
+#pragma unroll
+          for (int tau = 0; tau < 2; ++tau) {
+            const int ul = 8 * (4 * tau + q) + j8;
+#pragma unroll
+            for (int jc = 0; jc < CPW; ++jc)
+#pragma unroll
+              for (int e = 0; e < 2; ++e)
+                if (bidx[jc][e] >= 0)
+                  out16[((size_t)bidx[jc][e] * p.T + t) * kH + 64 * s + ul] =
+                      (!VARLEN || t < len_c[jc][e]) ? hw[tau][jc][e] : (uint16_t)0;
           }
         }
       }

@@ -23,6 +23,7 @@ from .packing import PackedLSTMLayerWeights, PackedLSTMWeights, PackedRegressorW
 _OFF = {"0", "false", "no", "off", "disable", "disabled"}
 _ON = {"1", "true", "yes", "on", "force", "forced", "assume"}
 _AUTO = {"", "auto", "detect"}
+_DEDUPE = {"dedupe", "rows"}
 
 
 class StandardLSTMRegressor(nn.Module):
@@ -208,31 +209,39 @@ class PersistentLSTMRegressor(nn.Module):
         """Optional duplicate-row shortcut of the reference (model.py:493-520):
         with PERSISTENT_LSTM_HIP_UNIFORM_BATCH=auto, a batch whose rows are all
         identical is computed once and broadcast.  Off by default here because
-        the detection costs a full pass over x and a host synchronisation."""
+        the detection costs a full pass over x and a host synchronisation.
+        The value "dedupe" selects the general form instead (any set of
+        identical rows computed once, on the GPU; `_dedupe_rows`)."""
         mode = os.environ.get("PERSISTENT_LSTM_HIP_UNIFORM_BATCH", "0").strip().lower()
-        if mode in _OFF or x.dim() != 3 or x.size(0) <= 1:
+        if mode in _OFF or mode in _DEDUPE or x.dim() != 3 or x.size(0) <= 1:
             return False
         if mode in _ON:
             return True
         if mode not in _AUTO:
-            raise ValueError("PERSISTENT_LSTM_HIP_UNIFORM_BATCH must be one of: auto, detect, assume, 1, 0")
+            raise ValueError("PERSISTENT_LSTM_HIP_UNIFORM_BATCH must be one of: auto, detect, assume, dedupe, 1, 0")
         key = (x.data_ptr(), x.device.index, str(x.dtype), tuple(x.shape), tuple(x.stride()), x._version)
         if self._uniform_key != key:
             self._uniform_value = bool(torch.equal(x, x.narrow(0, 0, 1).expand_as(x)))
             self._uniform_key = key
         return self._uniform_value
 
+    @staticmethod
+    def _dedupe_rows() -> bool:
+        mode = os.environ.get("PERSISTENT_LSTM_HIP_UNIFORM_BATCH", "0").strip().lower()
+        return mode in _DEDUPE
+
     def forward(self, x: torch.Tensor, lengths: Optional[torch.Tensor] = None) -> torch.Tensor:
         self._forced_backend()
+        dedupe = self._dedupe_rows()
         uniform = lengths is None and self._uniform_batch(x)
         xin = x.narrow(0, 0, 1) if uniform else x
         pw = self.packed_weights("last")
         if os.environ.get("PERSISTENT_LSTM_HIP_DEBUG", "0") == "1" and not self._debug_reported:
             print(f"persistent_lstm_hip_b200 debug: backend={pw.backend}, batch={int(x.size(0))}, "
-                  f"seq_len={int(x.size(1))}, uniform_batch_fast_path={uniform}")
+                  f"seq_len={int(x.size(1))}, uniform_batch_fast_path={uniform}, dedupe_rows={dedupe}")
             self._debug_reported = True
         with torch.no_grad():
-            out, _, _ = pw.forward(xin, lengths=lengths, need_state=False)
+            out, _, _ = pw.forward(xin, lengths=lengths, need_state=False, dedupe=dedupe)
         if uniform:
             from .ext import repeat_first_row
             return repeat_first_row(out, int(x.size(0)))
@@ -241,7 +250,8 @@ class PersistentLSTMRegressor(nn.Module):
     def forward_sequence(self, x: torch.Tensor, lengths: Optional[torch.Tensor] = None,
                          hx: Optional[Tuple[torch.Tensor, torch.Tensor]] = None):
         with torch.no_grad():
-            out, h_n, c_n = self.packed_weights("seq").forward(x, lengths=lengths, hx=hx)
+            out, h_n, c_n = self.packed_weights("seq").forward(x, lengths=lengths, hx=hx,
+                                                               dedupe=self._dedupe_rows())
         return out, (h_n, c_n)
 
 

@@ -89,3 +89,25 @@ def test_oracle_zero_length_rows_keep_initial_state():
     got = oracle.forward(x, w_ih, w_hh, b, None, None, None, lengths=lens, h0=h0, c0=c0, out_mode="hseq")
     for a, r in zip(got, ref):
         np.testing.assert_allclose(a, r, atol=1e-12)
+
+
+def test_unique_rows_restates_the_uniform_check():
+    """All rows equal (the reference's torch.equal(x, x[:1].expand_as(x)),
+    persistent_lstm_hip/model.py:515-518) <=> one distinct row; duplicates are
+    numbered by first occurrence; padding past a length and hx rows count as
+    the row's identity the way the forward reads them."""
+    rng = np.random.default_rng(5)
+    base = rng.standard_normal((1, 6, 3)).astype(np.float16)
+    x = np.repeat(base, 4, axis=0)
+    assert oracle.unique_rows(x)[2] == 1
+    x[2, 5, 1] += np.float16(1.0)
+    row_map, first, n = oracle.unique_rows(x)
+    assert n == 2 and list(row_map) == [0, 0, 1, 0] and list(first) == [0, 2]
+    # Row 2 differs only past its length 5: it joins row 0 (same length).
+    row_map, _, n = oracle.unique_rows(x, lengths=[5, 6, 5, 6])
+    assert list(row_map) == [0, 1, 0, 1] and n == 2
+    h0 = np.zeros((2, 4, 8), dtype=np.float16)
+    c0 = np.zeros_like(h0)
+    c0[1, 3, 7] = 1.0
+    row_map, _, n = oracle.unique_rows(x, lengths=[5, 6, 5, 6], h0=h0, c0=c0)
+    assert list(row_map) == [0, 1, 0, 2] and n == 3

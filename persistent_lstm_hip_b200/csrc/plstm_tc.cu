@@ -818,7 +818,11 @@ __global__ void __launch_bounds__(Smem<N>::kThreads, 1) wavefront_kernel(const P
 // the CTA's resident weights (TMEM columns [0, 256)) and the Linear head's A image.
 // Each slot's gate accumulator is single-buffered (TMEM holds A + 2 slots x 2 tiles x
 // NH columns + the Linear tiles): the next step's input MMAs wait until the compute
-// warps have loaded the current accumulator ("dfree").
+// warps have loaded the current accumulator ("dfree").  With [B][T][O] output the
+// Linear head's MMAs have their own commit barrier and a double-buffered accumulator,
+// read by one output warp per slot (warps 10 / 11, TMEM lane quadrants 2 / 3, where
+// the head's rows are replicated), so neither the gate math nor the global stores of
+// the outputs sit on the recurrence's critical path.
 template <int NH>
 struct Smem2 {
   static constexpr int kBKB = NH * 128;             // one 64-wide K block of a slot's B operand
@@ -828,9 +832,10 @@ struct Smem2 {
   static constexpr int kB = 0;
   static constexpr int kALin = kB + 2 * kSlotBytes;
   static constexpr int kBar = kALin + kALinBytes;
-  // Per slot: six barrier kinds, one per step parity (8 bytes each).
-  static constexpr int kFullIn = 0, kFullRec = 16, kEmpty = 32, kHReady = 48, kMma = 64, kDFree = 80;
-  static constexpr int kBarSlot = 96;
+  // Per slot: eight barrier kinds, one per buffer parity (8 bytes each).
+  static constexpr int kFullIn = 0, kFullRec = 16, kEmpty = 32, kHReady = 48, kMma = 64, kDFree = 80, kLin = 96,
+                       kLinFree = 112;
+  static constexpr int kBarSlot = 128;
   static constexpr int kTmemSlot = kBar + 2 * kBarSlot, kAbort = kTmemSlot + 4, kDone = kTmemSlot + 8;
   static constexpr int kPerm = kTmemSlot + 64, kLens = kPerm + 4 * 2 * NH;
   static constexpr int kEnd = kLens + 4 * 2 * NH;
@@ -838,13 +843,14 @@ struct Smem2 {
   static constexpr int CPW = NH / 8;               // 8-column chunks per compute warp (all NH columns)
   static constexpr int kSlotWarps = 4;             // compute warps per slot: one per TMEM lane quadrant
   static constexpr int kComputeWarps = 2 * kSlotWarps;
-  static constexpr int kThreads = (kComputeWarps + 2) * 32;  // + one control warp per slot
+  static constexpr int kOutWarp0 = kComputeWarps + 2;        // after one control warp per slot
+  static constexpr int kThreads = (kComputeWarps + 4) * 32;  // + one output warp per slot
   static constexpr bool kSplitLinear = (NH / 2) % 16 == 0;
   static constexpr int kNL = kSplitLinear ? NH / 2 : NH;
   static constexpr int kD = kTmemACols;            // D[slot][tau] at kD + (2 slot + tau) NH
-  static constexpr int kDLin = kD + 4 * NH;        // D_lin[slot] at kDLin + slot NL
-  static constexpr int kTmemCols = tmem_cols_for(kDLin + 2 * kNL);
-  static_assert(kDLin + 2 * kNL <= 512, "tile too wide for tensor memory");
+  static constexpr int kDLin = kD + 4 * NH;        // D_lin[slot][buffer] at kDLin + (2 slot + buffer) NL
+  static constexpr int kTmemCols = tmem_cols_for(kDLin + 4 * kNL);
+  static_assert(kDLin + 4 * kNL <= 512, "tile too wide for tensor memory");
   static_assert(NH % 16 == 0 && CPW >= 2 && CPW <= 4, "slot width must be 16 or 32");
 };
 
@@ -889,6 +895,8 @@ __global__ void __launch_bounds__(Smem2<NH>::kThreads, 1) wavefront2_kernel(cons
         ptx::mbar_init(bar(sl, S::kHReady, b), S::kSlotWarps);
         ptx::mbar_init(bar(sl, S::kMma, b), 1);
         ptx::mbar_init(bar(sl, S::kDFree, b), S::kSlotWarps);
+        ptx::mbar_init(bar(sl, S::kLin, b), 1);
+        ptx::mbar_init(bar(sl, S::kLinFree, b), 1);
       }
     *abort_flag = 0;
     reinterpret_cast<uint32_t*>(sm + S::kDone)[0] = 0;
@@ -907,9 +915,14 @@ __global__ void __launch_bounds__(Smem2<NH>::kThreads, 1) wavefront2_kernel(cons
     lens_s[i] = len;
   }
   if (does_linear) {
+    // The head's rows (O <= 32, rows 0-31 of the packed image) are replicated into
+    // every 32-row lane quadrant; 8-row swizzle groups keep their XOR pattern.
     const uint4* srcl = reinterpret_cast<const uint4*>(p.packed + packed_alin_off(p.L));
     uint4* dstl = reinterpret_cast<uint4*>(sm + S::kALin);
-    for (int i = tid; i < kALinBytes / 16; i += S::kThreads) dstl[i] = srcl[i];
+    for (int i = tid; i < kALinBytes / 16; i += S::kThreads) {
+      const int kb = i / (kATileKB / 16), r = (i / 8) % 128, c = i % 8;
+      dstl[i] = srcl[kb * (kATileKB / 16) + (r & 31) * 8 + c];
+    }
   }
   __syncthreads();  // perm_s / lens_s / tmem slot visible
   // Initial recurrent state h0 -> both recurrent K blocks of each slot's B buffer 0.
@@ -969,8 +982,66 @@ __global__ void __launch_bounds__(Smem2<NH>::kThreads, 1) wavefront2_kernel(cons
     return m;
   };
   auto dcol = [&](int sl, int tau) -> uint32_t { return tmem + (uint32_t)(S::kD + (2 * sl + tau) * NH); };
+  // The Linear MMAs issued at step t (on h_{t-1}; at t = T only in [B][O] mode) commit
+  // to kLin[lin_buf(t)] and accumulate into D_lin[sl][lin_buf(t)]; lin_phase(t) is the
+  // parity that commit completes.
+  auto lin_buf = [&](int t) -> int { return MODE == kModeSeq ? (t - 1) & 1 : 0; };
+  auto lin_phase = [&](int t) -> uint32_t { return MODE == kModeSeq ? (uint32_t)((t - 1) >> 1) & 1u : 0u; };
+  auto dlin_at = [&](int sl, int t) -> uint32_t {
+    return tmem + (uint32_t)(S::kDLin + (2 * sl + lin_buf(t)) * NL);
+  };
 
-  if (warp >= kComputeWarps) {
+  if (warp >= S::kOutWarp0) {
+    // ============================ output warps ===========================
+    // [B][T][O] mode: the Linear outputs of every step, read from the slot's Linear
+    // accumulator in this warp's lane quadrant and stored, off the critical path.
+    const int sl = warp - S::kOutWarp0;
+    bool active = false;
+    const int Tt = slot_len(sl, &active);
+    if (MODE == kModeSeq && does_linear && active) {
+      const int o = lane;
+      const float blin_o = o < p.O ? reinterpret_cast<const float*>(p.packed + packed_blin_off(p.L))[o] : 0.0f;
+      uint16_t* out16 = static_cast<uint16_t*>(p.out);
+      const int lin_n0 = sl * NH + (S::kSplitLinear ? s * NL : 0);
+      const uint32_t qlane = (uint32_t)(32 * (warp & 3)) << 16;
+      for (int t = 1; t <= Tt; ++t) {
+        if (*abort_flag) break;
+        if (!wait_phase(bar(sl, S::kLin, lin_buf(t)), lin_phase(t), abort_flag, p.timeout_ns)) {
+          if (lane == 0) raise_abort(p, sm + S::kAbort, ncta, t);
+          break;
+        }
+        ptx::tc_fence_after();
+        uint32_t r[NL / 8][8];
+#pragma unroll
+        for (int c = 0; c < NL / 8; ++c) ptx::tmem_ld_32x32b_x8(dlin_at(sl, t) + qlane + (uint32_t)(8 * c), r[c]);
+        ptx::tmem_wait_ld();
+        ptx::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(bar(sl, S::kLinFree, lin_buf(t)));
+        if (o < p.O) {
+#pragma unroll
+          for (int c = 0; c < NL / 8; ++c)
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const int n = lin_n0 + 8 * c + i;
+              const int b = perm_s[n];
+              if (b < 0) continue;
+              const float v = __uint_as_float(r[c][i]) + blin_o;
+              out16[((size_t)b * p.T + (t - 1)) * p.O + o] = to_bits<BF16>(t - 1 < lens_s[n] ? v : 0.0f);
+            }
+        }
+      }
+      // Outputs past the slot's last step are zero.
+      if (o < p.O && !*abort_flag) {
+        for (int i = 0; i < NL; ++i) {
+          const int n = lin_n0 + i;
+          const int b = perm_s[n];
+          if (b < 0) continue;
+          for (int ts = Tt; ts < p.T; ++ts) out16[((size_t)b * p.T + ts) * p.O + o] = 0;
+        }
+      }
+    }
+  } else if (warp >= kComputeWarps) {
     // ============================ control warps ==========================
     const int sl = warp - kComputeWarps;
     bool active = false;
@@ -986,9 +1057,8 @@ __global__ void __launch_bounds__(Smem2<NH>::kThreads, 1) wavefront2_kernel(cons
     const uint64_t dBx0 = ptx::desc_k_none(bbuf(sl, 0), 128, 256);
     constexpr uint64_t kBufStep = (uint64_t)(S::kBufBytes >> 4);
     const uint32_t lin_row_off = S::kSplitLinear ? (uint32_t)(s * NL) * 128u : 0u;
-    const uint32_t dlin = tmem + (uint32_t)(S::kDLin + sl * NL);
     const int steps = Tt + (does_linear ? 1 : 0);
-    int last_commit = -1;
+    int last_commit = -1, last_lin = -1;
     bool ok = true;
     const bool tracer = sl == p.trace_slot;
 
@@ -1031,12 +1101,16 @@ __global__ void __launch_bounds__(Smem2<NH>::kThreads, 1) wavefront2_kernel(cons
       }
       __syncwarp();
     };
+    // Commits the step's gate MMAs, then issues and commits the Linear MMAs on h_{t-1}
+    // (behind the gate MMAs in the tensor pipe, tracked by their own barrier).
     auto issue_lin_commit = [&](int t, bool lin) {
       const int b = t & 1;
       if (ptx::elect_one()) {
         ptx::tc_fence_after();
-        const uint64_t dB = dB0 + kBufStep * b;
+        ptx::mma_commit(bar(sl, S::kMma, b));
         if (lin) {
+          const uint64_t dB = dB0 + kBufStep * b;
+          const uint32_t dlin = dlin_at(sl, t);
 #pragma unroll
           for (int kb = 0; kb < 2; ++kb)
 #pragma unroll
@@ -1044,8 +1118,8 @@ __global__ void __launch_bounds__(Smem2<NH>::kThreads, 1) wavefront2_kernel(cons
               ptx::mma_f16_ss(dlin, dAl + (uint64_t)((kb * kATileKB + kk * 32) >> 4),
                               dB + (uint64_t)(((2 + kb) * S::kBKB + lin_row_off + kk * 32) >> 4), idesc_l,
                               (kb | kk) != 0 ? 1u : 0u);
+          ptx::mma_commit(bar(sl, S::kLin, lin_buf(t)));
         }
-        ptx::mma_commit(bar(sl, S::kMma, b));
       }
       __syncwarp();
     };
@@ -1086,7 +1160,7 @@ __global__ void __launch_bounds__(Smem2<NH>::kThreads, 1) wavefront2_kernel(cons
       for (int t = 0; ok && t < steps; ++t) {
         const int b = t & 1;
         const bool gates = t < Tt;
-        const bool lin = does_linear && (t == Tt || (MODE == kModeSeq && t >= 1));
+        const bool lin = does_linear && (MODE == kModeSeq ? t >= 1 : t == Tt);
         if (gates) issue_rec_half(t, s);  // own half of h_{t-1}: written before the previous step ended
         if (tracer && lane == 0) trace_mark(p, rank, t, 3);
         if (t >= 1) {
@@ -1100,8 +1174,16 @@ __global__ void __launch_bounds__(Smem2<NH>::kThreads, 1) wavefront2_kernel(cons
         }
         if (tracer && lane == 0) trace_mark(p, rank, t, 0);
         if (gates) issue_rec_half(t, 1 - s);
+        // The output warp must have read the Linear accumulator buffer this step reuses.
+        if (MODE == kModeSeq && lin && t >= 3 &&
+            !warp_wait_phase(bar(sl, S::kLinFree, lin_buf(t)), (uint32_t)((t - 3) >> 1) & 1u, abort_flag,
+                             p.timeout_ns)) {
+          fail(t);
+          break;
+        }
         issue_lin_commit(t, lin);
         last_commit = t;
+        if (lin) last_lin = t;
         if (tracer && lane == 0) trace_mark(p, rank, t, 1);
         if (!gates) break;  // drain step issued
         // This step's h hand-off, and the next step's input MMAs once the compute
@@ -1138,6 +1220,8 @@ __global__ void __launch_bounds__(Smem2<NH>::kThreads, 1) wavefront2_kernel(cons
       // All MMAs must have completed before TMEM is released.
       if (last_commit >= 0 && lane == 0)
         wait_phase(bar(sl, S::kMma, last_commit & 1), (last_commit >> 1) & 1, abort_flag, p.timeout_ns);
+      if (last_lin >= 0 && lane == 0)
+        wait_phase(bar(sl, S::kLin, lin_buf(last_lin)), lin_phase(last_lin), abort_flag, p.timeout_ns);
       __syncwarp();
     }
   } else {
@@ -1195,43 +1279,32 @@ __global__ void __launch_bounds__(Smem2<NH>::kThreads, 1) wavefront2_kernel(cons
     const float blin_o = (lin_warp && o < p.O) ? blin[o] : 0.0f;
     uint16_t* out16 = static_cast<uint16_t*>(p.out);
     const int lin_n0 = sl * NH + (S::kSplitLinear ? s * NL : 0);  // first tile row of this CTA's Linear columns
-    const uint32_t dlin = tmem + (uint32_t)(S::kDLin + sl * NL);
 
-    // The slot's Linear accumulator (lanes = output rows, registers = tile columns).
-    auto load_linear = [&](auto& r) {
+    // The Linear accumulator of the MMAs issued at step t (lanes = output rows,
+    // registers = tile columns), once their commit has completed.
+    auto load_linear = [&](int t, auto& r) -> bool {
+      if (!wait_phase(bar(sl, S::kLin, lin_buf(t)), lin_phase(t), abort_flag, p.timeout_ns)) return false;
+      ptx::tc_fence_after();
+      const uint32_t dlin = dlin_at(sl, t);
 #pragma unroll
       for (int c = 0; c < NL / 8; ++c) ptx::tmem_ld_32x32b_x8(dlin + (uint32_t)(8 * c), r[c]);
       ptx::tmem_wait_ld();
+      ptx::tc_fence_before();
+      return true;
     };
-    // Stores the Linear outputs of step `ts` (or, last_mode, the [B][O] result).  In the
-    // step loop this runs after the step's barrier arrivals: an arrive has release
-    // semantics and would wait for global stores issued before it to complete.
-    auto write_linear = [&](int ts, const auto& r, bool last_mode) {
+    // Stores the [B][O] result.
+    auto write_last = [&](const auto& r) {
       if (o >= p.O) return;
 #pragma unroll
       for (int c = 0; c < NL / 8; ++c)
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          const int n = lin_n0 + 8 * c + i;
-          const int b = perm_s[n];
-          if (b < 0) continue;
-          const float v = __uint_as_float(r[c][i]) + blin_o;
-          if (last_mode) {
-            out16[(size_t)b * p.O + o] = to_bits<BF16>(v);
-          } else {
-            const bool live = ts < lens_s[n];
-            out16[((size_t)b * p.T + ts) * p.O + o] = to_bits<BF16>(live ? v : 0.0f);
-          }
+          const int b = perm_s[lin_n0 + 8 * c + i];
+          if (b >= 0) out16[(size_t)b * p.O + o] = to_bits<BF16>(__uint_as_float(r[c][i]) + blin_o);
         }
-    };
-    auto store_linear = [&](int ts, bool last_mode) {
-      uint32_t r[NL / 8][8];
-      load_linear(r);
-      write_linear(ts, r, last_mode);
     };
 
     if (active) {
-      uint32_t lin_r[MODE == kModeSeq ? NL / 8 : 1][8];  // Linear accumulator of step t-1, stored at the end of step t
       for (int t = 0; t < Tt; ++t) {
         const int b = t & 1;
         if (*abort_flag) break;
@@ -1249,7 +1322,6 @@ __global__ void __launch_bounds__(Smem2<NH>::kThreads, 1) wavefront2_kernel(cons
           tmem_ld_chunks<CPW>(col + ((uint32_t)(32 * q + 16) << 16), rgo[tau]);
         }
         ptx::tmem_wait_ld();
-        if (MODE == kModeSeq && lin_warp && t >= 1) load_linear(lin_r);
         ptx::tc_fence_before();
         // The accumulator may now be re-initialised by the next step's input MMAs.
         __syncwarp();
@@ -1297,13 +1369,21 @@ __global__ void __launch_bounds__(Smem2<NH>::kThreads, 1) wavefront2_kernel(cons
           if (ptx::atom_add_acq_rel_smem(sbase + S::kDone + 4 * sl, 1u) % 4u == 3u) {
             const bool to_sibling = ((t + 1 < Tt) || (sibling_linear && t + 1 == Tt)) &&
                                     !(sl == 0 && rank == p.drop_rank && t == p.drop_step);
-            push_h(bbuf(sl, b ^ 1) + (uint32_t)((2 + s) * S::kBKB), S::kBKB, rank, to_sibling,
-                   bar(sl, S::kFullRec, b ^ 1), l + 1 < p.L, 2 * (l + 1), bbuf(sl, b) + (uint32_t)(s * S::kBKB),
-                   bar(sl, S::kFullIn, b));
+            // This step's Linear MMAs read h_{t-1} from the buffer the sibling refills with
+            // h_{t+1} once it has h_t: they must be done before h_t leaves.  (The output
+            // warp has usually long since seen this commit.)
+            if (MODE == kModeSeq && does_linear && t >= 1 &&
+                !wait_phase(bar(sl, S::kLin, lin_buf(t)), lin_phase(t), abort_flag, p.timeout_ns)) {
+              raise_abort(p, sm + S::kAbort, ncta, t);
+            } else {
+              push_h(bbuf(sl, b ^ 1) + (uint32_t)((2 + s) * S::kBKB), S::kBKB, rank, to_sibling,
+                     bar(sl, S::kFullRec, b ^ 1), l + 1 < p.L, 2 * (l + 1), bbuf(sl, b) + (uint32_t)(s * S::kBKB),
+                     bar(sl, S::kFullIn, b));
+            }
           }
         }
-        // Global outputs of the step, after its arrivals (see write_linear).
-        if (MODE == kModeSeq && lin_warp && t >= 1) write_linear(t - 1, lin_r, false);
+        // The h sequence output, after the step's arrivals: an arrive has release
+        // semantics and would wait for global stores issued before it to complete.
         if (MODE == kModeHSeq && last_layer) {
 #pragma unroll
           for (int tau = 0; tau < 2; ++tau) {
@@ -1318,28 +1398,13 @@ __global__ void __launch_bounds__(Smem2<NH>::kThreads, 1) wavefront2_kernel(cons
           }
         }
       }
-      // Drain: Linear of the last step's h.
-      if (lin_warp && !*abort_flag) {
-        if (wait_phase(bar(sl, S::kMma, Tt & 1), (Tt >> 1) & 1, abort_flag, p.timeout_ns)) {
-          ptx::tc_fence_after();
-          if (MODE == kModeSeq) {
-            if (Tt >= 1) store_linear(Tt - 1, false);
-          } else {
-            store_linear(0, true);
-          }
-          ptx::tc_fence_before();
-        } else if (lane == 0) {
+      // [B][O] mode: the Linear of the last step's h (issued at step Tt).
+      if (MODE == kModeLast && lin_warp && !*abort_flag) {
+        uint32_t r[NL / 8][8];
+        if (load_linear(Tt, r))
+          write_last(r);
+        else if (lane == 0)
           raise_abort(p, sm + S::kAbort, ncta, Tt);
-        }
-      }
-      // Outputs past the slot's last step are zero.
-      if (MODE == kModeSeq && lin_warp && o < p.O) {
-        for (int i = 0; i < NL; ++i) {
-          const int n = lin_n0 + i;
-          const int b = perm_s[n];
-          if (b < 0) continue;
-          for (int ts = Tt; ts < p.T; ++ts) out16[((size_t)b * p.T + ts) * p.O + o] = 0;
-        }
       }
       if (MODE == kModeHSeq && last_layer) {
 #pragma unroll

@@ -108,7 +108,7 @@ int32_t simt_forward(const Problem& p, const void* packed, const void* x, const 
                      const void* h0, const void* c0, void* out, void* h_n, void* c_n, void* ws,
                      cudaStream_t s);
 
-// tcgen05 cluster wavefront backend (H = 128, L <= 4, I <= 16, O <= 32, f16/bf16).
+// tcgen05 cluster wavefront backend (H = 128, L <= 8, I <= 128, O <= 32, f16/bf16).
 bool tc_supported(const Problem& p, std::string* why);
 size_t tc_packed_size(const Problem& p);
 size_t tc_workspace_size(const Problem& p);
@@ -126,10 +126,10 @@ int32_t tc_forward(const Problem& p, const void* packed, const void* x, const in
 int32_t tc_make_perm(const Problem& p, int N, int tiles, const int32_t* lengths, int32_t* perm, int32_t* tile_len,
                      int32_t* hist, int32_t* sorted, cudaStream_t s);
 
-// x[B][T][I] (I <= 16) -> xp[tiles][T][N rows x 16] 16-bit K-major core matrices
-// (8 rows x 16 bytes; K groups 128 bytes apart, row groups 256 bytes apart), rows in
-// tile order, zero for padding rows.
-int32_t tc_xpack(const Problem& p, int N, int tiles, const void* x, const int32_t* perm, uint8_t* xp,
+// x[B][T][I] (I <= kx) -> xp[tiles][T][N rows x kx] 16-bit K-major core matrices
+// (8 rows x 16 bytes; K groups 128 bytes apart, 8-row groups kx * 16 bytes apart), rows
+// in tile order, zero for padding rows and columns I..kx-1.  kx: multiple of 16.
+int32_t tc_xpack(const Problem& p, int N, int tiles, const void* x, const int32_t* perm, uint8_t* xp, int kx,
                  cudaStream_t s);
 
 // tcgen05 layer-sequential backend for H = 256 / 512 (plstm_tcl.cu): per layer a

@@ -59,7 +59,9 @@ namespace plstm {
 namespace tc {
 
 constexpr int kH = 128;  // hidden size served (64 units per CTA)
-constexpr int kXK = 16;  // padded layer-0 input width (one MMA K step)
+constexpr int kXK = 16;       // layer-0 input width step (one MMA K step); the single-slot kernel's width
+constexpr int kMaxXK = 128;   // widest padded layer-0 input: [W_ih | W_hh] fills the 256-wide A image
+constexpr int kMaxLayers = 8; // one cluster of 2L <= 16 CTAs (16 needs the non-portable cluster size)
 constexpr int kABytes = 128 * 1024;                 // A image slot per CTA: [tile 2][row 128][K 256] 16-bit
 constexpr int kAK = 256;                            // K extent of an A image row
 constexpr int kTmemACols = 256;                     // TMEM columns holding A: 2 tiles x 128
@@ -110,7 +112,7 @@ struct Smem {
 
 struct Params {
   const uint8_t* packed;
-  const uint8_t* xp;        // [tiles][T][N * 32 bytes]
+  const uint8_t* xp;        // [tiles][T][N * kx * 2 bytes]
   const int32_t* perm;      // [tiles * N], -1 = padding row
   const int32_t* lengths;   // [B] (varlen) or null
   const int32_t* tile_len;  // [tiles]
@@ -121,6 +123,7 @@ struct Params {
   void* c_n;
   int* status;
   int B, T, L, O, flags;
+  int kx;                   // padded layer-0 input width (multiple of 16, <= 128; 16 for the single-slot kernel)
   unsigned long long timeout_ns;
   int drop_rank, drop_step;  // fault injection: rank that skips one sibling hand-off (-1 = off)
   unsigned long long* trace;  // PLSTM_FLAG_TRACE: [2L][64][8] clock64 stamps of cluster 0, or null
@@ -826,7 +829,6 @@ __global__ void __launch_bounds__(Smem<N>::kThreads, 1) wavefront_kernel(const P
 template <int NH>
 struct Smem2 {
   static constexpr int kBKB = NH * 128;             // one 64-wide K block of a slot's B operand
-  static constexpr int kXBytes = NH * 32;           // a slot's layer-0 x tile (K = 16, no swizzle)
   static constexpr int kBufBytes = 4 * kBKB;        // [in0 | in1 | rec0 | rec1]
   static constexpr int kSlotBytes = 2 * kBufBytes;  // step-parity double buffer
   static constexpr int kB = 0;
@@ -1046,15 +1048,17 @@ __global__ void __launch_bounds__(Smem2<NH>::kThreads, 1) wavefront2_kernel(cons
     const int sl = warp - kComputeWarps;
     bool active = false;
     const int Tt = slot_len(sl, &active);
-    const uint32_t xbytes = S::kXBytes, bkb = S::kBKB;
+    // A slot's layer-0 x tile: NH rows x kx, no swizzle (fits the slot's two input K blocks).
+    const uint32_t xbytes = (uint32_t)(NH * p.kx * 2), bkb = S::kBKB;
     const uint32_t in_bytes = (l == 0) ? xbytes : 2 * bkb;
     constexpr uint32_t idesc_g = ptx::idesc_f16(128, NH, BF16);
     constexpr uint32_t idesc_l = ptx::idesc_f16(128, NL, BF16);
     const uint16_t up_mask = l > 0 ? (uint16_t)(3u << (2 * (l - 1))) : 0;
-    const uint32_t a_rec0 = l == 0 ? 8u : 64u;  // A columns of W_hh within a tile
+    const uint32_t a_rec0 = l == 0 ? (uint32_t)(p.kx / 2) : 64u;  // A columns of W_hh within a tile
     const uint64_t dAl = ptx::desc_k_sw128(sbase + S::kALin);
     const uint64_t dB0 = ptx::desc_k_sw128(bbuf(sl, 0));
-    const uint64_t dBx0 = ptx::desc_k_none(bbuf(sl, 0), 128, 256);
+    // x: K groups 128 bytes apart, 8-row groups kx * 16 bytes apart.
+    const uint64_t dBx0 = ptx::desc_k_none(bbuf(sl, 0), 128, (uint32_t)(p.kx * 16));
     constexpr uint64_t kBufStep = (uint64_t)(S::kBufBytes >> 4);
     const uint32_t lin_row_off = S::kSplitLinear ? (uint32_t)(s * NL) * 128u : 0u;
     const int steps = Tt + (does_linear ? 1 : 0);
@@ -1062,7 +1066,7 @@ __global__ void __launch_bounds__(Smem2<NH>::kThreads, 1) wavefront2_kernel(cons
     bool ok = true;
     const bool tracer = sl == p.trace_slot;
 
-    auto x_src = [&](int t) { return p.xp + (((size_t)tile * p.T + t) * N + (size_t)sl * NH) * 32; };
+    auto x_src = [&](int t) { return p.xp + (((size_t)tile * p.T + t) * N + (size_t)sl * NH) * (size_t)(p.kx * 2); };
     auto issue_in = [&](int t) {
       const int b = t & 1;
       if (ptx::elect_one()) {
@@ -1073,6 +1077,9 @@ __global__ void __launch_bounds__(Smem2<NH>::kThreads, 1) wavefront2_kernel(cons
           const uint32_t a = tmem + (uint32_t)(tau * 128);
           if (l == 0) {
             ptx::mma_f16_ts(dcol(sl, tau), a, dBx0 + kBufStep * b, idesc_g, 0u);
+            for (int kk = 1; kk < p.kx / 16; ++kk)  // inputs wider than 16
+              ptx::mma_f16_ts(dcol(sl, tau), a + (uint32_t)(8 * kk), dBx0 + kBufStep * b + (uint64_t)((kk * 256) >> 4),
+                              idesc_g, 1u);
           } else {
 #pragma unroll
             for (int kb = 0; kb < 2; ++kb)
@@ -1462,13 +1469,14 @@ __global__ void __launch_bounds__(Smem2<NH>::kThreads, 1) wavefront2_kernel(cons
 // ---- packing ----------------------------------------------------------------------
 // Writes the per-CTA A images, the Linear A image, the permuted bias and b_lin.
 struct PackArgs {
-  const void* w_ih[4];
-  const void* w_hh[4];
-  const void* b_ih[4];
-  const void* b_hh[4];
+  const void* w_ih[kMaxLayers];
+  const void* w_hh[kMaxLayers];
+  const void* b_ih[kMaxLayers];
+  const void* b_hh[kMaxLayers];
   const void* w_lin;
   const void* b_lin;
   int ih_layout, hh_layout, dtype, L, I, O;
+  int kx;  // padded layer-0 input width: A columns [0, kx) hold W_ih, [kx, kx + 128) W_hh
 };
 
 // Gate rows i, f, o are stored pre-scaled by 1/2 (exact in f16 / bf16 up to
@@ -1498,10 +1506,10 @@ __global__ void tc_pack_kernel(const PackArgs a, uint8_t* packed) {
       const int row = gate_row(s, tau, r);
       float v = 0.0f;
       if (l == 0) {
-        if (k < kXK) {
+        if (k < a.kx) {
           if (k < a.I) v = load_any(a.w_ih[0], a.dtype, weight_src_index(a.ih_layout, 4 * kH, a.I, row, k));
-        } else if (k < kXK + kH) {
-          v = load_any(a.w_hh[0], a.dtype, weight_src_index(a.hh_layout, 4 * kH, kH, row, k - kXK));
+        } else if (k < a.kx + kH) {
+          v = load_any(a.w_hh[0], a.dtype, weight_src_index(a.hh_layout, 4 * kH, kH, row, k - a.kx));
         }
       } else {
         v = k < kH ? load_any(a.w_ih[l], a.dtype, weight_src_index(a.ih_layout, 4 * kH, kH, row, k))
@@ -1573,31 +1581,36 @@ __global__ void tc_perm_varlen_kernel(const int32_t* sorted, const int32_t* leng
     if (i < tiles) tile_len[i] = min(max(lengths[sorted[i * N]], 0), T);
   }
 }
-// x[B][T][I] -> per-tile, per-step K-major no-swizzle 16-column tiles.
+// x[B][T][I] -> per-tile, per-step K-major no-swizzle tiles of kx columns: 8-row x
+// 8-column core matrices of 128 bytes, K groups 128 bytes apart, 8-row groups kx * 16
+// bytes apart.  One thread per (tile, step, row, K group).
 template <typename T16>
 __global__ void tc_xpack_kernel(const T16* __restrict__ x, const int32_t* __restrict__ perm,
-                                uint8_t* __restrict__ xp, int B, int T, int I, int N, int tiles) {
-  const int64_t total = (int64_t)tiles * T * N;
+                                uint8_t* __restrict__ xp, int B, int T, int I, int N, int tiles, int kx) {
+  const int kg_n = kx / 8;
+  const int64_t total = (int64_t)tiles * T * N * kg_n;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
-    const int n = (int)(i % N);
-    const int64_t tt = i / N;
+    const int kg = (int)(i % kg_n);
+    const int64_t r = i / kg_n;
+    const int n = (int)(r % N);
+    const int64_t tt = r / N;
     const int t = (int)(tt % T);
     const int tile = (int)(tt / T);
     const int b = perm[tile * N + n];
-    uint16_t v[16];
+    uint16_t v[8];
 #pragma unroll
-    for (int k = 0; k < 16; ++k) v[k] = 0;
+    for (int k = 0; k < 8; ++k) v[k] = 0;
     if (b >= 0) {
       const uint16_t* src = reinterpret_cast<const uint16_t*>(x) + ((size_t)b * T + t) * I;
-      for (int k = 0; k < I && k < 16; ++k) v[k] = src[k];
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        if (8 * kg + k < I) v[k] = src[8 * kg + k];
     }
-    uint8_t* dst = xp + (size_t)tt * N * 32 + (n >> 3) * 256 + (n & 7) * 16;
-    uint4 lo, hi;
-    lo.x = v[0] | (v[1] << 16); lo.y = v[2] | (v[3] << 16); lo.z = v[4] | (v[5] << 16); lo.w = v[6] | (v[7] << 16);
-    hi.x = v[8] | (v[9] << 16); hi.y = v[10] | (v[11] << 16); hi.z = v[12] | (v[13] << 16); hi.w = v[14] | (v[15] << 16);
-    *reinterpret_cast<uint4*>(dst) = lo;
-    *reinterpret_cast<uint4*>(dst + 128) = hi;
+    uint8_t* dst = xp + (size_t)tt * N * kx * 2 + (size_t)(n >> 3) * kx * 16 + kg * 128 + (n & 7) * 16;
+    uint4 q;
+    q.x = v[0] | (v[1] << 16); q.y = v[2] | (v[3] << 16); q.z = v[4] | (v[5] << 16); q.w = v[6] | (v[7] << 16);
+    *reinterpret_cast<uint4*>(dst) = q;
   }
 }
 
@@ -1685,10 +1698,19 @@ int plan_threads(const Plan& pl) {
   return threads_for(pl.N);
 }
 
-// Max clusters of 2L CTAs (one per SM) of a plan's kernel co-resident on `device`; cached.
+// Padded layer-0 input width of the H = 128 kernels.
+int tc_kx(const Problem& p) { return (p.I + kXK - 1) / kXK * kXK; }
+
+// Clusters of 2L > 8 CTAs need the non-portable cluster size (up to 16 on B200).
+cudaError_t allow_cluster(void* k, int L) {
+  return cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 2 * L > 8 ? 1 : 0);
+}
+
+// Max clusters of 2L CTAs (one per SM) of a plan's kernel co-resident on `device`
+// (0: the cluster does not fit); cached.
 int max_active_clusters(int device, int L, const Plan& pl) {
   static std::mutex mu;
-  static int cache[64][5][4][2];
+  static int cache[64][kMaxLayers + 1][4][2];
   static bool init = false;
   std::lock_guard<std::mutex> g(mu);
   if (!init) {
@@ -1699,11 +1721,12 @@ int max_active_clusters(int device, int L, const Plan& pl) {
     init = true;
   }
   const int ni = std::min(pl.N / 16, 4) - 1;
-  if (device < 0 || device >= 64 || L < 1 || L > 4) return 1;
+  if (device < 0 || device >= 64 || L < 1 || L > kMaxLayers) return 0;
   int& slot = cache[device][L][ni][pl.slots - 1];
   if (slot >= 0) return slot;
   void* k = plan_kernel(pl, false, false, kModeLast);
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, plan_smem(pl));
+  allow_cluster(k, L);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * L * 64, 1, 1);
   cfg.blockDim = dim3((unsigned)plan_threads(pl), 1, 1);
@@ -1716,9 +1739,9 @@ int max_active_clusters(int device, int L, const Plan& pl) {
   cfg.attrs = &attr;
   cfg.numAttrs = 1;
   int n = 0;
-  if (cudaOccupancyMaxActiveClusters(&n, k, &cfg) != cudaSuccess || n < 1) {
+  if (cudaOccupancyMaxActiveClusters(&n, k, &cfg) != cudaSuccess || n < 0) {
     cudaGetLastError();
-    n = 1;
+    n = 0;
   }
   slot = n;
   return n;
@@ -1728,21 +1751,22 @@ Plan make_plan(const Problem& p) {
   Plan pl;
   // Two-slot tiles of 32 or 64 rows by default (PLSTM_TC_KERNEL=1 selects the
   // single-slot kernel with 16 / 32 / 48-row tiles).  The smallest tile whose
-  // clusters all fit on the GPU at once (one wave); beyond that the widest tile.
+  // clusters all fit on the GPU at once (one wave); beyond that the widest tile (of
+  // those whose cluster fits at all: 16-CTA clusters for L > 4 need one 16-SM group).
   pl.slots = 2;
   if (const char* e = std::getenv("PLSTM_TC_KERNEL"))
-    if (std::atoi(e) == 1) pl.slots = 1;
+    if (std::atoi(e) == 1 && tc_kx(p) == kXK) pl.slots = 1;  // the single-slot kernel reads x 16 wide
   static constexpr int kTile2Ns[2] = {32, 64};
   const int* ns = pl.slots == 2 ? kTile2Ns : kTileNs;
   const int nn = pl.slots == 2 ? 2 : 3;
-  int N = ns[nn - 1];
+  int N = ns[0];
   for (int i = 0; i < nn; ++i) {
     Plan c = pl;
     c.N = ns[i];
-    if ((p.B + ns[i] - 1) / ns[i] <= max_active_clusters(p.device, p.L, c)) {
-      N = ns[i];
-      break;
-    }
+    const int m = max_active_clusters(p.device, p.L, c);
+    if (m < 1) continue;
+    N = ns[i];
+    if ((p.B + ns[i] - 1) / ns[i] <= m) break;
   }
   if (const char* e = std::getenv("PLSTM_TC_NTILE")) {
     const int v = std::atoi(e);
@@ -1762,7 +1786,7 @@ TcWs tc_ws(const Problem& p, const Plan& pl) {
   TcWs w;
   size_t off = kStatusBytes;
   w.xp = off;
-  off = align_up(off + (size_t)pl.tiles * std::max(p.T, 1) * pl.N * 32, 256);
+  off = align_up(off + (size_t)pl.tiles * std::max(p.T, 1) * pl.N * tc_kx(p) * 2, 256);
   w.perm = off;
   off = align_up(off + (size_t)pl.tiles * pl.N * 4, 256);
   w.tile_len = off;
@@ -1801,13 +1825,14 @@ int32_t tc_make_perm(const Problem& p, int N, int tiles, const int32_t* lengths,
   return PLSTM_OK;
 }
 
-int32_t tc_xpack(const Problem& p, int N, int tiles, const void* x, const int32_t* perm, uint8_t* xp,
+int32_t tc_xpack(const Problem& p, int N, int tiles, const void* x, const int32_t* perm, uint8_t* xp, int kx,
                  cudaStream_t s) {
   if (p.T <= 0) return PLSTM_OK;
   const int nthr = 256;
-  const int64_t total = (int64_t)tiles * p.T * N;
+  const int64_t total = (int64_t)tiles * p.T * N * (kx / 8);
   const int grid = (int)std::min<int64_t>((total + nthr - 1) / nthr, 148 * 32);
-  tc_xpack_kernel<uint16_t><<<grid, nthr, 0, s>>>(static_cast<const uint16_t*>(x), perm, xp, p.B, p.T, p.I, N, tiles);
+  tc_xpack_kernel<uint16_t><<<grid, nthr, 0, s>>>(static_cast<const uint16_t*>(x), perm, xp, p.B, p.T, p.I, N, tiles,
+                                                  kx);
   PLSTM_TRY_CUDA(cudaGetLastError());
   note_launches(1);
   return PLSTM_OK;
@@ -1821,8 +1846,8 @@ bool tc_supported(const Problem& p, std::string* why) {
   };
   if (p.dtype != PLSTM_F16 && p.dtype != PLSTM_BF16) return no("activation type must be f16 or bf16");
   if (p.H != kH) return no("hidden_size must be 128");
-  if (p.L < 1 || p.L > 4) return no("num_layers must be 1..4 (one 2L-CTA cluster)");
-  if (p.I > kXK) return no("input_size must be <= 16");
+  if (p.L < 1 || p.L > kMaxLayers) return no("num_layers must be 1..8 (one 2L-CTA cluster)");
+  if (p.I > kMaxXK) return no("input_size must be <= 128");
   if (p.has_linear() && p.O > 32) return no("output_size must be <= 32");
   if (p.T > 65535) return no("seq_len must be <= 65535");
   int dev = p.device, major = 0, minor = 0;
@@ -1832,6 +1857,10 @@ bool tc_supported(const Problem& p, std::string* why) {
     return no("no CUDA device");
   }
   if (major != 10 || minor != 0) return no("device is not sm_100 (B200)");
+  Plan c;
+  c.slots = 2;
+  c.N = 32;
+  if (max_active_clusters(dev, p.L, c) < 1) return no("the 2L-CTA cluster does not fit on this device");
   return true;
 }
 
@@ -1858,6 +1887,7 @@ int32_t tc_pack(const Problem& p, int ih_layout, int hh_layout, const void* cons
   a.L = p.L;
   a.I = p.I;
   a.O = p.has_linear() ? p.O : 0;
+  a.kx = tc_kx(p);
   tc_pack_kernel<<<148 * 4, 256, 0, s>>>(a, static_cast<uint8_t*>(packed));
   PLSTM_TRY_CUDA(cudaGetLastError());
   note_launches(1);
@@ -1879,7 +1909,7 @@ int32_t tc_forward(const Problem& p, const void* packed, const void* x, const in
     if (rc != PLSTM_OK) return rc;
   }
   {
-    const int32_t rc = tc_xpack(p, pl.N, pl.tiles, x, perm, wsb + w.xp, s);
+    const int32_t rc = tc_xpack(p, pl.N, pl.tiles, x, perm, wsb + w.xp, tc_kx(p), s);
     if (rc != PLSTM_OK) return rc;
   }
   Params kp = {};
@@ -1899,6 +1929,7 @@ int32_t tc_forward(const Problem& p, const void* packed, const void* x, const in
   kp.L = p.L;
   kp.O = p.O;
   kp.flags = p.flags;
+  kp.kx = tc_kx(p);
   kp.timeout_ns = (unsigned long long)p.timeout_ms * 1000000ull;
   kp.drop_rank = -1;
   kp.drop_step = -1;
@@ -1919,6 +1950,7 @@ int32_t tc_forward(const Problem& p, const void* packed, const void* x, const in
   void* k = plan_kernel(pl, bf16, lengths != nullptr, mode);
   const int smem = plan_smem(pl);
   PLSTM_TRY_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  PLSTM_TRY_CUDA(allow_cluster(k, p.L));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(pl.tiles * 2 * p.L), 1, 1);
   cfg.blockDim = dim3((unsigned)plan_threads(pl), 1, 1);

@@ -1189,7 +1189,7 @@ int32_t tcl_forward(const Problem& p, const void* packed, const void* x, const i
     if (rc != PLSTM_OK) return rc;
   }
   {
-    const int32_t rc = tc_xpack(p, kNT, tiles, x, perm, wsb + w.xp, s);
+    const int32_t rc = tc_xpack(p, kNT, tiles, x, perm, wsb + w.xp, kXK, s);
     if (rc != PLSTM_OK) return rc;
   }
   int sms = 148;

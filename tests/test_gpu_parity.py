@@ -276,3 +276,80 @@ def test_single_slot_wavefront_kernel(cuda_device, monkeypatch, mode, varlen):
     assert_close16(out, r_out, "out")
     assert_close16(h_n, r_h, "h_n")
     assert_close16(c_n, r_c, "c_n")
+
+
+# ---------------------------------------------------------------------------------------
+# Generic shapes on the H = 128 tensor-core kernel: layer-0 inputs wider than one
+# 16-column MMA step (I <= 128) and stacks of up to 8 layers (16-CTA clusters).
+@pytest.mark.parametrize("I", [16, 17, 40, 128])
+@pytest.mark.parametrize("mode", ["seq", "last"])
+def test_tc_wide_input(cuda_device, I, mode):
+    B, T, H, L, O = 70, 19, 128, 3, 24
+    m = make_model(I, H, L, O, seed=20 + I)
+    w = weights_of(m, L, torch.float16, cuda_device)
+    x = _rand_x(B, T, I, torch.float16, cuda_device, seed=I)
+    pw = core.PackedWeights(*w, out_mode=mode, backend="tc")
+    assert pw.backend == "tc"
+    out, h_n, c_n = pw.forward(x, check=True)
+    r_out, r_h, r_c = oracle_of(x, *w, out_mode=mode)
+    assert_close16(out, r_out, "out")
+    assert_close16(h_n, r_h, "h_n")
+    assert_close16(c_n, r_c, "c_n")
+
+
+@pytest.mark.parametrize("L", [5, 6, 8])
+def test_tc_more_layers(cuda_device, L):
+    B, T, I, H, O = 40, 17, 5, 128, 24
+    m = make_model(I, H, L, O, seed=30 + L)
+    w = weights_of(m, L, torch.float16, cuda_device)
+    x = _rand_x(B, T, I, torch.float16, cuda_device, seed=L)
+    pw = core.PackedWeights(*w, out_mode="seq", backend="tc")
+    assert pw.backend == "tc"
+    out, h_n, c_n = pw.forward(x, check=True)
+    r_out, r_h, r_c = oracle_of(x, *w, out_mode="seq")
+    assert_close16(out, r_out, "out")
+    assert_close16(h_n, r_h, "h_n")
+    assert_close16(c_n, r_c, "c_n")
+
+
+@pytest.mark.parametrize("mode", ["seq", "hseq"])
+def test_tc_wide_input_deep_varlen_state_bf16(cuda_device, mode):
+    B, T, I, H, L, O = 77, 23, 64, 128, 6, 12
+    m = make_model(I, H, L, O, seed=41)
+    w = weights_of(m, L, torch.bfloat16, cuda_device)
+    x = _rand_x(B, T, I, torch.bfloat16, cuda_device, seed=5)
+    lens = _rand_lengths(B, T, lo=0)
+    g = torch.Generator().manual_seed(8)
+    hx = ((0.5 * torch.randn(L, B, H, generator=g)).to(cuda_device, torch.bfloat16),
+          (0.5 * torch.randn(L, B, H, generator=g)).to(cuda_device, torch.bfloat16))
+    pw = core.PackedWeights(*w, out_mode=mode, backend="tc")
+    out, h_n, c_n = pw.forward(x, lengths=lens.to(cuda_device), hx=hx, check=True)
+    r_out, r_h, r_c = oracle_of(x, *w, lengths=lens, hx=hx, out_mode=mode)
+    assert_close16(out, r_out, "out")
+    assert_close16(h_n, r_h, "h_n")
+    assert_close16(c_n, r_c, "c_n")
+
+
+def test_tc_wide_input_ignores_single_slot_request(cuda_device, monkeypatch):
+    """PLSTM_TC_KERNEL=1 selects the single-slot kernel only for inputs of <= 16 columns."""
+    monkeypatch.setenv("PLSTM_TC_KERNEL", "1")
+    B, T, I, H, L, O = 30, 11, 33, 128, 2, 24
+    m = make_model(I, H, L, O, seed=43)
+    w = weights_of(m, L, torch.float16, cuda_device)
+    x = _rand_x(B, T, I, torch.float16, cuda_device, seed=6)
+    pw = core.PackedWeights(*w, out_mode="last", backend="tc")
+    out, h_n, c_n = pw.forward(x, check=True)
+    r_out, r_h, r_c = oracle_of(x, *w, out_mode="last")
+    assert_close16(out, r_out, "out")
+    assert_close16(h_n, r_h, "h_n")
+
+
+def test_tc_rejects_beyond_envelope(cuda_device):
+    """Shapes past the H = 128 kernel's envelope are refused by the forced TC backend
+    and served by the generic kernel under "auto"."""
+    for I, L in [(129, 2), (5, 9)]:
+        assert core.select_backend(input_size=I, hidden_size=128, num_layers=L, output_size=24,
+                                   dtype=torch.float16, device=cuda_device.index or 0) == "simt"
+        with pytest.raises(_lib.PlstmError):
+            core.select_backend(input_size=I, hidden_size=128, num_layers=L, output_size=24,
+                                dtype=torch.float16, backend="tc", device=cuda_device.index or 0)

@@ -1838,8 +1838,14 @@ int32_t tc_xpack(const Problem& p, int N, int tiles, const void* x, const int32_
   return PLSTM_OK;
 }
 
+// Shapes the H = 128 wavefront kernels take; every other tensor-core shape goes to the
+// layer-sequential backend (plstm_tcl.cu).
+bool wavefront_shape(const Problem& p) {
+  return p.H == kH && p.L >= 1 && p.L <= kMaxLayers && p.I <= kMaxXK && (!p.has_linear() || p.O <= 32);
+}
+
 bool tc_supported(const Problem& p, std::string* why) {
-  if (p.H == 256 || p.H == 512) return tcl_supported(p, why);
+  if (!wavefront_shape(p)) return tcl_supported(p, why);
   auto no = [&](const char* m) {
     if (why) *why = m;
     return false;
@@ -1864,14 +1870,16 @@ bool tc_supported(const Problem& p, std::string* why) {
   return true;
 }
 
-size_t tc_packed_size(const Problem& p) { return p.H == kH ? packed_total(p.L) : tcl_packed_size(p); }
+size_t tc_packed_size(const Problem& p) { return wavefront_shape(p) ? packed_total(p.L) : tcl_packed_size(p); }
 
-size_t tc_workspace_size(const Problem& p) { return p.H == kH ? tc_ws(p, make_plan(p)).total : tcl_workspace_size(p); }
+size_t tc_workspace_size(const Problem& p) {
+  return wavefront_shape(p) ? tc_ws(p, make_plan(p)).total : tcl_workspace_size(p);
+}
 
 int32_t tc_pack(const Problem& p, int ih_layout, int hh_layout, const void* const* w_ih,
                 const void* const* w_hh, const void* const* b_ih, const void* const* b_hh,
                 const void* w_lin, const void* b_lin, void* packed, cudaStream_t s) {
-  if (p.H != kH) return tcl_pack(p, ih_layout, hh_layout, w_ih, w_hh, b_ih, b_hh, w_lin, b_lin, packed, s);
+  if (!wavefront_shape(p)) return tcl_pack(p, ih_layout, hh_layout, w_ih, w_hh, b_ih, b_hh, w_lin, b_lin, packed, s);
   PackArgs a = {};
   for (int l = 0; l < p.L; ++l) {
     a.w_ih[l] = w_ih[l];
@@ -1897,7 +1905,7 @@ int32_t tc_pack(const Problem& p, int ih_layout, int hh_layout, const void* cons
 int32_t tc_forward(const Problem& p, const void* packed, const void* x, const int32_t* lengths,
                    const void* h0, const void* c0, void* out, void* h_n, void* c_n, void* ws,
                    cudaStream_t s) {
-  if (p.H != kH) return tcl_forward(p, packed, x, lengths, h0, c0, out, h_n, c_n, ws, s);
+  if (!wavefront_shape(p)) return tcl_forward(p, packed, x, lengths, h0, c0, out, h_n, c_n, ws, s);
   const Plan pl = make_plan(p);
   const TcWs w = tc_ws(p, pl);
   uint8_t* wsb = static_cast<uint8_t*>(ws);

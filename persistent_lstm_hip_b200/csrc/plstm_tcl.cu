@@ -1,4 +1,5 @@
-// plstm_tcl.cu — tcgen05 layer-sequential backend for H = 256 and H = 512.
+// plstm_tcl.cu — tcgen05 layer-sequential backend for hidden sizes other than the H = 128
+// wavefront kernel's (multiples of 64 up to 512; configs 3 and 4 are H = 256 / 512).
 //
 // What it replaces.  The reference runs these sizes through its adaptive path:
 // per layer an input-projection GEMM (adaptive_lstm_input_gemm_forward_workspace,
@@ -950,20 +951,41 @@ void* rec_ptr(bool bf16, bool varlen) {
   return varlen ? reinterpret_cast<void*>(&rec_kernel<H, NCW, false, true>)
                 : reinterpret_cast<void*>(&rec_kernel<H, NCW, false, false>);
 }
+// Hidden sizes of the recurrence: multiples of 64 up to 512 (C = H / 32 CTAs per cluster,
+// 2..16).  The 4-warp variant (PLSTM_TCL_WARPS=4) exists for 128 / 256 / 512 only.
 void* pick_rec(int H, bool bf16, bool varlen) {
-  if (rec_warps() == 8) {
-    if (H == 128) return rec_ptr<128, 8>(bf16, varlen);
-    return H == 256 ? rec_ptr<256, 8>(bf16, varlen) : rec_ptr<512, 8>(bf16, varlen);
+  if (rec_warps() == 4 && (H == 128 || H == 256 || H == 512))
+    return H == 128 ? rec_ptr<128, 4>(bf16, varlen) : H == 256 ? rec_ptr<256, 4>(bf16, varlen)
+                                                        : rec_ptr<512, 4>(bf16, varlen);
+  switch (H) {
+    case 64: return rec_ptr<64, 8>(bf16, varlen);
+    case 128: return rec_ptr<128, 8>(bf16, varlen);
+    case 192: return rec_ptr<192, 8>(bf16, varlen);
+    case 256: return rec_ptr<256, 8>(bf16, varlen);
+    case 320: return rec_ptr<320, 8>(bf16, varlen);
+    case 384: return rec_ptr<384, 8>(bf16, varlen);
+    case 448: return rec_ptr<448, 8>(bf16, varlen);
+    case 512: return rec_ptr<512, 8>(bf16, varlen);
+    default: return nullptr;
   }
-  if (H == 128) return rec_ptr<128, 4>(bf16, varlen);
-  return H == 256 ? rec_ptr<256, 4>(bf16, varlen) : rec_ptr<512, 4>(bf16, varlen);
 }
 int rec_smem(int H) {
-  return H == 128 ? RecSmem<128, 4>::kDyn : H == 256 ? RecSmem<256, 4>::kDyn : RecSmem<512, 4>::kDyn;
+  switch (H) {
+    case 64: return RecSmem<64, 8>::kDyn;
+    case 128: return RecSmem<128, 8>::kDyn;
+    case 192: return RecSmem<192, 8>::kDyn;
+    case 256: return RecSmem<256, 8>::kDyn;
+    case 320: return RecSmem<320, 8>::kDyn;
+    case 384: return RecSmem<384, 8>::kDyn;
+    case 448: return RecSmem<448, 8>::kDyn;
+    default: return RecSmem<512, 8>::kDyn;
+  }
 }
+bool rec_hidden_ok(int H) { return H >= 64 && H <= 512 && H % 64 == 0; }
 int rec_threads(int H) { return (rec_warps() + 1) * 32; }
 
 cudaError_t config_rec(void* k, int H) {
+  if (k == nullptr) return cudaErrorInvalidDeviceFunction;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, rec_smem(H));
   if (e == cudaSuccess && ctas_of(H) > 8) e = cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
   return e;
@@ -972,15 +994,16 @@ cudaError_t config_rec(void* k, int H) {
 // Clusters of C CTAs of the recurrence that fit on `device` at once (0 = none); cached.
 int rec_max_clusters(int device, int H) {
   static std::mutex mu;
-  static int cache[64][3];
+  static int cache[64][8];
   static bool init = false;
   std::lock_guard<std::mutex> g(mu);
   if (!init) {
-    for (auto& a : cache) a[0] = a[1] = a[2] = -1;
+    for (auto& a : cache)
+      for (auto& c : a) c = -1;
     init = true;
   }
-  if (device < 0 || device >= 64) return 0;
-  int& slot = cache[device][H == 512 ? 2 : H == 256 ? 1 : 0];
+  if (device < 0 || device >= 64 || !rec_hidden_ok(H)) return 0;
+  int& slot = cache[device][H / 64 - 1];
   if (slot >= 0) return slot;
   void* k = pick_rec(H, false, false);
   int n = 0;
@@ -1001,6 +1024,22 @@ int rec_max_clusters(int device, int H) {
   cudaGetLastError();
   slot = n;
   return n;
+}
+
+template <int KP, bool BF16>
+int32_t launch_proj(const GemmArgs& ga, int sms, cudaStream_t s);
+// Projection of a layer >= 1 (K = H).
+int32_t launch_proj_h(const GemmArgs& ga, bool bf16, int sms, cudaStream_t s) {
+#define PLSTM_TCL_PROJ(HH) \
+  case HH: return bf16 ? launch_proj<HH, true>(ga, sms, s) : launch_proj<HH, false>(ga, sms, s);
+  switch (ga.H) {
+    PLSTM_TCL_PROJ(64) PLSTM_TCL_PROJ(128) PLSTM_TCL_PROJ(192) PLSTM_TCL_PROJ(256)
+    PLSTM_TCL_PROJ(320) PLSTM_TCL_PROJ(384) PLSTM_TCL_PROJ(448) PLSTM_TCL_PROJ(512)
+    default: break;
+  }
+#undef PLSTM_TCL_PROJ
+  set_error("no projection kernel for this hidden size");
+  return PLSTM_ENOTSUP;
 }
 
 template <int KP, bool BF16>
@@ -1026,7 +1065,7 @@ bool tcl_supported(const Problem& p, std::string* why) {
     return false;
   };
   if (p.dtype != PLSTM_F16 && p.dtype != PLSTM_BF16) return no("activation type must be f16 or bf16");
-  if (p.H != 256 && p.H != 512) return no("hidden_size must be 256 or 512");
+  if (!rec_hidden_ok(p.H)) return no("hidden_size must be a multiple of 64 in [64, 512]");
   if (p.L < 1 || p.L > kMaxL) return no("num_layers must be 1..16");
   if (p.I > kXK) return no("input_size must be <= 16");
   if (p.T < 1 || p.T > 65535) return no("seq_len must be 1..65535");
@@ -1211,10 +1250,8 @@ int32_t tcl_forward(const Problem& p, const void* packed, const void* x, const i
     int32_t rc;
     if (l == 0)
       rc = bf16 ? launch_proj<kXK, true>(ga, sms, s) : launch_proj<kXK, false>(ga, sms, s);
-    else if (H == 256)
-      rc = bf16 ? launch_proj<256, true>(ga, sms, s) : launch_proj<256, false>(ga, sms, s);
     else
-      rc = bf16 ? launch_proj<512, true>(ga, sms, s) : launch_proj<512, false>(ga, sms, s);
+      rc = launch_proj_h(ga, bf16, sms, s);
     if (rc != PLSTM_OK) return rc;
 
     RecArgs ra = {};

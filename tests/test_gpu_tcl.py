@@ -1,4 +1,4 @@
-"""GPU parity of the tensor-core path for hidden sizes 256 and 512 (per layer a
+"""GPU parity of the layer-sequential tensor-core path (hidden sizes 64..512 in steps of 64; per layer a
 tcgen05 projection GEMM and a cluster recurrence with W_hh resident in tensor
 memory) against the f64 oracle, with the north star's 16-bit tolerances."""
 from __future__ import annotations
@@ -71,3 +71,63 @@ def test_tcl_is_the_auto_backend_and_matches_simt(cuda_device):
     a, _, _ = plstm.lstm_linear_forward(x, *w, out_mode="last", check=True)
     b, _, _ = plstm.lstm_linear_forward(x, *w, out_mode="last", backend="simt", check=True)
     assert (a.float() - b.float()).abs().max().item() <= 2e-2
+
+
+# Generic hidden sizes: every multiple of 64 up to 512 runs on the layer-sequential
+# tensor-core path (C = H / 32 CTAs per cluster, 2..16), as does H = 128 outside the
+# wavefront kernel's envelope (more than 8 layers, or a Linear head wider than 32).
+@pytest.mark.parametrize("H", [64, 192, 320, 384, 448])
+@pytest.mark.parametrize("mode", ["seq", "last", "hseq"])
+def test_tcl_generic_hidden_sizes(cuda_device, H, mode):
+    B, T, I, L, O = 70, 11, 5, 2, 24
+    dtype = torch.bfloat16 if H in (192, 448) else torch.float16
+    m = make_model(I, H, L, O, seed=H)
+    w = weights_of(m, L, dtype, cuda_device)
+    x = _x(B, T, I, dtype, cuda_device, seed=H + 1)
+    pw = core.PackedWeights(*w, out_mode=mode, backend="tc")
+    assert pw.backend == "tc"
+    out, h_n, c_n = pw.forward(x, check=True)
+    r_out, r_h, r_c = oracle_of(x, *w, out_mode=mode)
+    assert_close16(out, r_out, "out")
+    assert_close16(h_n, r_h, "h_n")
+    assert_close16(c_n, r_c, "c_n")
+
+
+@pytest.mark.parametrize("H", [64, 384])
+def test_tcl_generic_varlen_and_state(cuda_device, H):
+    B, T, I, L, O = 45, 14, 5, 3, 24
+    m = make_model(I, H, L, O, seed=H + 7)
+    w = weights_of(m, L, torch.float16, cuda_device)
+    x = _x(B, T, I, torch.float16, cuda_device)
+    g = torch.Generator().manual_seed(4)
+    lens = torch.randint(0, T + 1, (B,), generator=g, dtype=torch.int32)
+    lens[0] = T
+    hx = ((0.5 * torch.randn(L, B, H, generator=g)).to(cuda_device, torch.float16),
+          (0.5 * torch.randn(L, B, H, generator=g)).to(cuda_device, torch.float16))
+    pw = core.PackedWeights(*w, out_mode="seq", backend="tc")
+    out, h_n, c_n = pw.forward(x, lengths=lens.to(cuda_device), hx=hx, check=True)
+    r_out, r_h, r_c = oracle_of(x, *w, lengths=lens, hx=hx, out_mode="seq")
+    assert_close16(out, r_out, "out")
+    assert_close16(h_n, r_h, "h_n")
+    assert_close16(c_n, r_c, "c_n")
+
+
+@pytest.mark.parametrize("L, O", [(10, 24), (2, 40)])
+def test_tcl_h128_outside_wavefront_envelope(cuda_device, L, O):
+    B, T, I, H = 33, 9, 5, 128
+    m = make_model(I, H, L, O, seed=L + O)
+    w = weights_of(m, L, torch.float16, cuda_device)
+    x = _x(B, T, I, torch.float16, cuda_device, seed=L)
+    pw = core.PackedWeights(*w, out_mode="seq", backend="tc")
+    assert pw.backend == "tc"
+    out, h_n, c_n = pw.forward(x, check=True)
+    r_out, r_h, r_c = oracle_of(x, *w, out_mode="seq")
+    assert_close16(out, r_out, "out")
+    assert_close16(h_n, r_h, "h_n")
+    assert_close16(c_n, r_c, "c_n")
+
+
+def test_tcl_rejects_other_hidden_sizes(cuda_device):
+    for H in (96, 640, 1024):
+        assert core.select_backend(input_size=5, hidden_size=H, num_layers=2, output_size=24,
+                                   dtype=torch.float16, device=cuda_device.index or 0) == "simt"

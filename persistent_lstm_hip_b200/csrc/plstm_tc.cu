@@ -58,7 +58,7 @@
 namespace plstm {
 namespace tc {
 
-constexpr int kH = 128;  // hidden size served (64 units per CTA)
+constexpr int kH = 128;  // hidden size of the kernels (64 units per CTA); smaller H runs zero-padded
 constexpr int kXK = 16;       // layer-0 input width step (one MMA K step); the single-slot kernel's width
 constexpr int kMaxXK = 128;   // widest padded layer-0 input: [W_ih | W_hh] fills the 256-wide A image
 constexpr int kMaxLayers = 8; // one cluster of 2L <= 16 CTAs (16 needs the non-portable cluster size)
@@ -124,6 +124,8 @@ struct Params {
   int* status;
   int B, T, L, O, flags;
   int kx;                   // padded layer-0 input width (multiple of 16, <= 128; 16 for the single-slot kernel)
+  int hid;                  // the model's hidden size H <= 128: units >= H are zero padding (zero weights,
+                            // state and output), h0 / c0 / h_n / c_n / h-sequence rows are H wide
   unsigned long long timeout_ns;
   int drop_rank, drop_step;  // fault injection: rank that skips one sibling hand-off (-1 = off)
   unsigned long long* trace;  // PLSTM_FLAG_TRACE: [2L][64][8] clock64 stamps of cluster 0, or null
@@ -369,9 +371,9 @@ __global__ void __launch_bounds__(Smem<N>::kThreads, 1) wavefront_kernel(const P
       const int n = i / kH, k = i % kH;
       float v = 0.0f;
       const int b = perm_s[n];
-      if (p.h0 != nullptr && b >= 0) {
+      if (p.h0 != nullptr && b >= 0 && k < p.hid) {
         const uint16_t* h0 = static_cast<const uint16_t*>(p.h0);
-        v = from_bits<BF16>(h0[((size_t)l * p.B + b) * kH + k]);
+        v = from_bits<BF16>(h0[((size_t)l * p.B + b) * p.hid + k]);
       }
       *reinterpret_cast<uint16_t*>(b0 + (2 + (k >> 6)) * S::kBKB + sw128_off(n, k & 63)) = to_bits<BF16>(v);
     }
@@ -603,9 +605,9 @@ __global__ void __launch_bounds__(Smem<N>::kThreads, 1) wavefront_kernel(const P
           const int b = bidx[jc][e];
           uint16_t hv = 0;
           float cv = 0.0f;
-          if (b >= 0 && p.h0 != nullptr) {
-            hv = static_cast<const uint16_t*>(p.h0)[((size_t)l * p.B + b) * kH + u];
-            cv = from_bits<BF16>(static_cast<const uint16_t*>(p.c0)[((size_t)l * p.B + b) * kH + u]);
+          if (b >= 0 && p.h0 != nullptr && u < p.hid) {
+            hv = static_cast<const uint16_t*>(p.h0)[((size_t)l * p.B + b) * p.hid + u];
+            cv = from_bits<BF16>(static_cast<const uint16_t*>(p.c0)[((size_t)l * p.B + b) * p.hid + u]);
           }
           h_st[tau][jc][e] = hv;
           c_st[tau][jc][e] = cv;
@@ -729,8 +731,8 @@ __global__ void __launch_bounds__(Smem<N>::kThreads, 1) wavefront_kernel(const P
           for (int jc = 0; jc < CPW; ++jc)
 #pragma unroll
             for (int e = 0; e < 2; ++e)
-              if (bidx[jc][e] >= 0)
-                out16[((size_t)bidx[jc][e] * p.T + t) * kH + 64 * s + ul] =
+              if (bidx[jc][e] >= 0 && 64 * s + ul < p.hid)
+                out16[((size_t)bidx[jc][e] * p.T + t) * p.hid + 64 * s + ul] =
                     (!VARLEN || t < len_c[jc][e]) ? hw[tau][jc][e] : (uint16_t)0;
         }
       }
@@ -767,8 +769,8 @@ __global__ void __launch_bounds__(Smem<N>::kThreads, 1) wavefront_kernel(const P
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
             const int bb = bidx[jc][e];
-            if (bb < 0) continue;
-            for (int ts = Tt; ts < p.T; ++ts) out16[((size_t)bb * p.T + ts) * kH + u] = 0;
+            if (bb < 0 || u >= p.hid) continue;
+            for (int ts = Tt; ts < p.T; ++ts) out16[((size_t)bb * p.T + ts) * p.hid + u] = 0;
           }
       }
     }
@@ -781,8 +783,8 @@ __global__ void __launch_bounds__(Smem<N>::kThreads, 1) wavefront_kernel(const P
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
           const int bb = bidx[jc][e];
-          if (bb < 0) continue;
-          const size_t idx = ((size_t)l * p.B + bb) * kH + u;
+          if (bb < 0 || u >= p.hid) continue;
+          const size_t idx = ((size_t)l * p.B + bb) * p.hid + u;
           if (p.h_n != nullptr) static_cast<uint16_t*>(p.h_n)[idx] = h_st[tau][jc][e];
           if (p.c_n != nullptr) {
             if (p.flags & PLSTM_FLAG_CN_F32)
@@ -933,9 +935,9 @@ __global__ void __launch_bounds__(Smem2<NH>::kThreads, 1) wavefront2_kernel(cons
     const int sl = n / NH, nn = n % NH;
     float v = 0.0f;
     const int b = perm_s[n];
-    if (p.h0 != nullptr && b >= 0) {
+    if (p.h0 != nullptr && b >= 0 && k < p.hid) {
       const uint16_t* h0 = static_cast<const uint16_t*>(p.h0);
-      v = from_bits<BF16>(h0[((size_t)l * p.B + b) * kH + k]);
+      v = from_bits<BF16>(h0[((size_t)l * p.B + b) * p.hid + k]);
     }
     *reinterpret_cast<uint16_t*>(sm + S::kB + sl * S::kSlotBytes + (2 + (k >> 6)) * S::kBKB +
                                  sw128_off(nn, k & 63)) = to_bits<BF16>(v);
@@ -1262,9 +1264,9 @@ __global__ void __launch_bounds__(Smem2<NH>::kThreads, 1) wavefront2_kernel(cons
           const int b = bidx[jc][e];
           uint16_t hv = 0;
           float cv = 0.0f;
-          if (b >= 0 && p.h0 != nullptr) {
-            hv = static_cast<const uint16_t*>(p.h0)[((size_t)l * p.B + b) * kH + u];
-            cv = from_bits<BF16>(static_cast<const uint16_t*>(p.c0)[((size_t)l * p.B + b) * kH + u]);
+          if (b >= 0 && p.h0 != nullptr && u < p.hid) {
+            hv = static_cast<const uint16_t*>(p.h0)[((size_t)l * p.B + b) * p.hid + u];
+            cv = from_bits<BF16>(static_cast<const uint16_t*>(p.c0)[((size_t)l * p.B + b) * p.hid + u]);
           }
           h_st[tau][jc][e] = hv;
           c_st[tau][jc][e] = cv;
@@ -1399,8 +1401,8 @@ __global__ void __launch_bounds__(Smem2<NH>::kThreads, 1) wavefront2_kernel(cons
             for (int jc = 0; jc < CPW; ++jc)
 #pragma unroll
               for (int e = 0; e < 2; ++e)
-                if (bidx[jc][e] >= 0)
-                  out16[((size_t)bidx[jc][e] * p.T + t) * kH + 64 * s + ul] =
+                if (bidx[jc][e] >= 0 && 64 * s + ul < p.hid)
+                  out16[((size_t)bidx[jc][e] * p.T + t) * p.hid + 64 * s + ul] =
                       (!VARLEN || t < len_c[jc][e]) ? hw[tau][jc][e] : (uint16_t)0;
           }
         }
@@ -1422,8 +1424,8 @@ __global__ void __launch_bounds__(Smem2<NH>::kThreads, 1) wavefront2_kernel(cons
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
               const int bb = bidx[jc][e];
-              if (bb < 0) continue;
-              for (int ts = Tt; ts < p.T; ++ts) out16[((size_t)bb * p.T + ts) * kH + u] = 0;
+              if (bb < 0 || u >= p.hid) continue;
+              for (int ts = Tt; ts < p.T; ++ts) out16[((size_t)bb * p.T + ts) * p.hid + u] = 0;
             }
         }
       }
@@ -1436,8 +1438,8 @@ __global__ void __launch_bounds__(Smem2<NH>::kThreads, 1) wavefront2_kernel(cons
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
             const int bb = bidx[jc][e];
-            if (bb < 0) continue;
-            const size_t idx = ((size_t)l * p.B + bb) * kH + u;
+            if (bb < 0 || u >= p.hid) continue;
+            const size_t idx = ((size_t)l * p.B + bb) * p.hid + u;
             if (p.h_n != nullptr) static_cast<uint16_t*>(p.h_n)[idx] = h_st[tau][jc][e];
             if (p.c_n != nullptr) {
               if (p.flags & PLSTM_FLAG_CN_F32)
@@ -1476,16 +1478,20 @@ struct PackArgs {
   const void* w_lin;
   const void* b_lin;
   int ih_layout, hh_layout, dtype, L, I, O;
-  int kx;  // padded layer-0 input width: A columns [0, kx) hold W_ih, [kx, kx + 128) W_hh
+  int kx;   // padded layer-0 input width: A columns [0, kx) hold W_ih, [kx, kx + 128) W_hh
+  int hid;  // the model's hidden size (<= 128; the rest of the 128 units is zero padding)
 };
 
 // Gate rows i, f, o are stored pre-scaled by 1/2 (exact in f16 / bf16 up to
 // subnormals) so that the kernel's sigmoid(z) = (1 + tanh(z / 2)) / 2 needs no multiply.
 __device__ __forceinline__ float gate_scale(int r) { return ((r & 31) >> 3) == 2 ? 1.0f : 0.5f; }
 
-__device__ __forceinline__ int gate_row(int s, int tau, int r) {
+// PyTorch gate row (of a model with hidden size hid) of row r of tile tau of CTA half s,
+// or -1 for a padding unit (unit >= hid).
+__device__ __forceinline__ int gate_row(int s, int tau, int r, int hid) {
   const int q = r >> 5, rr = r & 31, gate = rr >> 3, j = rr & 7;
-  return gate * kH + 64 * s + 8 * (4 * tau + q) + j;
+  const int unit = 64 * s + 8 * (4 * tau + q) + j;
+  return unit < hid ? gate * hid + unit : -1;
 }
 
 __global__ void tc_pack_kernel(const PackArgs a, uint8_t* packed) {
@@ -1503,17 +1509,20 @@ __global__ void tc_pack_kernel(const PackArgs a, uint8_t* packed) {
       const int within = (int)(i % (kABytes / 2));
       const int tau = within / (128 * kAK), r = (within / kAK) % 128, k = within % kAK;
       const int l = rank >> 1, s = rank & 1;
-      const int row = gate_row(s, tau, r);
+      const int row = gate_row(s, tau, r, a.hid);
+      const int G = 4 * a.hid;
       float v = 0.0f;
-      if (l == 0) {
+      if (row < 0) {
+      } else if (l == 0) {
         if (k < a.kx) {
-          if (k < a.I) v = load_any(a.w_ih[0], a.dtype, weight_src_index(a.ih_layout, 4 * kH, a.I, row, k));
-        } else if (k < a.kx + kH) {
-          v = load_any(a.w_hh[0], a.dtype, weight_src_index(a.hh_layout, 4 * kH, kH, row, k - a.kx));
+          if (k < a.I) v = load_any(a.w_ih[0], a.dtype, weight_src_index(a.ih_layout, G, a.I, row, k));
+        } else if (k - a.kx < a.hid) {
+          v = load_any(a.w_hh[0], a.dtype, weight_src_index(a.hh_layout, G, a.hid, row, k - a.kx));
         }
-      } else {
-        v = k < kH ? load_any(a.w_ih[l], a.dtype, weight_src_index(a.ih_layout, 4 * kH, kH, row, k))
-                   : load_any(a.w_hh[l], a.dtype, weight_src_index(a.hh_layout, 4 * kH, kH, row, k - kH));
+      } else if (k < kH) {
+        if (k < a.hid) v = load_any(a.w_ih[l], a.dtype, weight_src_index(a.ih_layout, G, a.hid, row, k));
+      } else if (k - kH < a.hid) {
+        v = load_any(a.w_hh[l], a.dtype, weight_src_index(a.hh_layout, G, a.hid, row, k - kH));
       }
       v *= gate_scale(r);
       img[i] = a.dtype == PLSTM_BF16 ? to_bits<true>(v) : to_bits<false>(v);
@@ -1523,16 +1532,17 @@ __global__ void tc_pack_kernel(const PackArgs a, uint8_t* packed) {
       const int r = within / 128, chunk = (within % 128) >> 4, e = (within & 15) >> 1;
       const int kk = ((chunk ^ (r & 7)) << 3) + e;
       float v = 0.0f;
-      if (r < a.O && a.w_lin != nullptr) v = load_any(a.w_lin, a.dtype, (int64_t)r * kH + kb * 64 + kk);
+      if (r < a.O && a.w_lin != nullptr && kb * 64 + kk < a.hid)
+        v = load_any(a.w_lin, a.dtype, (int64_t)r * a.hid + kb * 64 + kk);
       img[i] = a.dtype == PLSTM_BF16 ? to_bits<true>(v) : to_bits<false>(v);
     } else if (i < n_a + n_lin + n_bias) {
       const int64_t j = i - n_a - n_lin;
       const int rank = (int)(j / 256), rr = (int)(j % 256);
       const int l = rank >> 1, s = rank & 1;
-      const int row = gate_row(s, rr >> 7, rr & 127);
+      const int row = gate_row(s, rr >> 7, rr & 127, a.hid);
       float v = 0.0f;
-      if (a.b_ih[l] != nullptr) v += load_any(a.b_ih[l], a.dtype, row);
-      if (a.b_hh[l] != nullptr) v += load_any(a.b_hh[l], a.dtype, row);
+      if (row >= 0 && a.b_ih[l] != nullptr) v += load_any(a.b_ih[l], a.dtype, row);
+      if (row >= 0 && a.b_hh[l] != nullptr) v += load_any(a.b_hh[l], a.dtype, row);
       reinterpret_cast<float*>(packed + packed_bias_off(a.L))[j] = v * gate_scale(rr & 127);
     } else {
       const int o = (int)(i - n_a - n_lin - n_bias);
@@ -1841,7 +1851,7 @@ int32_t tc_xpack(const Problem& p, int N, int tiles, const void* x, const int32_
 // Shapes the H = 128 wavefront kernels take; every other tensor-core shape goes to the
 // layer-sequential backend (plstm_tcl.cu).
 bool wavefront_shape(const Problem& p) {
-  return p.H == kH && p.L >= 1 && p.L <= kMaxLayers && p.I <= kMaxXK && (!p.has_linear() || p.O <= 32);
+  return p.H >= 1 && p.H <= kH && p.L >= 1 && p.L <= kMaxLayers && p.I <= kMaxXK && (!p.has_linear() || p.O <= 32);
 }
 
 bool tc_supported(const Problem& p, std::string* why) {
@@ -1851,7 +1861,7 @@ bool tc_supported(const Problem& p, std::string* why) {
     return false;
   };
   if (p.dtype != PLSTM_F16 && p.dtype != PLSTM_BF16) return no("activation type must be f16 or bf16");
-  if (p.H != kH) return no("hidden_size must be 128");
+  if (p.H < 1 || p.H > kH) return no("hidden_size must be <= 128");
   if (p.L < 1 || p.L > kMaxLayers) return no("num_layers must be 1..8 (one 2L-CTA cluster)");
   if (p.I > kMaxXK) return no("input_size must be <= 128");
   if (p.has_linear() && p.O > 32) return no("output_size must be <= 32");
@@ -1896,6 +1906,7 @@ int32_t tc_pack(const Problem& p, int ih_layout, int hh_layout, const void* cons
   a.I = p.I;
   a.O = p.has_linear() ? p.O : 0;
   a.kx = tc_kx(p);
+  a.hid = p.H;
   tc_pack_kernel<<<148 * 4, 256, 0, s>>>(a, static_cast<uint8_t*>(packed));
   PLSTM_TRY_CUDA(cudaGetLastError());
   note_launches(1);
@@ -1938,6 +1949,7 @@ int32_t tc_forward(const Problem& p, const void* packed, const void* x, const in
   kp.O = p.O;
   kp.flags = p.flags;
   kp.kx = tc_kx(p);
+  kp.hid = p.H;
   kp.timeout_ns = (unsigned long long)p.timeout_ms * 1000000ull;
   kp.drop_rank = -1;
   kp.drop_step = -1;

@@ -151,10 +151,17 @@ struct PackArgs {
   const void* w_lin;
   const void* b_lin;
   int ih_layout, hh_layout, dtype, L, I, H, O;
+  int hid;  // the model's hidden size (<= H; units >= hid are zero padding)
 };
 
 __global__ void pack_kernel(const PackArgs a, uint8_t* packed) {
-  const int H = a.H, L = a.L, G = 4 * H;
+  const int H = a.H, L = a.L, G = 4 * H, GR = 4 * a.hid;
+  // nn.LSTM row of permuted row rho of CTA r in a model of hidden size hid; -1 = padding unit.
+  auto real_row = [&](int r, int rho) -> int {
+    const int q = rho >> 5, gate = (rho >> 3) & 3, j = rho & 7;
+    const int unit = kU * r + 8 * q + j;
+    return unit < a.hid ? gate * a.hid + unit : -1;
+  };
   const int64_t n_hh = (int64_t)L * G * H;
   const int64_t n_ih = (int64_t)G * kXK + (int64_t)(L - 1) * G * H;
   const int64_t n_b = (int64_t)L * G;
@@ -173,7 +180,9 @@ __global__ void pack_kernel(const PackArgs a, uint8_t* packed) {
       const int64_t rem = i % ((int64_t)G * H);
       const int rp = (int)(rem / H), k = (int)(rem % H);
       const int r = rp / kRows, rho = rp % kRows;
-      const float v = load_any(a.w_hh[l], a.dtype, weight_src_index(a.hh_layout, G, H, src_row(H, r, rho), k));
+      const int sr = real_row(r, rho);
+      float v = 0.0f;
+      if (sr >= 0 && k < a.hid) v = load_any(a.w_hh[l], a.dtype, weight_src_index(a.hh_layout, GR, a.hid, sr, k));
       put16(off_whh(l, H), rem, v * row_scale(rho));
     } else if (i < n_hh + n_ih) {
       int64_t j = i - n_hh;
@@ -186,24 +195,26 @@ __global__ void pack_kernel(const PackArgs a, uint8_t* packed) {
       }
       const int rp = (int)(j / kin), k = (int)(j % kin);
       const int r = rp / kRows, rho = rp % kRows;
-      const int kreal = l == 0 ? a.I : H;
+      const int kreal = l == 0 ? a.I : a.hid;
+      const int sr = real_row(r, rho);
       float v = 0.0f;
-      if (k < kreal) v = load_any(a.w_ih[l], a.dtype, weight_src_index(a.ih_layout, G, kreal, src_row(H, r, rho), k));
+      if (sr >= 0 && k < kreal) v = load_any(a.w_ih[l], a.dtype, weight_src_index(a.ih_layout, GR, kreal, sr, k));
       put16(off_wih(l, H, L), j, v * row_scale(rho));
     } else if (i < n_hh + n_ih + n_b) {
       const int64_t j = i - n_hh - n_ih;
       const int l = (int)(j / G), rp = (int)(j % G);
       const int r = rp / kRows, rho = rp % kRows;
-      const int sr = src_row(H, r, rho);
+      const int sr = real_row(r, rho);
       float v = 0.0f;
-      if (a.b_ih[l] != nullptr) v += load_any(a.b_ih[l], a.dtype, sr);
-      if (a.b_hh[l] != nullptr) v += load_any(a.b_hh[l], a.dtype, sr);
+      if (sr >= 0 && a.b_ih[l] != nullptr) v += load_any(a.b_ih[l], a.dtype, sr);
+      if (sr >= 0 && a.b_hh[l] != nullptr) v += load_any(a.b_hh[l], a.dtype, sr);
       reinterpret_cast<float*>(packed + off_bias(H, L))[j] = v * row_scale(rho);
     } else if (i < n_hh + n_ih + n_b + n_wl) {
       const int64_t j = i - n_hh - n_ih - n_b;
       const int o = (int)(j / H), k = (int)(j % H);
       float v = 0.0f;
-      if (a.w_lin != nullptr) v = load_any(a.w_lin, a.dtype, weight_src_index(PLSTM_W_NATIVE, a.O, H, o, k));
+      if (a.w_lin != nullptr && k < a.hid)
+        v = load_any(a.w_lin, a.dtype, weight_src_index(PLSTM_W_NATIVE, a.O, a.hid, o, k));
       put16(off_wlin(H, L), j, v);
     } else {
       const int o = (int)(i - n_hh - n_ih - n_b - n_wl);
@@ -444,6 +455,7 @@ struct RecArgs {
   uint16_t* hlast;         // [B][H] (last layer, Linear input) or null
   int* status;
   int B, T, layer, flags;
+  int hid;                 // the model's hidden size (<= H): h0 / c0 / h_n / c_n rows are hid wide
   unsigned long long timeout_ns;
   unsigned long long* trace;  // PLSTM_FLAG_TRACE: [C][64][8] clock64 stamps of cluster 0, or null
   int trace_t0;
@@ -513,7 +525,7 @@ __global__ void __launch_bounds__(RecSmem<H, NCW>::kThreads, 1) rec_kernel(const
     const int n = i / H, k = i % H;
     uint16_t v = 0;
     const int b = perm_s[n];
-    if (a.h0 != nullptr && b >= 0) v = static_cast<const uint16_t*>(a.h0)[((size_t)l * a.B + b) * H + k];
+    if (a.h0 != nullptr && b >= 0 && k < a.hid) v = static_cast<const uint16_t*>(a.h0)[((size_t)l * a.B + b) * a.hid + k];
     *reinterpret_cast<uint16_t*>(sm + S::kB + hoff(k, n)) = v;
   }
   ptx::fence_proxy_async_smem();
@@ -649,9 +661,9 @@ __global__ void __launch_bounds__(RecSmem<H, NCW>::kThreads, 1) rec_kernel(const
         len_c[jc][e] = lens_s[n];
         uint16_t hv = 0;
         float cv = 0.0f;
-        if (bb >= 0 && a.h0 != nullptr) {
-          hv = static_cast<const uint16_t*>(a.h0)[((size_t)l * a.B + bb) * H + u];
-          cv = from_bits<BF16>(static_cast<const uint16_t*>(a.c0)[((size_t)l * a.B + bb) * H + u]);
+        if (bb >= 0 && a.h0 != nullptr && u < a.hid) {
+          hv = static_cast<const uint16_t*>(a.h0)[((size_t)l * a.B + bb) * a.hid + u];
+          cv = from_bits<BF16>(static_cast<const uint16_t*>(a.c0)[((size_t)l * a.B + bb) * a.hid + u]);
         }
         h_st[jc][e] = hv;
         c_st[jc][e] = cv;
@@ -748,7 +760,9 @@ __global__ void __launch_bounds__(RecSmem<H, NCW>::kThreads, 1) rec_kernel(const
       for (int e = 0; e < 2; ++e) {
         const int bb = bidx[jc][e];
         if (bb < 0) continue;
-        const size_t idx = ((size_t)l * a.B + bb) * H + u;
+        if (a.hlast != nullptr) a.hlast[(size_t)bb * H + u] = h_st[jc][e];
+        if (u >= a.hid) continue;
+        const size_t idx = ((size_t)l * a.B + bb) * a.hid + u;
         if (a.h_n != nullptr) static_cast<uint16_t*>(a.h_n)[idx] = h_st[jc][e];
         if (a.c_n != nullptr) {
           if (a.flags & PLSTM_FLAG_CN_F32)
@@ -756,7 +770,6 @@ __global__ void __launch_bounds__(RecSmem<H, NCW>::kThreads, 1) rec_kernel(const
           else
             static_cast<uint16_t*>(a.c_n)[idx] = to_bits<BF16>(c_st[jc][e]);
         }
-        if (a.hlast != nullptr) a.hlast[(size_t)bb * H + u] = h_st[jc][e];
       }
   }
 
@@ -798,7 +811,7 @@ template <bool BF16, bool LINEAR>
 __global__ void seq_out_kernel(const uint8_t* __restrict__ hseq, const int32_t* __restrict__ perm,
                                const int32_t* __restrict__ lengths, const uint16_t* __restrict__ wlin,
                                const float* __restrict__ blin, uint16_t* __restrict__ out, int B, int T, int H,
-                               int O, int tiles, int out_seq_major) {
+                               int O, int tiles, int out_seq_major, int hid) {
   extern __shared__ uint8_t smem_o[];
   float* hs = reinterpret_cast<float*>(smem_o);  // [kNT][H + 1]
   const int C = ctas_of(H);
@@ -810,7 +823,7 @@ __global__ void seq_out_kernel(const uint8_t* __restrict__ hseq, const int32_t* 
         base + (size_t)(k >> 3) * kKG + (n >> 3) * 128 + (n & 7) * 16 + (k & 7) * 2));
   }
   __syncthreads();
-  const int W = LINEAR ? O : H;
+  const int W = LINEAR ? O : hid;  // h-sequence output rows are the model's hid units
   for (int i = threadIdx.x; i < kNT * W; i += blockDim.x) {
     const int n = i / W, w = i % W;
     const int b = perm[tile * kNT + n];
@@ -1059,13 +1072,21 @@ int32_t launch_proj(const GemmArgs& ga, int sms, cudaStream_t s) {
 
 using namespace tcl;
 
+// The padded hidden size the kernels run (a multiple of 64); units >= p.H are zero.
+int tcl_hp(int H) { return (H + 63) / 64 * 64; }
+Problem padded(const Problem& p) {
+  Problem q = p;
+  q.H = tcl_hp(p.H);
+  return q;
+}
+
 bool tcl_supported(const Problem& p, std::string* why) {
   auto no = [&](const char* m) {
     if (why) *why = m;
     return false;
   };
   if (p.dtype != PLSTM_F16 && p.dtype != PLSTM_BF16) return no("activation type must be f16 or bf16");
-  if (!rec_hidden_ok(p.H)) return no("hidden_size must be a multiple of 64 in [64, 512]");
+  if (p.H < 1 || !rec_hidden_ok(tcl_hp(p.H))) return no("hidden_size must be <= 512");
   if (p.L < 1 || p.L > kMaxL) return no("num_layers must be 1..16");
   if (p.I > kXK) return no("input_size must be <= 16");
   if (p.T < 1 || p.T > 65535) return no("seq_len must be 1..65535");
@@ -1076,13 +1097,13 @@ bool tcl_supported(const Problem& p, std::string* why) {
     return no("no CUDA device");
   }
   if (major != 10 || minor != 0) return no("device is not sm_100 (B200)");
-  if (rec_max_clusters(dev, p.H) < 1) return no("the recurrence's CTA cluster does not fit on this device");
+  if (rec_max_clusters(dev, tcl_hp(p.H)) < 1) return no("the recurrence's CTA cluster does not fit on this device");
   return true;
 }
 
-size_t tcl_packed_size(const Problem& p) { return packed_total(p.H, p.L, p.has_linear() ? p.O : 0); }
+size_t tcl_packed_size(const Problem& p) { return packed_total(tcl_hp(p.H), p.L, p.has_linear() ? p.O : 0); }
 
-size_t tcl_workspace_size(const Problem& p) { return ws_layout(p).total; }
+size_t tcl_workspace_size(const Problem& p) { return ws_layout(padded(p)).total; }
 
 int32_t tcl_pack(const Problem& p, int ih_layout, int hh_layout, const void* const* w_ih, const void* const* w_hh,
                  const void* const* b_ih, const void* const* b_hh, const void* w_lin, const void* b_lin,
@@ -1101,7 +1122,8 @@ int32_t tcl_pack(const Problem& p, int ih_layout, int hh_layout, const void* con
   a.dtype = p.dtype;
   a.L = p.L;
   a.I = p.I;
-  a.H = p.H;
+  a.H = tcl_hp(p.H);
+  a.hid = p.H;
   a.O = p.has_linear() ? p.O : 0;
   pack_kernel<<<148 * 4, 256, 0, s>>>(a, static_cast<uint8_t*>(packed));
   PLSTM_TRY_CUDA(cudaGetLastError());
@@ -1175,6 +1197,7 @@ int32_t tcl_hidden_update(const HuProblem& p, const void* gate_proj, const void*
   ra.B = p.B;
   ra.T = p.T;
   ra.layer = 0;
+  ra.hid = H;
   ra.flags = PLSTM_FLAG_CN_F32;
   ra.timeout_ns = 2000000000ull;
   ra.trace = nullptr;
@@ -1201,7 +1224,7 @@ int32_t tcl_hidden_update(const HuProblem& p, const void* gate_proj, const void*
     auto k = bf16 ? seq_out_kernel<true, false> : seq_out_kernel<false, false>;
     PLSTM_TRY_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     k<<<p.T * tiles, 256, smem, s>>>(wsb + w.hseq, perm, nullptr, nullptr, nullptr, static_cast<uint16_t*>(out), p.B,
-                                     p.T, H, 0, tiles, p.seq_major() ? 1 : 0);
+                                     p.T, H, 0, tiles, p.seq_major() ? 1 : 0, H);
     PLSTM_TRY_CUDA(cudaGetLastError());
     note_launches(1);
   } else {
@@ -1212,9 +1235,9 @@ int32_t tcl_hidden_update(const HuProblem& p, const void* gate_proj, const void*
 
 int32_t tcl_forward(const Problem& p, const void* packed, const void* x, const int32_t* lengths, const void* h0,
                     const void* c0, void* out, void* h_n, void* c_n, void* ws, cudaStream_t s) {
-  const int H = p.H, L = p.L, C = ctas_of(H);
+  const int H = tcl_hp(p.H), L = p.L, C = ctas_of(H);
   const int tiles = (p.B + kNT - 1) / kNT;
-  const Ws w = ws_layout(p);
+  const Ws w = ws_layout(padded(p));
   uint8_t* wsb = static_cast<uint8_t*>(ws);
   const uint8_t* pk = static_cast<const uint8_t*>(packed);
   int32_t* perm = reinterpret_cast<int32_t*>(wsb + w.perm);
@@ -1270,6 +1293,7 @@ int32_t tcl_forward(const Problem& p, const void* packed, const void* x, const i
     ra.B = p.B;
     ra.T = p.T;
     ra.layer = l;
+    ra.hid = p.H;
     ra.flags = p.flags;
     ra.timeout_ns = (unsigned long long)p.timeout_ms * 1000000ull;
     ra.trace = nullptr;
@@ -1313,11 +1337,11 @@ int32_t tcl_forward(const Problem& p, const void* packed, const void* x, const i
     if (p.has_linear()) {
       auto k = bf16 ? seq_out_kernel<true, true> : seq_out_kernel<false, true>;
       PLSTM_TRY_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-      k<<<grid, 256, smem, s>>>(wsb + w.hseq, perm, lengths, wlin, blin, o16, p.B, p.T, H, O, tiles, 0);
+      k<<<grid, 256, smem, s>>>(wsb + w.hseq, perm, lengths, wlin, blin, o16, p.B, p.T, H, O, tiles, 0, p.H);
     } else {
       auto k = bf16 ? seq_out_kernel<true, false> : seq_out_kernel<false, false>;
       PLSTM_TRY_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-      k<<<grid, 256, smem, s>>>(wsb + w.hseq, perm, lengths, wlin, blin, o16, p.B, p.T, H, 0, tiles, 0);
+      k<<<grid, 256, smem, s>>>(wsb + w.hseq, perm, lengths, wlin, blin, o16, p.B, p.T, H, 0, tiles, 0, p.H);
     }
   }
   PLSTM_TRY_CUDA(cudaGetLastError());

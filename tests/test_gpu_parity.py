@@ -345,11 +345,50 @@ def test_tc_wide_input_ignores_single_slot_request(cuda_device, monkeypatch):
 
 
 def test_tc_rejects_beyond_envelope(cuda_device):
-    """Shapes past the H = 128 kernel's envelope are refused by the forced TC backend
-    and served by the generic kernel under "auto"."""
-    for I, L in [(129, 2), (5, 9)]:
+    """Shapes past both tensor-core envelopes (H = 128 wavefront: I <= 128, L <= 8; layer
+    path: I <= 16, L <= 16) are refused by the forced TC backend and served by the generic
+    kernel under "auto"; H = 128 with 9 layers and I <= 16 runs on the layer path."""
+    assert core.select_backend(input_size=5, hidden_size=128, num_layers=9, output_size=24,
+                               dtype=torch.float16, device=cuda_device.index or 0) == "tc"
+    for I, L in [(129, 2), (40, 9)]:
         assert core.select_backend(input_size=I, hidden_size=128, num_layers=L, output_size=24,
                                    dtype=torch.float16, device=cuda_device.index or 0) == "simt"
         with pytest.raises(_lib.PlstmError):
             core.select_backend(input_size=I, hidden_size=128, num_layers=L, output_size=24,
                                 dtype=torch.float16, backend="tc", device=cuda_device.index or 0)
+
+
+# Hidden sizes below 128 run on the H = 128 wavefront kernel with the extra units zero
+# padded (zero weights, bias and state: they stay zero and feed nothing).
+@pytest.mark.parametrize("H", [1, 40, 64, 100])
+@pytest.mark.parametrize("mode", ["seq", "last", "hseq"])
+def test_tc_small_hidden_sizes_padded(cuda_device, H, mode):
+    B, T, I, L, O = 37, 13, 5, 3, 24
+    m = make_model(I, H, L, O, seed=50 + H)
+    w = weights_of(m, L, torch.float16, cuda_device)
+    x = _rand_x(B, T, I, torch.float16, cuda_device, seed=H)
+    pw = core.PackedWeights(*w, out_mode=mode)
+    assert pw.backend == "tc"
+    out, h_n, c_n = pw.forward(x, check=True)
+    r_out, r_h, r_c = oracle_of(x, *w, out_mode=mode)
+    assert_close16(out, r_out, "out")
+    assert_close16(h_n, r_h, "h_n")
+    assert_close16(c_n, r_c, "c_n")
+
+
+def test_tc_small_hidden_varlen_state_bf16(cuda_device):
+    B, T, I, H, L, O = 51, 19, 20, 72, 4, 10
+    m = make_model(I, H, L, O, seed=61)
+    w = weights_of(m, L, torch.bfloat16, cuda_device)
+    x = _rand_x(B, T, I, torch.bfloat16, cuda_device, seed=9)
+    lens = _rand_lengths(B, T, lo=0)
+    g = torch.Generator().manual_seed(10)
+    hx = ((0.5 * torch.randn(L, B, H, generator=g)).to(cuda_device, torch.bfloat16),
+          (0.5 * torch.randn(L, B, H, generator=g)).to(cuda_device, torch.bfloat16))
+    for mode in ("seq", "hseq"):
+        pw = core.PackedWeights(*w, out_mode=mode, backend="tc")
+        out, h_n, c_n = pw.forward(x, lengths=lens.to(cuda_device), hx=hx, check=True, c_n_f32=True)
+        r_out, r_h, r_c = oracle_of(x, *w, lengths=lens, hx=hx, out_mode=mode)
+        assert_close16(out, r_out, "out")
+        assert_close16(h_n, r_h, "h_n")
+        assert_close16(c_n, r_c, "c_n")

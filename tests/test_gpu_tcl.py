@@ -1,4 +1,4 @@
-"""GPU parity of the layer-sequential tensor-core path (hidden sizes 64..512 in steps of 64; per layer a
+"""GPU parity of the layer-sequential tensor-core path (any hidden size up to 512; per layer a
 tcgen05 projection GEMM and a cluster recurrence with W_hh resident in tensor
 memory) against the f64 oracle, with the north star's 16-bit tolerances."""
 from __future__ import annotations
@@ -128,6 +128,28 @@ def test_tcl_h128_outside_wavefront_envelope(cuda_device, L, O):
 
 
 def test_tcl_rejects_other_hidden_sizes(cuda_device):
-    for H in (96, 640, 1024):
+    for H in (513, 640, 1024):
         assert core.select_backend(input_size=5, hidden_size=H, num_layers=2, output_size=24,
                                    dtype=torch.float16, device=cuda_device.index or 0) == "simt"
+
+
+# Any hidden size up to 512 runs on the layer path, zero-padded to the next multiple of 64.
+@pytest.mark.parametrize("H, L", [(150, 2), (200, 3), (300, 2), (500, 1), (100, 10)])
+def test_tcl_padded_hidden_sizes(cuda_device, H, L):
+    B, T, I, O = 41, 10, 5, 24
+    m = make_model(I, H, L, O, seed=H + L)
+    w = weights_of(m, L, torch.float16, cuda_device)
+    x = _x(B, T, I, torch.float16, cuda_device, seed=H)
+    g = torch.Generator().manual_seed(H)
+    lens = torch.randint(0, T + 1, (B,), generator=g, dtype=torch.int32)
+    lens[0] = T
+    hx = ((0.5 * torch.randn(L, B, H, generator=g)).to(cuda_device, torch.float16),
+          (0.5 * torch.randn(L, B, H, generator=g)).to(cuda_device, torch.float16))
+    for mode in ("seq", "last", "hseq"):
+        pw = core.PackedWeights(*w, out_mode=mode, backend="tc")
+        assert pw.backend == "tc"
+        out, h_n, c_n = pw.forward(x, lengths=lens.to(cuda_device), hx=hx, check=True)
+        r_out, r_h, r_c = oracle_of(x, *w, lengths=lens, hx=hx, out_mode=mode)
+        assert_close16(out, r_out, f"{mode} out")
+        assert_close16(h_n, r_h, f"{mode} h_n")
+        assert_close16(c_n, r_c, f"{mode} c_n")

@@ -132,8 +132,8 @@ int32_t tc_make_perm(const Problem& p, int N, int tiles, const int32_t* lengths,
 int32_t tc_xpack(const Problem& p, int N, int tiles, const void* x, const int32_t* perm, uint8_t* xp, int kx,
                  cudaStream_t s);
 
-// tcgen05 layer-sequential backend (plstm_tcl.cu) for H = 64..512 in steps of 64, L <= 16,
-// I <= 16: per layer a projection GEMM and a cluster-wide recurrence; the tc_* entry
+// tcgen05 layer-sequential backend (plstm_tcl.cu) for any H <= 512 (zero-padded to a multiple
+// of 64), L <= 16, I <= 128: per layer a projection GEMM and a cluster-wide recurrence; the tc_* entry
 // points above forward every shape outside the H = 128 wavefront kernel's envelope to it.
 bool tcl_supported(const Problem& p, std::string* why);
 size_t tcl_packed_size(const Problem& p);

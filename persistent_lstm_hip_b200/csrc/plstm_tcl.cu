@@ -44,7 +44,10 @@ namespace tcl {
 
 constexpr int kU = 32;      // hidden units per recurrent CTA (4 x 32 = 128 gate rows)
 constexpr int kRows = 128;  // gate rows per CTA
-constexpr int kXK = 16;     // padded layer-0 input width
+constexpr int kXK = 16;     // layer-0 input width step (one MMA K step)
+constexpr int kMaxXK = 128; // widest padded layer-0 input
+// Layer-0 input width rounded up to one MMA K step.
+__host__ __device__ inline int kx_of(int I) { return (I + kXK - 1) / kXK * kXK; }
 constexpr int kNT = 64;     // batch rows per cluster tile (N of the recurrent MMAs)
 constexpr int kGRow = kNT + 8;              // gate block row stride in elements (+16 bytes: no bank conflicts)
 constexpr int kGBlock = kRows * kGRow * 2;  // bytes of one (step, tile, CTA) gate block
@@ -53,13 +56,13 @@ constexpr int kKG = (kNT / 8) * 128;        // bytes of one 8-unit K group of a 
 constexpr int kMaxL = 16;
 
 __host__ __device__ inline int ctas_of(int H) { return H / kU; }
-__host__ __device__ inline int kin_of(int l, int H) { return l == 0 ? kXK : H; }
 
-// Packed image: [W_hh images L x 4H x H][W_ih images per layer 4H x Kin][bias f32 L x 4H]
-// [W_lin 16-bit O x H][b_lin f32 O]; gate rows in the recurrent CTA order below.
+// Packed image: [W_hh images L x 4H x H][W_ih images per layer 4H x Kin (layer 0: Kin = kx, the
+// input width rounded up to 16, in a region sized for 128)][bias f32 L x 4H][W_lin 16-bit O x H]
+// [b_lin f32 O]; gate rows in the recurrent CTA order below.
 __host__ __device__ inline size_t off_whh(int l, int H) { return (size_t)l * 4 * H * H * 2; }
 __host__ __device__ inline size_t off_wih(int l, int H, int L) {
-  return off_whh(L, H) + (l == 0 ? 0 : (size_t)4 * H * kXK * 2 + (size_t)(l - 1) * 4 * H * H * 2);
+  return off_whh(L, H) + (l == 0 ? 0 : (size_t)4 * H * kMaxXK * 2 + (size_t)(l - 1) * 4 * H * H * 2);
 }
 __host__ __device__ inline size_t off_bias(int H, int L) { return off_wih(L, H, L); }
 __host__ __device__ inline size_t off_wlin(int H, int L) { return off_bias(H, L) + (size_t)L * 4 * H * 4; }
@@ -152,6 +155,7 @@ struct PackArgs {
   const void* b_lin;
   int ih_layout, hh_layout, dtype, L, I, H, O;
   int hid;  // the model's hidden size (<= H; units >= hid are zero padding)
+  int kx;   // layer-0 input width rounded up to 16 (<= 128)
 };
 
 __global__ void pack_kernel(const PackArgs a, uint8_t* packed) {
@@ -163,7 +167,7 @@ __global__ void pack_kernel(const PackArgs a, uint8_t* packed) {
     return unit < a.hid ? gate * a.hid + unit : -1;
   };
   const int64_t n_hh = (int64_t)L * G * H;
-  const int64_t n_ih = (int64_t)G * kXK + (int64_t)(L - 1) * G * H;
+  const int64_t n_ih = (int64_t)G * a.kx + (int64_t)(L - 1) * G * H;
   const int64_t n_b = (int64_t)L * G;
   const int64_t n_wl = (int64_t)a.O * H;
   const int64_t total = n_hh + n_ih + n_b + n_wl + a.O;
@@ -186,9 +190,9 @@ __global__ void pack_kernel(const PackArgs a, uint8_t* packed) {
       put16(off_whh(l, H), rem, v * row_scale(rho));
     } else if (i < n_hh + n_ih) {
       int64_t j = i - n_hh;
-      int l = 0, kin = kXK;
-      if (j >= (int64_t)G * kXK) {
-        j -= (int64_t)G * kXK;
+      int l = 0, kin = a.kx;
+      if (j >= (int64_t)G * a.kx) {
+        j -= (int64_t)G * a.kx;
         l = 1 + (int)(j / ((int64_t)G * H));
         j %= (int64_t)G * H;
         kin = H;
@@ -238,16 +242,18 @@ __global__ void pack_kernel(const PackArgs a, uint8_t* packed) {
 constexpr int kGemmThreads = 6 * 32;  // warp 0 loads, warp 1 issues MMAs, warps 2-5 epilogue
 constexpr int kBStages = 3;
 
-template <int KP>
+// XIN: the input is the packed x tile of layer 0 (KP = kx columns, no swizzle, 8-row groups
+// KP * 16 bytes apart); otherwise layer l-1's h pieces (KP = H).
+template <int KP, bool XIN>
 struct GemmSmem {
-  static constexpr int kStage = KP <= kXK ? kNT * 32 : KP * kNT * 2;  // one step's input tile
+  static constexpr int kStage = KP * kNT * 2;  // one step's input tile
   static constexpr int kB = 0;
   static constexpr int kBias = kB + kBStages * kStage;
   static constexpr int kBar = kBias + kRows * 4;
   static constexpr int kTmemSlot = kBar + 96;
   static constexpr int kEnd = kBar + 128;
   static constexpr int kDyn = kEnd + 1024;
-  static constexpr int kACols = KP <= kXK ? 8 : KP / 2;  // W_ih slice: 128 lanes x KP 16-bit values
+  static constexpr int kACols = KP / 2;  // W_ih slice: 128 lanes x KP 16-bit values
   static constexpr int kTmemCols = kACols + 2 * kNT <= 256 ? 256 : 512;
   static_assert(kDyn <= 232448, "shared memory");
 };
@@ -262,9 +268,9 @@ struct GemmArgs {
   int T, H, tiles;
 };
 
-template <int KP, bool BF16>
+template <int KP, bool BF16, bool XIN>
 __global__ void __launch_bounds__(kGemmThreads, 1) proj_kernel(const GemmArgs a) {
-  using S = GemmSmem<KP>;
+  using S = GemmSmem<KP, XIN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = ptx::smem_u32(sm);
@@ -301,11 +307,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1) proj_kernel(const GemmArgs a)
     const int row = 32 * q + lane;
     const uint32_t* src = reinterpret_cast<const uint32_t*>(a.wih + ((size_t)r * kRows + row) * KP);
     const uint32_t lane_off = (uint32_t)(32 * q) << 16;
-    if (KP <= kXK) {
-      uint32_t v[8];
+    if (S::kACols % 32 != 0) {  // 8 columns at a time (layer-0 widths that are not a multiple of 64)
+#pragma unroll 1
+      for (int c = 0; c < S::kACols; c += 8) {
+        uint32_t v[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) v[i] = src[i];
-      ptx::tmem_st_32x32b_x8(tmem + lane_off, v);
+        for (int i = 0; i < 8; ++i) v[i] = src[c + i];
+        ptx::tmem_st_32x32b_x8(tmem + lane_off + (uint32_t)c, v);
+      }
     } else {
 #pragma unroll 1
       for (int c = 0; c < S::kACols; c += 32) {
@@ -333,7 +342,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) proj_kernel(const GemmArgs a)
     const int t = (int)(ts / a.tiles), tile = (int)(ts % a.tiles);
     *t_out = t;
     *tile_out = tile;
-    if (KP <= kXK) return a.xp + ((size_t)tile * a.T + t) * (size_t)(kNT * 32);
+    if (XIN) return a.xp + ((size_t)tile * a.T + t) * (size_t)(kNT * KP * 2);
     return a.hseq + ((size_t)t * a.tiles + tile) * (size_t)C * kPiece;
   };
 
@@ -368,8 +377,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1) proj_kernel(const GemmArgs a)
         ptx::tc_fence_after();
         const uint32_t d = tmem + (uint32_t)(S::kACols + db * kNT);
         const uint32_t b0 = sbase + S::kB + s * S::kStage;
-        if (KP <= kXK) {
-          ptx::mma_f16_ts(d, tmem, ptx::desc_k_none(b0, 128, 256), idesc, 0u);
+        if (XIN) {
+#pragma unroll
+          for (int i = 0; i < KP / 16; ++i)
+            ptx::mma_f16_ts(d, tmem + (uint32_t)(8 * i), ptx::desc_k_none(b0 + (uint32_t)(256 * i), 128, KP * 16), idesc,
+                            i != 0 ? 1u : 0u);
         } else {
 #pragma unroll 4
           for (int i = 0; i < KP / 16; ++i)
@@ -935,7 +947,7 @@ Ws ws_layout(const Problem& p) {
   w.sorted = off;
   off = align_up(off + (size_t)std::max(p.B, 1) * 4, 256);
   w.xp = off;
-  off = align_up(off + (size_t)tiles * p.T * kNT * 32, 256);
+  off = align_up(off + (size_t)tiles * p.T * kNT * kx_of(p.I) * 2, 256);
   w.gates = off;
   off = align_up(off + (size_t)p.T * tiles * C * kGBlock, 256);
   w.hseq = off;
@@ -1039,12 +1051,25 @@ int rec_max_clusters(int device, int H) {
   return n;
 }
 
-template <int KP, bool BF16>
+template <int KP, bool BF16, bool XIN>
 int32_t launch_proj(const GemmArgs& ga, int sms, cudaStream_t s);
+// Projection of layer 0 (K = kx, the packed x tile).
+int32_t launch_proj_x(const GemmArgs& ga, int kx, bool bf16, int sms, cudaStream_t s) {
+#define PLSTM_TCL_PROJX(KX) \
+  case KX: return bf16 ? launch_proj<KX, true, true>(ga, sms, s) : launch_proj<KX, false, true>(ga, sms, s);
+  switch (kx) {
+    PLSTM_TCL_PROJX(16) PLSTM_TCL_PROJX(32) PLSTM_TCL_PROJX(48) PLSTM_TCL_PROJX(64)
+    PLSTM_TCL_PROJX(80) PLSTM_TCL_PROJX(96) PLSTM_TCL_PROJX(112) PLSTM_TCL_PROJX(128)
+    default: break;
+  }
+#undef PLSTM_TCL_PROJX
+  set_error("no projection kernel for this input width");
+  return PLSTM_ENOTSUP;
+}
 // Projection of a layer >= 1 (K = H).
 int32_t launch_proj_h(const GemmArgs& ga, bool bf16, int sms, cudaStream_t s) {
 #define PLSTM_TCL_PROJ(HH) \
-  case HH: return bf16 ? launch_proj<HH, true>(ga, sms, s) : launch_proj<HH, false>(ga, sms, s);
+  case HH: return bf16 ? launch_proj<HH, true, false>(ga, sms, s) : launch_proj<HH, false, false>(ga, sms, s);
   switch (ga.H) {
     PLSTM_TCL_PROJ(64) PLSTM_TCL_PROJ(128) PLSTM_TCL_PROJ(192) PLSTM_TCL_PROJ(256)
     PLSTM_TCL_PROJ(320) PLSTM_TCL_PROJ(384) PLSTM_TCL_PROJ(448) PLSTM_TCL_PROJ(512)
@@ -1055,14 +1080,14 @@ int32_t launch_proj_h(const GemmArgs& ga, bool bf16, int sms, cudaStream_t s) {
   return PLSTM_ENOTSUP;
 }
 
-template <int KP, bool BF16>
+template <int KP, bool BF16, bool XIN>
 int32_t launch_proj(const GemmArgs& ga, int sms, cudaStream_t s) {
-  auto k = proj_kernel<KP, BF16>;
-  PLSTM_TRY_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmSmem<KP>::kDyn));
+  auto k = proj_kernel<KP, BF16, XIN>;
+  PLSTM_TRY_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmSmem<KP, XIN>::kDyn));
   const int C = ctas_of(ga.H);
   const long long jobs = (long long)ga.T * ga.tiles * C;
   const int grid = (int)std::max<long long>(C, std::min<long long>((sms / C) * C, jobs));
-  k<<<grid, kGemmThreads, GemmSmem<KP>::kDyn, s>>>(ga);
+  k<<<grid, kGemmThreads, GemmSmem<KP, XIN>::kDyn, s>>>(ga);
   PLSTM_TRY_CUDA(cudaGetLastError());
   note_launches(1);
   return PLSTM_OK;
@@ -1088,7 +1113,7 @@ bool tcl_supported(const Problem& p, std::string* why) {
   if (p.dtype != PLSTM_F16 && p.dtype != PLSTM_BF16) return no("activation type must be f16 or bf16");
   if (p.H < 1 || !rec_hidden_ok(tcl_hp(p.H))) return no("hidden_size must be <= 512");
   if (p.L < 1 || p.L > kMaxL) return no("num_layers must be 1..16");
-  if (p.I > kXK) return no("input_size must be <= 16");
+  if (p.I > kMaxXK) return no("input_size must be <= 128");
   if (p.T < 1 || p.T > 65535) return no("seq_len must be 1..65535");
   int dev = p.device, major = 0, minor = 0;
   if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
@@ -1124,6 +1149,7 @@ int32_t tcl_pack(const Problem& p, int ih_layout, int hh_layout, const void* con
   a.I = p.I;
   a.H = tcl_hp(p.H);
   a.hid = p.H;
+  a.kx = kx_of(p.I);
   a.O = p.has_linear() ? p.O : 0;
   pack_kernel<<<148 * 4, 256, 0, s>>>(a, static_cast<uint8_t*>(packed));
   PLSTM_TRY_CUDA(cudaGetLastError());
@@ -1251,7 +1277,7 @@ int32_t tcl_forward(const Problem& p, const void* packed, const void* x, const i
     if (rc != PLSTM_OK) return rc;
   }
   {
-    const int32_t rc = tc_xpack(p, kNT, tiles, x, perm, wsb + w.xp, kXK, s);
+    const int32_t rc = tc_xpack(p, kNT, tiles, x, perm, wsb + w.xp, kx_of(p.I), s);
     if (rc != PLSTM_OK) return rc;
   }
   int sms = 148;
@@ -1272,7 +1298,7 @@ int32_t tcl_forward(const Problem& p, const void* packed, const void* x, const i
     ga.tiles = tiles;
     int32_t rc;
     if (l == 0)
-      rc = bf16 ? launch_proj<kXK, true>(ga, sms, s) : launch_proj<kXK, false>(ga, sms, s);
+      rc = launch_proj_x(ga, kx_of(p.I), bf16, sms, s);
     else
       rc = launch_proj_h(ga, bf16, sms, s);
     if (rc != PLSTM_OK) return rc;

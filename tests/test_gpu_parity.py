@@ -346,11 +346,11 @@ def test_tc_wide_input_ignores_single_slot_request(cuda_device, monkeypatch):
 
 def test_tc_rejects_beyond_envelope(cuda_device):
     """Shapes past both tensor-core envelopes (H = 128 wavefront: I <= 128, L <= 8; layer
-    path: I <= 16, L <= 16) are refused by the forced TC backend and served by the generic
-    kernel under "auto"; H = 128 with 9 layers and I <= 16 runs on the layer path."""
-    assert core.select_backend(input_size=5, hidden_size=128, num_layers=9, output_size=24,
+    path: I <= 128, L <= 16) are refused by the forced TC backend and served by the generic
+    kernel under "auto"; H = 128 with 9 layers runs on the layer path."""
+    assert core.select_backend(input_size=40, hidden_size=128, num_layers=9, output_size=24,
                                dtype=torch.float16, device=cuda_device.index or 0) == "tc"
-    for I, L in [(129, 2), (40, 9)]:
+    for I, L in [(129, 2), (5, 17)]:
         assert core.select_backend(input_size=I, hidden_size=128, num_layers=L, output_size=24,
                                    dtype=torch.float16, device=cuda_device.index or 0) == "simt"
         with pytest.raises(_lib.PlstmError):

@@ -153,3 +153,21 @@ def test_tcl_padded_hidden_sizes(cuda_device, H, L):
         assert_close16(out, r_out, f"{mode} out")
         assert_close16(h_n, r_h, f"{mode} h_n")
         assert_close16(c_n, r_c, f"{mode} c_n")
+
+
+# Layer-0 inputs up to 128 columns (the projection's K = I rounded up to 16).
+@pytest.mark.parametrize("H, I", [(256, 17), (192, 64), (512, 100), (256, 128), (128, 48)])
+def test_tcl_wide_inputs(cuda_device, H, I):
+    B, T, O = 39, 9, 24
+    L = 9 if H == 128 else 2  # H = 128 takes the layer path beyond 8 layers
+    m = make_model(I, H, L, O, seed=H + I)
+    w = weights_of(m, L, torch.bfloat16, cuda_device)
+    x = _x(B, T, I, torch.bfloat16, cuda_device, seed=I)
+    for mode in ("seq", "last"):
+        pw = core.PackedWeights(*w, out_mode=mode, backend="tc")
+        assert pw.backend == "tc"
+        out, h_n, c_n = pw.forward(x, check=True)
+        r_out, r_h, r_c = oracle_of(x, *w, out_mode=mode)
+        assert_close16(out, r_out, f"{mode} out")
+        assert_close16(h_n, r_h, f"{mode} h_n")
+        assert_close16(c_n, r_c, f"{mode} c_n")

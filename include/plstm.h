@@ -66,7 +66,7 @@ extern "C" {
 /* ---- backends ----------------------------------------------------------- */
 #define PLSTM_BACKEND_AUTO 0 /* tensor-core wavefront kernel when it applies, else SIMT */
 #define PLSTM_BACKEND_SIMT 1 /* generic layer-sequential FFMA kernel (any shape, f32) */
-#define PLSTM_BACKEND_TC 2   /* tcgen05 kernels, f16/bf16: H=128 (L<=8, I<=128, O<=32); otherwise any H<=512 (L<=16, I<=128) */
+#define PLSTM_BACKEND_TC 2   /* tcgen05 kernels, f16/bf16: H<=128 with L<=8, I<=128, O<=32 (wavefront); else any H<=512, L<=16, I<=128 */
 
 /* ---- flags -------------------------------------------------------------- */
 #define PLSTM_FLAG_OUT_SEQ 0x1      /* out is [B][T][O]: Linear on every step, zero past each length */

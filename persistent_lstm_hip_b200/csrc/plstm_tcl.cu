@@ -48,11 +48,22 @@ constexpr int kXK = 16;     // layer-0 input width step (one MMA K step)
 constexpr int kMaxXK = 128; // widest padded layer-0 input
 // Layer-0 input width rounded up to one MMA K step.
 __host__ __device__ inline int kx_of(int I) { return (I + kXK - 1) / kXK * kXK; }
-constexpr int kNT = 64;     // batch rows per cluster tile (N of the recurrent MMAs)
+// Batch rows per cluster tile (N of the recurrent MMAs): 64, or 80 where 64-row tiles
+// would need a second wave of clusters.  The kernels are templated on it (NT) and
+// declare these quantities locally; the constants below are the 64-row defaults.
+constexpr int kNT = 64;
 constexpr int kGRow = kNT + 8;              // gate block row stride in elements (+16 bytes: no bank conflicts)
 constexpr int kGBlock = kRows * kGRow * 2;  // bytes of one (step, tile, CTA) gate block
 constexpr int kPiece = kNT * kU * 2;        // bytes of one CTA's h piece (32 units x 64 rows)
-constexpr int kKG = (kNT / 8) * 128;        // bytes of one 8-unit K group of a piece (8 row groups x 128 B)
+__host__ __device__ constexpr int gblock_of(int nt) { return kRows * (nt + 8) * 2; }
+__host__ __device__ constexpr int piece_of(int nt) { return nt * kU * 2; }
+#define PLSTM_TCL_TILE_CONSTANTS(NT)                                                             \
+  constexpr int kNT = NT, kGRow = NT + 8, kGBlock = kRows * (NT + 8) * 2, kPiece = NT * kU * 2, \
+                kKG = (NT / 8) * 128;                                                             \
+  (void)kGRow;                                                                                    \
+  (void)kGBlock;                                                                                  \
+  (void)kPiece;                                                                                   \
+  (void)kKG
 constexpr int kMaxL = 16;
 
 __host__ __device__ inline int ctas_of(int H) { return H / kU; }
@@ -118,8 +129,9 @@ __device__ __forceinline__ uint32_t none16_off(int row, int k) {
 // Byte offset of (unit k, tile row n) in an h tile of H units: pieces of 32 units,
 // each [4 K groups][8 row groups][8 rows][8 units] (K-major, no swizzle: the K
 // groups of the whole tile are kKG bytes apart, row groups 128 bytes apart).
+template <int NT>
 __device__ __forceinline__ uint32_t hoff(int k, int n) {
-  return (uint32_t)((k >> 3) * kKG + (n >> 3) * 128 + (n & 7) * 16 + (k & 7) * 2);
+  return (uint32_t)((k >> 3) * ((NT / 8) * 128) + (n >> 3) * 128 + (n & 7) * 16 + (k & 7) * 2);
 }
 
 // Bounded mbarrier wait; false = gave up (timeout or abort).
@@ -244,17 +256,19 @@ constexpr int kBStages = 3;
 
 // XIN: the input is the packed x tile of layer 0 (KP = kx columns, no swizzle, 8-row groups
 // KP * 16 bytes apart); otherwise layer l-1's h pieces (KP = H).
-template <int KP, bool XIN>
+template <int KP, bool XIN, int NT>
 struct GemmSmem {
-  static constexpr int kStage = KP * kNT * 2;  // one step's input tile
+  static constexpr int kStage = KP * NT * 2;  // one step's input tile
+  // Input ring: kBStages deep, 2 where three stages do not fit (K = 512 with 80-row tiles).
+  static constexpr int kStages = kBStages * kStage + 4096 <= 232448 ? kBStages : 2;
   static constexpr int kB = 0;
-  static constexpr int kBias = kB + kBStages * kStage;
+  static constexpr int kBias = kB + kStages * kStage;
   static constexpr int kBar = kBias + kRows * 4;
   static constexpr int kTmemSlot = kBar + 96;
   static constexpr int kEnd = kBar + 128;
   static constexpr int kDyn = kEnd + 1024;
   static constexpr int kACols = KP / 2;  // W_ih slice: 128 lanes x KP 16-bit values
-  static constexpr int kTmemCols = kACols + 2 * kNT <= 256 ? 256 : 512;
+  static constexpr int kTmemCols = kACols + 2 * NT <= 256 ? 256 : 512;
   static_assert(kDyn <= 232448, "shared memory");
 };
 
@@ -268,9 +282,10 @@ struct GemmArgs {
   int T, H, tiles;
 };
 
-template <int KP, bool BF16, bool XIN>
+template <int KP, bool BF16, bool XIN, int NT>
 __global__ void __launch_bounds__(kGemmThreads, 1) proj_kernel(const GemmArgs a) {
-  using S = GemmSmem<KP, XIN>;
+  using S = GemmSmem<KP, XIN, NT>;
+  PLSTM_TCL_TILE_CONSTANTS(NT);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = ptx::smem_u32(sm);
@@ -284,7 +299,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) proj_kernel(const GemmArgs a)
   const uint32_t b_full = bar, b_empty = bar + 24, d_full = bar + 48, d_empty = bar + 64;
   float* bias_s = reinterpret_cast<float*>(sm + S::kBias);
   if (tid == 0) {
-    for (int s = 0; s < kBStages; ++s) {
+    for (int s = 0; s < S::kStages; ++s) {
       ptx::mbar_init(b_full + 8 * s, 1);
       ptx::mbar_init(b_empty + 8 * s, 1);
     }
@@ -350,8 +365,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) proj_kernel(const GemmArgs a)
     // ---------------- loads ----------------
     if (lane == 0) {
       for (int k = 0; k < my; ++k) {
-        const int s = k % kBStages;
-        if (k >= kBStages && !wait_bar(b_empty + 8 * s, ((k / kBStages) - 1) & 1, nullptr, kTimeout)) {
+        const int s = k % S::kStages;
+        if (k >= S::kStages && !wait_bar(b_empty + 8 * s, ((k / S::kStages) - 1) & 1, nullptr, kTimeout)) {
           report_status(a.status, PLSTM_ETIMEOUT, 0x7ffe0000);
           break;
         }
@@ -366,11 +381,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1) proj_kernel(const GemmArgs a)
     // ---------------- MMA issue ----------------
     constexpr uint32_t idesc = ptx::idesc_f16(128, kNT, BF16);
     for (int k = 0; k < my; ++k) {
-      const int s = k % kBStages, db = k & 1;
+      const int s = k % S::kStages, db = k & 1;
       int w = 1;
       if (lane == 0) {
         if (k >= 2) w = wait_bar(d_empty + 8 * db, ((k - 2) >> 1) & 1, nullptr, kTimeout) ? 1 : 0;
-        if (w) w = wait_bar(b_full + 8 * s, (k / kBStages) & 1, nullptr, kTimeout) ? 1 : 0;
+        if (w) w = wait_bar(b_full + 8 * s, (k / S::kStages) & 1, nullptr, kTimeout) ? 1 : 0;
       }
       if (!__shfl_sync(0xffffffffu, w, 0)) break;
       if (ptx::elect_one()) {
@@ -433,23 +448,24 @@ __global__ void __launch_bounds__(kGemmThreads, 1) proj_kernel(const GemmArgs a)
 }
 
 // ---- recurrence -----------------------------------------------------------------------
-template <int H, int NCW>
+template <int H, int NCW, int NT>
 struct RecSmem {
   static constexpr int C = H / kU;
-  static constexpr int kTile = H * kNT * 2;  // one h tile (all units x 64 rows)
+  static constexpr int kTile = H * NT * 2;   // one h tile (all units x NT rows)
   static constexpr int kB = 0;               // h tiles, double-buffered by step parity
-  static constexpr int kG = kB + 2 * kTile;  // gate blocks, ring of 3
-  static constexpr int kBar = kG + 3 * kGBlock;
+  static constexpr int kG = kB + 2 * kTile;  // gate blocks: a ring of kGS (3, or 2 if 3 do not fit)
+  static constexpr int kGS = 2 * kTile + 3 * gblock_of(NT) + 2048 <= 232448 ? 3 : 2;
+  static constexpr int kBar = kG + kGS * gblock_of(NT);
   // barriers: full_rec[2] @0, mma[2] @16, hready[2] @32, gfull[3] @48
   static constexpr int kTmemSlot = kBar + 80, kAbort = kBar + 84, kDone = kBar + 88;
-  static constexpr int kPerm = kBar + 128, kLens = kPerm + 4 * kNT;
-  static constexpr int kEnd = kLens + 4 * kNT;
+  static constexpr int kPerm = kBar + 128, kLens = kPerm + 4 * NT;
+  static constexpr int kEnd = kLens + 4 * NT;
   static constexpr int kDyn = kEnd + 1024;
   static constexpr int kComputeWarps = NCW;  // NCW / 4 per TMEM lane quadrant, 256 / NCW columns each
   static constexpr int kThreads = (kComputeWarps + 1) * 32;
   static constexpr int kACols = H / 2;  // W_hh slice: 128 lanes x H 16-bit values
-  static constexpr int kD = kACols;     // gate accumulator [128 x 64] (single buffer)
-  static constexpr int kTmemCols = kACols + kNT <= 256 ? 256 : 512;
+  static constexpr int kD = kACols;     // gate accumulator [128 x NT] (single buffer)
+  static constexpr int kTmemCols = kACols + NT <= 256 ? 256 : 512;
   static_assert(kDyn <= 232448, "shared memory");
 };
 
@@ -489,11 +505,14 @@ __device__ __forceinline__ void rec_abort(const RecArgs& a, uint8_t* sm_abort, i
   report_status(a.status, PLSTM_ETIMEOUT, (int)((blockIdx.x & 0x7fff) << 16) | (step & 0xffff));
 }
 
-template <int H, int NCW, bool BF16, bool VARLEN>
-__global__ void __launch_bounds__(RecSmem<H, NCW>::kThreads, 1) rec_kernel(const RecArgs a) {
-  using S = RecSmem<H, NCW>;
+template <int H, int NCW, bool BF16, bool VARLEN, int NT>
+__global__ void __launch_bounds__(RecSmem<H, NCW, NT>::kThreads, 1) rec_kernel(const RecArgs a) {
+  using S = RecSmem<H, NCW, NT>;
+  PLSTM_TCL_TILE_CONSTANTS(NT);
   constexpr int C = S::C;
+  constexpr int GS = S::kGS;
   constexpr int CPW = kNT * 4 / (NCW * 8);  // 8-column chunks per compute warp
+  static_assert(CPW * NCW * 8 == kNT * 4, "tile rows must split evenly over the compute warps");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = ptx::smem_u32(sm);
@@ -515,7 +534,7 @@ __global__ void __launch_bounds__(RecSmem<H, NCW>::kThreads, 1) rec_kernel(const
       ptx::mbar_init(bar_mma + 8 * b, 1);
       ptx::mbar_init(bar_hready + 8 * b, S::kComputeWarps);
     }
-    for (int s = 0; s < 3; ++s) ptx::mbar_init(bar_g + 8 * s, 1);
+    for (int s = 0; s < GS; ++s) ptx::mbar_init(bar_g + 8 * s, 1);
     *abort_flag = 0;
     *reinterpret_cast<uint32_t*>(sm + S::kDone) = 0;
     ptx::fence_mbar_init_cluster();
@@ -538,7 +557,7 @@ __global__ void __launch_bounds__(RecSmem<H, NCW>::kThreads, 1) rec_kernel(const
     uint16_t v = 0;
     const int b = perm_s[n];
     if (a.h0 != nullptr && b >= 0 && k < a.hid) v = static_cast<const uint16_t*>(a.h0)[((size_t)l * a.B + b) * a.hid + k];
-    *reinterpret_cast<uint16_t*>(sm + S::kB + hoff(k, n)) = v;
+    *reinterpret_cast<uint16_t*>(sm + S::kB + hoff<NT>(k, n)) = v;
   }
   ptx::fence_proxy_async_smem();
   ptx::tc_fence_after();
@@ -605,7 +624,7 @@ __global__ void __launch_bounds__(RecSmem<H, NCW>::kThreads, 1) rec_kernel(const
     };
     auto load_gates = [&](int t) {
       if (ptx::elect_one()) {
-        const int s = t % 3;
+        const int s = t % GS;
         ptx::mbar_arrive_expect_tx(bar_g + 8 * s, kGBlock);
         ptx::bulk_g2s(gslot(s), gates_src(t), kGBlock, bar_g + 8 * s);
       }
@@ -618,7 +637,7 @@ __global__ void __launch_bounds__(RecSmem<H, NCW>::kThreads, 1) rec_kernel(const
       ok = false;
     };
     if (Tt > 0) {
-      for (int t = 0; t < 3 && t < Tt; ++t) load_gates(t);
+      for (int t = 0; t < GS && t < Tt; ++t) load_gates(t);
       if (ptx::elect_one())
         for (int t = 1; t <= 2 && t < Tt; ++t) ptx::mbar_arrive_expect_tx(bar_rec + 8 * (t & 1), rec_bytes);
       __syncwarp();
@@ -681,9 +700,9 @@ __global__ void __launch_bounds__(RecSmem<H, NCW>::kThreads, 1) rec_kernel(const
         c_st[jc][e] = cv;
       }
     for (int t = 0; t < Tt; ++t) {
-      const int b = t & 1, gs = t % 3;
+      const int b = t & 1, gs = t % GS;
       if (*abort_flag) break;
-      if (!wait_bar(bar_g + 8 * gs, (t / 3) & 1, abort_flag, a.timeout_ns) ||
+      if (!wait_bar(bar_g + 8 * gs, (t / GS) & 1, abort_flag, a.timeout_ns) ||
           !wait_bar(bar_mma + 8 * b, (t >> 1) & 1, abort_flag, a.timeout_ns)) {
         if (lane == 0) rec_abort(a, sm + S::kAbort, C, t);
         break;
@@ -696,6 +715,14 @@ __global__ void __launch_bounds__(RecSmem<H, NCW>::kThreads, 1) rec_kernel(const
       for (int i = 0; i < CPW / 4; ++i) {
         ptx::tmem_ld_16x256b_x4(dcol + lo + (uint32_t)(n0 + 32 * i), *reinterpret_cast<uint32_t(*)[16]>(&rif[16 * i]));
         ptx::tmem_ld_16x256b_x4(dcol + hi + (uint32_t)(n0 + 32 * i), *reinterpret_cast<uint32_t(*)[16]>(&rgo[16 * i]));
+      }
+      if (CPW % 4 != 0) {  // 80-row tiles: 5 chunks per warp
+        constexpr int c0 = CPW / 4 * 4;
+#pragma unroll
+        for (int c = c0; c < CPW; ++c) {
+          ptx::tmem_ld_16x256b_x1(dcol + lo + (uint32_t)(n0 + 8 * c), *reinterpret_cast<uint32_t(*)[4]>(&rif[4 * c]));
+          ptx::tmem_ld_16x256b_x1(dcol + hi + (uint32_t)(n0 + 8 * c), *reinterpret_cast<uint32_t(*)[4]>(&rgo[4 * c]));
+        }
       }
       ptx::tmem_wait_ld();
       ptx::tc_fence_before();
@@ -735,7 +762,7 @@ __global__ void __launch_bounds__(RecSmem<H, NCW>::kThreads, 1) rec_kernel(const
             c_st[jc][e] = cn[e];
             h_st[jc][e] = (uint16_t)(e == 0 ? bits & 0xffffu : bits >> 16);
           }
-          const uint32_t off = hoff(u, n0 + 8 * jc + cpair + e);
+          const uint32_t off = hoff<NT>(u, n0 + 8 * jc + cpair + e);
           *reinterpret_cast<uint16_t*>(dst + off) = h_st[jc][e];
           if (gdst != nullptr) *reinterpret_cast<uint16_t*>(gdst + off) = h_st[jc][e];
         }
@@ -747,7 +774,7 @@ __global__ void __launch_bounds__(RecSmem<H, NCW>::kThreads, 1) rec_kernel(const
         ptx::mbar_arrive(bar_hready + 8 * b);
         // The last warp to finish pushes the piece to the peers (acquire-release
         // counter: the other warps' writes, fenced for the async proxy, come first).
-        // It then prefetches the gate block of step t + 3 into this step's slot
+        // It then prefetches the gate block of step t + GS into this step's slot
         // (after the pushes: they are on the critical path).
         if (t + 1 < Tt && ptx::atom_add_acq_rel_smem(sbase + S::kDone, 1u) % (uint32_t)S::kComputeWarps ==
                               (uint32_t)S::kComputeWarps - 1u) {
@@ -757,9 +784,9 @@ __global__ void __launch_bounds__(RecSmem<H, NCW>::kThreads, 1) rec_kernel(const
             ptx::bulk_s2c(ptx::mapa(piece, (uint32_t)pr), piece, kPiece,
                           ptx::mapa(bar_rec + 8 * (b ^ 1), (uint32_t)pr));
           }
-          if (t + 3 < Tt) {
+          if (t + GS < Tt) {
             ptx::mbar_arrive_expect_tx(bar_g + 8 * gs, kGBlock);
-            ptx::bulk_g2s(gslot(gs), gates_src(t + 3), kGBlock, bar_g + 8 * gs);
+            ptx::bulk_g2s(gslot(gs), gates_src(t + GS), kGBlock, bar_g + 8 * gs);
           }
           trace_mark(a, tile, r, t, 7);
         }
@@ -819,11 +846,12 @@ __global__ void linear_last_kernel(const uint16_t* __restrict__ hlast, const uin
 
 // One block per (step, tile): the tile's h from its C pieces, then either the Linear
 // head (out[b][t][o]) or the h sequence itself (out[b][t][u]); zero past each length.
-template <bool BF16, bool LINEAR>
+template <bool BF16, bool LINEAR, int NT>
 __global__ void seq_out_kernel(const uint8_t* __restrict__ hseq, const int32_t* __restrict__ perm,
                                const int32_t* __restrict__ lengths, const uint16_t* __restrict__ wlin,
                                const float* __restrict__ blin, uint16_t* __restrict__ out, int B, int T, int H,
                                int O, int tiles, int out_seq_major, int hid) {
+  PLSTM_TCL_TILE_CONSTANTS(NT);
   extern __shared__ uint8_t smem_o[];
   float* hs = reinterpret_cast<float*>(smem_o);  // [kNT][H + 1]
   const int C = ctas_of(H);
@@ -933,13 +961,14 @@ struct Ws {
   size_t perm, tile_len, hist, sorted, xp, gates, hseq, hlast, trace, total;
 };
 
-Ws ws_layout(const Problem& p) {
+// nt: batch rows per tile (64 or 80).
+Ws ws_layout(const Problem& p, int nt) {
   Ws w;
-  const int tiles = (p.B + kNT - 1) / kNT;
+  const int tiles = (p.B + nt - 1) / nt;
   const int C = ctas_of(p.H);
   size_t off = kStatusBytes;
   w.perm = off;
-  off = align_up(off + (size_t)tiles * kNT * 4, 256);
+  off = align_up(off + (size_t)tiles * nt * 4, 256);
   w.tile_len = off;
   off = align_up(off + (size_t)tiles * 4, 256);
   w.hist = off;
@@ -947,11 +976,11 @@ Ws ws_layout(const Problem& p) {
   w.sorted = off;
   off = align_up(off + (size_t)std::max(p.B, 1) * 4, 256);
   w.xp = off;
-  off = align_up(off + (size_t)tiles * p.T * kNT * kx_of(p.I) * 2, 256);
+  off = align_up(off + (size_t)tiles * p.T * nt * kx_of(p.I) * 2, 256);
   w.gates = off;
-  off = align_up(off + (size_t)p.T * tiles * C * kGBlock, 256);
+  off = align_up(off + (size_t)p.T * tiles * C * gblock_of(nt), 256);
   w.hseq = off;
-  off = align_up(off + (size_t)p.T * tiles * C * kPiece, 256);
+  off = align_up(off + (size_t)p.T * tiles * C * piece_of(nt), 256);
   w.hlast = off;
   off = align_up(off + (size_t)std::max(p.B, 1) * p.H * 2, 256);
   w.trace = off;
@@ -969,74 +998,86 @@ int rec_warps() {
   }();
   return w;
 }
-template <int H, int NCW>
+template <int H, int NCW, int NT>
 void* rec_ptr(bool bf16, bool varlen) {
-  if (bf16) return varlen ? reinterpret_cast<void*>(&rec_kernel<H, NCW, true, true>)
-                          : reinterpret_cast<void*>(&rec_kernel<H, NCW, true, false>);
-  return varlen ? reinterpret_cast<void*>(&rec_kernel<H, NCW, false, true>)
-                : reinterpret_cast<void*>(&rec_kernel<H, NCW, false, false>);
+  if (bf16) return varlen ? reinterpret_cast<void*>(&rec_kernel<H, NCW, true, true, NT>)
+                          : reinterpret_cast<void*>(&rec_kernel<H, NCW, true, false, NT>);
+  return varlen ? reinterpret_cast<void*>(&rec_kernel<H, NCW, false, true, NT>)
+                : reinterpret_cast<void*>(&rec_kernel<H, NCW, false, false, NT>);
 }
 // Hidden sizes of the recurrence: multiples of 64 up to 512 (C = H / 32 CTAs per cluster,
-// 2..16).  The 4-warp variant (PLSTM_TCL_WARPS=4) exists for 128 / 256 / 512 only.
-void* pick_rec(int H, bool bf16, bool varlen) {
+// 2..16).  The 4-warp variant (PLSTM_TCL_WARPS=4) exists for 128 / 256 / 512 with 64-row
+// tiles only; 80-row tiles exist for H >= 384 (C >= 12: the sizes whose clusters run out).
+bool rec_nt80(int H) { return H >= 384 && H <= 512 && H % 64 == 0; }
+void* pick_rec(int H, bool bf16, bool varlen, int nt) {
+  if (nt == 80) {
+    switch (H) {
+      case 384: return rec_ptr<384, 8, 80>(bf16, varlen);
+      case 448: return rec_ptr<448, 8, 80>(bf16, varlen);
+      case 512: return rec_ptr<512, 8, 80>(bf16, varlen);
+      default: return nullptr;
+    }
+  }
   if (rec_warps() == 4 && (H == 128 || H == 256 || H == 512))
-    return H == 128 ? rec_ptr<128, 4>(bf16, varlen) : H == 256 ? rec_ptr<256, 4>(bf16, varlen)
-                                                        : rec_ptr<512, 4>(bf16, varlen);
+    return H == 128 ? rec_ptr<128, 4, 64>(bf16, varlen) : H == 256 ? rec_ptr<256, 4, 64>(bf16, varlen)
+                                                            : rec_ptr<512, 4, 64>(bf16, varlen);
   switch (H) {
-    case 64: return rec_ptr<64, 8>(bf16, varlen);
-    case 128: return rec_ptr<128, 8>(bf16, varlen);
-    case 192: return rec_ptr<192, 8>(bf16, varlen);
-    case 256: return rec_ptr<256, 8>(bf16, varlen);
-    case 320: return rec_ptr<320, 8>(bf16, varlen);
-    case 384: return rec_ptr<384, 8>(bf16, varlen);
-    case 448: return rec_ptr<448, 8>(bf16, varlen);
-    case 512: return rec_ptr<512, 8>(bf16, varlen);
+    case 64: return rec_ptr<64, 8, 64>(bf16, varlen);
+    case 128: return rec_ptr<128, 8, 64>(bf16, varlen);
+    case 192: return rec_ptr<192, 8, 64>(bf16, varlen);
+    case 256: return rec_ptr<256, 8, 64>(bf16, varlen);
+    case 320: return rec_ptr<320, 8, 64>(bf16, varlen);
+    case 384: return rec_ptr<384, 8, 64>(bf16, varlen);
+    case 448: return rec_ptr<448, 8, 64>(bf16, varlen);
+    case 512: return rec_ptr<512, 8, 64>(bf16, varlen);
     default: return nullptr;
   }
 }
-int rec_smem(int H) {
+int rec_smem(int H, int nt) {
+  if (nt == 80) return H == 384 ? RecSmem<384, 8, 80>::kDyn : H == 448 ? RecSmem<448, 8, 80>::kDyn
+                                                                       : RecSmem<512, 8, 80>::kDyn;
   switch (H) {
-    case 64: return RecSmem<64, 8>::kDyn;
-    case 128: return RecSmem<128, 8>::kDyn;
-    case 192: return RecSmem<192, 8>::kDyn;
-    case 256: return RecSmem<256, 8>::kDyn;
-    case 320: return RecSmem<320, 8>::kDyn;
-    case 384: return RecSmem<384, 8>::kDyn;
-    case 448: return RecSmem<448, 8>::kDyn;
-    default: return RecSmem<512, 8>::kDyn;
+    case 64: return RecSmem<64, 8, 64>::kDyn;
+    case 128: return RecSmem<128, 8, 64>::kDyn;
+    case 192: return RecSmem<192, 8, 64>::kDyn;
+    case 256: return RecSmem<256, 8, 64>::kDyn;
+    case 320: return RecSmem<320, 8, 64>::kDyn;
+    case 384: return RecSmem<384, 8, 64>::kDyn;
+    case 448: return RecSmem<448, 8, 64>::kDyn;
+    default: return RecSmem<512, 8, 64>::kDyn;
   }
 }
 bool rec_hidden_ok(int H) { return H >= 64 && H <= 512 && H % 64 == 0; }
-int rec_threads(int H) { return (rec_warps() + 1) * 32; }
+int rec_threads(int H, int nt) { return ((nt == 80 ? 8 : rec_warps()) + 1) * 32; }
 
-cudaError_t config_rec(void* k, int H) {
+cudaError_t config_rec(void* k, int H, int nt) {
   if (k == nullptr) return cudaErrorInvalidDeviceFunction;
-  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, rec_smem(H));
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, rec_smem(H, nt));
   if (e == cudaSuccess && ctas_of(H) > 8) e = cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
   return e;
 }
 
 // Clusters of C CTAs of the recurrence that fit on `device` at once (0 = none); cached.
-int rec_max_clusters(int device, int H) {
+int rec_max_clusters(int device, int H, int nt) {
   static std::mutex mu;
-  static int cache[64][8];
+  static int cache[64][8][2];
   static bool init = false;
   std::lock_guard<std::mutex> g(mu);
   if (!init) {
     for (auto& a : cache)
-      for (auto& c : a) c = -1;
+      for (auto& c : a) c[0] = c[1] = -1;
     init = true;
   }
-  if (device < 0 || device >= 64 || !rec_hidden_ok(H)) return 0;
-  int& slot = cache[device][H / 64 - 1];
+  if (device < 0 || device >= 64 || !rec_hidden_ok(H) || (nt == 80 && !rec_nt80(H))) return 0;
+  int& slot = cache[device][H / 64 - 1][nt == 80 ? 1 : 0];
   if (slot >= 0) return slot;
-  void* k = pick_rec(H, false, false);
+  void* k = pick_rec(H, false, false, nt);
   int n = 0;
-  if (config_rec(k, H) == cudaSuccess) {
+  if (config_rec(k, H, nt) == cudaSuccess) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(ctas_of(H) * 16), 1, 1);
-    cfg.blockDim = dim3((unsigned)rec_threads(H), 1, 1);
-    cfg.dynamicSmemBytes = rec_smem(H);
+    cfg.blockDim = dim3((unsigned)rec_threads(H, nt), 1, 1);
+    cfg.dynamicSmemBytes = rec_smem(H, nt);
     cudaLaunchAttribute attr;
     attr.id = cudaLaunchAttributeClusterDimension;
     attr.val.clusterDim.x = ctas_of(H);
@@ -1051,12 +1092,23 @@ int rec_max_clusters(int device, int H) {
   return n;
 }
 
-template <int KP, bool BF16, bool XIN>
+// Tile rows of a forward: 64, or 80 when 64-row tiles need more clusters than fit at
+// once and 80-row tiles do not (B = 512 at H = 384..512: 8 tiles of 64 but 7 clusters).
+int choose_nt(const Problem& q) {
+  if (!rec_nt80(q.H)) return 64;
+  const int m64 = rec_max_clusters(q.device, q.H, 64), m80 = rec_max_clusters(q.device, q.H, 80);
+  const int t64 = (q.B + 63) / 64, t80 = (q.B + 79) / 80;
+  if (m64 >= 1 && m80 >= 1 && t64 > m64 && (t80 + m80 - 1) / m80 < (t64 + m64 - 1) / m64) return 80;
+  return 64;
+}
+
+template <int KP, bool BF16, bool XIN, int NT>
 int32_t launch_proj(const GemmArgs& ga, int sms, cudaStream_t s);
 // Projection of layer 0 (K = kx, the packed x tile).
+template <int NT>
 int32_t launch_proj_x(const GemmArgs& ga, int kx, bool bf16, int sms, cudaStream_t s) {
 #define PLSTM_TCL_PROJX(KX) \
-  case KX: return bf16 ? launch_proj<KX, true, true>(ga, sms, s) : launch_proj<KX, false, true>(ga, sms, s);
+  case KX: return bf16 ? launch_proj<KX, true, true, NT>(ga, sms, s) : launch_proj<KX, false, true, NT>(ga, sms, s);
   switch (kx) {
     PLSTM_TCL_PROJX(16) PLSTM_TCL_PROJX(32) PLSTM_TCL_PROJX(48) PLSTM_TCL_PROJX(64)
     PLSTM_TCL_PROJX(80) PLSTM_TCL_PROJX(96) PLSTM_TCL_PROJX(112) PLSTM_TCL_PROJX(128)
@@ -1067,9 +1119,9 @@ int32_t launch_proj_x(const GemmArgs& ga, int kx, bool bf16, int sms, cudaStream
   return PLSTM_ENOTSUP;
 }
 // Projection of a layer >= 1 (K = H).
-int32_t launch_proj_h(const GemmArgs& ga, bool bf16, int sms, cudaStream_t s) {
+int32_t launch_proj_h64(const GemmArgs& ga, bool bf16, int sms, cudaStream_t s) {
 #define PLSTM_TCL_PROJ(HH) \
-  case HH: return bf16 ? launch_proj<HH, true, false>(ga, sms, s) : launch_proj<HH, false, false>(ga, sms, s);
+  case HH: return bf16 ? launch_proj<HH, true, false, 64>(ga, sms, s) : launch_proj<HH, false, false, 64>(ga, sms, s);
   switch (ga.H) {
     PLSTM_TCL_PROJ(64) PLSTM_TCL_PROJ(128) PLSTM_TCL_PROJ(192) PLSTM_TCL_PROJ(256)
     PLSTM_TCL_PROJ(320) PLSTM_TCL_PROJ(384) PLSTM_TCL_PROJ(448) PLSTM_TCL_PROJ(512)
@@ -1079,15 +1131,26 @@ int32_t launch_proj_h(const GemmArgs& ga, bool bf16, int sms, cudaStream_t s) {
   set_error("no projection kernel for this hidden size");
   return PLSTM_ENOTSUP;
 }
+int32_t launch_proj_h80(const GemmArgs& ga, bool bf16, int sms, cudaStream_t s) {
+#define PLSTM_TCL_PROJ(HH) \
+  case HH: return bf16 ? launch_proj<HH, true, false, 80>(ga, sms, s) : launch_proj<HH, false, false, 80>(ga, sms, s);
+  switch (ga.H) {
+    PLSTM_TCL_PROJ(384) PLSTM_TCL_PROJ(448) PLSTM_TCL_PROJ(512)
+    default: break;
+  }
+#undef PLSTM_TCL_PROJ
+  set_error("no projection kernel for this hidden size");
+  return PLSTM_ENOTSUP;
+}
 
-template <int KP, bool BF16, bool XIN>
+template <int KP, bool BF16, bool XIN, int NT>
 int32_t launch_proj(const GemmArgs& ga, int sms, cudaStream_t s) {
-  auto k = proj_kernel<KP, BF16, XIN>;
-  PLSTM_TRY_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmSmem<KP, XIN>::kDyn));
+  auto k = proj_kernel<KP, BF16, XIN, NT>;
+  PLSTM_TRY_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmSmem<KP, XIN, NT>::kDyn));
   const int C = ctas_of(ga.H);
   const long long jobs = (long long)ga.T * ga.tiles * C;
   const int grid = (int)std::max<long long>(C, std::min<long long>((sms / C) * C, jobs));
-  k<<<grid, kGemmThreads, GemmSmem<KP, XIN>::kDyn, s>>>(ga);
+  k<<<grid, kGemmThreads, GemmSmem<KP, XIN, NT>::kDyn, s>>>(ga);
   PLSTM_TRY_CUDA(cudaGetLastError());
   note_launches(1);
   return PLSTM_OK;
@@ -1122,13 +1185,16 @@ bool tcl_supported(const Problem& p, std::string* why) {
     return no("no CUDA device");
   }
   if (major != 10 || minor != 0) return no("device is not sm_100 (B200)");
-  if (rec_max_clusters(dev, tcl_hp(p.H)) < 1) return no("the recurrence's CTA cluster does not fit on this device");
+  if (rec_max_clusters(dev, tcl_hp(p.H), 64) < 1) return no("the recurrence's CTA cluster does not fit on this device");
   return true;
 }
 
 size_t tcl_packed_size(const Problem& p) { return packed_total(tcl_hp(p.H), p.L, p.has_linear() ? p.O : 0); }
 
-size_t tcl_workspace_size(const Problem& p) { return ws_layout(padded(p)).total; }
+size_t tcl_workspace_size(const Problem& p) {
+  const Problem q = padded(p);
+  return ws_layout(q, choose_nt(q)).total;
+}
 
 int32_t tcl_pack(const Problem& p, int ih_layout, int hh_layout, const void* const* w_ih, const void* const* w_hh,
                  const void* const* b_ih, const void* const* b_hh, const void* w_lin, const void* b_lin,
@@ -1167,7 +1233,7 @@ bool tcl_hu_supported(const HuProblem& p) {
     cudaGetLastError();
     return false;
   }
-  return major == 10 && minor == 0 && rec_max_clusters(p.device, p.H) >= 1;
+  return major == 10 && minor == 0 && rec_max_clusters(p.device, p.H, 64) >= 1;
 }
 
 size_t tcl_hu_workspace_size(const HuProblem& p) { return hu_ws(p).total; }
@@ -1205,8 +1271,8 @@ int32_t tcl_hidden_update(const HuProblem& p, const void* gate_proj, const void*
   PLSTM_TRY_CUDA(cudaGetLastError());
   note_launches(2);
 
-  void* rk = pick_rec(H, bf16, false);
-  PLSTM_TRY_CUDA(config_rec(rk, H));
+  void* rk = pick_rec(H, bf16, false, 64);
+  PLSTM_TRY_CUDA(config_rec(rk, H, 64));
   RecArgs ra = {};
   ra.whh = reinterpret_cast<const uint8_t*>(img);
   ra.gates = gates;
@@ -1230,8 +1296,8 @@ int32_t tcl_hidden_update(const HuProblem& p, const void* gate_proj, const void*
   ra.trace_t0 = 0;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(tiles * C), 1, 1);
-  cfg.blockDim = dim3((unsigned)rec_threads(H), 1, 1);
-  cfg.dynamicSmemBytes = rec_smem(H);
+  cfg.blockDim = dim3((unsigned)rec_threads(H, 64), 1, 1);
+  cfg.dynamicSmemBytes = rec_smem(H, 64);
   cfg.stream = s;
   cudaLaunchAttribute attr;
   attr.id = cudaLaunchAttributeClusterDimension;
@@ -1247,7 +1313,7 @@ int32_t tcl_hidden_update(const HuProblem& p, const void* gate_proj, const void*
   note_launches(1);
   if (p.write_seq()) {
     const int smem = kNT * (H + 1) * 4;
-    auto k = bf16 ? seq_out_kernel<true, false> : seq_out_kernel<false, false>;
+    auto k = bf16 ? seq_out_kernel<true, false, 64> : seq_out_kernel<false, false, 64>;
     PLSTM_TRY_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     k<<<p.T * tiles, 256, smem, s>>>(wsb + w.hseq, perm, nullptr, nullptr, nullptr, static_cast<uint16_t*>(out), p.B,
                                      p.T, H, 0, tiles, p.seq_major() ? 1 : 0, H);
@@ -1262,8 +1328,9 @@ int32_t tcl_hidden_update(const HuProblem& p, const void* gate_proj, const void*
 int32_t tcl_forward(const Problem& p, const void* packed, const void* x, const int32_t* lengths, const void* h0,
                     const void* c0, void* out, void* h_n, void* c_n, void* ws, cudaStream_t s) {
   const int H = tcl_hp(p.H), L = p.L, C = ctas_of(H);
-  const int tiles = (p.B + kNT - 1) / kNT;
-  const Ws w = ws_layout(padded(p));
+  const int nt = choose_nt(padded(p));
+  const int tiles = (p.B + nt - 1) / nt;
+  const Ws w = ws_layout(padded(p), nt);
   uint8_t* wsb = static_cast<uint8_t*>(ws);
   const uint8_t* pk = static_cast<const uint8_t*>(packed);
   int32_t* perm = reinterpret_cast<int32_t*>(wsb + w.perm);
@@ -1272,18 +1339,18 @@ int32_t tcl_forward(const Problem& p, const void* packed, const void* x, const i
   const bool varlen = lengths != nullptr;
   const int O = p.has_linear() ? p.O : 0;
   {
-    const int32_t rc = tc_make_perm(p, kNT, tiles, lengths, perm, tile_len, reinterpret_cast<int32_t*>(wsb + w.hist),
+    const int32_t rc = tc_make_perm(p, nt, tiles, lengths, perm, tile_len, reinterpret_cast<int32_t*>(wsb + w.hist),
                                     reinterpret_cast<int32_t*>(wsb + w.sorted), s);
     if (rc != PLSTM_OK) return rc;
   }
   {
-    const int32_t rc = tc_xpack(p, kNT, tiles, x, perm, wsb + w.xp, kx_of(p.I), s);
+    const int32_t rc = tc_xpack(p, nt, tiles, x, perm, wsb + w.xp, kx_of(p.I), s);
     if (rc != PLSTM_OK) return rc;
   }
   int sms = 148;
   PLSTM_TRY_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, p.device));
-  void* rk = pick_rec(H, bf16, varlen);
-  PLSTM_TRY_CUDA(config_rec(rk, H));
+  void* rk = pick_rec(H, bf16, varlen, nt);
+  PLSTM_TRY_CUDA(config_rec(rk, H, nt));
   const bool seq_out = !p.has_linear() || p.out_seq();
   for (int l = 0; l < L; ++l) {
     GemmArgs ga = {};
@@ -1298,9 +1365,9 @@ int32_t tcl_forward(const Problem& p, const void* packed, const void* x, const i
     ga.tiles = tiles;
     int32_t rc;
     if (l == 0)
-      rc = launch_proj_x(ga, kx_of(p.I), bf16, sms, s);
+      rc = nt == 80 ? launch_proj_x<80>(ga, kx_of(p.I), bf16, sms, s) : launch_proj_x<64>(ga, kx_of(p.I), bf16, sms, s);
     else
-      rc = launch_proj_h(ga, bf16, sms, s);
+      rc = nt == 80 ? launch_proj_h80(ga, bf16, sms, s) : launch_proj_h64(ga, bf16, sms, s);
     if (rc != PLSTM_OK) return rc;
 
     RecArgs ra = {};
@@ -1330,8 +1397,8 @@ int32_t tcl_forward(const Problem& p, const void* packed, const void* x, const i
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(tiles * C), 1, 1);
-    cfg.blockDim = dim3((unsigned)rec_threads(H), 1, 1);
-    cfg.dynamicSmemBytes = rec_smem(H);
+    cfg.blockDim = dim3((unsigned)rec_threads(H, nt), 1, 1);
+    cfg.dynamicSmemBytes = rec_smem(H, nt);
     cfg.stream = s;
     cudaLaunchAttribute attr;
     attr.id = cudaLaunchAttributeClusterDimension;
@@ -1358,14 +1425,16 @@ int32_t tcl_forward(const Problem& p, const void* packed, const void* x, const i
       linear_last_kernel<false><<<(n + 255) / 256, 256, 0, s>>>(reinterpret_cast<const uint16_t*>(wsb + w.hlast), wlin,
                                                                 blin, o16, p.B, H, O);
   } else {
-    const int smem = kNT * (H + 1) * 4;
+    const int smem = nt * (H + 1) * 4;
     const int grid = p.T * tiles;
     if (p.has_linear()) {
-      auto k = bf16 ? seq_out_kernel<true, true> : seq_out_kernel<false, true>;
+      auto k = nt == 80 ? (bf16 ? seq_out_kernel<true, true, 80> : seq_out_kernel<false, true, 80>)
+                        : (bf16 ? seq_out_kernel<true, true, 64> : seq_out_kernel<false, true, 64>);
       PLSTM_TRY_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
       k<<<grid, 256, smem, s>>>(wsb + w.hseq, perm, lengths, wlin, blin, o16, p.B, p.T, H, O, tiles, 0, p.H);
     } else {
-      auto k = bf16 ? seq_out_kernel<true, false> : seq_out_kernel<false, false>;
+      auto k = nt == 80 ? (bf16 ? seq_out_kernel<true, false, 80> : seq_out_kernel<false, false, 80>)
+                        : (bf16 ? seq_out_kernel<true, false, 64> : seq_out_kernel<false, false, 64>);
       PLSTM_TRY_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
       k<<<grid, 256, smem, s>>>(wsb + w.hseq, perm, lengths, wlin, blin, o16, p.B, p.T, H, 0, tiles, 0, p.H);
     }

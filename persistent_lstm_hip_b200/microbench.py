@@ -7,6 +7,10 @@
         and TFLOP/s over 2*M*N*K.
     python -m persistent_lstm_hip_b200.microbench step [--batch 16 --seq 1000]
         The recurrent wavefront kernel on one cluster: per-step latency floor.
+    python -m persistent_lstm_hip_b200.microbench forward [--hidden 512 --layers 4 --batch 512
+            --seq 1000 --input 5 --dtype bf16 --out last]
+        One whole forward (lstm_linear_forward's packed call, PyTorch-default weights,
+        N(0, 1) x) of any shape: configs 3 and 4, the generic shapes, the [B,T,O] mode.
 """
 from __future__ import annotations
 
@@ -75,6 +79,28 @@ def step(args) -> dict:
             "us_per_step": k_ms * 1e3 / (args.seq + 4)}
 
 
+def forward(args) -> dict:
+    from . import core
+
+    dev = torch.device("cuda:0")
+    dt = {"f16": torch.float16, "bf16": torch.bfloat16, "f32": torch.float32}[args.dtype]
+    torch.manual_seed(0)
+    lstm = torch.nn.LSTM(args.input, args.hidden, args.layers, batch_first=True)
+    lin = torch.nn.Linear(args.hidden, 24)
+    h = lambda t: t.detach().to(dev, dt).contiguous()
+    L = args.layers
+    pw = core.PackedWeights([h(getattr(lstm, f"weight_ih_l{l}")) for l in range(L)],
+                            [h(getattr(lstm, f"weight_hh_l{l}")) for l in range(L)],
+                            [h(getattr(lstm, f"bias_ih_l{l}")) for l in range(L)],
+                            [h(getattr(lstm, f"bias_hh_l{l}")) for l in range(L)], h(lin.weight), h(lin.bias),
+                            out_mode=args.out)
+    x = torch.randn(args.batch, args.seq, args.input, generator=torch.Generator().manual_seed(1)).to(dev, dt)
+    ms = _time(lambda: pw.forward(x, need_state=False), args.iters, 2)
+    return {"backend": pw.backend, "hidden": args.hidden, "layers": L, "batch": args.batch, "seq": args.seq,
+            "input": args.input, "dtype": args.dtype, "out": args.out, "ms": ms,
+            "seq_timesteps_per_s": args.batch * args.seq / (ms / 1e3)}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     sub = ap.add_subparsers(dest="cmd", required=True)
@@ -87,8 +113,17 @@ def main() -> None:
     s.add_argument("--batch", type=int, default=16)
     s.add_argument("--seq", type=int, default=1000)
     s.add_argument("--iters", type=int, default=10)
+    f = sub.add_parser("forward")
+    f.add_argument("--hidden", type=int, default=128)
+    f.add_argument("--layers", type=int, default=4)
+    f.add_argument("--batch", type=int, default=512)
+    f.add_argument("--seq", type=int, default=1000)
+    f.add_argument("--input", type=int, default=5)
+    f.add_argument("--dtype", choices=["f16", "bf16", "f32"], default="f16")
+    f.add_argument("--out", choices=["last", "seq", "hseq"], default="last")
+    f.add_argument("--iters", type=int, default=5)
     args = ap.parse_args()
-    print(json.dumps(gemm(args) if args.cmd == "gemm" else step(args)))
+    print(json.dumps({"gemm": gemm, "step": step, "forward": forward}[args.cmd](args)))
 
 
 if __name__ == "__main__":

@@ -171,3 +171,25 @@ def test_tcl_wide_inputs(cuda_device, H, I):
         assert_close16(out, r_out, f"{mode} out")
         assert_close16(h_n, r_h, f"{mode} h_n")
         assert_close16(c_n, r_c, f"{mode} c_n")
+
+
+# Batches whose 64-row tiles need a second wave of 12..16-CTA clusters run 80-row tiles.
+@pytest.mark.parametrize("H", [384, 448, 512])
+def test_tcl_80_row_tiles(cuda_device, H):
+    B, T, I, L, O = 520, 5, 5, 2, 24
+    m = make_model(I, H, L, O, seed=H + 3)
+    w = weights_of(m, L, torch.bfloat16, cuda_device)
+    x = _x(B, T, I, torch.bfloat16, cuda_device, seed=H)
+    g = torch.Generator().manual_seed(H + 1)
+    lens = torch.randint(0, T + 1, (B,), generator=g, dtype=torch.int32)
+    lens[0] = T
+    hx = ((0.5 * torch.randn(L, B, H, generator=g)).to(cuda_device, torch.bfloat16),
+          (0.5 * torch.randn(L, B, H, generator=g)).to(cuda_device, torch.bfloat16))
+    for mode, kw in (("seq", {"lengths": lens.to(cuda_device), "hx": hx}), ("last", {})):
+        pw = core.PackedWeights(*w, out_mode=mode, backend="tc")
+        out, h_n, c_n = pw.forward(x, check=True, **kw)
+        okw = {"lengths": lens, "hx": hx} if kw else {}
+        r_out, r_h, r_c = oracle_of(x, *w, out_mode=mode, **okw)
+        assert_close16(out, r_out, f"{mode} out")
+        assert_close16(h_n, r_h, f"{mode} h_n")
+        assert_close16(c_n, r_c, f"{mode} c_n")

@@ -48,8 +48,9 @@ constexpr int kXK = 16;     // layer-0 input width step (one MMA K step)
 constexpr int kMaxXK = 128; // widest padded layer-0 input
 // Layer-0 input width rounded up to one MMA K step.
 __host__ __device__ inline int kx_of(int I) { return (I + kXK - 1) / kXK * kXK; }
-// Batch rows per cluster tile (N of the recurrent MMAs): 64, or 80 where 64-row tiles
-// would need a second wave of clusters.  The kernels are templated on it (NT) and
+// Batch rows per cluster tile (N of the recurrent MMAs): 64; 32 or 48 for H <= 256 when
+// the batch then still runs in one wave of clusters (more, shorter steps in flight); 80
+// for H >= 384 where 64-row tiles would need a second wave.  The kernels are templated on it (NT) and
 // declare these quantities locally; the constants below are the 64-row defaults.
 constexpr int kNT = 64;
 constexpr int kGRow = kNT + 8;              // gate block row stride in elements (+16 bytes: no bank conflicts)
@@ -1007,9 +1008,24 @@ void* rec_ptr(bool bf16, bool varlen) {
 }
 // Hidden sizes of the recurrence: multiples of 64 up to 512 (C = H / 32 CTAs per cluster,
 // 2..16).  The 4-warp variant (PLSTM_TCL_WARPS=4) exists for 128 / 256 / 512 with 64-row
-// tiles only; 80-row tiles exist for H >= 384 (C >= 12: the sizes whose clusters run out).
+// tiles only; 80-row tiles exist for H >= 384 (C >= 12: the sizes whose clusters run out),
+// 32- and 48-row tiles for H <= 256 (C <= 8).
 bool rec_nt80(int H) { return H >= 384 && H <= 512 && H % 64 == 0; }
+bool rec_nt32(int H) { return H >= 64 && H <= 256 && H % 64 == 0; }
 void* pick_rec(int H, bool bf16, bool varlen, int nt) {
+  if (nt == 32 || nt == 48) {
+    switch (H * 100 + nt) {
+      case 6432: return rec_ptr<64, 8, 32>(bf16, varlen);
+      case 12832: return rec_ptr<128, 8, 32>(bf16, varlen);
+      case 19232: return rec_ptr<192, 8, 32>(bf16, varlen);
+      case 25632: return rec_ptr<256, 8, 32>(bf16, varlen);
+      case 6448: return rec_ptr<64, 8, 48>(bf16, varlen);
+      case 12848: return rec_ptr<128, 8, 48>(bf16, varlen);
+      case 19248: return rec_ptr<192, 8, 48>(bf16, varlen);
+      case 25648: return rec_ptr<256, 8, 48>(bf16, varlen);
+      default: return nullptr;
+    }
+  }
   if (nt == 80) {
     switch (H) {
       case 384: return rec_ptr<384, 8, 80>(bf16, varlen);
@@ -1034,6 +1050,12 @@ void* pick_rec(int H, bool bf16, bool varlen, int nt) {
   }
 }
 int rec_smem(int H, int nt) {
+  if (nt == 32)
+    return H == 64 ? RecSmem<64, 8, 32>::kDyn : H == 128 ? RecSmem<128, 8, 32>::kDyn
+                   : H == 192 ? RecSmem<192, 8, 32>::kDyn : RecSmem<256, 8, 32>::kDyn;
+  if (nt == 48)
+    return H == 64 ? RecSmem<64, 8, 48>::kDyn : H == 128 ? RecSmem<128, 8, 48>::kDyn
+                   : H == 192 ? RecSmem<192, 8, 48>::kDyn : RecSmem<256, 8, 48>::kDyn;
   if (nt == 80) return H == 384 ? RecSmem<384, 8, 80>::kDyn : H == 448 ? RecSmem<448, 8, 80>::kDyn
                                                                        : RecSmem<512, 8, 80>::kDyn;
   switch (H) {
@@ -1048,7 +1070,7 @@ int rec_smem(int H, int nt) {
   }
 }
 bool rec_hidden_ok(int H) { return H >= 64 && H <= 512 && H % 64 == 0; }
-int rec_threads(int H, int nt) { return ((nt == 80 ? 8 : rec_warps()) + 1) * 32; }
+int rec_threads(int H, int nt) { return ((nt != 64 ? 8 : rec_warps()) + 1) * 32; }
 
 cudaError_t config_rec(void* k, int H, int nt) {
   if (k == nullptr) return cudaErrorInvalidDeviceFunction;
@@ -1060,16 +1082,18 @@ cudaError_t config_rec(void* k, int H, int nt) {
 // Clusters of C CTAs of the recurrence that fit on `device` at once (0 = none); cached.
 int rec_max_clusters(int device, int H, int nt) {
   static std::mutex mu;
-  static int cache[64][8][2];
+  static int cache[64][8][4];
   static bool init = false;
   std::lock_guard<std::mutex> g(mu);
   if (!init) {
     for (auto& a : cache)
-      for (auto& c : a) c[0] = c[1] = -1;
+      for (auto& c : a) c[0] = c[1] = c[2] = c[3] = -1;
     init = true;
   }
-  if (device < 0 || device >= 64 || !rec_hidden_ok(H) || (nt == 80 && !rec_nt80(H))) return 0;
-  int& slot = cache[device][H / 64 - 1][nt == 80 ? 1 : 0];
+  if (device < 0 || device >= 64 || !rec_hidden_ok(H) || (nt == 80 && !rec_nt80(H)) ||
+      ((nt == 32 || nt == 48) && !rec_nt32(H)))
+    return 0;
+  int& slot = cache[device][H / 64 - 1][nt == 80 ? 1 : nt == 32 ? 2 : nt == 48 ? 3 : 0];
   if (slot >= 0) return slot;
   void* k = pick_rec(H, false, false, nt);
   int n = 0;
@@ -1092,9 +1116,23 @@ int rec_max_clusters(int device, int H, int nt) {
   return n;
 }
 
-// Tile rows of a forward: 64, or 80 when 64-row tiles need more clusters than fit at
-// once and 80-row tiles do not (B = 512 at H = 384..512: 8 tiles of 64 but 7 clusters).
+// Tile rows of a forward: 32 for H <= 256 when 32-row tiles still fit in one wave of
+// clusters; 80 when 64-row tiles need more clusters than fit at once and 80-row tiles
+// need fewer waves (B = 512 at H = 384..512: 8 tiles of 64 but 7 clusters); else 64.
+// PLSTM_TCL_NT=32|48|64|80 forces a tile height the hidden size has (tests, diagnostics).
 int choose_nt(const Problem& q) {
+  if (const char* e = std::getenv("PLSTM_TCL_NT")) {
+    const int v = std::atoi(e);
+    const bool has = v == 64 || (v == 80 && rec_nt80(q.H)) || ((v == 32 || v == 48) && rec_nt32(q.H));
+    if (has && rec_max_clusters(q.device, q.H, v) >= 1) return v;
+  }
+  if (rec_nt32(q.H)) {
+    for (int nt : {32, 48}) {
+      const int m = rec_max_clusters(q.device, q.H, nt);
+      if (m >= 1 && (q.B + nt - 1) / nt <= m) return nt;
+    }
+    return 64;
+  }
   if (!rec_nt80(q.H)) return 64;
   const int m64 = rec_max_clusters(q.device, q.H, 64), m80 = rec_max_clusters(q.device, q.H, 80);
   const int t64 = (q.B + 63) / 64, t80 = (q.B + 79) / 80;
@@ -1125,6 +1163,18 @@ int32_t launch_proj_h64(const GemmArgs& ga, bool bf16, int sms, cudaStream_t s) 
   switch (ga.H) {
     PLSTM_TCL_PROJ(64) PLSTM_TCL_PROJ(128) PLSTM_TCL_PROJ(192) PLSTM_TCL_PROJ(256)
     PLSTM_TCL_PROJ(320) PLSTM_TCL_PROJ(384) PLSTM_TCL_PROJ(448) PLSTM_TCL_PROJ(512)
+    default: break;
+  }
+#undef PLSTM_TCL_PROJ
+  set_error("no projection kernel for this hidden size");
+  return PLSTM_ENOTSUP;
+}
+template <int NT>
+int32_t launch_proj_hs(const GemmArgs& ga, bool bf16, int sms, cudaStream_t s) {
+#define PLSTM_TCL_PROJ(HH) \
+  case HH: return bf16 ? launch_proj<HH, true, false, NT>(ga, sms, s) : launch_proj<HH, false, false, NT>(ga, sms, s);
+  switch (ga.H) {
+    PLSTM_TCL_PROJ(64) PLSTM_TCL_PROJ(128) PLSTM_TCL_PROJ(192) PLSTM_TCL_PROJ(256)
     default: break;
   }
 #undef PLSTM_TCL_PROJ
@@ -1365,9 +1415,15 @@ int32_t tcl_forward(const Problem& p, const void* packed, const void* x, const i
     ga.tiles = tiles;
     int32_t rc;
     if (l == 0)
-      rc = nt == 80 ? launch_proj_x<80>(ga, kx_of(p.I), bf16, sms, s) : launch_proj_x<64>(ga, kx_of(p.I), bf16, sms, s);
+      rc = nt == 80   ? launch_proj_x<80>(ga, kx_of(p.I), bf16, sms, s)
+           : nt == 32 ? launch_proj_x<32>(ga, kx_of(p.I), bf16, sms, s)
+           : nt == 48 ? launch_proj_x<48>(ga, kx_of(p.I), bf16, sms, s)
+                      : launch_proj_x<64>(ga, kx_of(p.I), bf16, sms, s);
     else
-      rc = nt == 80 ? launch_proj_h80(ga, bf16, sms, s) : launch_proj_h64(ga, bf16, sms, s);
+      rc = nt == 80   ? launch_proj_h80(ga, bf16, sms, s)
+           : nt == 32 ? launch_proj_hs<32>(ga, bf16, sms, s)
+           : nt == 48 ? launch_proj_hs<48>(ga, bf16, sms, s)
+                      : launch_proj_h64(ga, bf16, sms, s);
     if (rc != PLSTM_OK) return rc;
 
     RecArgs ra = {};
@@ -1428,13 +1484,17 @@ int32_t tcl_forward(const Problem& p, const void* packed, const void* x, const i
     const int smem = nt * (H + 1) * 4;
     const int grid = p.T * tiles;
     if (p.has_linear()) {
-      auto k = nt == 80 ? (bf16 ? seq_out_kernel<true, true, 80> : seq_out_kernel<false, true, 80>)
-                        : (bf16 ? seq_out_kernel<true, true, 64> : seq_out_kernel<false, true, 64>);
+      auto k = nt == 80   ? (bf16 ? seq_out_kernel<true, true, 80> : seq_out_kernel<false, true, 80>)
+               : nt == 32 ? (bf16 ? seq_out_kernel<true, true, 32> : seq_out_kernel<false, true, 32>)
+               : nt == 48 ? (bf16 ? seq_out_kernel<true, true, 48> : seq_out_kernel<false, true, 48>)
+                          : (bf16 ? seq_out_kernel<true, true, 64> : seq_out_kernel<false, true, 64>);
       PLSTM_TRY_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
       k<<<grid, 256, smem, s>>>(wsb + w.hseq, perm, lengths, wlin, blin, o16, p.B, p.T, H, O, tiles, 0, p.H);
     } else {
-      auto k = nt == 80 ? (bf16 ? seq_out_kernel<true, false, 80> : seq_out_kernel<false, false, 80>)
-                        : (bf16 ? seq_out_kernel<true, false, 64> : seq_out_kernel<false, false, 64>);
+      auto k = nt == 80   ? (bf16 ? seq_out_kernel<true, false, 80> : seq_out_kernel<false, false, 80>)
+               : nt == 32 ? (bf16 ? seq_out_kernel<true, false, 32> : seq_out_kernel<false, false, 32>)
+               : nt == 48 ? (bf16 ? seq_out_kernel<true, false, 48> : seq_out_kernel<false, false, 48>)
+                          : (bf16 ? seq_out_kernel<true, false, 64> : seq_out_kernel<false, false, 64>);
       PLSTM_TRY_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
       k<<<grid, 256, smem, s>>>(wsb + w.hseq, perm, lengths, wlin, blin, o16, p.B, p.T, H, 0, tiles, 0, p.H);
     }

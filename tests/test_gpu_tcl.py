@@ -193,3 +193,26 @@ def test_tcl_80_row_tiles(cuda_device, H):
         assert_close16(out, r_out, f"{mode} out")
         assert_close16(h_n, r_h, f"{mode} h_n")
         assert_close16(c_n, r_c, f"{mode} c_n")
+
+
+# Every tile height (PLSTM_TCL_NT forces one the hidden size has): 32 / 48 / 64 rows for
+# H <= 256, 64 / 80 for H >= 384; the automatic choice is the smallest that runs the batch
+# in one wave of clusters.
+@pytest.mark.parametrize("H, L, nt", [(256, 2, 32), (256, 2, 48), (256, 2, 64), (64, 3, 48), (128, 9, 32),
+                                      (512, 2, 64), (512, 2, 80), (448, 1, 80)])
+def test_tcl_tile_heights(cuda_device, monkeypatch, H, L, nt):
+    monkeypatch.setenv("PLSTM_TCL_NT", str(nt))
+    B, T, I, O = 171, 4, 5, 24
+    m = make_model(I, H, L, O, seed=H + nt)
+    w = weights_of(m, L, torch.float16, cuda_device)
+    x = _x(B, T, I, torch.float16, cuda_device, seed=nt)
+    g = torch.Generator().manual_seed(nt)
+    lens = torch.randint(0, T + 1, (B,), generator=g, dtype=torch.int32)
+    lens[0] = T
+    for mode in ("seq", "last", "hseq"):
+        pw = core.PackedWeights(*w, out_mode=mode, backend="tc")
+        out, h_n, c_n = pw.forward(x, lengths=lens.to(cuda_device), check=True)
+        r_out, r_h, r_c = oracle_of(x, *w, lengths=lens, out_mode=mode)
+        assert_close16(out, r_out, f"{mode} out")
+        assert_close16(h_n, r_h, f"{mode} h_n")
+        assert_close16(c_n, r_c, f"{mode} c_n")

@@ -260,10 +260,13 @@ constexpr int kBStages = 3;
 template <int KP, bool XIN, int NT>
 struct GemmSmem {
   static constexpr int kStage = KP * NT * 2;  // one step's input tile
-  // Input ring: kBStages deep, 2 where three stages do not fit (K = 512 with 80-row tiles).
-  static constexpr int kStages = kBStages * kStage + 4096 <= 232448 ? kBStages : 2;
+  static constexpr int kOut = gblock_of(NT);  // one staged gate block (bulk-stored by the epilogue)
+  // Input ring kBStages deep and two staged output blocks; a 2-deep ring where that does
+  // not fit (K = 512 with 64- or 80-row tiles).
+  static constexpr int kStages = kBStages * kStage + 2 * kOut + 4096 <= 232448 ? kBStages : 2;
   static constexpr int kB = 0;
-  static constexpr int kBias = kB + kStages * kStage;
+  static constexpr int kO = kB + kStages * kStage;
+  static constexpr int kBias = kO + 2 * kOut;
   static constexpr int kBar = kBias + kRows * 4;
   static constexpr int kTmemSlot = kBar + 96;
   static constexpr int kEnd = kBar + 128;
@@ -410,13 +413,31 @@ __global__ void __launch_bounds__(kGemmThreads, 1) proj_kernel(const GemmArgs a)
       __syncwarp();
     }
   } else {
-    // ---------------- epilogue: lane = gate row, columns = the tile's 64 batch rows ----------------
+    // ---------------- epilogue: lane = gate row, columns = the tile's batch rows ----------------
+    // Each job's gate block (128 rows x kGRow, contiguous in global memory) is staged in
+    // shared memory and written with one bulk copy (two staging buffers).
     const int q = warp & 3;
     const int row = 32 * q + lane;
+    // Every epilogue warp runs all `my` iterations and both named barriers of each (after a
+    // timed-out wait it only skips the work), so no warp is left waiting on the others.
+    const bool issuer = warp == 2 && lane == 0;
     const float bv = bias_s[row];
+    bool ok = true;
     for (int k = 0; k < my; ++k) {
       const int db = k & 1;
-      if (!wait_bar(d_full + 8 * db, (k >> 1) & 1, nullptr, kTimeout)) break;
+      uint8_t* ob = sm + S::kO + db * S::kOut;
+      if (k >= 2) {  // staging buffer db was last bulk-stored two jobs ago
+        if (issuer) ptx::bulk_wait_group_read<1>();
+        ptx::named_bar_sync(1, 128);
+      }
+      if (ok && !wait_bar(d_full + 8 * db, (k >> 1) & 1, nullptr, kTimeout)) {
+        ok = false;
+        if (lane == 0) report_status(a.status, PLSTM_ETIMEOUT, 0x7ffd0000);
+      }
+      if (!ok) {
+        ptx::named_bar_sync(1, 128);
+        continue;
+      }
       ptx::tc_fence_after();
       uint32_t v[kNT];
       const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(S::kACols + db * kNT);
@@ -428,7 +449,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) proj_kernel(const GemmArgs a)
       if (lane == 0) ptx::mbar_arrive(d_empty + 8 * db);
       int t, tile;
       job_src(k, &t, &tile);
-      uint4* dst = reinterpret_cast<uint4*>(a.gates + ((((size_t)t * a.tiles + tile) * C + r) * kRows + row) * kGRow);
+      uint4* dst = reinterpret_cast<uint4*>(ob + (size_t)row * kGRow * 2);
 #pragma unroll
       for (int c = 0; c < kNT / 8; ++c) {
         uint4 o;
@@ -438,7 +459,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1) proj_kernel(const GemmArgs a)
         o.w = pack2_bits<BF16>(__uint_as_float(v[8 * c + 6]) + bv, __uint_as_float(v[8 * c + 7]) + bv);
         dst[c] = o;
       }
+      ptx::fence_proxy_async_smem();
+      ptx::named_bar_sync(1, 128);
+      if (issuer && ok) {
+        ptx::bulk_s2g(a.gates + (((size_t)t * a.tiles + tile) * C + r) * kRows * kGRow, ptx::smem_u32(ob),
+                      (uint32_t)S::kOut);
+        ptx::bulk_commit_group();
+      }
     }
+    if (issuer) ptx::bulk_wait_group_all();  // stores complete before the CTA's shared memory goes away
   }
   ptx::tc_fence_before();
   __syncthreads();

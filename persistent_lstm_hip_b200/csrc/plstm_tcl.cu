@@ -51,11 +51,9 @@ __host__ __device__ inline int kx_of(int I) { return (I + kXK - 1) / kXK * kXK; 
 // Batch rows per cluster tile (N of the recurrent MMAs): 64; 32 or 48 for H <= 256 when
 // the batch then still runs in one wave of clusters (more, shorter steps in flight); 80
 // for H >= 384 where 64-row tiles would need a second wave.  The kernels are templated on it (NT) and
-// declare these quantities locally; the constants below are the 64-row defaults.
-constexpr int kNT = 64;
-constexpr int kGRow = kNT + 8;              // gate block row stride in elements (+16 bytes: no bank conflicts)
-constexpr int kGBlock = kRows * kGRow * 2;  // bytes of one (step, tile, CTA) gate block
-constexpr int kPiece = kNT * kU * 2;        // bytes of one CTA's h piece (32 units x 64 rows)
+// declare these quantities locally (PLSTM_TCL_TILE_CONSTANTS).
+// Gate block rows are NT + 8 elements (+16 bytes against bank conflicts); one CTA's h piece
+// is 32 units x NT rows.
 __host__ __device__ constexpr int gblock_of(int nt) { return kRows * (nt + 8) * 2; }
 __host__ __device__ constexpr int piece_of(int nt) { return nt * kU * 2; }
 #define PLSTM_TCL_TILE_CONSTANTS(NT)                                                             \
@@ -935,10 +933,11 @@ __global__ void hu_pack_whh_kernel(const void* w_hh, int dtype, int layout, int 
 // (rows permuted per CTA and pre-scaled like the weights; padding rows zero).  One
 // block per (step, tile, CTA): reads 64 rows x 4 runs of 32 gate values, writes the
 // 128 x 64 block row by row.
-template <bool BF16>
+template <bool BF16, int NT>
 __global__ void hu_gates_kernel(const uint16_t* __restrict__ gp, const uint16_t* __restrict__ bias, int B, int T,
                                 int H, int tiles, int seq_major, uint16_t* __restrict__ gates) {
-  __shared__ float blk[kRows][kNT + 1];
+  PLSTM_TCL_TILE_CONSTANTS(NT);
+  __shared__ float blk[kRows][NT + 1];
   const int C = ctas_of(H);
   const int r = blockIdx.x % C;
   const int ts = blockIdx.x / C;
@@ -967,21 +966,21 @@ __global__ void hu_gates_kernel(const uint16_t* __restrict__ gp, const uint16_t*
 struct HuWs {
   size_t perm, tile_len, whh, gates, hseq, total;
 };
-HuWs hu_ws(const HuProblem& p) {
+HuWs hu_ws(const HuProblem& p, int nt) {
   HuWs w;
-  const int tiles = (p.B + kNT - 1) / kNT;
+  const int tiles = (p.B + nt - 1) / nt;
   const int C = ctas_of(p.H);
   size_t off = kStatusBytes;
   w.perm = off;
-  off = align_up(off + (size_t)tiles * kNT * 4, 256);
+  off = align_up(off + (size_t)tiles * nt * 4, 256);
   w.tile_len = off;
   off = align_up(off + (size_t)tiles * 4, 256);
   w.whh = off;
   off = align_up(off + (size_t)4 * p.H * p.H * 2, 256);
   w.gates = off;
-  off = align_up(off + (size_t)p.T * tiles * C * kGBlock, 256);
+  off = align_up(off + (size_t)p.T * tiles * C * gblock_of(nt), 256);
   w.hseq = off;
-  if (p.write_seq()) off = align_up(off + (size_t)p.T * tiles * C * kPiece, 256);
+  if (p.write_seq()) off = align_up(off + (size_t)p.T * tiles * C * piece_of(nt), 256);
   w.total = off;
   return w;
 }
@@ -1315,13 +1314,26 @@ bool tcl_hu_supported(const HuProblem& p) {
   return major == 10 && minor == 0 && rec_max_clusters(p.device, p.H, 64) >= 1;
 }
 
-size_t tcl_hu_workspace_size(const HuProblem& p) { return hu_ws(p).total; }
+// Tile rows of a hidden update: the forward's choice for the same batch and hidden size.
+int hu_nt(const HuProblem& p) {
+  Problem q = {};
+  q.B = p.B;
+  q.T = p.T;
+  q.H = p.H;
+  q.L = 1;
+  q.dtype = p.dtype;
+  q.device = p.device;
+  return choose_nt(q);
+}
+
+size_t tcl_hu_workspace_size(const HuProblem& p) { return hu_ws(p, hu_nt(p)).total; }
 
 int32_t tcl_hidden_update(const HuProblem& p, const void* gate_proj, const void* w_hh, const void* bias, void* h_state,
                           float* c_state, void* out, void* ws, cudaStream_t s) {
   const int H = p.H, C = ctas_of(H);
-  const int tiles = (p.B + kNT - 1) / kNT;
-  const HuWs w = hu_ws(p);
+  const int nt = hu_nt(p);
+  const int tiles = (p.B + nt - 1) / nt;
+  const HuWs w = hu_ws(p, nt);
   uint8_t* wsb = static_cast<uint8_t*>(ws);
   const bool bf16 = p.dtype == PLSTM_BF16;
   int32_t* perm = reinterpret_cast<int32_t*>(wsb + w.perm);
@@ -1334,7 +1346,7 @@ int32_t tcl_hidden_update(const HuProblem& p, const void* gate_proj, const void*
   pp.dtype = p.dtype;
   pp.device = p.device;
   {
-    const int32_t rc = tc_make_perm(pp, kNT, tiles, nullptr, perm, tile_len, nullptr, nullptr, s);
+    const int32_t rc = tc_make_perm(pp, nt, tiles, nullptr, perm, tile_len, nullptr, nullptr, s);
     if (rc != PLSTM_OK) return rc;
   }
   uint16_t* img = reinterpret_cast<uint16_t*>(wsb + w.whh);
@@ -1343,15 +1355,16 @@ int32_t tcl_hidden_update(const HuProblem& p, const void* gate_proj, const void*
   const uint16_t* gp = static_cast<const uint16_t*>(gate_proj);
   const uint16_t* bp = static_cast<const uint16_t*>(bias);
   uint16_t* gates = reinterpret_cast<uint16_t*>(wsb + w.gates);
-  if (bf16)
-    hu_gates_kernel<true><<<gblocks, 256, 0, s>>>(gp, bp, p.B, p.T, H, tiles, p.seq_major() ? 1 : 0, gates);
-  else
-    hu_gates_kernel<false><<<gblocks, 256, 0, s>>>(gp, bp, p.B, p.T, H, tiles, p.seq_major() ? 1 : 0, gates);
+  auto gk = nt == 80   ? (bf16 ? hu_gates_kernel<true, 80> : hu_gates_kernel<false, 80>)
+            : nt == 48 ? (bf16 ? hu_gates_kernel<true, 48> : hu_gates_kernel<false, 48>)
+            : nt == 32 ? (bf16 ? hu_gates_kernel<true, 32> : hu_gates_kernel<false, 32>)
+                       : (bf16 ? hu_gates_kernel<true, 64> : hu_gates_kernel<false, 64>);
+  gk<<<gblocks, 256, 0, s>>>(gp, bp, p.B, p.T, H, tiles, p.seq_major() ? 1 : 0, gates);
   PLSTM_TRY_CUDA(cudaGetLastError());
   note_launches(2);
 
-  void* rk = pick_rec(H, bf16, false, 64);
-  PLSTM_TRY_CUDA(config_rec(rk, H, 64));
+  void* rk = pick_rec(H, bf16, false, nt);
+  PLSTM_TRY_CUDA(config_rec(rk, H, nt));
   RecArgs ra = {};
   ra.whh = reinterpret_cast<const uint8_t*>(img);
   ra.gates = gates;
@@ -1375,8 +1388,8 @@ int32_t tcl_hidden_update(const HuProblem& p, const void* gate_proj, const void*
   ra.trace_t0 = 0;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(tiles * C), 1, 1);
-  cfg.blockDim = dim3((unsigned)rec_threads(H, 64), 1, 1);
-  cfg.dynamicSmemBytes = rec_smem(H, 64);
+  cfg.blockDim = dim3((unsigned)rec_threads(H, nt), 1, 1);
+  cfg.dynamicSmemBytes = rec_smem(H, nt);
   cfg.stream = s;
   cudaLaunchAttribute attr;
   attr.id = cudaLaunchAttributeClusterDimension;
@@ -1391,8 +1404,11 @@ int32_t tcl_hidden_update(const HuProblem& p, const void* gate_proj, const void*
   profile_end(s);
   note_launches(1);
   if (p.write_seq()) {
-    const int smem = kNT * (H + 1) * 4;
-    auto k = bf16 ? seq_out_kernel<true, false, 64> : seq_out_kernel<false, false, 64>;
+    const int smem = nt * (H + 1) * 4;
+    auto k = nt == 80   ? (bf16 ? seq_out_kernel<true, false, 80> : seq_out_kernel<false, false, 80>)
+             : nt == 48 ? (bf16 ? seq_out_kernel<true, false, 48> : seq_out_kernel<false, false, 48>)
+             : nt == 32 ? (bf16 ? seq_out_kernel<true, false, 32> : seq_out_kernel<false, false, 32>)
+                        : (bf16 ? seq_out_kernel<true, false, 64> : seq_out_kernel<false, false, 64>);
     PLSTM_TRY_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     k<<<p.T * tiles, 256, smem, s>>>(wsb + w.hseq, perm, nullptr, nullptr, nullptr, static_cast<uint16_t*>(out), p.B,
                                      p.T, H, 0, tiles, p.seq_major() ? 1 : 0, H);

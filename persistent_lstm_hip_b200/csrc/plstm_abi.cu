@@ -107,10 +107,11 @@ size_t backend_ws(int backend, const Problem& p) {
 }
 
 // Scratch plstm_forward_packed needs: the backend's, then (PLSTM_FLAG_DEDUPE)
-// the row grouping and the distinct-row copies.
+// the row grouping and the distinct-row copies; a multiple of 256 bytes, so the
+// packed image plstm_forward places after it stays aligned.
 size_t forward_ws(int backend, const Problem& p) {
-  const size_t inner = backend_ws(backend, p);
-  return (p.flags & PLSTM_FLAG_DEDUPE) ? align_up(inner, 256) + dedupe_scratch_size(p) : inner;
+  const size_t inner = align_up(backend_ws(backend, p), 256);
+  return (p.flags & PLSTM_FLAG_DEDUPE) ? align_up(inner + dedupe_scratch_size(p), 256) : inner;
 }
 
 struct BackendCtx {
@@ -231,6 +232,7 @@ static int32_t pack_impl(const plstm_desc* d, int ih_layout, int hh_layout, cons
     PLSTM_CHECK_ARG(b_hh == nullptr, "PLSTM_FLAG_BIAS_SUMMED requires b_hh == NULL");
   if (p.has_linear()) PLSTM_CHECK_ARG(w_lin != nullptr, "w_lin is NULL");
   PLSTM_CHECK_ARG(packed != nullptr, "packed is NULL");
+  PLSTM_CHECK_ARG(aligned16(packed), "packed must be 16-byte aligned");
   int b = 0;
   if ((rc = pick_backend(d, p, &b)) != PLSTM_OK) return rc;
   const size_t need = b == PLSTM_BACKEND_TC ? tc_packed_size(p) : simt_packed_size(p);
@@ -264,6 +266,7 @@ int32_t plstm_forward_packed(const plstm_desc* d, const void* packed, const void
   if (rc != PLSTM_OK) return rc;
   PLSTM_CHECK_ARG(packed != nullptr, "packed is NULL");
   PLSTM_CHECK_ARG(workspace != nullptr, "workspace is NULL");
+  PLSTM_CHECK_ARG(aligned16(packed) && aligned16(workspace), "packed and workspace must be 16-byte aligned");
   PLSTM_CHECK_ARG(p.B == 0 || p.T == 0 || x != nullptr, "x is NULL");
   PLSTM_CHECK_ARG(p.B == 0 || out != nullptr, "out is NULL");
   PLSTM_CHECK_ARG((h0 == nullptr) == (c0 == nullptr), "h0 and c0 must both be given or both be NULL");
@@ -344,6 +347,7 @@ int32_t plstm_unique_rows(const plstm_desc* d, const void* x, const int32_t* len
   PLSTM_CHECK_ARG(p.B == 0 || (row_map != nullptr && unique_index != nullptr), "row_map / unique_index is NULL");
   PLSTM_CHECK_ARG(p.B == 0 || p.T == 0 || x != nullptr, "x is NULL");
   PLSTM_CHECK_ARG((h0 == nullptr) == (c0 == nullptr), "h0 and c0 must both be given or both be NULL");
+  PLSTM_CHECK_ARG(aligned16(workspace), "workspace must be 16-byte aligned");
   const size_t need = unique_rows_scratch_size(p);
   if (workspace == nullptr || workspace_bytes < need) {
     set_error("workspace too small: need " + std::to_string(need) + " bytes");

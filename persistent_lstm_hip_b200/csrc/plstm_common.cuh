@@ -53,6 +53,8 @@ void profile_end(cudaStream_t s);
 constexpr size_t kStatusBytes = 256;
 
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+// Caller buffers are read with 16-byte vector loads and bulk copies.
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 inline size_t dtype_size(int32_t dt) { return dt == PLSTM_F32 ? 4 : 2; }
 

@@ -137,6 +137,7 @@ int32_t plstm_hidden_update(const void* gate_proj, int32_t batch, int32_t seq_le
   PLSTM_CHECK_ARG(w_hh != nullptr && h_state != nullptr && c_state != nullptr && out != nullptr,
                   "plstm_hidden_update: w_hh, h_state, c_state and out must not be NULL");
   PLSTM_CHECK_ARG(seq_len == 0 || batch == 0 || gate_proj != nullptr, "plstm_hidden_update: gate_proj is NULL");
+  PLSTM_CHECK_ARG(aligned16(workspace), "plstm_hidden_update: workspace must be 16-byte aligned");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const size_t es = dtype_size(dtype);
   if (batch == 0) return PLSTM_OK;

@@ -79,6 +79,7 @@ extern "C" int32_t plstm_forward_packed_noalloc(const plstm_desc* d, const void*
   PLSTM_CHECK_ARG(!(d->flags & PLSTM_FLAG_DEDUPE), "PLSTM_FLAG_DEDUPE needs a caller workspace");
   if (!(d->flags & PLSTM_FLAG_NO_LINEAR)) PLSTM_CHECK_ARG(d->output_size > 0, "output_size must be > 0");
   PLSTM_CHECK_ARG(packed != nullptr, "packed is NULL");
+  PLSTM_CHECK_ARG(aligned16(packed), "packed must be 16-byte aligned");
   PLSTM_CHECK_ARG(d->batch == 0 || d->seq_len == 0 || x != nullptr, "x is NULL");
   PLSTM_CHECK_ARG(d->batch == 0 || out != nullptr, "out is NULL");
   PLSTM_CHECK_ARG((h0 == nullptr) == (c0 == nullptr), "h0 and c0 must both be given or both be NULL");

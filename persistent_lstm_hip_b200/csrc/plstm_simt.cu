@@ -104,13 +104,97 @@ __global__ void pack_bias_kernel(const void* a, const void* b, int dtype, int n,
   }
 }
 
-constexpr int kSimtThreads = 256;
+constexpr int kSimtThreads = 512;
+constexpr size_t kSimtSmemMax = 227 * 1024;
+
+// Four consecutive gate rows of one transposed weight row, as f32.
+__device__ __forceinline__ float4 ld_w4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
+__device__ __forceinline__ float4 ld_w4(const __half* p) {
+  const uint2 raw = __ldg(reinterpret_cast<const uint2*>(p));
+  const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
+  const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+  return make_float4(a.x, a.y, b.x, b.y);
+}
+__device__ __forceinline__ float4 ld_w4(const __nv_bfloat16* p) {
+  const uint2 raw = __ldg(reinterpret_cast<const uint2*>(p));
+  const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.x));
+  const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.y));
+  return make_float4(a.x, a.y, b.x, b.y);
+}
+
+template <int NB>
+__device__ __forceinline__ void fma_quad(const float4 w, const float* v, int ld, float (&acc)[NB][4]) {
+#pragma unroll
+  for (int n = 0; n < NB; ++n) {
+    const float x = v[n * ld];
+    acc[n][0] = fmaf(w.x, x, acc[n][0]);
+    acc[n][1] = fmaf(w.y, x, acc[n][1]);
+    acc[n][2] = fmaf(w.z, x, acc[n][2]);
+    acc[n][3] = fmaf(w.w, x, acc[n][3]);
+  }
+}
+
+// acc[n][i] += sum_{k < nk} w[k * G + i] * v[n * ld + k] for the four rows i of one quad, in
+// increasing k.  The contraction is bound by the latency of the L2 weight reads, so each
+// round issues U predicated loads before any of their FMAs.
+template <typename T, int NB>
+__device__ __forceinline__ void quad_dot(const T* __restrict__ w, int G, const float* v, int ld, int nk,
+                                         float (&acc)[NB][4]) {
+  constexpr int U = NB >= 8 ? 8 : 16;
+  for (int k = 0; k < nk; k += U) {
+    float4 wv[U];
+#pragma unroll
+    for (int j = 0; j < U; ++j)
+      wv[j] = k + j < nk ? ld_w4(w + (int64_t)(k + j) * G) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+    for (int j = 0; j < U; ++j)
+      if (k + j < nk) fma_quad<NB>(wv[j], v + k + j, ld, acc);
+  }
+}
+
+// Launch shape of one layer: NB batch rows per CTA, the combined [x_t ; h_{t-1}] contraction
+// split into `ks` k-slices whose partial gate sums are added in slice order.
+struct SimtShape {
+  int nb, ks;
+  size_t smem;
+};
+
+size_t simt_smem(int nb, int ks, int K, int H) {
+  const size_t ldx = align_up((size_t)K + H, 4);
+  return sizeof(float) * nb * (ldx + (size_t)ks * 4 * H + H);
+}
+
+// Fewest batch rows per CTA that keep the grid within one wave of 148 CTAs (the per-step cost
+// of a CTA is set by streaming the layer's weights from L2, not by its row count), then the
+// k-split that best fills whole rounds of kSimtThreads quad-slices with at least 16 k per slice.
+SimtShape simt_shape(int B, int K, int H) {
+  int nb = 1;
+  while (nb < 8 && (B + nb - 1) / nb > 148) nb *= 2;
+  while (nb > 1 && simt_smem(nb, 1, K, H) > kSimtSmemMax) nb /= 2;
+  int best = 1;
+  double best_eff = 0.0;
+  for (int ks = 1; ks <= 8; ++ks) {
+    if (ks > 1 && (K + H) / ks < 16) break;
+    if (simt_smem(nb, ks, K, H) > kSimtSmemMax) break;
+    const int items = ks * H;
+    const int rounds = (items + kSimtThreads - 1) / kSimtThreads;
+    const double eff = (double)items / ((double)rounds * kSimtThreads);
+    if (eff > best_eff + 1e-9) {
+      best_eff = eff;
+      best = ks;
+    }
+  }
+  return {nb, best, simt_smem(nb, best, K, H)};
+}
 
 // One layer, whole sequence, NB batch rows per CTA.
 // xin: layer input [B][T][K] (activation type T).  seq_out[b * out_sb + t * out_st + u].
 // gin: optional precomputed input projection added to the gates, gin[b * gin_sb + t * gin_st + r]
 // (the hidden-update entry point runs with K = 0 and gin set).
 // hfin/cfin: final state of this layer [B][H] (T / f32).
+// Each step a work item (quad q, slice s) accumulates gate rows 4q..4q+3 over the slice's k range
+// of [x_t ; h_{t-1}], reading each transposed weight row as one vector; the gate phase adds
+// bias, gin and the slices' partial sums in that order.
 template <typename T, int NB>
 __global__ void __launch_bounds__(kSimtThreads)
     simt_layer_kernel(const T* __restrict__ xin, int K, const T* __restrict__ wih_t,
@@ -118,16 +202,19 @@ __global__ void __launch_bounds__(kSimtThreads)
                       const int32_t* __restrict__ lengths, const T* __restrict__ h0,
                       const T* __restrict__ c0, T* __restrict__ seq_out, T* __restrict__ hfin,
                       float* __restrict__ cfin, int B, int Tn, int H, const T* __restrict__ gin,
-                      int64_t gin_sb, int64_t gin_st, int64_t out_sb, int64_t out_st) {
-  extern __shared__ float smem[];
+                      int64_t gin_sb, int64_t gin_st, int64_t out_sb, int64_t out_st, int ks_n) {
+  extern __shared__ float4 smem4[];
+  float* smem = reinterpret_cast<float*>(smem4);
   const int G = 4 * H;
   const int KH = K + H;
-  float* xh = smem;                 // [NB][K + H]: x_t then h_{t-1}
-  float* gates = xh + NB * KH;      // [NB][4H]
-  float* cst = gates + NB * G;      // [NB][H]
+  const int ldx = (KH + 3) & ~3;
+  float* xh = smem;                        // [NB][ldx]: x_t then h_{t-1}
+  float* part = xh + NB * ldx;             // [ks_n][NB][4H] partial gate sums
+  float* cst = part + (size_t)ks_n * NB * G;  // [NB][H]
   __shared__ int lens[NB];
   const int b0 = blockIdx.x * NB;
   const int tid = threadIdx.x;
+  const int chunk = ((KH + ks_n - 1) / ks_n + 3) & ~3;
 
   if (tid < NB) {
     const int b = b0 + tid;
@@ -142,7 +229,7 @@ __global__ void __launch_bounds__(kSimtThreads)
       if (h0 != nullptr) hv = to_f32(h0[(int64_t)b * H + u]);
       if (c0 != nullptr) cv = to_f32(c0[(int64_t)b * H + u]);
     }
-    xh[n * KH + K + u] = hv;
+    xh[n * ldx + K + u] = hv;
     cst[i] = cv;
   }
   __syncthreads();
@@ -153,73 +240,44 @@ __global__ void __launch_bounds__(kSimtThreads)
   for (int t = 0; t < tmax; ++t) {
     for (int i = tid; i < NB * K; i += blockDim.x) {
       const int n = i / K, k = i % K, b = b0 + n;
-      xh[n * KH + k] = (b < B) ? to_f32(xin[((int64_t)b * Tn + t) * K + k]) : 0.0f;
+      xh[n * ldx + k] = (b < B) ? to_f32(xin[((int64_t)b * Tn + t) * K + k]) : 0.0f;
     }
     __syncthreads();
-    for (int r = tid; r < G; r += blockDim.x) {
-      float acc[NB];
-      const float bv = bias != nullptr ? bias[r] : 0.0f;
+    for (int item = tid; item < ks_n * H; item += blockDim.x) {
+      const int q = item % H, s = item / H;
+      const int k0 = s * chunk, k1 = min(KH, k0 + chunk);
+      float acc[NB][4];
 #pragma unroll
-      for (int n = 0; n < NB; ++n) {
-        acc[n] = bv;
-        if (gin != nullptr && b0 + n < B) acc[n] += to_f32(gin[(int64_t)(b0 + n) * gin_sb + (int64_t)t * gin_st + r]);
-      }
-      int k = 0;
-      for (; k + 4 <= K; k += 4) {
-        const float w0 = to_f32(wih_t[(int64_t)(k + 0) * G + r]);
-        const float w1 = to_f32(wih_t[(int64_t)(k + 1) * G + r]);
-        const float w2 = to_f32(wih_t[(int64_t)(k + 2) * G + r]);
-        const float w3 = to_f32(wih_t[(int64_t)(k + 3) * G + r]);
+      for (int n = 0; n < NB; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.0f;
+      if (k0 < K) quad_dot<T, NB>(wih_t + (int64_t)k0 * G + 4 * q, G, xh + k0, ldx, min(k1, K) - k0, acc);
+      const int j0 = max(k0, K);
+      if (j0 < k1) quad_dot<T, NB>(whh_t + (int64_t)(j0 - K) * G + 4 * q, G, xh + j0, ldx, k1 - j0, acc);
 #pragma unroll
-        for (int n = 0; n < NB; ++n) {
-          const float* v = xh + n * KH + k;
-          acc[n] = fmaf(w0, v[0], acc[n]);
-          acc[n] = fmaf(w1, v[1], acc[n]);
-          acc[n] = fmaf(w2, v[2], acc[n]);
-          acc[n] = fmaf(w3, v[3], acc[n]);
-        }
-      }
-      for (; k < K; ++k) {
-        const float w = to_f32(wih_t[(int64_t)k * G + r]);
-#pragma unroll
-        for (int n = 0; n < NB; ++n) acc[n] = fmaf(w, xh[n * KH + k], acc[n]);
-      }
-      int j = 0;
-      for (; j + 4 <= H; j += 4) {
-        const float w0 = to_f32(whh_t[(int64_t)(j + 0) * G + r]);
-        const float w1 = to_f32(whh_t[(int64_t)(j + 1) * G + r]);
-        const float w2 = to_f32(whh_t[(int64_t)(j + 2) * G + r]);
-        const float w3 = to_f32(whh_t[(int64_t)(j + 3) * G + r]);
-#pragma unroll
-        for (int n = 0; n < NB; ++n) {
-          const float* v = xh + n * KH + K + j;
-          acc[n] = fmaf(w0, v[0], acc[n]);
-          acc[n] = fmaf(w1, v[1], acc[n]);
-          acc[n] = fmaf(w2, v[2], acc[n]);
-          acc[n] = fmaf(w3, v[3], acc[n]);
-        }
-      }
-      for (; j < H; ++j) {
-        const float w = to_f32(whh_t[(int64_t)j * G + r]);
-#pragma unroll
-        for (int n = 0; n < NB; ++n) acc[n] = fmaf(w, xh[n * KH + K + j], acc[n]);
-      }
-#pragma unroll
-      for (int n = 0; n < NB; ++n) gates[n * G + r] = acc[n];
+      for (int n = 0; n < NB; ++n)
+        *reinterpret_cast<float4*>(part + ((size_t)s * NB + n) * G + 4 * q) =
+            make_float4(acc[n][0], acc[n][1], acc[n][2], acc[n][3]);
     }
     __syncthreads();
     for (int i = tid; i < NB * H; i += blockDim.x) {
       const int n = i / H, u = i % H, b = b0 + n;
-      const float* g = gates + n * G;
       if (t < lens[n]) {
-        const float ig = sigmoid_acc(g[u]);
-        const float fg = sigmoid_acc(g[H + u]);
-        const float gg = tanh_acc(g[2 * H + u]);
-        const float og = sigmoid_acc(g[3 * H + u]);
+        float g[4];
+#pragma unroll
+        for (int gi = 0; gi < 4; ++gi) {
+          const int r = gi * H + u;
+          float v = bias != nullptr ? bias[r] : 0.0f;
+          if (gin != nullptr) v += to_f32(gin[(int64_t)b * gin_sb + (int64_t)t * gin_st + r]);
+          for (int s = 0; s < ks_n; ++s) v += part[((size_t)s * NB + n) * G + r];
+          g[gi] = v;
+        }
+        const float ig = sigmoid_acc(g[0]);
+        const float fg = sigmoid_acc(g[1]);
+        const float gg = tanh_acc(g[2]);
+        const float og = sigmoid_acc(g[3]);
         const float c = fg * cst[i] + ig * gg;
         cst[i] = c;
         const T hq = from_f32<T>(og * tanh_acc(c));  // h is kept in the activation type
-        xh[n * KH + K + u] = to_f32(hq);
+        xh[n * ldx + K + u] = to_f32(hq);
         seq_out[(int64_t)b * out_sb + (int64_t)t * out_st + u] = hq;
       } else if (b < B) {
         seq_out[(int64_t)b * out_sb + (int64_t)t * out_st + u] = from_f32<T>(0.0f);
@@ -238,10 +296,33 @@ __global__ void __launch_bounds__(kSimtThreads)
   for (int i = tid; i < NB * H; i += blockDim.x) {
     const int n = i / H, u = i % H, b = b0 + n;
     if (b < B) {
-      hfin[(int64_t)b * H + u] = from_f32<T>(xh[n * KH + K + u]);
+      hfin[(int64_t)b * H + u] = from_f32<T>(xh[n * ldx + K + u]);
       cfin[(int64_t)b * H + u] = cst[i];
     }
   }
+}
+
+// Launches simt_layer_kernel with the shape simt_shape picks.
+template <typename T>
+int32_t launch_simt_layer(const T* xin, int K, const T* wih_t, const T* whh_t, const float* bias,
+                          const int32_t* lengths, const T* h0, const T* c0, T* seq_out, T* hfin, float* cfin,
+                          int B, int Tn, int H, const T* gin, int64_t gin_sb, int64_t gin_st, int64_t out_sb,
+                          int64_t out_st, cudaStream_t s) {
+  const SimtShape sh = simt_shape(B, K, H);
+  if (sh.smem > kSimtSmemMax) {
+    set_error("hidden size too large for the FFMA backend's shared-memory tile");
+    return PLSTM_ENOTSUP;
+  }
+  auto kern = simt_layer_kernel<T, 1>;
+  if (sh.nb == 2) kern = simt_layer_kernel<T, 2>;
+  if (sh.nb == 4) kern = simt_layer_kernel<T, 4>;
+  if (sh.nb == 8) kern = simt_layer_kernel<T, 8>;
+  PLSTM_TRY_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sh.smem));
+  kern<<<(B + sh.nb - 1) / sh.nb, kSimtThreads, sh.smem, s>>>(xin, K, wih_t, whh_t, bias, lengths, h0, c0,
+                                                              seq_out, hfin, cfin, B, Tn, H, gin, gin_sb, gin_st,
+                                                              out_sb, out_st, sh.ks);
+  PLSTM_TRY_CUDA(cudaGetLastError());
+  return PLSTM_OK;
 }
 
 // out[b][t][o] (SEQ) or out[b][o] (LAST) = b_lin[o] + W_lin[o] . h, zero past each length (SEQ).
@@ -301,25 +382,19 @@ int32_t simt_forward_t(const Problem& p, const void* packed, const void* x, cons
   T* seq[2] = {reinterpret_cast<T*>(wsb + w.seq[0]), reinterpret_cast<T*>(wsb + w.seq[1])};
   T* hfin = reinterpret_cast<T*>(wsb + w.hfin);
   float* cfin = reinterpret_cast<float*>(wsb + w.cfin);
-  constexpr int NB = 4;
-  const int grid = (p.B + NB - 1) / NB;
   const T* layer_in = static_cast<const T*>(x);
   int K = p.I;
   for (int l = 0; l < p.L; ++l) {
     const bool last = l == p.L - 1;
     T* dst = (last && !p.has_linear()) ? static_cast<T*>(out) : seq[l & 1];
-    const size_t smem = sizeof(float) * NB * ((size_t)(K + p.H) + 4 * (size_t)p.H + p.H);
-    auto kern = simt_layer_kernel<T, NB>;
-    PLSTM_TRY_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     const T* h0l = h0 ? static_cast<const T*>(h0) + (size_t)l * p.B * p.H : nullptr;
     const T* c0l = c0 ? static_cast<const T*>(c0) + (size_t)l * p.B * p.H : nullptr;
     if (l == 0) profile_begin(s);
-    kern<<<grid, kSimtThreads, smem, s>>>(
-        layer_in, K, reinterpret_cast<const T*>(pk + lo.wih[l]),
-        reinterpret_cast<const T*>(pk + lo.whh[l]), reinterpret_cast<const float*>(pk + lo.bias[l]),
-        lengths, h0l, c0l, dst, hfin + (size_t)l * p.B * p.H, cfin + (size_t)l * p.B * p.H, p.B,
-        p.T, p.H, nullptr, 0, 0, (int64_t)p.T * p.H, p.H);
-    PLSTM_TRY_CUDA(cudaGetLastError());
+    const int32_t rc = launch_simt_layer<T>(
+        layer_in, K, reinterpret_cast<const T*>(pk + lo.wih[l]), reinterpret_cast<const T*>(pk + lo.whh[l]),
+        reinterpret_cast<const float*>(pk + lo.bias[l]), lengths, h0l, c0l, dst, hfin + (size_t)l * p.B * p.H,
+        cfin + (size_t)l * p.B * p.H, p.B, p.T, p.H, nullptr, 0, 0, (int64_t)p.T * p.H, p.H, s);
+    if (rc != PLSTM_OK) return rc;
     note_launches(1);
     if (l == p.L - 1) profile_end(s);
     layer_in = dst;
@@ -380,16 +455,12 @@ int32_t simt_hu_t(const HuProblem& p, const void* gate_proj, const void* w_hh, c
   const int64_t out_st = (p.write_seq() && sm) ? (int64_t)p.B * p.H : p.H;
   const int64_t gin_sb = sm ? G : (int64_t)p.T * G;
   const int64_t gin_st = sm ? (int64_t)p.B * G : G;
-  constexpr int NB = 4;
-  const size_t smem = sizeof(float) * NB * ((size_t)p.H + 4 * (size_t)p.H + p.H);
-  auto kern = simt_layer_kernel<T, NB>;
-  PLSTM_TRY_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   profile_begin(s);
-  kern<<<(p.B + NB - 1) / NB, kSimtThreads, smem, s>>>(
+  const int32_t rc = launch_simt_layer<T>(
       nullptr, 0, nullptr, reinterpret_cast<const T*>(wsb + w.whh), reinterpret_cast<const float*>(wsb + w.bias),
       nullptr, nullptr, nullptr, seq, static_cast<T*>(h_state), c_state, p.B, p.T, p.H,
-      static_cast<const T*>(gate_proj), gin_sb, gin_st, out_sb, out_st);
-  PLSTM_TRY_CUDA(cudaGetLastError());
+      static_cast<const T*>(gate_proj), gin_sb, gin_st, out_sb, out_st, s);
+  if (rc != PLSTM_OK) return rc;
   profile_end(s);
   note_launches(1);
   if (!p.write_seq())

@@ -82,6 +82,20 @@ def test_forward_rejects_null_and_small_workspace():
     assert rc == _lib.EWORKSPACE
 
 
+def test_forward_rejects_unaligned_buffers():
+    # Packed images and workspaces are read with 16-byte vector loads and bulk copies; a
+    # misaligned pointer is refused on the host before any launch (no pointer is dereferenced).
+    lib = _lib.load()
+    d = _desc()
+    for packed, ws in ((24, 16), (16, 8), (1040, 1028)):
+        rc = lib.plstm_forward_packed(ctypes.byref(d), packed, 16, None, None, None, 16, None, None, ws, 1 << 30,
+                                      None)
+        assert rc == _lib.EINVAL and "16-byte aligned" in _lib.last_error()
+    ptrs = (ctypes.c_void_p * 2)(16, 16)
+    rc = lib.plstm_pack(ctypes.byref(d), ptrs, ptrs, None, None, 16, None, 24, 1 << 30, None)
+    assert rc == _lib.EINVAL and "16-byte aligned" in _lib.last_error()
+
+
 def test_tc_backend_refused_without_b200():
     # Forcing the tensor-core backend on a host without an sm_100 device is ENOTSUP, not a fallback.
     import torch

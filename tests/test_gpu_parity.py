@@ -94,6 +94,40 @@ def test_simt_16bit_other_hidden_sizes(cuda_device, H, L):
         assert_close16(h_n, r_h, f"{dt} h_n")
 
 
+# The FFMA layer kernel's launch shapes: 1, 2, 4 or 8 batch rows per CTA (by B), the
+# [x ; h] contraction split into 1..8 k-slices (by H and K), H above the thread count,
+# odd and wide inputs.
+@pytest.mark.parametrize("B, T, I, H, L", [(600, 6, 3, 24, 2), (300, 7, 5, 40, 2), (200, 5, 7, 300, 2),
+                                           (9, 8, 130, 100, 3), (150, 10, 1, 72, 2)])
+def test_simt_f32_launch_shapes(cuda_device, B, T, I, H, L):
+    O = 3
+    m = make_model(I, H, L, O, seed=5)
+    w = weights_of(m, L, torch.float32, cuda_device)
+    x = _rand_x(B, T, I, torch.float32, cuda_device, seed=6)
+    lens = _rand_lengths(B, T, seed=7)
+    g = torch.Generator().manual_seed(8)
+    h0 = (0.5 * torch.randn(L, B, H, generator=g)).to(cuda_device)
+    c0 = (0.5 * torch.randn(L, B, H, generator=g)).to(cuda_device)
+    for mode in ("seq", "hseq"):
+        out, h_n, c_n = plstm.lstm_linear_forward(x, *w, lengths=lens, hx=(h0, c0), out_mode=mode, check=True)
+        r_out, r_h, r_c = oracle_of(x, *w, lengths=lens, hx=(h0, c0), out_mode=mode)
+        assert_close32(out, r_out, f"{mode} out")
+        assert_close32(h_n, r_h, "h_n")
+        assert_close32(c_n, r_c, "c_n")
+
+
+def test_simt_16bit_beyond_tensor_core_hidden(cuda_device):
+    B, T, I, H, L, O = 3, 4, 5, 640, 2, 6
+    m = make_model(I, H, L, O, seed=9)
+    for dt in (torch.float16, torch.bfloat16):
+        w = weights_of(m, L, dt, cuda_device)
+        x = _rand_x(B, T, I, dt, cuda_device, seed=10)
+        out, h_n, c_n = plstm.lstm_linear_forward(x, *w, out_mode="seq", check=True)
+        r_out, r_h, r_c = oracle_of(x, *w, out_mode="seq")
+        assert_close16(out, r_out, f"{dt} out")
+        assert_close16(c_n, r_c, f"{dt} c_n")
+
+
 # ---------------------------------------------------------------------------------------
 TC_SHAPES = [(1, 1, 1), (3, 7, 2), (17, 33, 4), (40, 9, 3), (70, 20, 4)]
 

@@ -10,8 +10,8 @@
 // consecutive gate rows.
 //
 // Packed image (all offsets 256-byte aligned), per layer l:
-//   wih_t[l]  [K_l][4H]  activation type   (K_0 = I, K_l = H)
-//   whh_t[l]  [H][4H]    activation type
+//   wih_t[l]  [K4_l][4H] activation type   (K_0 = I, K_l = H; K4 = K rounded up to 4, pad rows zero)
+//   whh_t[l]  [H4][4H]   activation type   (H4 = H rounded up to 4, pad rows zero)
 //   bias[l]   [4H]       f32, b_ih + b_hh summed in f32
 // then W_lin [O][H] (activation type) and b_lin [O] (f32).
 #include <algorithm>
@@ -35,9 +35,9 @@ SimtLayout simt_layout(const Problem& p) {
   for (int l = 0; l < p.L; ++l) {
     const size_t K = l == 0 ? p.I : p.H;
     lo.wih.push_back(off);
-    off = align_up(off + K * G * es, 256);
+    off = align_up(off + align_up(K, 4) * G * es, 256);
     lo.whh.push_back(off);
-    off = align_up(off + (size_t)p.H * G * es, 256);
+    off = align_up(off + align_up(p.H, 4) * G * es, 256);
     lo.bias.push_back(off);
     off = align_up(off + G * 4, 256);
   }
@@ -70,15 +70,16 @@ SimtWs simt_ws(const Problem& p) {
   return w;
 }
 
-// dst[k][r] = W[r][k] (transposed to [K][rows]) converted to the activation type.
+// dst[k][r] = W[r][k] (transposed to [K4][rows], K4 = K rounded up to 4, rows k >= K zero) converted to
+// the activation type.
 __global__ void pack_transposed_kernel(const void* src, int src_dtype, int layout, int rows, int K,
                                        void* dst, int dst_dtype) {
-  const int64_t n = (int64_t)rows * K;
+  const int64_t n = (int64_t)rows * ((K + 3) & ~3);
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
     const int k = (int)(i / rows);
     const int r = (int)(i % rows);
-    store_any(dst, dst_dtype, i, load_any(src, src_dtype, weight_src_index(layout, rows, K, r, k)));
+    store_any(dst, dst_dtype, i, k < K ? load_any(src, src_dtype, weight_src_index(layout, rows, K, r, k)) : 0.0f);
   }
 }
 
@@ -122,33 +123,37 @@ __device__ __forceinline__ float4 ld_w4(const __nv_bfloat16* p) {
   return make_float4(a.x, a.y, b.x, b.y);
 }
 
-template <int NB>
-__device__ __forceinline__ void fma_quad(const float4 w, const float* v, int ld, float (&acc)[NB][4]) {
-#pragma unroll
-  for (int n = 0; n < NB; ++n) {
-    const float x = v[n * ld];
-    acc[n][0] = fmaf(w.x, x, acc[n][0]);
-    acc[n][1] = fmaf(w.y, x, acc[n][1]);
-    acc[n][2] = fmaf(w.z, x, acc[n][2]);
-    acc[n][3] = fmaf(w.w, x, acc[n][3]);
-  }
-}
-
-// acc[n][i] += sum_{k < nk} w[k * G + i] * v[n * ld + k] for the four rows i of one quad, in
-// increasing k.  The contraction is bound by the latency of the L2 weight reads, so each
-// round issues U predicated loads before any of their FMAs.
+// acc[n][i] += sum_{k < nk} w[k * G + i] * v[n * ld + k] for the four rows i of one quad, in increasing
+// k; nk, v and ld are multiples of 4 (zero-padded rows), so each group of four k takes four vector weight
+// loads and one 16-byte shared load per batch row.  The loop is bound by the latency of the L2 weight
+// reads: each round issues the loads of U groups before any of their FMAs.
 template <typename T, int NB>
 __device__ __forceinline__ void quad_dot(const T* __restrict__ w, int G, const float* v, int ld, int nk,
                                          float (&acc)[NB][4]) {
-  constexpr int U = NB >= 8 ? 8 : 16;
-  for (int k = 0; k < nk; k += U) {
-    float4 wv[U];
+  constexpr int U = NB >= 8 ? 2 : 4;  // groups of four k per round
+  for (int k = 0; k < nk; k += 4 * U) {
+    float4 wv[U][4];
 #pragma unroll
-    for (int j = 0; j < U; ++j)
-      wv[j] = k + j < nk ? ld_w4(w + (int64_t)(k + j) * G) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    for (int g = 0; g < U; ++g)
 #pragma unroll
-    for (int j = 0; j < U; ++j)
-      if (k + j < nk) fma_quad<NB>(wv[j], v + k + j, ld, acc);
+      for (int j = 0; j < 4; ++j)
+        wv[g][j] = k + 4 * g < nk ? ld_w4(w + (int64_t)(k + 4 * g + j) * G) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+    for (int g = 0; g < U; ++g) {
+      if (k + 4 * g >= nk) break;
+#pragma unroll
+      for (int n = 0; n < NB; ++n) {
+        const float4 x = *reinterpret_cast<const float4*>(v + n * ld + k + 4 * g);
+        const float xs[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          acc[n][0] = fmaf(wv[g][j].x, xs[j], acc[n][0]);
+          acc[n][1] = fmaf(wv[g][j].y, xs[j], acc[n][1]);
+          acc[n][2] = fmaf(wv[g][j].z, xs[j], acc[n][2]);
+          acc[n][3] = fmaf(wv[g][j].w, xs[j], acc[n][3]);
+        }
+      }
+    }
   }
 }
 
@@ -160,7 +165,7 @@ struct SimtShape {
 };
 
 size_t simt_smem(int nb, int ks, int K, int H) {
-  const size_t ldx = align_up((size_t)K + H, 4);
+  const size_t ldx = align_up(K, 4) + align_up(H, 4);
   return sizeof(float) * nb * (ldx + (size_t)ks * 4 * H + H);
 }
 
@@ -174,7 +179,7 @@ SimtShape simt_shape(int B, int K, int H) {
   int best = 1;
   double best_eff = 0.0;
   for (int ks = 1; ks <= 8; ++ks) {
-    if (ks > 1 && (K + H) / ks < 16) break;
+    if (ks > 1 && (K + H) / ks < 16) break;  // at least 16 k per slice
     if (simt_smem(nb, ks, K, H) > kSimtSmemMax) break;
     const int items = ks * H;
     const int rounds = (items + kSimtThreads - 1) / kSimtThreads;
@@ -193,8 +198,9 @@ SimtShape simt_shape(int B, int K, int H) {
 // (the hidden-update entry point runs with K = 0 and gin set).
 // hfin/cfin: final state of this layer [B][H] (T / f32).
 // Each step a work item (quad q, slice s) accumulates gate rows 4q..4q+3 over the slice's k range
-// of [x_t ; h_{t-1}], reading each transposed weight row as one vector; the gate phase adds
-// bias, gin and the slices' partial sums in that order.
+// of [x_t ; 0 ; h_{t-1} ; 0] (x and h each zero-padded to a multiple of 4, like the weight rows),
+// reading each transposed weight row as one vector; the gate phase adds bias, gin and the slices'
+// partial sums in that order.
 template <typename T, int NB>
 __global__ void __launch_bounds__(kSimtThreads)
     simt_layer_kernel(const T* __restrict__ xin, int K, const T* __restrict__ wih_t,
@@ -206,15 +212,15 @@ __global__ void __launch_bounds__(kSimtThreads)
   extern __shared__ float4 smem4[];
   float* smem = reinterpret_cast<float*>(smem4);
   const int G = 4 * H;
-  const int KH = K + H;
-  const int ldx = (KH + 3) & ~3;
-  float* xh = smem;                        // [NB][ldx]: x_t then h_{t-1}
+  const int K4 = (K + 3) & ~3;
+  const int ldx = K4 + ((H + 3) & ~3);
+  float* xh = smem;                        // [NB][ldx]: x_t at 0, h_{t-1} at K4, pads zero
   float* part = xh + NB * ldx;             // [ks_n][NB][4H] partial gate sums
   float* cst = part + (size_t)ks_n * NB * G;  // [NB][H]
   __shared__ int lens[NB];
   const int b0 = blockIdx.x * NB;
   const int tid = threadIdx.x;
-  const int chunk = ((KH + ks_n - 1) / ks_n + 3) & ~3;
+  const int chunk = ((ldx + ks_n - 1) / ks_n + 3) & ~3;
 
   if (tid < NB) {
     const int b = b0 + tid;
@@ -222,6 +228,8 @@ __global__ void __launch_bounds__(kSimtThreads)
     if (b < B) len = lengths != nullptr ? min(max(lengths[b], 0), Tn) : Tn;
     lens[tid] = len;
   }
+  for (int i = tid; i < NB * ldx; i += blockDim.x) xh[i] = 0.0f;
+  __syncthreads();
   for (int i = tid; i < NB * H; i += blockDim.x) {
     const int n = i / H, u = i % H, b = b0 + n;
     float hv = 0.0f, cv = 0.0f;
@@ -229,7 +237,7 @@ __global__ void __launch_bounds__(kSimtThreads)
       if (h0 != nullptr) hv = to_f32(h0[(int64_t)b * H + u]);
       if (c0 != nullptr) cv = to_f32(c0[(int64_t)b * H + u]);
     }
-    xh[n * ldx + K + u] = hv;
+    xh[n * ldx + K4 + u] = hv;
     cst[i] = cv;
   }
   __syncthreads();
@@ -245,13 +253,13 @@ __global__ void __launch_bounds__(kSimtThreads)
     __syncthreads();
     for (int item = tid; item < ks_n * H; item += blockDim.x) {
       const int q = item % H, s = item / H;
-      const int k0 = s * chunk, k1 = min(KH, k0 + chunk);
+      const int k0 = s * chunk, k1 = min(ldx, k0 + chunk);
       float acc[NB][4];
 #pragma unroll
       for (int n = 0; n < NB; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.0f;
-      if (k0 < K) quad_dot<T, NB>(wih_t + (int64_t)k0 * G + 4 * q, G, xh + k0, ldx, min(k1, K) - k0, acc);
-      const int j0 = max(k0, K);
-      if (j0 < k1) quad_dot<T, NB>(whh_t + (int64_t)(j0 - K) * G + 4 * q, G, xh + j0, ldx, k1 - j0, acc);
+      if (k0 < K4) quad_dot<T, NB>(wih_t + (int64_t)k0 * G + 4 * q, G, xh + k0, ldx, min(k1, K4) - k0, acc);
+      const int j0 = max(k0, K4);
+      if (j0 < k1) quad_dot<T, NB>(whh_t + (int64_t)(j0 - K4) * G + 4 * q, G, xh + j0, ldx, k1 - j0, acc);
 #pragma unroll
       for (int n = 0; n < NB; ++n)
         *reinterpret_cast<float4*>(part + ((size_t)s * NB + n) * G + 4 * q) =
@@ -277,7 +285,7 @@ __global__ void __launch_bounds__(kSimtThreads)
         const float c = fg * cst[i] + ig * gg;
         cst[i] = c;
         const T hq = from_f32<T>(og * tanh_acc(c));  // h is kept in the activation type
-        xh[n * ldx + K + u] = to_f32(hq);
+        xh[n * ldx + K4 + u] = to_f32(hq);
         seq_out[(int64_t)b * out_sb + (int64_t)t * out_st + u] = hq;
       } else if (b < B) {
         seq_out[(int64_t)b * out_sb + (int64_t)t * out_st + u] = from_f32<T>(0.0f);
@@ -296,7 +304,7 @@ __global__ void __launch_bounds__(kSimtThreads)
   for (int i = tid; i < NB * H; i += blockDim.x) {
     const int n = i / H, u = i % H, b = b0 + n;
     if (b < B) {
-      hfin[(int64_t)b * H + u] = from_f32<T>(xh[n * ldx + K + u]);
+      hfin[(int64_t)b * H + u] = from_f32<T>(xh[n * ldx + K4 + u]);
       cfin[(int64_t)b * H + u] = cst[i];
     }
   }
@@ -429,7 +437,7 @@ HuWs hu_ws(const HuProblem& p) {
   const size_t es = dtype_size(p.dtype);
   size_t off = kStatusBytes;
   w.whh = off;
-  off = align_up(off + (size_t)p.H * 4 * p.H * es, 256);
+  off = align_up(off + align_up(p.H, 4) * 4 * p.H * es, 256);
   w.bias = off;
   off = align_up(off + (size_t)4 * p.H * 4, 256);
   w.seq = off;
@@ -444,7 +452,7 @@ int32_t simt_hu_t(const HuProblem& p, const void* gate_proj, const void* w_hh, c
   const HuWs w = hu_ws(p);
   char* wsb = static_cast<char*>(ws);
   const int G = 4 * p.H;
-  pack_transposed_kernel<<<grid_for((int64_t)G * p.H, 256), 256, 0, s>>>(w_hh, p.dtype, p.w_layout, G, p.H,
+  pack_transposed_kernel<<<grid_for((int64_t)G * (p.H + 3), 256), 256, 0, s>>>(w_hh, p.dtype, p.w_layout, G, p.H,
                                                                           wsb + w.whh, p.dtype);
   pack_bias_kernel<<<grid_for(G, 256), 256, 0, s>>>(bias, nullptr, p.dtype, G, reinterpret_cast<float*>(wsb + w.bias));
   PLSTM_TRY_CUDA(cudaGetLastError());
@@ -495,9 +503,9 @@ int32_t simt_pack(const Problem& p, int ih_layout, int hh_layout, const void* co
   const int G = 4 * p.H;
   for (int l = 0; l < p.L; ++l) {
     const int K = l == 0 ? p.I : p.H;
-    pack_transposed_kernel<<<grid_for((int64_t)G * K, 256), 256, 0, s>>>(
+    pack_transposed_kernel<<<grid_for((int64_t)G * (K + 3), 256), 256, 0, s>>>(
         w_ih[l], p.dtype, ih_layout, G, K, pk + lo.wih[l], p.dtype);
-    pack_transposed_kernel<<<grid_for((int64_t)G * p.H, 256), 256, 0, s>>>(
+    pack_transposed_kernel<<<grid_for((int64_t)G * (p.H + 3), 256), 256, 0, s>>>(
         w_hh[l], p.dtype, hh_layout, G, p.H, pk + lo.whh[l], p.dtype);
     pack_bias_kernel<<<grid_for(G, 256), 256, 0, s>>>(b_ih ? b_ih[l] : nullptr,
                                                        b_hh ? b_hh[l] : nullptr, p.dtype, G,

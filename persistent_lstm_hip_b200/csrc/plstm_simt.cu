@@ -166,7 +166,7 @@ struct SimtShape {
 
 size_t simt_smem(int nb, int ks, int K, int H) {
   const size_t ldx = align_up(K, 4) + align_up(H, 4);
-  return sizeof(float) * nb * (ldx + (size_t)ks * 4 * H + H);
+  return sizeof(float) * (nb * (ldx + (size_t)ks * 4 * H + H) + 4 * (size_t)H);
 }
 
 // Fewest batch rows per CTA that keep the grid within one wave of 148 CTAs (the per-step cost
@@ -217,6 +217,7 @@ __global__ void __launch_bounds__(kSimtThreads)
   float* xh = smem;                        // [NB][ldx]: x_t at 0, h_{t-1} at K4, pads zero
   float* part = xh + NB * ldx;             // [ks_n][NB][4H] partial gate sums
   float* cst = part + (size_t)ks_n * NB * G;  // [NB][H]
+  float* bsm = cst + NB * H;                // [4H] bias
   __shared__ int lens[NB];
   const int b0 = blockIdx.x * NB;
   const int tid = threadIdx.x;
@@ -229,6 +230,7 @@ __global__ void __launch_bounds__(kSimtThreads)
     lens[tid] = len;
   }
   for (int i = tid; i < NB * ldx; i += blockDim.x) xh[i] = 0.0f;
+  for (int r = tid; r < G; r += blockDim.x) bsm[r] = bias != nullptr ? bias[r] : 0.0f;
   __syncthreads();
   for (int i = tid; i < NB * H; i += blockDim.x) {
     const int n = i / H, u = i % H, b = b0 + n;
@@ -245,12 +247,24 @@ __global__ void __launch_bounds__(kSimtThreads)
 #pragma unroll
   for (int n = 0; n < NB; ++n) tmax = max(tmax, lens[n]);
 
-  for (int t = 0; t < tmax; ++t) {
-    for (int i = tid; i < NB * K; i += blockDim.x) {
-      const int n = i / K, k = i % K, b = b0 + n;
-      xh[n * ldx + k] = (b < B) ? to_f32(xin[((int64_t)b * Tn + t) * K + k]) : 0.0f;
-    }
+  // x_t of batch row n, element k (zero for rows past B).
+  auto x_at = [&](int i, int t) {
+    const int n = i / K, k = i % K, b = b0 + n;
+    return b < B ? to_f32(xin[((int64_t)b * Tn + t) * K + k]) : 0.0f;
+  };
+  if (tmax > 0) {
+    for (int i = tid; i < NB * K; i += blockDim.x) xh[(i / K) * ldx + i % K] = x_at(i, 0);
     __syncthreads();
+  }
+  constexpr int kXPre = 2;  // x_{t+1} items per thread loaded under step t's contraction
+  for (int t = 0; t < tmax; ++t) {
+    const bool next = t + 1 < tmax;
+    float xr[kXPre];
+#pragma unroll
+    for (int m = 0; m < kXPre; ++m) {
+      const int i = tid + m * blockDim.x;
+      xr[m] = next && i < NB * K ? x_at(i, t + 1) : 0.0f;
+    }
     for (int item = tid; item < ks_n * H; item += blockDim.x) {
       const int q = item % H, s = item / H;
       const int k0 = s * chunk, k1 = min(ldx, k0 + chunk);
@@ -273,7 +287,7 @@ __global__ void __launch_bounds__(kSimtThreads)
 #pragma unroll
         for (int gi = 0; gi < 4; ++gi) {
           const int r = gi * H + u;
-          float v = bias != nullptr ? bias[r] : 0.0f;
+          float v = bsm[r];
           if (gin != nullptr) v += to_f32(gin[(int64_t)b * gin_sb + (int64_t)t * gin_st + r]);
           for (int s = 0; s < ks_n; ++s) v += part[((size_t)s * NB + n) * G + r];
           g[gi] = v;
@@ -290,6 +304,14 @@ __global__ void __launch_bounds__(kSimtThreads)
       } else if (b < B) {
         seq_out[(int64_t)b * out_sb + (int64_t)t * out_st + u] = from_f32<T>(0.0f);
       }
+    }
+    if (next) {  // the x part of xh is not read by the gate phase
+#pragma unroll
+      for (int m = 0; m < kXPre; ++m) {
+        const int i = tid + m * blockDim.x;
+        if (i < NB * K) xh[(i / K) * ldx + i % K] = xr[m];
+      }
+      for (int i = tid + kXPre * blockDim.x; i < NB * K; i += blockDim.x) xh[(i / K) * ldx + i % K] = x_at(i, t + 1);
     }
     __syncthreads();
   }

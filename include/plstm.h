@@ -8,7 +8,9 @@
  *   - `miopen_adaptive_lstm_hip._C`      (miopen_adaptive_lstm_hip/csrc/bindings.cpp:5-78)
  * Every entry point below takes plain device pointers, sizes and a
  * `cudaStream_t` passed as `void*`; no torch type crosses this boundary.  The
- * caller owns every buffer (inputs, outputs, workspace).  Each function only
+ * caller owns every buffer (inputs, outputs, workspace); packed images and
+ * workspaces must be 16-byte aligned (cudaMalloc and torch allocations are),
+ * else the call returns PLSTM_EINVAL.  Each function only
  * enqueues work on `stream` and returns; device-side failures (a bounded
  * inter-CTA wait that ran out) are recorded in the workspace status word and
  * reported by `plstm_read_status` or, with PLSTM_FLAG_SYNC_CHECK, by the call

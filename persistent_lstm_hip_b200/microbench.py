@@ -94,11 +94,18 @@ def forward(args) -> dict:
                             [h(getattr(lstm, f"bias_ih_l{l}")) for l in range(L)],
                             [h(getattr(lstm, f"bias_hh_l{l}")) for l in range(L)], h(lin.weight), h(lin.bias),
                             out_mode=args.out)
-    x = torch.randn(args.batch, args.seq, args.input, generator=torch.Generator().manual_seed(1)).to(dev, dt)
-    ms = _time(lambda: pw.forward(x, need_state=False), args.iters, 2)
+    gen = torch.Generator().manual_seed(1)
+    x = torch.randn(args.batch, args.seq, args.input, generator=gen).to(dev, dt)
+    lengths = None
+    steps = args.batch * args.seq
+    if args.min_len is not None:  # lengths uniform in [min_len, seq], seeded (config 5 draws from [200, 1000])
+        lengths = torch.randint(args.min_len, args.seq + 1, (args.batch,), generator=gen, dtype=torch.int32)
+        steps = int(lengths.sum())
+        lengths = lengths.to(dev)
+    ms = _time(lambda: pw.forward(x, lengths=lengths, need_state=False), args.iters, 2)
     return {"backend": pw.backend, "hidden": args.hidden, "layers": L, "batch": args.batch, "seq": args.seq,
-            "input": args.input, "dtype": args.dtype, "out": args.out, "ms": ms,
-            "seq_timesteps_per_s": args.batch * args.seq / (ms / 1e3)}
+            "input": args.input, "dtype": args.dtype, "out": args.out, "min_len": args.min_len, "ms": ms,
+            "seq_timesteps_per_s": steps / (ms / 1e3)}
 
 
 def main() -> None:
@@ -122,6 +129,8 @@ def main() -> None:
     f.add_argument("--dtype", choices=["f16", "bf16", "f32"], default="f16")
     f.add_argument("--out", choices=["last", "seq", "hseq"], default="last")
     f.add_argument("--iters", type=int, default=5)
+    f.add_argument("--min-len", type=int, default=None,
+                   help="variable lengths uniform in [min_len, seq]; throughput counts the valid steps")
     args = ap.parse_args()
     print(json.dumps({"gemm": gemm, "step": step, "forward": forward}[args.cmd](args)))
 

@@ -106,7 +106,7 @@ __global__ void pack_bias_kernel(const void* a, const void* b, int dtype, int n,
 }
 
 constexpr int kSimtThreads = 512;
-constexpr size_t kSimtSmemMax = 227 * 1024;
+constexpr size_t kSimtSmemMax = 227 * 1024 - 256;  // dynamic shared memory; the static lens[] needs the rest
 
 // Four consecutive gate rows of one transposed weight row, as f32.
 __device__ __forceinline__ float4 ld_w4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }

@@ -130,9 +130,10 @@ int32_t tc_make_perm(const Problem& p, int N, int tiles, const int32_t* lengths,
 
 // x[B][T][I] (I <= kx) -> xp[tiles][T][N rows x kx] 16-bit K-major core matrices
 // (8 rows x 16 bytes; K groups 128 bytes apart, 8-row groups kx * 16 bytes apart), rows
-// in tile order, zero for padding rows and columns I..kx-1.  kx: multiple of 16.
+// in tile order, zero for padding rows and columns I..kx-1.  kx: multiple of 16.  With
+// `choice`, the launch packs only if *choice == N (device-side choice of the tile height).
 int32_t tc_xpack(const Problem& p, int N, int tiles, const void* x, const int32_t* perm, uint8_t* xp, int kx,
-                 cudaStream_t s);
+                 cudaStream_t s, const int* choice = nullptr);
 
 // tcgen05 layer-sequential backend (plstm_tcl.cu) for any H <= 512 (zero-padded to a multiple
 // of 64), L <= 16, I <= 128: per layer a projection GEMM and a cluster-wide recurrence; the tc_* entry

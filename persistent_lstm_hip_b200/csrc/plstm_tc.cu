@@ -131,6 +131,7 @@ struct Params {
   unsigned long long* trace;  // PLSTM_FLAG_TRACE: [2L][64][8] clock64 stamps of cluster 0, or null
   int trace_t0;
   int trace_slot;  // two-slot kernel: the slot whose events are recorded
+  const int* choice;  // two tile heights enqueued (variable lengths): run only if *choice == N, else null
 };
 
 // Trace events: control warp 0 sibling h landed, 1 recurrent MMAs + commit issued,
@@ -866,6 +867,8 @@ __global__ void __launch_bounds__(Smem2<NH>::kThreads, 1) wavefront2_kernel(cons
   constexpr int NL = S::kNL;
   constexpr int kComputeWarps = S::kComputeWarps;
   constexpr bool kHasLinear = MODE != kModeHSeq;
+  // The launch of the tile height not chosen ends here, before any barrier, TMEM or cluster traffic.
+  if (p.choice != nullptr && *p.choice != N) return;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = ptx::smem_u32(sm);
@@ -1591,12 +1594,46 @@ __global__ void tc_perm_varlen_kernel(const int32_t* sorted, const int32_t* leng
     if (i < tiles) tile_len[i] = min(max(lengths[sorted[i * N]], 0), T);
   }
 }
+
+// Device-side choice between 32- and 64-row two-slot tiles for a length-sorted batch.
+// len32 holds the 32-row tiles' lengths (longest first); the 64-row tile j is 32-row tiles
+// 2j and 2j+1, so its length is len32[2j].  Each height's launch is list-scheduled in tile
+// order onto its m co-resident clusters (a tile holds a cluster for len + L wavefront
+// steps); 32-row tiles step kStep32 times as long as 64-row ones (measured 1.476 / 1.86 ms
+// at 480 / 512 rows).  Writes len64 and *choice = 32 or 64.
+constexpr float kStep32 = 0.8f;
+constexpr int kMaxChoiceClusters = 16;
+__global__ void tc_tile_choice_kernel(const int32_t* __restrict__ len32, int tiles32, int tiles64, int L, int m32,
+                                      int m64, int32_t* __restrict__ len64, int* __restrict__ choice) {
+  if (blockIdx.x != 0 || threadIdx.x != 0) return;
+  float end[2][kMaxChoiceClusters];
+  const int m[2] = {min(m32, kMaxChoiceClusters), min(m64, kMaxChoiceClusters)};
+  for (int h = 0; h < 2; ++h)
+    for (int c = 0; c < kMaxChoiceClusters; ++c) end[h][c] = 0.0f;
+  float span[2] = {0.0f, 0.0f};
+  for (int h = 0; h < 2; ++h) {
+    const int tiles = h == 0 ? tiles32 : tiles64;
+    const float step = h == 0 ? kStep32 : 1.0f;
+    for (int j = 0; j < tiles; ++j) {
+      const int len = h == 0 ? len32[j] : len32[2 * j];
+      if (h == 1) len64[j] = len;
+      int c = 0;
+      for (int k = 1; k < m[h]; ++k)
+        if (end[h][k] < end[h][c]) c = k;
+      end[h][c] += step * (float)(len + L);
+      span[h] = fmaxf(span[h], end[h][c]);
+    }
+  }
+  *choice = span[0] < span[1] ? 32 : 64;
+}
 // x[B][T][I] -> per-tile, per-step K-major no-swizzle tiles of kx columns: 8-row x
 // 8-column core matrices of 128 bytes, K groups 128 bytes apart, 8-row groups kx * 16
 // bytes apart.  One thread per (tile, step, row, K group).
 template <typename T16>
 __global__ void tc_xpack_kernel(const T16* __restrict__ x, const int32_t* __restrict__ perm,
-                                uint8_t* __restrict__ xp, int B, int T, int I, int N, int tiles, int kx) {
+                                uint8_t* __restrict__ xp, int B, int T, int I, int N, int tiles, int kx,
+                                const int* choice) {
+  if (choice != nullptr && *choice != N) return;  // packs for the chosen tile height only
   const int kg_n = kx / 8;
   const int64_t total = (int64_t)tiles * T * N * kg_n;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
@@ -1792,6 +1829,28 @@ struct TcWs {
   size_t xp, perm, tile_len, hist, sorted, trace, total;
 };
 
+// A variable-length batch whose 32-row tiles need more than one wave (so the plan took
+// 64-row tiles) enqueues both heights and lets tc_tile_choice_kernel pick from the sorted
+// lengths: with widely spread lengths the tail 32-row tiles fit in the long tiles' slack.
+struct DualPlan {
+  bool on = false;
+  int tiles32 = 0, m32 = 0, m64 = 0;
+};
+DualPlan dual_plan(const Problem& p, const Plan& pl, bool varlen) {
+  DualPlan d;
+  if (!varlen || pl.slots != 2 || pl.N != 64 || std::getenv("PLSTM_TC_NTILE") != nullptr) return d;
+  if (p.flags & (PLSTM_FLAG_TRACE | PLSTM_FLAG_TEST_DROP)) return d;
+  Plan c = pl;
+  c.N = 32;
+  d.tiles32 = (p.B + 31) / 32;
+  d.m32 = max_active_clusters(p.device, p.L, c);
+  d.m64 = max_active_clusters(p.device, p.L, pl);
+  // Beyond two waves of 32-row tiles the 64-row plan won at every measured length spread
+  // (B = 1024, 4096 with lengths in [200, 1000]); there the extra launches would only cost.
+  d.on = d.m32 >= 1 && d.m64 >= 1 && d.tiles32 > d.m32 && d.tiles32 <= 2 * d.m32;
+  return d;
+}
+
 TcWs tc_ws(const Problem& p, const Plan& pl) {
   TcWs w;
   size_t off = kStatusBytes;
@@ -1799,8 +1858,8 @@ TcWs tc_ws(const Problem& p, const Plan& pl) {
   off = align_up(off + (size_t)pl.tiles * std::max(p.T, 1) * pl.N * tc_kx(p) * 2, 256);
   w.perm = off;
   off = align_up(off + (size_t)pl.tiles * pl.N * 4, 256);
-  w.tile_len = off;
-  off = align_up(off + (size_t)pl.tiles * 4, 256);
+  w.tile_len = off;  // [tiles], then (two tile heights enqueued) the 32-row tiles' lengths and the choice word
+  off = align_up(off + (size_t)(3 * pl.tiles + 1) * 4, 256);
   w.hist = off;
   off = align_up(off + (size_t)(p.T + 1) * 4, 256);
   w.sorted = off;
@@ -1836,13 +1895,13 @@ int32_t tc_make_perm(const Problem& p, int N, int tiles, const int32_t* lengths,
 }
 
 int32_t tc_xpack(const Problem& p, int N, int tiles, const void* x, const int32_t* perm, uint8_t* xp, int kx,
-                 cudaStream_t s) {
+                 cudaStream_t s, const int* choice) {
   if (p.T <= 0) return PLSTM_OK;
   const int nthr = 256;
   const int64_t total = (int64_t)tiles * p.T * N * (kx / 8);
   const int grid = (int)std::min<int64_t>((total + nthr - 1) / nthr, 148 * 32);
   tc_xpack_kernel<uint16_t><<<grid, nthr, 0, s>>>(static_cast<const uint16_t*>(x), perm, xp, p.B, p.T, p.I, N, tiles,
-                                                  kx);
+                                                  kx, choice);
   PLSTM_TRY_CUDA(cudaGetLastError());
   note_launches(1);
   return PLSTM_OK;
@@ -1922,13 +1981,27 @@ int32_t tc_forward(const Problem& p, const void* packed, const void* x, const in
   uint8_t* wsb = static_cast<uint8_t*>(ws);
   int32_t* perm = reinterpret_cast<int32_t*>(wsb + w.perm);
   int32_t* tile_len = reinterpret_cast<int32_t*>(wsb + w.tile_len);
-  {
-    const int32_t rc = tc_make_perm(p, pl.N, pl.tiles, lengths, perm, tile_len,
-                                    reinterpret_cast<int32_t*>(wsb + w.hist), reinterpret_cast<int32_t*>(wsb + w.sorted), s);
+  const DualPlan dual = dual_plan(p, pl, lengths != nullptr);
+  int32_t* len32 = tile_len + pl.tiles;
+  int* choice = dual.on ? reinterpret_cast<int*>(len32 + dual.tiles32) : nullptr;
+  int32_t* hist = reinterpret_cast<int32_t*>(wsb + w.hist);
+  int32_t* sorted = reinterpret_cast<int32_t*>(wsb + w.sorted);
+  if (!dual.on) {
+    int32_t rc = tc_make_perm(p, pl.N, pl.tiles, lengths, perm, tile_len, hist, sorted, s);
+    if (rc == PLSTM_OK) rc = tc_xpack(p, pl.N, pl.tiles, x, perm, wsb + w.xp, tc_kx(p), s);
     if (rc != PLSTM_OK) return rc;
-  }
-  {
-    const int32_t rc = tc_xpack(p, pl.N, pl.tiles, x, perm, wsb + w.xp, tc_kx(p), s);
+  } else {
+    // One length-sorted order serves both heights (64-row tile j = 32-row tiles 2j, 2j+1);
+    // the 64-row launch's last 32 perm entries may be padding.
+    const int tail = pl.tiles * 64 - dual.tiles32 * 32;
+    if (tail > 0) PLSTM_TRY_CUDA(cudaMemsetAsync(perm + dual.tiles32 * 32, 0xff, (size_t)tail * 4, s));
+    int32_t rc = tc_make_perm(p, 32, dual.tiles32, lengths, perm, len32, hist, sorted, s);
+    if (rc != PLSTM_OK) return rc;
+    tc_tile_choice_kernel<<<1, 32, 0, s>>>(len32, dual.tiles32, pl.tiles, p.L, dual.m32, dual.m64, tile_len, choice);
+    PLSTM_TRY_CUDA(cudaGetLastError());
+    note_launches(1);
+    rc = tc_xpack(p, 32, dual.tiles32, x, perm, wsb + w.xp, tc_kx(p), s, choice);
+    if (rc == PLSTM_OK) rc = tc_xpack(p, 64, pl.tiles, x, perm, wsb + w.xp, tc_kx(p), s, choice);
     if (rc != PLSTM_OK) return rc;
   }
   Params kp = {};
@@ -1956,6 +2029,7 @@ int32_t tc_forward(const Problem& p, const void* packed, const void* x, const in
   kp.trace = nullptr;
   kp.trace_t0 = p.T / 2;
   kp.trace_slot = 0;
+  kp.choice = choice;
   if (const char* e = std::getenv("PLSTM_TC_TRACE_SLOT")) kp.trace_slot = std::atoi(e) == 1 ? 1 : 0;
   if (p.flags & PLSTM_FLAG_TRACE) {
     kp.trace = reinterpret_cast<unsigned long long*>(wsb + w.trace);
@@ -1967,28 +2041,40 @@ int32_t tc_forward(const Problem& p, const void* packed, const void* x, const in
   }
   const bool bf16 = p.dtype == PLSTM_BF16;
   const int mode = mode_of(p);
-  void* k = plan_kernel(pl, bf16, lengths != nullptr, mode);
-  const int smem = plan_smem(pl);
-  PLSTM_TRY_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-  PLSTM_TRY_CUDA(allow_cluster(k, p.L));
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)(pl.tiles * 2 * p.L), 1, 1);
-  cfg.blockDim = dim3((unsigned)plan_threads(pl), 1, 1);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = s;
-  cudaLaunchAttribute attr;
-  attr.id = cudaLaunchAttributeClusterDimension;
-  attr.val.clusterDim.x = 2 * p.L;
-  attr.val.clusterDim.y = 1;
-  attr.val.clusterDim.z = 1;
-  cfg.attrs = &attr;
-  cfg.numAttrs = 1;
-  void* args[] = {&kp};
+  auto launch = [&](const Plan& lp, const int32_t* lp_tile_len) -> int32_t {
+    void* k = plan_kernel(lp, bf16, lengths != nullptr, mode);
+    const int smem = plan_smem(lp);
+    PLSTM_TRY_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    PLSTM_TRY_CUDA(allow_cluster(k, p.L));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(lp.tiles * 2 * p.L), 1, 1);
+    cfg.blockDim = dim3((unsigned)plan_threads(lp), 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 2 * p.L;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    Params lkp = kp;
+    lkp.tile_len = lp_tile_len;
+    void* args[] = {&lkp};
+    PLSTM_TRY_CUDA(cudaLaunchKernelExC(&cfg, k, args));
+    note_launches(1);
+    return PLSTM_OK;
+  };
   profile_begin(s);
-  PLSTM_TRY_CUDA(cudaLaunchKernelExC(&cfg, k, args));
+  int32_t rc = launch(pl, tile_len);
+  if (rc == PLSTM_OK && dual.on) {
+    Plan p32 = pl;
+    p32.N = 32;
+    p32.tiles = dual.tiles32;
+    rc = launch(p32, len32);
+  }
   profile_end(s);
-  note_launches(1);
-  return PLSTM_OK;
+  return rc;
 }
 
 }  // namespace plstm

@@ -278,6 +278,39 @@ def test_tc_full_size_cfg5_varlen_sampled(cuda_device):
     assert_close16(h_n[:, rows], r_h, "h_n")
 
 
+@pytest.mark.parametrize("spread", [True, False])
+@pytest.mark.parametrize("B, mode", [(512, "seq"), (520, "last"), (700, "hseq")])
+def test_tc_varlen_tile_height_choice(cuda_device, monkeypatch, spread, B, mode):
+    """Variable-length batches past one wave of 32-row tiles enqueue both tile heights and
+    pick one on the device.  A row's arithmetic does not depend on the other rows of its
+    tile, so the result equals, bit for bit, both forced heights; sampled rows against the
+    oracle.  Spread lengths favour 32-row tiles, equal lengths 64-row ones."""
+    T, I, H, L, O = 120, 5, 128, 4, 24
+    m = make_model(I, H, L, O, seed=40)
+    w = weights_of(m, L, torch.float16, cuda_device)
+    x = _rand_x(B, T, I, torch.float16, cuda_device, seed=41)
+    g = torch.Generator().manual_seed(42)
+    lens = torch.randint(1, T + 1, (B,), generator=g, dtype=torch.int32) if spread else \
+        torch.full((B,), T, dtype=torch.int32)
+    h0 = (0.3 * torch.randn(L, B, H, generator=g)).half().to(cuda_device)
+    c0 = (0.3 * torch.randn(L, B, H, generator=g)).half().to(cuda_device)
+    pw = core.PackedWeights(*w, out_mode=mode)
+    assert pw.backend == "tc"
+    run = lambda: pw.forward(x, lengths=lens.to(cuda_device), hx=(h0, c0), check=True)
+    auto = run()
+    for nt in ("32", "64"):
+        monkeypatch.setenv("PLSTM_TC_NTILE", nt)
+        forced = run()
+        for a, f in zip(auto, forced):
+            assert torch.equal(a, f), nt
+    monkeypatch.delenv("PLSTM_TC_NTILE")
+    rows = np.linspace(0, B - 1, 12).astype(int)
+    r_out, r_h, r_c = oracle_of(x, *w, lengths=lens, hx=(h0, c0), out_mode=mode, rows=rows)
+    assert_close16(auto[0][rows], r_out, "out")
+    assert_close16(auto[1][:, rows], r_h, "h_n")
+    assert_close16(auto[2][:, rows], r_c, "c_n")
+
+
 def test_timeout_is_reported_not_hung(cuda_device):
     """A producer CTA that skips one h hand-off makes its consumer's bounded
     wait run out; the call returns PLSTM_ETIMEOUT and the context stays usable."""

@@ -95,6 +95,11 @@ struct Problem {
   int flags;
   int timeout_ms;
   int device;
+  // Batch size that chooses between kernels whose per-row arithmetic differs (-1: B).  The
+  // deduplicated forward runs the distinct rows with the full batch's value, so that its
+  // results stay bit-identical to the full forward's.
+  int route_B = -1;
+  int route_batch() const { return route_B >= 0 ? route_B : B; }
   bool has_linear() const { return (flags & PLSTM_FLAG_NO_LINEAR) == 0; }
   bool out_seq() const { return (flags & PLSTM_FLAG_OUT_SEQ) != 0; }
   bool out_last() const { return (flags & PLSTM_FLAG_OUT_LAST) != 0; }

@@ -353,6 +353,7 @@ int32_t dedupe_forward(const Problem& p, const DedupeInner& inner, const void* x
     set_error("duplicate-row grouping returned an impossible distinct count " + std::to_string(U));
     return PLSTM_ECUDA;
   }
+  q.route_B = p.route_batch();
   q.B = U;
   const size_t es = dtype_size(p.dtype);
   const size_t srow = (size_t)p.H * es, crow = (size_t)p.H * cn_elem(p);

@@ -15,9 +15,11 @@
 //   bias[l]   [4H]       f32, b_ih + b_hh summed in f32
 // then W_lin [O][H] (activation type) and b_lin [O] (f32).
 #include <algorithm>
+#include <type_traits>
 #include <vector>
 
 #include "plstm_common.cuh"
+#include "sm100_ptx.cuh"
 
 namespace plstm {
 namespace {
@@ -355,6 +357,218 @@ int32_t launch_simt_layer(const T* xin, int K, const T* wih_t, const T* whh_t, c
   return PLSTM_OK;
 }
 
+// ---- cluster-resident f32 layer kernel (H a multiple of 16, H <= 128, K <= 128) -----------
+// A cluster of kClC CTAs runs one layer for NB batch rows.  CTA c owns the units
+// [c U, (c + 1) U), U = H / kClC, with all four gates: its LR = 4U = H gate rows of
+// W_ih^T / W_hh^T (local row g U + j = global row g H + c U + j) stay in shared memory for
+// the whole sequence instead of streaming from L2 every step.  Each step every CTA
+// contracts [x_t ; h_{t-1}] (its own full copy) against its rows in k-slices, applies the
+// gate math to its units and stores h_t into the next step's buffer of every CTA of the
+// cluster (distributed shared memory); one cluster barrier per step orders those stores.
+// The contraction order per row (k-slices of the same width, partial sums added in slice
+// order) does not depend on the row's companions, the batch size or the tile.
+constexpr int kClC = 4;
+constexpr int kClThreads = 256;
+
+struct ClShape {
+  int nb, slices;
+  size_t smem;
+};
+
+// Floats: w [K4 + H4][H] | part [slices][NB][H] | xh [2][NB][K4 + H4] | cst [NB][U] | bias [H].
+size_t simt_cl_smem(int nb, int slices, int K, int H) {
+  const size_t ldx = align_up(K, 4) + align_up(H, 4);
+  return sizeof(float) * (ldx * H + (size_t)slices * nb * H + 2 * (size_t)nb * ldx + (size_t)nb * (H / kClC) + H);
+}
+
+// Shapes the cluster kernel serves, for batches it runs in one wave of 37 clusters of at
+// most 16 rows; larger batches stream the weights from L2 (simt_layer_kernel), which is
+// faster there (f32, H = 128, L = 4, B = 1024: 45.8 ms against 58.7 ms in two waves).
+bool simt_cl_supported(int dtype, int K, int H, int route_batch) {
+  return dtype == PLSTM_F32 && H % 16 == 0 && H >= 16 && H <= 128 && K >= 0 && K <= 128 &&
+         route_batch <= 148 / kClC * 16;
+}
+
+// Quads of consecutive local rows (H / 4 of them) times k-slices fill the CTA's threads (at most 16 slices).
+int simt_cl_slices(int H) { return std::min(kClThreads / (H / 4), 16); }
+
+// Fewest batch rows per cluster (4, 8 or 16) that keep the clusters within 37 (148 SMs /
+// 4), then fewer while the shared memory does not fit.
+ClShape simt_cl_shape(int B, int K, int H) {
+  const int slices = simt_cl_slices(H);
+  int nb = 4;
+  while (nb < 16 && (B + nb - 1) / nb > 148 / kClC) nb *= 2;
+  while (nb > 4 && simt_cl_smem(nb, slices, K, H) > kSimtSmemMax) nb /= 2;
+  return {nb, slices, simt_cl_smem(nb, slices, K, H)};
+}
+
+template <int NB>
+__global__ void __cluster_dims__(kClC, 1, 1) __launch_bounds__(kClThreads)
+    simt_cl_layer_kernel(const float* __restrict__ xin, int K, const float* __restrict__ wih_t,
+                         const float* __restrict__ whh_t, const float* __restrict__ bias,
+                         const int32_t* __restrict__ lengths, const float* __restrict__ h0,
+                         const float* __restrict__ c0, float* __restrict__ seq_out, float* __restrict__ hfin,
+                         float* __restrict__ cfin, int B, int Tn, int H, int slices, int64_t out_sb, int64_t out_st) {
+  extern __shared__ float4 smem4[];
+  float* smem = reinterpret_cast<float*>(smem4);
+  const int G = 4 * H;
+  const int U = H / kClC;   // units of this CTA
+  const int LR = 4 * U;     // its gate rows (= H)
+  const int K4 = (K + 3) & ~3;
+  const int ldx = K4 + H;   // H is a multiple of 16
+  float* w = smem;                               // [ldx][LR]
+  float* part = w + (size_t)ldx * LR;            // [slices][NB][LR]
+  float* xh = part + (size_t)slices * NB * LR;   // [2][NB][ldx]
+  float* cst = xh + 2 * NB * ldx;                // [NB][U]
+  float* bsm = cst + NB * U;                     // [LR]
+  __shared__ int lens[NB];
+  const int c = (int)ptx::cluster_ctarank();
+  const int b0 = (blockIdx.x / kClC) * NB;
+  const int tid = threadIdx.x;
+  const int chunk = ((ldx + slices - 1) / slices + 3) & ~3;
+  auto grow = [&](int lr) { return (lr / U) * H + c * U + lr % U; };  // local -> global gate row
+
+  if (tid < NB) {
+    const int b = b0 + tid;
+    lens[tid] = b < B ? (lengths != nullptr ? min(max(lengths[b], 0), Tn) : Tn) : 0;
+  }
+  for (int i = tid; i < ldx * LR; i += blockDim.x) {
+    const int k = i / LR, lr = i % LR;
+    float v = 0.0f;
+    if (k < K) v = wih_t[(int64_t)k * G + grow(lr)];
+    else if (k >= K4) v = whh_t[(int64_t)(k - K4) * G + grow(lr)];
+    w[i] = v;
+  }
+  for (int i = tid; i < LR; i += blockDim.x) bsm[i] = bias[grow(i)];
+  for (int i = tid; i < 2 * NB * ldx; i += blockDim.x) xh[i] = 0.0f;
+  __syncthreads();
+  for (int i = tid; i < NB * H; i += blockDim.x) {
+    const int n = i / H, u = i % H, b = b0 + n;
+    if (b < B && h0 != nullptr) xh[n * ldx + K4 + u] = h0[(int64_t)b * H + u];
+  }
+  for (int i = tid; i < NB * U; i += blockDim.x) {
+    const int n = i / U, j = i % U, b = b0 + n;
+    cst[i] = (b < B && c0 != nullptr) ? c0[(int64_t)b * H + c * U + j] : 0.0f;
+  }
+  int tmax = 0;
+#pragma unroll
+  for (int n = 0; n < NB; ++n) tmax = max(tmax, lens[n]);
+  for (int i = tid; i < NB * K; i += blockDim.x) {
+    const int n = i / K, k = i % K, b = b0 + n;
+    if (b < B && tmax > 0) xh[n * ldx + k] = xin[((int64_t)b * Tn) * K + k];
+  }
+  // Every CTA's buffers are initialised before any sibling stores into them.
+  ptx::cluster_sync();
+  uint32_t peer[kClC];
+  for (int r = 0; r < kClC; ++r) peer[r] = ptx::mapa(ptx::smem_u32(xh), (uint32_t)r);
+  constexpr int kXPre = 8;  // NB * K <= 16 * 128 = kXPre * kClThreads
+  for (int t = 0; t < tmax; ++t) {
+    const float* xc = xh + (t & 1) * NB * ldx;
+    const int nxt = ((t + 1) & 1) * NB * ldx;  // float offset of the next step's buffer
+    float xr[kXPre];                           // x_{t+1}, loaded under the contraction
+#pragma unroll
+    for (int m = 0; m < kXPre; ++m) {
+      const int i = tid + m * kClThreads;
+      const int n = i / max(K, 1), b = b0 + n;
+      xr[m] = (t + 1 < tmax && i < NB * K && b < B) ? xin[((int64_t)b * Tn + t + 1) * K + i % K] : 0.0f;
+    }
+    for (int item = tid; item < U * slices; item += blockDim.x) {
+      const int q = item % U, s = item / U;
+      const int k0 = s * chunk, k1 = min(ldx, k0 + chunk);
+      float acc[NB][4];
+#pragma unroll
+      for (int n = 0; n < NB; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.0f;
+      for (int k = k0; k < k1; k += 4) {
+        float4 wv[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) wv[j] = *reinterpret_cast<const float4*>(w + (size_t)(k + j) * LR + 4 * q);
+#pragma unroll
+        for (int n = 0; n < NB; ++n) {
+          const float4 xv = *reinterpret_cast<const float4*>(xc + n * ldx + k);
+          const float xs[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            acc[n][0] = fmaf(wv[j].x, xs[j], acc[n][0]);
+            acc[n][1] = fmaf(wv[j].y, xs[j], acc[n][1]);
+            acc[n][2] = fmaf(wv[j].z, xs[j], acc[n][2]);
+            acc[n][3] = fmaf(wv[j].w, xs[j], acc[n][3]);
+          }
+        }
+      }
+#pragma unroll
+      for (int n = 0; n < NB; ++n)
+        *reinterpret_cast<float4*>(part + ((size_t)s * NB + n) * LR + 4 * q) =
+            make_float4(acc[n][0], acc[n][1], acc[n][2], acc[n][3]);
+    }
+    __syncthreads();
+    for (int i = tid; i < NB * U; i += blockDim.x) {
+      const int n = i / U, j = i % U, b = b0 + n, u = c * U + j;
+      float hv;
+      if (t < lens[n]) {
+        float g[4];
+#pragma unroll
+        for (int gi = 0; gi < 4; ++gi) {
+          const int lr = gi * U + j;
+          float v = bsm[lr];
+          for (int s = 0; s < slices; ++s) v += part[((size_t)s * NB + n) * LR + lr];
+          g[gi] = v;
+        }
+        const float cn = sigmoid_acc(g[1]) * cst[i] + sigmoid_acc(g[0]) * tanh_acc(g[2]);
+        cst[i] = cn;
+        hv = sigmoid_acc(g[3]) * tanh_acc(cn);
+        seq_out[(int64_t)b * out_sb + (int64_t)t * out_st + u] = hv;
+      } else {
+        hv = xc[n * ldx + K4 + u];  // finished rows keep h
+        if (b < B) seq_out[(int64_t)b * out_sb + (int64_t)t * out_st + u] = 0.0f;
+      }
+      const uint32_t off = (uint32_t)(nxt + n * ldx + K4 + u) * 4u;
+#pragma unroll
+      for (int r = 0; r < kClC; ++r) ptx::st_cluster_u32(peer[r] + off, __float_as_uint(hv));
+    }
+#pragma unroll
+    for (int m = 0; m < kXPre; ++m) {
+      const int i = tid + m * kClThreads;
+      if (t + 1 < tmax && i < NB * K) xh[nxt + (i / K) * ldx + i % K] = xr[m];
+    }
+    // h_t of every unit is in every CTA's next buffer before the step after reads it.
+    ptx::cluster_sync();
+  }
+  const float* xl = xh + (tmax & 1) * NB * ldx;
+  for (int n = 0; n < NB; ++n) {
+    const int b = b0 + n;
+    if (b >= B) break;
+    const int64_t cnt = (int64_t)(Tn - tmax) * U;
+    for (int64_t i = tid; i < cnt; i += blockDim.x)
+      seq_out[(int64_t)b * out_sb + (int64_t)(tmax + i / U) * out_st + c * U + i % U] = 0.0f;
+  }
+  for (int i = tid; i < NB * U; i += blockDim.x) {
+    const int n = i / U, j = i % U, b = b0 + n;
+    if (b < B) {
+      hfin[(int64_t)b * H + c * U + j] = xl[n * ldx + K4 + c * U + j];
+      cfin[(int64_t)b * H + c * U + j] = cst[i];
+    }
+  }
+}
+
+int32_t launch_simt_cl_layer(const float* xin, int K, const float* wih_t, const float* whh_t, const float* bias,
+                             const int32_t* lengths, const float* h0, const float* c0, float* seq_out, float* hfin,
+                             float* cfin, int B, int Tn, int H, int64_t out_sb, int64_t out_st, cudaStream_t s) {
+  const ClShape sh = simt_cl_shape(B, K, H);
+  if (sh.smem > kSimtSmemMax) {
+    set_error("cluster FFMA kernel: shared-memory tile too large");
+    return PLSTM_ENOTSUP;
+  }
+  auto kern = simt_cl_layer_kernel<4>;
+  if (sh.nb == 8) kern = simt_cl_layer_kernel<8>;
+  if (sh.nb == 16) kern = simt_cl_layer_kernel<16>;
+  PLSTM_TRY_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sh.smem));
+  const int grid = (B + sh.nb - 1) / sh.nb * kClC;
+  kern<<<grid, kClThreads, sh.smem, s>>>(xin, K, wih_t, whh_t, bias, lengths, h0, c0, seq_out, hfin, cfin, B, Tn, H,
+                                         sh.slices, out_sb, out_st);
+  PLSTM_TRY_CUDA(cudaGetLastError());
+  return PLSTM_OK;
+}
+
 // out[b][t][o] (SEQ) or out[b][o] (LAST) = b_lin[o] + W_lin[o] . h, zero past each length (SEQ).
 template <typename T>
 __global__ void simt_linear_kernel(const T* __restrict__ hseq, const T* __restrict__ hlast,
@@ -420,7 +634,23 @@ int32_t simt_forward_t(const Problem& p, const void* packed, const void* x, cons
     const T* h0l = h0 ? static_cast<const T*>(h0) + (size_t)l * p.B * p.H : nullptr;
     const T* c0l = c0 ? static_cast<const T*>(c0) + (size_t)l * p.B * p.H : nullptr;
     if (l == 0) profile_begin(s);
-    const int32_t rc = launch_simt_layer<T>(
+    int32_t rc;
+    if constexpr (std::is_same<T, float>::value) {
+      if (simt_cl_supported(p.dtype, K, p.H, p.route_batch())) {
+        rc = launch_simt_cl_layer(layer_in, K, reinterpret_cast<const float*>(pk + lo.wih[l]),
+                                  reinterpret_cast<const float*>(pk + lo.whh[l]),
+                                  reinterpret_cast<const float*>(pk + lo.bias[l]), lengths, h0l, c0l, dst,
+                                  hfin + (size_t)l * p.B * p.H, cfin + (size_t)l * p.B * p.H, p.B, p.T, p.H,
+                                  (int64_t)p.T * p.H, p.H, s);
+        if (rc != PLSTM_OK) return rc;
+        note_launches(1);
+        if (l == p.L - 1) profile_end(s);
+        layer_in = dst;
+        K = p.H;
+        continue;
+      }
+    }
+    rc = launch_simt_layer<T>(
         layer_in, K, reinterpret_cast<const T*>(pk + lo.wih[l]), reinterpret_cast<const T*>(pk + lo.whh[l]),
         reinterpret_cast<const float*>(pk + lo.bias[l]), lengths, h0l, c0l, dst, hfin + (size_t)l * p.B * p.H,
         cfin + (size_t)l * p.B * p.H, p.B, p.T, p.H, nullptr, 0, 0, (int64_t)p.T * p.H, p.H, s);

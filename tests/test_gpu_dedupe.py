@@ -138,6 +138,22 @@ def test_dedupe_forward_simt_f32_hseq():
     _assert_same(a, b)
 
 
+def test_dedupe_f32_keeps_the_full_batch_kernel():
+    # 700 rows run the L2-streaming FFMA kernel; their 40 distinct rows alone would fit the
+    # cluster kernel, whose per-row summation order differs.  The deduplicated forward keeps
+    # the full batch's kernel, so the results stay bit-identical.
+    B, T, I, H, L, O = 700, 12, 5, 64, 2, 6
+    m = make_model(I, H, L, O, seed=32)
+    wts = weights_of(m, L, torch.float32, "cuda")
+    x, pick = _rows_with_duplicates(B, T, I, 40, torch.float32, 33)
+    a, b = _forward_pair(x, wts, out_mode="seq")
+    _assert_same(a, b)
+    rows = sorted(set(int(i) for i in torch.unique(pick)))[:6]
+    first = [int((pick == r).nonzero()[0]) for r in rows]
+    ref = oracle_of(x, *wts, out_mode="seq", rows=first)
+    assert (b[0][first].double().cpu() - torch.from_numpy(ref[0])).abs().max() <= 1e-4
+
+
 def test_dedupe_no_duplicates_and_uniform():
     B, T, I, H, L, O = 64, 30, 5, 128, 4, 24
     m = make_model(I, H, L, O, seed=28)

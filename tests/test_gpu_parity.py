@@ -116,6 +116,34 @@ def test_simt_f32_launch_shapes(cuda_device, B, T, I, H, L):
         assert_close32(c_n, r_c, "c_n")
 
 
+# The cluster-resident f32 kernel (H a multiple of 16 up to 128, I <= 128): 4, 8 and 16 batch
+# rows per 4-CTA cluster, k-slices from 8 to 16, layer-0 inputs of 1 to 128 columns.
+@pytest.mark.parametrize("B, T, I, H, L", [(3, 9, 5, 128, 2), (100, 12, 1, 64, 3), (300, 7, 128, 16, 2),
+                                           (592, 5, 17, 112, 2), (150, 10, 40, 32, 1)])
+def test_simt_f32_cluster_kernel(cuda_device, B, T, I, H, L):
+    O = 5
+    m = make_model(I, H, L, O, seed=11)
+    w = weights_of(m, L, torch.float32, cuda_device)
+    x = _rand_x(B, T, I, torch.float32, cuda_device, seed=12)
+    lens = _rand_lengths(B, T, seed=13, lo=0)
+    g = torch.Generator().manual_seed(14)
+    h0 = (0.5 * torch.randn(L, B, H, generator=g)).to(cuda_device)
+    c0 = (0.5 * torch.randn(L, B, H, generator=g)).to(cuda_device)
+    for mode in ("seq", "hseq"):
+        out, h_n, c_n = plstm.lstm_linear_forward(x, *w, lengths=lens, hx=(h0, c0), out_mode=mode, check=True)
+        r_out, r_h, r_c = oracle_of(x, *w, lengths=lens, hx=(h0, c0), out_mode=mode)
+        assert_close32(out, r_out, f"{mode} out")
+        assert_close32(h_n, r_h, "h_n")
+        assert_close32(c_n, r_c, "c_n")
+    # A row's arithmetic does not depend on its cluster companions or the batch size.
+    rows = torch.arange(0, B, 3)
+    s_out, s_h, s_c = plstm.lstm_linear_forward(x[rows], *w, lengths=lens[rows], hx=(h0[:, rows], c0[:, rows]),
+                                                out_mode="hseq")
+    assert torch.equal(out[rows], s_out)
+    assert torch.equal(h_n[:, rows], s_h)
+    assert torch.equal(c_n[:, rows], s_c)
+
+
 def test_simt_16bit_beyond_tensor_core_hidden(cuda_device):
     B, T, I, H, L, O = 3, 4, 5, 640, 2, 6
     m = make_model(I, H, L, O, seed=9)

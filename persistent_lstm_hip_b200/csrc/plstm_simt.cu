@@ -368,7 +368,8 @@ int32_t launch_simt_layer(const T* xin, int K, const T* wih_t, const T* whh_t, c
 // The contraction order per row (k-slices of the same width, partial sums added in slice
 // order) does not depend on the row's companions, the batch size or the tile.
 constexpr int kClC = 4;
-constexpr int kClThreads = 256;
+constexpr int kClThreads = 512;
+constexpr int kClRowGroups = 2;  // a work item holds NB / 2 batch rows, so 512 threads fit the registers
 
 struct ClShape {
   int nb, slices;
@@ -389,8 +390,9 @@ bool simt_cl_supported(int dtype, int K, int H, int route_batch) {
          route_batch <= 148 / kClC * 16;
 }
 
-// Quads of consecutive local rows (H / 4 of them) times k-slices fill the CTA's threads (at most 16 slices).
-int simt_cl_slices(int H) { return std::min(kClThreads / (H / 4), 16); }
+// Quads of consecutive local rows (H / 4 of them) times k-slices times the two row groups
+// fill the CTA's threads (at most 16 slices).
+int simt_cl_slices(int H) { return std::min(kClThreads / kClRowGroups / (H / 4), 16); }
 
 // Fewest batch rows per cluster (4, 8 or 16) that keep the clusters within 37 (148 SMs /
 // 4), then fewer while the shared memory does not fit.
@@ -461,7 +463,8 @@ __global__ void __cluster_dims__(kClC, 1, 1) __launch_bounds__(kClThreads)
   ptx::cluster_sync();
   uint32_t peer[kClC];
   for (int r = 0; r < kClC; ++r) peer[r] = ptx::mapa(ptx::smem_u32(xh), (uint32_t)r);
-  constexpr int kXPre = 8;  // NB * K <= 16 * 128 = kXPre * kClThreads
+  constexpr int NR = NB / kClRowGroups;  // batch rows of one work item
+  constexpr int kXPre = 4;                // NB * K <= 16 * 128 = kXPre * kClThreads
   for (int t = 0; t < tmax; ++t) {
     const float* xc = xh + (t & 1) * NB * ldx;
     const int nxt = ((t + 1) & 1) * NB * ldx;  // float offset of the next step's buffer
@@ -472,19 +475,19 @@ __global__ void __cluster_dims__(kClC, 1, 1) __launch_bounds__(kClThreads)
       const int n = i / max(K, 1), b = b0 + n;
       xr[m] = (t + 1 < tmax && i < NB * K && b < B) ? xin[((int64_t)b * Tn + t + 1) * K + i % K] : 0.0f;
     }
-    for (int item = tid; item < U * slices; item += blockDim.x) {
-      const int q = item % U, s = item / U;
+    for (int item = tid; item < U * slices * kClRowGroups; item += blockDim.x) {
+      const int q = item % U, s = (item / U) % slices, n0 = item / (U * slices) * NR;
       const int k0 = s * chunk, k1 = min(ldx, k0 + chunk);
-      float acc[NB][4];
+      float acc[NR][4];
 #pragma unroll
-      for (int n = 0; n < NB; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.0f;
+      for (int n = 0; n < NR; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.0f;
       for (int k = k0; k < k1; k += 4) {
         float4 wv[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) wv[j] = *reinterpret_cast<const float4*>(w + (size_t)(k + j) * LR + 4 * q);
 #pragma unroll
-        for (int n = 0; n < NB; ++n) {
-          const float4 xv = *reinterpret_cast<const float4*>(xc + n * ldx + k);
+        for (int n = 0; n < NR; ++n) {
+          const float4 xv = *reinterpret_cast<const float4*>(xc + (n0 + n) * ldx + k);
           const float xs[4] = {xv.x, xv.y, xv.z, xv.w};
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
@@ -496,8 +499,8 @@ __global__ void __cluster_dims__(kClC, 1, 1) __launch_bounds__(kClThreads)
         }
       }
 #pragma unroll
-      for (int n = 0; n < NB; ++n)
-        *reinterpret_cast<float4*>(part + ((size_t)s * NB + n) * LR + 4 * q) =
+      for (int n = 0; n < NR; ++n)
+        *reinterpret_cast<float4*>(part + ((size_t)s * NB + n0 + n) * LR + 4 * q) =
             make_float4(acc[n][0], acc[n][1], acc[n][2], acc[n][3]);
     }
     __syncthreads();

@@ -357,10 +357,11 @@ int32_t launch_simt_layer(const T* xin, int K, const T* wih_t, const T* whh_t, c
   return PLSTM_OK;
 }
 
-// ---- cluster-resident f32 layer kernel (H a multiple of 16, H <= 128, K <= 128) -----------
+// ---- cluster-resident f32 layer kernel (H <= 128, K <= 128) -------------------------------
 // A cluster of kClC CTAs runs one layer for NB batch rows.  CTA c owns the units
-// [c U, (c + 1) U), U = H / kClC, with all four gates: its LR = 4U = H gate rows of
-// W_ih^T / W_hh^T (local row g U + j = global row g H + c U + j) stay in shared memory for
+// [c U, (c + 1) U), U = ceil(H / 16) * 4 (units >= H are zero padding), with all four gates:
+// its LR = 4U gate rows of W_ih^T / W_hh^T (local row g U + j = global row g H + c U + j;
+// zero for padding units) stay in shared memory for
 // the whole sequence instead of streaming from L2 every step.  Each step every CTA
 // contracts [x_t ; h_{t-1}] (its own full copy) against its rows in k-slices, applies the
 // gate math to its units and stores h_t into the next step's buffer of every CTA of the
@@ -371,28 +372,32 @@ constexpr int kClC = 4;
 constexpr int kClThreads = 512;
 constexpr int kClRowGroups = 2;  // a work item holds NB / 2 batch rows, so 512 threads fit the registers
 
+// Units per CTA: a multiple of 4, so quads of local rows stay inside one gate.
+__host__ __device__ inline int cl_units(int H) { return (H + 15) / 16 * 4; }
+
 struct ClShape {
   int nb, slices;
   size_t smem;
 };
 
-// Floats: w [K4 + H4][H] | part [slices][NB][H] | xh [2][NB][K4 + H4] | cst [NB][U] | bias [H].
+// Floats: w [K4 + H4][LR] | part [slices][NB][LR] | xh [2][NB][K4 + H4] | cst [NB][U] | bias [LR].
 size_t simt_cl_smem(int nb, int slices, int K, int H) {
   const size_t ldx = align_up(K, 4) + align_up(H, 4);
-  return sizeof(float) * (ldx * H + (size_t)slices * nb * H + 2 * (size_t)nb * ldx + (size_t)nb * (H / kClC) + H);
+  const size_t U = cl_units(H), LR = 4 * U;
+  return sizeof(float) * (ldx * LR + (size_t)slices * nb * LR + 2 * (size_t)nb * ldx + (size_t)nb * U + LR);
 }
 
 // Shapes the cluster kernel serves, for batches it runs in one wave of 37 clusters of at
 // most 16 rows; larger batches stream the weights from L2 (simt_layer_kernel), which is
 // faster there (f32, H = 128, L = 4, B = 1024: 45.8 ms against 58.7 ms in two waves).
 bool simt_cl_supported(int dtype, int K, int H, int route_batch) {
-  return dtype == PLSTM_F32 && H % 16 == 0 && H >= 16 && H <= 128 && K >= 0 && K <= 128 &&
+  return dtype == PLSTM_F32 && H >= 1 && H <= 128 && K >= 0 && K <= 128 &&
          route_batch <= 148 / kClC * 16;
 }
 
-// Quads of consecutive local rows (H / 4 of them) times k-slices times the two row groups
-// fill the CTA's threads (at most 16 slices).
-int simt_cl_slices(int H) { return std::min(kClThreads / kClRowGroups / (H / 4), 16); }
+// Quads of consecutive local rows (U of them) times k-slices times the two row groups fill
+// the CTA's threads (at most 16 slices).
+int simt_cl_slices(int H) { return std::min(kClThreads / kClRowGroups / cl_units(H), 16); }
 
 // Fewest batch rows per cluster (4, 8 or 16) that keep the clusters within 37 (148 SMs /
 // 4), then fewer while the shared memory does not fit.
@@ -414,10 +419,10 @@ __global__ void __cluster_dims__(kClC, 1, 1) __launch_bounds__(kClThreads)
   extern __shared__ float4 smem4[];
   float* smem = reinterpret_cast<float*>(smem4);
   const int G = 4 * H;
-  const int U = H / kClC;   // units of this CTA
-  const int LR = 4 * U;     // its gate rows (= H)
+  const int U = cl_units(H);  // units of this CTA (c U + j >= H: padding)
+  const int LR = 4 * U;       // its gate rows
   const int K4 = (K + 3) & ~3;
-  const int ldx = K4 + H;   // H is a multiple of 16
+  const int ldx = K4 + ((H + 3) & ~3);
   float* w = smem;                               // [ldx][LR]
   float* part = w + (size_t)ldx * LR;            // [slices][NB][LR]
   float* xh = part + (size_t)slices * NB * LR;   // [2][NB][ldx]
@@ -429,6 +434,7 @@ __global__ void __cluster_dims__(kClC, 1, 1) __launch_bounds__(kClThreads)
   const int tid = threadIdx.x;
   const int chunk = ((ldx + slices - 1) / slices + 3) & ~3;
   auto grow = [&](int lr) { return (lr / U) * H + c * U + lr % U; };  // local -> global gate row
+  auto real = [&](int lr) { return c * U + lr % U < H; };
 
   if (tid < NB) {
     const int b = b0 + tid;
@@ -437,11 +443,13 @@ __global__ void __cluster_dims__(kClC, 1, 1) __launch_bounds__(kClThreads)
   for (int i = tid; i < ldx * LR; i += blockDim.x) {
     const int k = i / LR, lr = i % LR;
     float v = 0.0f;
-    if (k < K) v = wih_t[(int64_t)k * G + grow(lr)];
-    else if (k >= K4) v = whh_t[(int64_t)(k - K4) * G + grow(lr)];
+    if (real(lr)) {
+      if (k < K) v = wih_t[(int64_t)k * G + grow(lr)];
+      else if (k >= K4) v = whh_t[(int64_t)(k - K4) * G + grow(lr)];
+    }
     w[i] = v;
   }
-  for (int i = tid; i < LR; i += blockDim.x) bsm[i] = bias[grow(i)];
+  for (int i = tid; i < LR; i += blockDim.x) bsm[i] = real(i) ? bias[grow(i)] : 0.0f;
   for (int i = tid; i < 2 * NB * ldx; i += blockDim.x) xh[i] = 0.0f;
   __syncthreads();
   for (int i = tid; i < NB * H; i += blockDim.x) {
@@ -450,7 +458,7 @@ __global__ void __cluster_dims__(kClC, 1, 1) __launch_bounds__(kClThreads)
   }
   for (int i = tid; i < NB * U; i += blockDim.x) {
     const int n = i / U, j = i % U, b = b0 + n;
-    cst[i] = (b < B && c0 != nullptr) ? c0[(int64_t)b * H + c * U + j] : 0.0f;
+    cst[i] = (b < B && c0 != nullptr && c * U + j < H) ? c0[(int64_t)b * H + c * U + j] : 0.0f;
   }
   int tmax = 0;
 #pragma unroll
@@ -506,6 +514,7 @@ __global__ void __cluster_dims__(kClC, 1, 1) __launch_bounds__(kClThreads)
     __syncthreads();
     for (int i = tid; i < NB * U; i += blockDim.x) {
       const int n = i / U, j = i % U, b = b0 + n, u = c * U + j;
+      if (u >= H) continue;  // padding unit
       float hv;
       if (t < lens[n]) {
         float g[4];
@@ -542,11 +551,11 @@ __global__ void __cluster_dims__(kClC, 1, 1) __launch_bounds__(kClThreads)
     if (b >= B) break;
     const int64_t cnt = (int64_t)(Tn - tmax) * U;
     for (int64_t i = tid; i < cnt; i += blockDim.x)
-      seq_out[(int64_t)b * out_sb + (int64_t)(tmax + i / U) * out_st + c * U + i % U] = 0.0f;
+      if (c * U + i % U < H) seq_out[(int64_t)b * out_sb + (int64_t)(tmax + i / U) * out_st + c * U + i % U] = 0.0f;
   }
   for (int i = tid; i < NB * U; i += blockDim.x) {
     const int n = i / U, j = i % U, b = b0 + n;
-    if (b < B) {
+    if (b < B && c * U + j < H) {
       hfin[(int64_t)b * H + c * U + j] = xl[n * ldx + K4 + c * U + j];
       cfin[(int64_t)b * H + c * U + j] = cst[i];
     }

@@ -116,10 +116,12 @@ def test_simt_f32_launch_shapes(cuda_device, B, T, I, H, L):
         assert_close32(c_n, r_c, "c_n")
 
 
-# The cluster-resident f32 kernel (H a multiple of 16 up to 128, I <= 128): 4, 8 and 16 batch
-# rows per 4-CTA cluster, k-slices from 8 to 16, layer-0 inputs of 1 to 128 columns.
+# The cluster-resident f32 kernel (H up to 128, I <= 128, batches up to 592 rows): 4, 8 and
+# 16 batch rows per 4-CTA cluster, k-slices from 8 to 16, layer-0 inputs of 1 to 128
+# columns, hidden sizes that leave padding units in the CTAs (1, 40, 100).
 @pytest.mark.parametrize("B, T, I, H, L", [(3, 9, 5, 128, 2), (100, 12, 1, 64, 3), (300, 7, 128, 16, 2),
-                                           (592, 5, 17, 112, 2), (150, 10, 40, 32, 1)])
+                                           (592, 5, 17, 112, 2), (150, 10, 40, 32, 1), (40, 8, 3, 100, 2),
+                                           (7, 6, 2, 1, 2), (260, 9, 9, 40, 3)])
 def test_simt_f32_cluster_kernel(cuda_device, B, T, I, H, L):
     O = 5
     m = make_model(I, H, L, O, seed=11)

@@ -469,8 +469,7 @@ __global__ void __cluster_dims__(kClC, 1, 1) __launch_bounds__(kClThreads)
   }
   // Every CTA's buffers are initialised before any sibling stores into them.
   ptx::cluster_sync();
-  uint32_t peer[kClC];
-  for (int r = 0; r < kClC; ++r) peer[r] = ptx::mapa(ptx::smem_u32(xh), (uint32_t)r);
+  const uint32_t xh_u32 = ptx::smem_u32(xh);
   constexpr int NR = NB / kClRowGroups;  // batch rows of one work item
   constexpr int kXPre = 4;                // NB * K <= 16 * 128 = kXPre * kClThreads
   for (int t = 0; t < tmax; ++t) {
@@ -533,9 +532,9 @@ __global__ void __cluster_dims__(kClC, 1, 1) __launch_bounds__(kClThreads)
         hv = xc[n * ldx + K4 + u];  // finished rows keep h
         if (b < B) seq_out[(int64_t)b * out_sb + (int64_t)t * out_st + u] = 0.0f;
       }
-      const uint32_t off = (uint32_t)(nxt + n * ldx + K4 + u) * 4u;
+      const uint32_t addr = xh_u32 + (uint32_t)(nxt + n * ldx + K4 + u) * 4u;
 #pragma unroll
-      for (int r = 0; r < kClC; ++r) ptx::st_cluster_u32(peer[r] + off, __float_as_uint(hv));
+      for (int r = 0; r < kClC; ++r) ptx::st_cluster_u32(ptx::mapa(addr, (uint32_t)r), __float_as_uint(hv));
     }
 #pragma unroll
     for (int m = 0; m < kXPre; ++m) {

@@ -18,7 +18,7 @@ import sys
 from . import adaptive, adaptive_ext, ext
 from ._lib import PlstmError, PlstmUnavailable
 from .api import convert_lstm_module, convert_model_copy, convert_regressor_module, replace_lstm_inplace
-from .core import PackedWeights, lstm_linear_forward, select_backend, unique_rows
+from .core import PackedWeights, check_device_status, lstm_linear_forward, select_backend, unique_rows
 from .model import (NativeModuleFallback, PersistentLSTM, PersistentLSTM4LayerRegressor, PersistentLSTMRegressor,
                     StandardLSTMRegressor)
 
@@ -36,6 +36,7 @@ __all__ = [
     "PackedWeights",
     "select_backend",
     "unique_rows",
+    "check_device_status",
     "PlstmError",
     "PlstmUnavailable",
     "ext",

@@ -10,7 +10,7 @@ import ctypes
 import torch
 
 from . import _lib
-from .core import _stream
+from .core import _stream, device_status
 
 _DT = {torch.float16: _lib.F16, torch.bfloat16: _lib.BF16}
 
@@ -69,11 +69,14 @@ def _hidden_update(what, gate, weight, w_layout, bias, h_state, c_state, out, wr
     g = gate.contiguous()
     w = weight.contiguous()
     b = None if bias is None else bias.contiguous()
+    watcher = device_status(dev)
+    watcher.poll()  # a device failure of an earlier call surfaces here
     with torch.cuda.device(dev):
         _lib.check(lib.plstm_hidden_update(g.data_ptr(), B, T, H, w.data_ptr(), w_layout,
                                            None if b is None else b.data_ptr(), codes[dt], flags, h_state.data_ptr(),
                                            c_state.data_ptr(), out.data_ptr(), ws.data_ptr(), ws.numel(),
                                            _stream(dev)))
+    watcher.watch(ws, torch.cuda.current_stream(dev))
 
 
 def _check_cuda(what, *ts):

@@ -14,7 +14,9 @@ current CUDA stream here; all computation happens in lib/libplstm.so.
 from __future__ import annotations
 
 import ctypes
+import collections
 import os
+import threading
 from typing import Optional, Sequence, Tuple
 
 import torch
@@ -48,6 +50,84 @@ def _require_cuda(t: torch.Tensor, name: str, device: torch.device, dtype=None) 
     if dtype is not None and t.dtype != dtype:
         raise ValueError(f"{name} has dtype {t.dtype}, expected {dtype}")
     return t.contiguous()
+
+
+class DeviceStatus:
+    """Reports device-side failures of forwards that ran without a synchronising check.
+
+    The kernels record a bounded inter-CTA wait that gave up (PLSTM_ETIMEOUT and
+    the failing CTA / step) in the status word at the start of the call's
+    workspace.  Without PLSTM_FLAG_SYNC_CHECK nothing reads that word before the
+    temporary workspace is freed, so after every such forward the word is copied
+    asynchronously into pinned host memory, on the same stream, behind an event.
+    The next forward on the device (or ``check_device_status``) looks at every
+    copy whose event has completed, without synchronising, and raises
+    ``PlstmError(PLSTM_ETIMEOUT)`` for the first failure it finds.
+    """
+
+    RING = 64  # copies in flight per device before the oldest one is waited for
+
+    def __init__(self, device: torch.device):
+        self.device = device
+        self.host = torch.zeros(self.RING, 2, dtype=torch.int32, pin_memory=True)
+        self.events = [None] * self.RING
+        self.pending = collections.deque()
+        self.next = 0
+        self.lock = threading.Lock()
+
+    def _retire(self, wait: bool) -> None:
+        while self.pending:
+            slot = self.pending[0]
+            ev = self.events[slot]
+            if not wait and not ev.query():
+                return
+            ev.synchronize()
+            self.pending.popleft()
+            self.events[slot] = None
+            st, detail = (int(v) for v in self.host[slot].tolist())
+            if st != _lib.OK:
+                raise _lib.PlstmError(
+                    st, f"device status {st} (cta {detail >> 16}, step {detail & 0xffff}) of an earlier forward "
+                        f"on {self.device}: a bounded inter-CTA wait gave up; its outputs are incomplete")
+
+    def poll(self, wait: bool = False) -> None:
+        """Raises for a failed earlier forward whose status copy has landed (all of them with wait=True)."""
+        with self.lock:
+            self._retire(wait)
+
+    def watch(self, ws: torch.Tensor, stream: torch.cuda.Stream) -> None:
+        """Enqueues the status copy of the forward just enqueued on `stream` with workspace `ws`."""
+        with self.lock:
+            while len(self.pending) >= self.RING:  # only when the host runs 64 forwards ahead of the GPU
+                self._retire(True)
+            slot = self.next
+            self.next = (slot + 1) % self.RING
+            with torch.cuda.stream(stream):
+                self.host[slot].copy_(ws[:8].view(torch.int32), non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record(stream)
+            self.events[slot] = ev
+            self.pending.append(slot)
+
+
+_status_lock = threading.Lock()
+_status = {}
+
+
+def device_status(device: torch.device) -> DeviceStatus:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    with _status_lock:
+        st = _status.get(idx)
+        if st is None:
+            st = _status[idx] = DeviceStatus(torch.device("cuda", idx))
+        return st
+
+
+def check_device_status(device: Optional[torch.device] = None) -> None:
+    """Waits for the status copies of every unchecked forward on `device` (default: the
+    current device) and raises PlstmError(PLSTM_ETIMEOUT) if one of them failed."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    device_status(dev).poll(wait=True)
 
 
 def make_desc(*, batch: int, seq_len: int, input_size: int, hidden_size: int, num_layers: int,
@@ -204,8 +284,11 @@ class PackedWeights:
             h_n = torch.empty(L, B, H, dtype=self.dtype, device=dev)
             c_n = torch.empty(L, B, H, dtype=torch.float32 if c_n_f32 else self.dtype, device=dev)
         flags = extra_flags | (_lib.FLAG_CN_F32 if c_n_f32 else 0) | (_lib.FLAG_DEDUPE if dedupe else 0)
-        if check if check is not None else _env_check():
+        sync_check = check if check is not None else _env_check()
+        if sync_check:
             flags |= _lib.FLAG_SYNC_CHECK
+        watcher = device_status(dev)
+        watcher.poll()  # a failure of an earlier unchecked forward surfaces here
         d = self.desc(batch=B, seq_len=T, extra_flags=flags, timeout_ms=timeout_ms)
         nbytes = ctypes.c_size_t(0)
         _lib.check(lib.plstm_workspace_size(ctypes.byref(d), ctypes.byref(nbytes)))
@@ -215,6 +298,8 @@ class PackedWeights:
                                           _ptr(c0), _ptr(out), _ptr(h_n), _ptr(c_n), ws.data_ptr(), ws.numel(),
                                           _stream(dev))
         _lib.check(rc)
+        if not sync_check:
+            watcher.watch(ws, torch.cuda.current_stream(dev))
         return out, h_n, c_n
 
 

@@ -45,8 +45,6 @@ void profile_end(cudaStream_t s) {
   t_prof_start = nullptr;
 }
 
-namespace {
-
 int32_t make_problem(const plstm_desc* d, Problem* p) {
   PLSTM_CHECK_ARG(d != nullptr, "descriptor is NULL");
   PLSTM_CHECK_ARG(d->batch >= 0, "batch must be >= 0");
@@ -77,6 +75,8 @@ int32_t make_problem(const plstm_desc* d, Problem* p) {
   return PLSTM_OK;
 }
 
+namespace {
+
 // Picks the backend; fails if the caller forced one that cannot serve `p`.
 int32_t pick_backend(const plstm_desc* d, const Problem& p, int* backend) {
   std::string why;
@@ -92,13 +92,6 @@ int32_t pick_backend(const plstm_desc* d, const Problem& p, int* backend) {
   } else {
     *backend = tc_ok ? PLSTM_BACKEND_TC : PLSTM_BACKEND_SIMT;
   }
-  return PLSTM_OK;
-}
-
-int32_t check_device(const Problem& p) {
-  int cur = -1;
-  PLSTM_TRY_CUDA(cudaGetDevice(&cur));
-  if (cur != p.device) PLSTM_TRY_CUDA(cudaSetDevice(p.device));
   return PLSTM_OK;
 }
 
@@ -240,7 +233,8 @@ static int32_t pack_impl(const plstm_desc* d, int ih_layout, int hh_layout, cons
     set_error("packed buffer too small: need " + std::to_string(need) + " bytes");
     return PLSTM_EWORKSPACE;
   }
-  if ((rc = check_device(p)) != PLSTM_OK) return rc;
+  DeviceGuard dev_guard;
+  if ((rc = dev_guard.enter(p.device)) != PLSTM_OK) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return b == PLSTM_BACKEND_TC
              ? tc_pack(p, ih_layout, hh_layout, w_ih, w_hh, b_ih, b_hh, w_lin, b_lin, packed, s)
@@ -277,7 +271,8 @@ int32_t plstm_forward_packed(const plstm_desc* d, const void* packed, const void
     set_error("workspace too small: need " + std::to_string(need) + " bytes");
     return PLSTM_EWORKSPACE;
   }
-  if ((rc = check_device(p)) != PLSTM_OK) return rc;
+  DeviceGuard dev_guard;
+  if ((rc = dev_guard.enter(p.device)) != PLSTM_OK) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if ((p.flags & PLSTM_FLAG_DEDUPE) && (rc = dedupe_stream_ok(s)) != PLSTM_OK) return rc;
   PLSTM_TRY_CUDA(cudaMemsetAsync(workspace, 0, kStatusBytes, s));
@@ -355,7 +350,8 @@ int32_t plstm_unique_rows(const plstm_desc* d, const void* x, const int32_t* len
   }
   *count = 0;
   if (p.B == 0) return PLSTM_OK;
-  if ((rc = check_device(p)) != PLSTM_OK) return rc;
+  DeviceGuard dev_guard;
+  if ((rc = dev_guard.enter(p.device)) != PLSTM_OK) return rc;
   return unique_rows(p, x, lengths, h0, c0, row_map, unique_index, count, workspace,
                      static_cast<cudaStream_t>(stream));
 }

@@ -58,6 +58,31 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 
 inline size_t dtype_size(int32_t dt) { return dt == PLSTM_F32 ? 4 : 2; }
 
+// Makes a device current for the lifetime of the guard and puts the caller's
+// device back on every return path, so that no entry point leaves the calling
+// thread on another device.
+class DeviceGuard {
+ public:
+  DeviceGuard() = default;
+  DeviceGuard(const DeviceGuard&) = delete;
+  DeviceGuard& operator=(const DeviceGuard&) = delete;
+  ~DeviceGuard() {
+    if (prev_ >= 0) cudaSetDevice(prev_);
+  }
+  int32_t enter(int dev) {
+    int cur = -1;
+    PLSTM_TRY_CUDA(cudaGetDevice(&cur));
+    if (cur != dev) {
+      PLSTM_TRY_CUDA(cudaSetDevice(dev));
+      prev_ = cur;
+    }
+    return PLSTM_OK;
+  }
+
+ private:
+  int prev_ = -1;
+};
+
 // ---- element conversion ----------------------------------------------------
 template <typename T>
 __device__ __forceinline__ float to_f32(T v);
@@ -104,6 +129,10 @@ struct Problem {
   bool out_seq() const { return (flags & PLSTM_FLAG_OUT_SEQ) != 0; }
   bool out_last() const { return (flags & PLSTM_FLAG_OUT_LAST) != 0; }
 };
+
+// Validates a descriptor and fills the Problem every backend reads (plstm_abi.cu);
+// PLSTM_EINVAL with the message set on a bad field.
+int32_t make_problem(const plstm_desc* d, Problem* p);
 
 // Generic layer-sequential FFMA backend (any shape, f32/f16/bf16).
 size_t simt_packed_size(const Problem& p);

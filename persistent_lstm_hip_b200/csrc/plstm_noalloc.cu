@@ -65,35 +65,22 @@ extern "C" int32_t plstm_forward_packed_noalloc(const plstm_desc* d, const void*
                                                 const int32_t* lengths, const void* h0, const void* c0,
                                                 void* out, void* h_n, void* c_n, void* stream) {
   clear_error();
-  PLSTM_CHECK_ARG(d != nullptr, "descriptor is NULL");
-  PLSTM_CHECK_ARG(d->batch >= 0 && d->seq_len >= 0, "batch and seq_len must be >= 0");
-  PLSTM_CHECK_ARG(d->input_size > 0 && d->hidden_size > 0 && d->num_layers > 0, "sizes must be > 0");
+  Problem p;
+  int32_t rc = make_problem(d, &p);  // the same argument checks as every other entry point
+  if (rc != PLSTM_OK) return rc;
+  // What this entry point adds: the 16-bit tensor-core path only, and no option
+  // whose scratch lives outside the fixed array.
   PLSTM_CHECK_ARG(d->dtype == PLSTM_F16 || d->dtype == PLSTM_BF16,
                   "plstm_forward_packed_noalloc serves the f16 / bf16 tensor-core path only");
   PLSTM_CHECK_ARG(d->backend == PLSTM_BACKEND_AUTO || d->backend == PLSTM_BACKEND_TC,
                   "plstm_forward_packed_noalloc serves the tensor-core backend only");
-  const int outs = ((d->flags & PLSTM_FLAG_OUT_SEQ) ? 1 : 0) + ((d->flags & PLSTM_FLAG_OUT_LAST) ? 1 : 0) +
-                   ((d->flags & PLSTM_FLAG_NO_LINEAR) ? 1 : 0);
-  PLSTM_CHECK_ARG(outs == 1, "exactly one of PLSTM_FLAG_OUT_SEQ, _OUT_LAST, _NO_LINEAR must be set");
   PLSTM_CHECK_ARG(!(d->flags & PLSTM_FLAG_TRACE), "PLSTM_FLAG_TRACE needs a caller workspace");
   PLSTM_CHECK_ARG(!(d->flags & PLSTM_FLAG_DEDUPE), "PLSTM_FLAG_DEDUPE needs a caller workspace");
-  if (!(d->flags & PLSTM_FLAG_NO_LINEAR)) PLSTM_CHECK_ARG(d->output_size > 0, "output_size must be > 0");
   PLSTM_CHECK_ARG(packed != nullptr, "packed is NULL");
   PLSTM_CHECK_ARG(aligned16(packed), "packed must be 16-byte aligned");
-  PLSTM_CHECK_ARG(d->batch == 0 || d->seq_len == 0 || x != nullptr, "x is NULL");
-  PLSTM_CHECK_ARG(d->batch == 0 || out != nullptr, "out is NULL");
+  PLSTM_CHECK_ARG(p.B == 0 || p.T == 0 || x != nullptr, "x is NULL");
+  PLSTM_CHECK_ARG(p.B == 0 || out != nullptr, "out is NULL");
   PLSTM_CHECK_ARG((h0 == nullptr) == (c0 == nullptr), "h0 and c0 must both be given or both be NULL");
-  Problem p;
-  p.B = d->batch;
-  p.T = d->seq_len;
-  p.I = d->input_size;
-  p.H = d->hidden_size;
-  p.L = d->num_layers;
-  p.O = (d->flags & PLSTM_FLAG_NO_LINEAR) ? 0 : d->output_size;
-  p.dtype = d->dtype;
-  p.flags = d->flags;
-  p.timeout_ms = d->timeout_ms > 0 ? d->timeout_ms : 2000;
-  p.device = d->device;
   std::string why;
   if (!tc_supported(p, &why)) {
     set_error("plstm_forward_packed_noalloc: tensor-core backend cannot serve this problem: " + why);
@@ -106,11 +93,10 @@ extern "C" int32_t plstm_forward_packed_noalloc(const plstm_desc* d, const void*
               " bytes (24 MiB) the no-allocation entry point holds; use plstm_forward_packed with a workspace");
     return PLSTM_EINVAL;
   }
-  int cur = -1;
-  PLSTM_TRY_CUDA(cudaGetDevice(&cur));
-  if (cur != p.device) PLSTM_TRY_CUDA(cudaSetDevice(p.device));
+  DeviceGuard dev_guard;  // the caller's current device is restored on return
+  if ((rc = dev_guard.enter(p.device)) != PLSTM_OK) return rc;
   void* ws = nullptr;
-  int32_t rc = scratch_for_current_device(p.device, &ws);
+  rc = scratch_for_current_device(p.device, &ws);
   if (rc != PLSTM_OK) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   PLSTM_TRY_CUDA(cudaMemsetAsync(ws, 0, kStatusBytes, s));

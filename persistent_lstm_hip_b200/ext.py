@@ -18,7 +18,7 @@ from typing import Sequence
 import torch
 
 from . import _lib
-from .core import _stream
+from .core import _stream, device_status
 
 
 def _check(cond: bool, msg: str) -> None:
@@ -63,10 +63,13 @@ def _ref4_call(fn_name: str, x, tensors, *, hidden_size: int, ih_kpair_k: int = 
     a_ih, k1 = _lib.ptr_array([t.data_ptr() for t in w_ih])
     a_hh, k2 = _lib.ptr_array([t.data_ptr() for t in w_hh])
     a_b, k3 = _lib.ptr_array([t.data_ptr() for t in bias])
+    watcher = device_status(dev)
+    watcher.poll()  # a device failure of an earlier forward surfaces here
     with torch.cuda.device(dev):
         rc = getattr(lib, fn_name)(x.data_ptr(), B, T, I, H, O, a_ih, a_hh, a_b, w_lin.data_ptr(),
                                    b_lin.data_ptr(), out.data_ptr(), ws.data_ptr(), ws.numel(), _stream(dev))
     _lib.check(rc)
+    watcher.watch(ws, torch.cuda.current_stream(dev))
     return out
 
 

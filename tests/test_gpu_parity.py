@@ -357,6 +357,33 @@ def test_timeout_is_reported_not_hung(cuda_device):
     assert_close16(out, r_out, "after timeout")
 
 
+def test_unchecked_timeout_raises_by_the_next_call(cuda_device):
+    """Without a synchronising check the failure of a forward is not lost: its status word
+    is copied back asynchronously and the next forward on the device raises PLSTM_ETIMEOUT
+    (the wait is host-armed: a producer skips one hand-off, bounded to 50 ms)."""
+    B, T, I, H, L, O = 32, 16, 5, 128, 4, 24
+    m = make_model(I, H, L, O, seed=11)
+    w = weights_of(m, L, torch.float16, cuda_device)
+    x = _rand_x(B, T, I, torch.float16, cuda_device)
+    pw = core.PackedWeights(*w, out_mode="last", backend="tc")
+    core.check_device_status(cuda_device)  # nothing pending from earlier tests
+    pw.forward(x, check=False, timeout_ms=50, extra_flags=_lib.FLAG_TEST_DROP)  # returns without an error
+    torch.cuda.synchronize()
+    with pytest.raises(plstm.PlstmError) as ei:
+        pw.forward(x, check=False)
+    assert ei.value.code == _lib.ETIMEOUT
+    assert "earlier forward" in str(ei.value)
+    # Reported once; the context stays usable and later forwards are correct.
+    out, _, _ = pw.forward(x, check=False)
+    core.check_device_status(cuda_device)
+    r_out, _, _ = oracle_of(x, *w, out_mode="last")
+    assert_close16(out, r_out, "after timeout")
+    # check_device_status waits for the copy itself.
+    pw.forward(x, check=False, timeout_ms=50, extra_flags=_lib.FLAG_TEST_DROP)
+    with pytest.raises(plstm.PlstmError):
+        core.check_device_status(cuda_device)
+
+
 @pytest.mark.parametrize("mode", ["seq", "last", "hseq"])
 @pytest.mark.parametrize("varlen", [False, True])
 def test_single_slot_wavefront_kernel(cuda_device, monkeypatch, mode, varlen):

@@ -111,3 +111,47 @@ def test_unique_rows_restates_the_uniform_check():
     c0[1, 3, 7] = 1.0
     row_map, _, n = oracle.unique_rows(x, lengths=[5, 6, 5, 6], h0=h0, c0=c0)
     assert list(row_map) == [0, 1, 0, 2] and n == 3
+
+
+# ---- against the reference's own C++ CPU path (oracle/_ref, built from
+# persistent_lstm_hip/csrc/persistent_lstm_reference.cpp by oracle/build_ref.py) ----
+def _ref_or_skip():
+    from oracle import ref
+
+    if not ref.available():
+        pytest.skip("oracle/_ref/libplstm_ref.so is not built (needs the reference checkout at build time)")
+    return ref
+
+
+def _cfg2_like_weights(seed, I=5, H=128, O=24):
+    rng = np.random.default_rng(seed)
+    k = 1.0 / np.sqrt(H)
+    u = lambda *s: rng.uniform(-k, k, size=s)
+    w_ih = [u(4 * H, I if l == 0 else H) for l in range(4)]
+    w_hh = [u(4 * H, H) for _ in range(4)]
+    b_ih = [u(4 * H) for _ in range(4)]
+    b_hh = [u(4 * H) for _ in range(4)]
+    return w_ih, w_hh, b_ih, b_hh, u(O, H), u(O)
+
+
+@pytest.mark.parametrize("B, T, I, H", [(6, 40, 5, 128), (3, 17, 7, 32)])
+def test_oracle_matches_reference_cpp_path(B, T, I, H):
+    """The C restatement equals persistent_lstm4_forward_reference (f64) on the same inputs."""
+    ref = _ref_or_skip()
+    w = _cfg2_like_weights(B * 131 + T, I=I, H=H)
+    x = np.random.default_rng(7).standard_normal((B, T, I))
+    got, _, _ = oracle.forward(x, *w, out_mode="last")
+    want = ref.forward(x, *w, precision="f64", threads=2)
+    np.testing.assert_allclose(got, want, atol=1e-12, rtol=0)
+
+
+def test_oracle_matches_reference_cpp_path_cfg2_rows():
+    """Config-2 shape (T = 1000 dependent steps) on 4 rows: f64 to 1e-12, and the f32
+    restatement (the timed CPU port) within 1e-4 of the reference's f32 run."""
+    ref = _ref_or_skip()
+    w = _cfg2_like_weights(0)
+    x = np.random.default_rng(1).standard_normal((4, 1000, 5))
+    got, _, _ = oracle.forward(x, *w, out_mode="last")
+    np.testing.assert_allclose(got, ref.forward(x, *w, precision="f64", threads=2), atol=1e-12, rtol=0)
+    got32, _, _ = oracle.forward(x, *w, out_mode="last", precision="f32")
+    np.testing.assert_allclose(got32, ref.forward(x, *w, precision="f32", threads=2), atol=1e-4, rtol=0)

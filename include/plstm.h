@@ -299,6 +299,19 @@ PLSTM_API int32_t plstm_profile_read(float* ms, int32_t* launches);
  * (tmem lane << 8 | column). */
 PLSTM_API int32_t plstm_diag_tmem_layout(uint32_t* out, void* stream);
 
+/* Dependent-step latency probe (no counterpart in the reference; its serial
+ * per-step loop is persistent_lstm_hip.cu:493-558): one cluster of two CTAs runs
+ * the wavefront kernel's per-step dependency chain alone for `steps` steps of a
+ * `rows`-row (16 or 32) slot: the sibling's h lands, 8 tcgen05 MMAs over it
+ * (two M = 128 tiles x K = 64) and their commit, one tcgen05.ld, the kernel's gate
+ * math, h written to shared memory and one bulk copy of this CTA's 64 units into
+ * the sibling.  out (device, 16 uint64) receives [0] status (0 ok, 1 a bounded
+ * wait gave up), [1] SM cycles over [2] steps (from steps / 4 on), [3..8] summed
+ * cycles of the phases landed -> commit issued -> accumulator seen -> loaded ->
+ * h written -> copy issued -> next h landed.  The latency floor of the roofline. */
+PLSTM_API int32_t plstm_diag_step_latency(int32_t rows, int32_t steps, uint64_t* out, int32_t timeout_ms,
+                                          void* stream);
+
 #ifdef __cplusplus
 }
 #endif

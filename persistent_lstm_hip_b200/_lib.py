@@ -69,6 +69,7 @@ PROTOTYPES = {
     "plstm_hidden_update_workspace_size": (_I32, [_I32, _I32, _I32, _I32, _I32, _I32, ctypes.POINTER(_SZ)]),
     "plstm_hidden_update": (_I32, [_P, _I32, _I32, _I32, _P, _I32, _P, _I32, _I32, _P, _P, _P, _P, _SZ, _P]),
     "plstm_diag_tmem_layout": (_I32, [_P, _P]),
+    "plstm_diag_step_latency": (_I32, [_I32, _I32, _P, _I32, _P]),
     "plstm_launch_count": (ctypes.c_int64, []),
     "plstm_profile": (_I32, [_I32]),
     "plstm_profile_read": (_I32, [ctypes.POINTER(ctypes.c_float), ctypes.POINTER(_I32)]),

@@ -1870,6 +1870,217 @@ TcWs tc_ws(const Problem& p, const Plan& pl) {
   return w;
 }
 
+// ---- dependent-step latency probe ---------------------------------------------------
+// The dependency chain of one wavefront layer-step, measured alone: a cluster of two
+// CTAs, each owning 64 hidden units (256 gate rows: two M = 128 tiles whose A slice,
+// K = 64, sits in tensor memory), runs `steps` times
+//   sibling's h lands -> 8 MMAs over it (2 tiles x 4 K steps, N = NH) + commit ->
+//   mbarrier -> tcgen05.ld -> the kernel's gate math (lstm_cells, 2 x NH / 4 x 2 cells
+//   per thread) -> h to shared memory -> one bulk copy of this CTA's NH x 64 units
+//   (4 KB at NH = 32) into the sibling, completing on its barrier.
+// Nothing else runs: no input MMAs, no own-half MMAs, no layer pipeline, no Linear head,
+// no second slot.  It is the north-star "dependent-step microbenchmark": its cycles per
+// step are a floor for any step of that shape.  CTA 0 records clock64 stamps of every
+// step and writes, for the steps from steps / 4 on:
+//   out[0] status (0 ok, 1 a bounded wait gave up), out[1] cycles, out[2] steps counted,
+//   out[3..8] summed cycles of: landed -> commit issued, commit -> accumulator seen,
+//   seen -> loaded, loaded -> h written (warp 0), h written -> copy issued (last warp),
+//   copy issued -> next sibling h landed.
+constexpr int kProbeOut = 16;
+
+template <int NH>
+__global__ void __launch_bounds__(160, 1) step_probe_kernel(int steps, unsigned long long timeout_ns,
+                                                             unsigned long long* out) {
+  constexpr int CPW = NH / 8;
+  constexpr uint32_t kHalf = NH * 128;  // one 64-unit K block of h: NH rows x 128 bytes (128-byte swizzle)
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = ptx::smem_u32(sm);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int s = (int)ptx::cluster_ctarank();
+  constexpr uint32_t kBar = 4 * kHalf;  // [parity 2][unit half 2] h buffers, then the barriers
+  auto full = [&](int b) { return sbase + kBar + 8u * b; };
+  auto mma = [&](int b) { return sbase + kBar + 16u + 8u * b; };
+  auto hready = [&](int b) { return sbase + kBar + 32u + 8u * b; };
+  auto hbuf = [&](int b, int half) { return sbase + (uint32_t)(2 * b + half) * kHalf; };
+  uint32_t* counter = reinterpret_cast<uint32_t*>(sm + kBar + 48);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + kBar + 52);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + kBar + 56);
+  volatile unsigned long long* stamp = reinterpret_cast<volatile unsigned long long*>(sm + kBar + 64);  // [8]
+
+  for (int i = tid; i < (int)(4 * kHalf / 4); i += blockDim.x) reinterpret_cast<uint32_t*>(sm)[i] = 0u;  // h0 = 0
+  if (tid == 0) {
+    for (int b = 0; b < 2; ++b) {
+      ptx::mbar_init(full(b), 1);
+      ptx::mbar_init(mma(b), 1);
+      ptx::mbar_init(hready(b), 4);
+    }
+    *counter = 0;
+    *abort_flag = 0;
+    ptx::fence_mbar_init_cluster();
+    // The sibling's h of steps 1 and 2.
+    if (steps > 1) ptx::mbar_arrive_expect_tx(full(1), kHalf);
+    if (steps > 2) ptx::mbar_arrive_expect_tx(full(0), kHalf);
+  }
+  if (warp == 0) {
+    ptx::tmem_alloc(sbase + kBar + 56, 128);
+    ptx::tmem_relinquish();
+  }
+  ptx::fence_proxy_async_smem();
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(tslot);
+  if (warp < 4) {  // A = small alternating values, two tiles of 32 columns (K = 64) per lane
+    uint32_t r[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) r[i] = ((i + lane) & 1) ? 0x20002000u : 0xa000a000u;  // +-2^-7 in f16
+#pragma unroll
+    for (int tau = 0; tau < 2; ++tau)
+      ptx::tmem_st_32x32b_x32(tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)(32 * tau), r);
+    ptx::tmem_wait_st();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  ptx::cluster_sync();
+  const uint32_t dcol = tmem + 64;  // D[tau] at 64 + tau NH
+  bool ok = true;
+  auto give_up = [&]() {
+    if (lane == 0 && !*abort_flag) {
+      for (int r = 0; r < 2; ++r) ptx::st_cluster_u32(ptx::mapa(ptx::smem_u32((void*)abort_flag), (uint32_t)r), 1u);
+      if (s == 0) out[0] = 1ull;
+    }
+    ok = false;
+  };
+
+  if (warp == 4) {
+    // ---- control warp: waits for the sibling's h, issues the 8 MMAs and the commit ----
+    constexpr uint32_t idesc = ptx::idesc_f16(128, NH, false);
+    const int t0 = steps / 4;
+    unsigned long long sum[6] = {0, 0, 0, 0, 0, 0}, first = 0, prev_push = 0, landed = 0;
+    int counted = 0;
+    for (int t = 0; t < steps && ok; ++t) {
+      const int b = t & 1;
+      if (t >= 1) {
+        if (!warp_wait_phase(full(b), ((t - 1) >> 1) & 1, abort_flag, timeout_ns)) {
+          give_up();
+          break;
+        }
+        if (t + 2 < steps && ptx::elect_one()) ptx::mbar_arrive_expect_tx(full(b), kHalf);
+        __syncwarp();
+      }
+      landed = clock64();
+      if (t == t0) first = landed;
+      if (t > t0) sum[5] += landed - prev_push;
+      if (ptx::elect_one()) {
+        ptx::tc_fence_after();
+        const uint64_t dB = ptx::desc_k_sw128(hbuf(b, 1 - s));
+#pragma unroll
+        for (int tau = 0; tau < 2; ++tau)
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            ptx::mma_f16_ts(dcol + (uint32_t)(tau * NH), tmem + (uint32_t)(32 * tau + 8 * kk),
+                            dB + (uint64_t)((kk * 32) >> 4), idesc, kk != 0 ? 1u : 0u);
+        ptx::mma_commit(mma(b));
+      }
+      __syncwarp();
+      const unsigned long long committed = clock64();
+      if (!warp_wait_phase(hready(b), (t >> 1) & 1, abort_flag, timeout_ns)) {
+        give_up();
+        break;
+      }
+      if (t >= t0) {
+        sum[0] += committed - landed;
+        sum[1] += stamp[0] - committed;
+        sum[2] += stamp[1] - stamp[0];
+        sum[3] += stamp[2] - stamp[1];
+        sum[4] += stamp[3] - stamp[2];
+        prev_push = stamp[3];
+        ++counted;
+      }
+    }
+    if (s == 0 && lane == 0 && ok) {
+      out[0] = 0ull;
+      out[1] = landed - first;
+      out[2] = (unsigned long long)max(counted - 1, 0);
+      for (int i = 0; i < 6; ++i) out[3 + i] = sum[i];
+    }
+    // The last step's MMAs completed before its gate math ran, so TMEM is idle here.
+  } else {
+    // ---- compute warps: lane quadrant `warp`, the kernel's gate math ----
+    const int q = warp, j8 = lane >> 2, cpair = (lane & 3) * 2;
+    float c_st[2][CPW][2];
+    uint16_t h_st[2][CPW][2];
+    int len_c[CPW][2];
+    const float bz[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+    for (int tau = 0; tau < 2; ++tau)
+#pragma unroll
+      for (int jc = 0; jc < CPW; ++jc)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          c_st[tau][jc][e] = 0.f;
+          h_st[tau][jc][e] = 0;
+          len_c[jc][e] = steps;
+        }
+    for (int t = 0; t < steps && ok; ++t) {
+      const int b = t & 1;
+      if (!warp_wait_phase(mma(b), (t >> 1) & 1, abort_flag, timeout_ns)) {
+        give_up();
+        break;
+      }
+      ptx::tc_fence_after();
+      if (q == 0 && lane == 0) stamp[0] = clock64();
+      uint32_t rif[2][4 * CPW], rgo[2][4 * CPW];
+#pragma unroll
+      for (int tau = 0; tau < 2; ++tau) {
+        const uint32_t col = dcol + (uint32_t)(tau * NH);
+        tmem_ld_chunks<CPW>(col + ((uint32_t)(32 * q) << 16), rif[tau]);
+        tmem_ld_chunks<CPW>(col + ((uint32_t)(32 * q + 16) << 16), rgo[tau]);
+      }
+      ptx::tmem_wait_ld();
+      ptx::tc_fence_before();
+      if (q == 0 && lane == 0) stamp[1] = clock64();
+      uint16_t hw[2][CPW][2];
+      lstm_cells<CPW, false, false>(rif, rgo, bz, c_st, h_st, len_c, t, hw);
+      uint8_t* dst = sm + (size_t)(2 * (b ^ 1) + s) * kHalf;
+#pragma unroll
+      for (int tau = 0; tau < 2; ++tau)
+#pragma unroll
+        for (int jc = 0; jc < CPW; ++jc)
+#pragma unroll
+          for (int e = 0; e < 2; ++e)
+            *reinterpret_cast<uint16_t*>(dst + sw128_off(8 * jc + cpair + e, 8 * (4 * tau + q) + j8)) = hw[tau][jc][e];
+      ptx::fence_proxy_async_smem();
+      if (q == 0 && lane == 0) stamp[2] = clock64();
+      __syncwarp();
+      if (lane == 0) {
+        if (ptx::atom_add_acq_rel_smem(ptx::smem_u32(counter), 1u) % 4u == 3u) {
+          stamp[3] = clock64();
+          if (t + 1 < steps) {
+            const uint32_t src = hbuf(b ^ 1, s);
+            ptx::bulk_s2c(ptx::mapa(src, (uint32_t)(s ^ 1)), src, kHalf, ptx::mapa(full(b ^ 1), (uint32_t)(s ^ 1)));
+          }
+        }
+        ptx::mbar_arrive(hready(b));
+      }
+    }
+  }
+  if (*abort_flag) {  // copies already in flight toward the sibling land before either CTA leaves
+    const unsigned long long w0 = ptx::globaltimer();
+    while (ptx::globaltimer() - w0 < 50000ull) {
+    }
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem, 128);
+  }
+  ptx::cluster_sync();
+}
+
 }  // namespace tc
 
 using namespace tc;
@@ -2078,3 +2289,40 @@ int32_t tc_forward(const Problem& p, const void* packed, const void* x, const in
 }
 
 }  // namespace plstm
+
+using namespace plstm;
+using namespace plstm::tc;
+
+// Dependent-step latency probe (see step_probe_kernel).  out: device buffer of
+// kProbeOut uint64 words.
+extern "C" int32_t plstm_diag_step_latency(int32_t rows, int32_t steps, uint64_t* out, int32_t timeout_ms,
+                                           void* stream) {
+  clear_error();
+  PLSTM_CHECK_ARG(rows == 16 || rows == 32, "rows must be 16 or 32");
+  PLSTM_CHECK_ARG(steps >= 8 && steps <= 1000000, "steps must be in [8, 1000000]");
+  PLSTM_CHECK_ARG(out != nullptr, "out is NULL");
+  PLSTM_CHECK_ARG(timeout_ms >= 0, "timeout_ms must be >= 0");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  void* k = rows == 16 ? (void*)step_probe_kernel<16> : (void*)step_probe_kernel<32>;
+  const int smem = 4 * rows * 128 + 1024 + 1024;
+  PLSTM_TRY_CUDA(cudaMemsetAsync(out, 0, kProbeOut * sizeof(uint64_t), s));
+  PLSTM_TRY_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2, 1, 1);
+  cfg.blockDim = dim3(160, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeClusterDimension;
+  attr.val.clusterDim.x = 2;
+  attr.val.clusterDim.y = 1;
+  attr.val.clusterDim.z = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  int st = steps;
+  unsigned long long tns = (unsigned long long)(timeout_ms > 0 ? timeout_ms : 2000) * 1000000ull;
+  void* args[] = {&st, &tns, &out};
+  PLSTM_TRY_CUDA(cudaLaunchKernelExC(&cfg, k, args));
+  note_launches(1);
+  return PLSTM_OK;
+}

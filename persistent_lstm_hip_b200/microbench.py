@@ -11,6 +11,10 @@
             --seq 1000 --input 5 --dtype bf16 --out last]
         One whole forward (lstm_linear_forward's packed call, PyTorch-default weights,
         N(0, 1) x) of any shape: configs 3 and 4, the generic shapes, the [B,T,O] mode.
+    python -m persistent_lstm_hip_b200.microbench probe [--rows 16 --steps 20000]
+        The dependent-step latency probe (plstm_diag_step_latency): one wavefront
+        layer-step's dependency chain alone, cycles and microseconds per step and
+        its phases; the latency floor of the roofline.
 """
 from __future__ import annotations
 
@@ -79,6 +83,40 @@ def step(args) -> dict:
             "us_per_step": k_ms * 1e3 / (args.seq + 4)}
 
 
+def step_latency(rows: int = 16, steps: int = 20000, device: int = 0) -> dict:
+    """The dependent-step latency probe (plstm_diag_step_latency): cycles and microseconds of one
+    wavefront layer-step's dependency chain run alone, with its phases."""
+    from . import _lib
+
+    dev = torch.device("cuda", device)
+    lib = _lib.load()
+    out = torch.zeros(16, dtype=torch.int64, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(2):  # warm-up (module load, clocks)
+        _lib.check(lib.plstm_diag_step_latency(rows, 1000, out.data_ptr(), 0, stream.cuda_stream))
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    _lib.check(lib.plstm_diag_step_latency(rows, steps, out.data_ptr(), 0, stream.cuda_stream))
+    b.record(stream)
+    torch.cuda.synchronize(dev)
+    o = [int(v) for v in out.cpu().tolist()]
+    if o[0] != 0:
+        raise _lib.PlstmError(_lib.ETIMEOUT, "step-latency probe: a bounded wait gave up")
+    n = max(o[2], 1)
+    phases = ["landed->commit issued", "commit->accumulator seen", "seen->loaded", "loaded->h written",
+              "h written->copy issued", "copy issued->next h landed"]
+    return {"rows": rows, "steps": steps, "cycles_per_step": o[1] / n,
+            "us_per_step": a.elapsed_time(b) * 1e3 / steps,
+            "phase_cycles": {k: o[3 + i] / n for i, k in enumerate(phases)},
+            "method": "plstm_diag_step_latency: 2-CTA cluster; per step the sibling's h lands, 8 tcgen05 MMAs "
+                      "(2 x M128, K64, N=rows) + commit, tcgen05.ld, the kernel's gate math, h to shared memory, "
+                      "one bulk DSMEM copy to the sibling; CUDA events over the launch / steps"}
+
+
+def probe(args) -> dict:
+    return step_latency(args.rows, args.steps)
+
+
 def forward(args) -> dict:
     from . import core
 
@@ -131,8 +169,11 @@ def main() -> None:
     f.add_argument("--iters", type=int, default=5)
     f.add_argument("--min-len", type=int, default=None,
                    help="variable lengths uniform in [min_len, seq]; throughput counts the valid steps")
+    pr = sub.add_parser("probe")
+    pr.add_argument("--rows", type=int, choices=[16, 32], default=16)
+    pr.add_argument("--steps", type=int, default=20000)
     args = ap.parse_args()
-    print(json.dumps({"gemm": gemm, "step": step, "forward": forward}[args.cmd](args)))
+    print(json.dumps({"gemm": gemm, "step": step, "forward": forward, "probe": probe}[args.cmd](args)))
 
 
 if __name__ == "__main__":

@@ -308,9 +308,13 @@ PLSTM_API int32_t plstm_diag_tmem_layout(uint32_t* out, void* stream);
  * the sibling.  out (device, 16 uint64) receives [0] status (0 ok, 1 a bounded
  * wait gave up), [1] SM cycles over [2] steps (from steps / 4 on), [3..8] summed
  * cycles of the phases landed -> commit issued -> accumulator seen -> loaded ->
- * h written -> copy issued -> next h landed.  The latency floor of the roofline. */
-PLSTM_API int32_t plstm_diag_step_latency(int32_t rows, int32_t steps, uint64_t* out, int32_t timeout_ms,
-                                          void* stream);
+ * h written -> copy issued -> next h landed.  The latency floor of the roofline.
+ * `variant` 0 runs the chain as the kernel does; its bits select alternatives
+ * (1: spin on mbarrier.test_wait for the sibling's h, 2: spin for the
+ * accumulator, 4: hand-off by st.async 16-byte stores from all compute threads,
+ * 8: the two tiles' accumulators loaded one after the other under the gate math). */
+PLSTM_API int32_t plstm_diag_step_latency(int32_t rows, int32_t steps, int32_t variant, uint64_t* out,
+                                          int32_t timeout_ms, void* stream);
 
 #ifdef __cplusplus
 }

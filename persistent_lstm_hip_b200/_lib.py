@@ -25,6 +25,7 @@ FLAG_SYNC_CHECK = 0x10
 FLAG_CN_F32 = 0x20
 FLAG_DEDUPE = 0x40
 FLAG_TEST_DROP = 0x100
+FLAG_TRACE = 0x200
 
 _CODE_NAMES = {EINVAL: "PLSTM_EINVAL", ENOTSUP: "PLSTM_ENOTSUP", ETIMEOUT: "PLSTM_ETIMEOUT",
                ECUDA: "PLSTM_ECUDA", EWORKSPACE: "PLSTM_EWORKSPACE"}
@@ -69,7 +70,7 @@ PROTOTYPES = {
     "plstm_hidden_update_workspace_size": (_I32, [_I32, _I32, _I32, _I32, _I32, _I32, ctypes.POINTER(_SZ)]),
     "plstm_hidden_update": (_I32, [_P, _I32, _I32, _I32, _P, _I32, _P, _I32, _I32, _P, _P, _P, _P, _SZ, _P]),
     "plstm_diag_tmem_layout": (_I32, [_P, _P]),
-    "plstm_diag_step_latency": (_I32, [_I32, _I32, _P, _I32, _P]),
+    "plstm_diag_step_latency": (_I32, [_I32, _I32, _I32, _P, _I32, _P]),
     "plstm_launch_count": (ctypes.c_int64, []),
     "plstm_profile": (_I32, [_I32]),
     "plstm_profile_read": (_I32, [ctypes.POINTER(ctypes.c_float), ctypes.POINTER(_I32)]),

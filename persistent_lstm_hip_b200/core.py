@@ -62,7 +62,9 @@ class DeviceStatus:
     asynchronously into pinned host memory, on the same stream, behind an event.
     The next forward on the device (or ``check_device_status``) looks at every
     copy whose event has completed, without synchronising, and raises
-    ``PlstmError(PLSTM_ETIMEOUT)`` for the first failure it finds.
+    ``PlstmError(PLSTM_ETIMEOUT)`` for the first failure it finds.  Forwards
+    captured into a CUDA graph are not watched (read their status with
+    ``plstm_read_status`` on a workspace the caller keeps).
     """
 
     RING = 64  # copies in flight per device before the oldest one is waited for
@@ -91,12 +93,19 @@ class DeviceStatus:
                         f"on {self.device}: a bounded inter-CTA wait gave up; its outputs are incomplete")
 
     def poll(self, wait: bool = False) -> None:
-        """Raises for a failed earlier forward whose status copy has landed (all of them with wait=True)."""
+        """Raises for a failed earlier forward whose status copy has landed (all of them with wait=True).
+        Does nothing while the current stream is being captured into a CUDA graph (event queries
+        are not allowed then)."""
+        if torch.cuda.is_current_stream_capturing():
+            return
         with self.lock:
             self._retire(wait)
 
     def watch(self, ws: torch.Tensor, stream: torch.cuda.Stream) -> None:
-        """Enqueues the status copy of the forward just enqueued on `stream` with workspace `ws`."""
+        """Enqueues the status copy of the forward just enqueued on `stream` with workspace `ws`.
+        Forwards captured into a CUDA graph are not watched."""
+        if torch.cuda.is_current_stream_capturing():
+            return
         with self.lock:
             while len(self.pending) >= self.RING:  # only when the host runs 64 forwards ahead of the GPU
                 self._retire(True)

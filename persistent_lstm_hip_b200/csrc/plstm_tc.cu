@@ -232,6 +232,53 @@ __device__ __forceinline__ void lstm_cells(const uint32_t (&rif)[2][4 * CPW], co
     }
 }
 
+// Registers written by an asynchronous tcgen05.ld: the compiler sees them defined at the load,
+// so an empty asm that rewrites them, placed after tcgen05.wait::ld, keeps every use behind the
+// wait (volatile asm statements stay in order).
+template <int N>
+__device__ __forceinline__ void reg_after_wait(uint32_t (&r)[N]) {
+#pragma unroll
+  for (int i = 0; i < N; ++i) asm volatile("" : "+r"(r[i])::"memory");
+}
+
+// lstm_cells restricted to tile `tau` (the same arithmetic per cell), so that one tile's gate
+// math can run while the other tile's accumulators are still being loaded.
+template <int CPW, bool BF16, bool VARLEN>
+__device__ __forceinline__ void lstm_cells_tile(int tau, const uint32_t (&rif)[2][4 * CPW],
+                                                const uint32_t (&rgo)[2][4 * CPW], const float (&bz)[2][4],
+                                                float (&c_st)[2][CPW][2], uint16_t (&h_st)[2][CPW][2],
+                                                const int (&len_c)[CPW][2], int t, uint16_t (&hw)[2][CPW][2]) {
+  float ti[CPW][2], tf[CPW][2], tg[CPW][2], to[CPW][2];
+#pragma unroll
+  for (int jc = 0; jc < CPW; ++jc)
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      ti[jc][e] = ptx::tanh_approx(__uint_as_float(rif[tau][4 * jc + e]) + bz[tau][0]);
+      tf[jc][e] = ptx::tanh_approx(__uint_as_float(rif[tau][4 * jc + 2 + e]) + bz[tau][1]);
+      tg[jc][e] = ptx::tanh_approx(__uint_as_float(rgo[tau][4 * jc + e]) + bz[tau][2]);
+      to[jc][e] = ptx::tanh_approx(__uint_as_float(rgo[tau][4 * jc + 2 + e]) + bz[tau][3]);
+    }
+#pragma unroll
+  for (int jc = 0; jc < CPW; ++jc) {
+    float h[2], c_new[2];
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      c_new[e] = fmaf(fmaf(0.5f, tf[jc][e], 0.5f), c_st[tau][jc][e], fmaf(0.5f, ti[jc][e], 0.5f) * tg[jc][e]);
+      h[e] = fmaf(0.5f, to[jc][e], 0.5f) * ptx::tanh_approx(c_new[e]);
+    }
+    const uint32_t bits = pack2_bits<BF16>(h[0], h[1]);
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const uint16_t hb = (uint16_t)(e == 0 ? bits & 0xffffu : bits >> 16);
+      if (!VARLEN || t < len_c[jc][e]) {
+        c_st[tau][jc][e] = c_new[e];
+        h_st[tau][jc][e] = hb;
+      }
+      hw[tau][jc][e] = h_st[tau][jc][e];
+    }
+  }
+}
+
 // Bounded wait on an mbarrier phase; false = gave up (timeout or cluster abort).
 __device__ __forceinline__ bool wait_phase(uint32_t bar, uint32_t parity, volatile int* abort_flag,
                                            unsigned long long timeout_ns) {
@@ -1888,8 +1935,34 @@ TcWs tc_ws(const Problem& p, const Plan& pl) {
 //   copy issued -> next sibling h landed.
 constexpr int kProbeOut = 16;
 
+// `variant` bits select alternatives of the chain's parts (0 = the kernel's current form):
+//   1: the control warp spins on mbarrier.test_wait instead of try_wait for the sibling's h;
+//   2: the compute warps spin on test_wait for the accumulator;
+//   4: the hand-off is st.async 16-byte stores by all 128 compute threads (after a named
+//      barrier) instead of one bulk copy;
+//   8: the two tiles' accumulators are loaded one after the other, the second load in flight
+//      under the first tile's gate math.
+constexpr int kProbeSpinLanded = 1, kProbeSpinMma = 2, kProbeStAsync = 4, kProbeSplitLoad = 8;
+
+__device__ __forceinline__ bool warp_spin_phase(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                                unsigned long long timeout_ns) {
+  int ok = 0;
+  if ((threadIdx.x & 31) == 0) {
+    const unsigned long long t0 = ptx::globaltimer();
+    unsigned n = 0;
+    while (true) {
+      if (ptx::mbar_test_wait(bar, parity)) {
+        ok = 1;
+        break;
+      }
+      if ((++n & 63) == 0 && (*abort_flag || ptx::globaltimer() - t0 > timeout_ns)) break;
+    }
+  }
+  return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+
 template <int NH>
-__global__ void __launch_bounds__(160, 1) step_probe_kernel(int steps, unsigned long long timeout_ns,
+__global__ void __launch_bounds__(160, 1) step_probe_kernel(int steps, int variant, unsigned long long timeout_ns,
                                                              unsigned long long* out) {
   constexpr int CPW = NH / 8;
   constexpr uint32_t kHalf = NH * 128;  // one 64-unit K block of h: NH rows x 128 bytes (128-byte swizzle)
@@ -1963,7 +2036,9 @@ __global__ void __launch_bounds__(160, 1) step_probe_kernel(int steps, unsigned 
     for (int t = 0; t < steps && ok; ++t) {
       const int b = t & 1;
       if (t >= 1) {
-        if (!warp_wait_phase(full(b), ((t - 1) >> 1) & 1, abort_flag, timeout_ns)) {
+        const bool got = (variant & kProbeSpinLanded) ? warp_spin_phase(full(b), ((t - 1) >> 1) & 1, abort_flag, timeout_ns)
+                                                      : warp_wait_phase(full(b), ((t - 1) >> 1) & 1, abort_flag, timeout_ns);
+        if (!got) {
           give_up();
           break;
         }
@@ -2026,24 +2101,42 @@ __global__ void __launch_bounds__(160, 1) step_probe_kernel(int steps, unsigned 
         }
     for (int t = 0; t < steps && ok; ++t) {
       const int b = t & 1;
-      if (!warp_wait_phase(mma(b), (t >> 1) & 1, abort_flag, timeout_ns)) {
+      const bool got = (variant & kProbeSpinMma) ? warp_spin_phase(mma(b), (t >> 1) & 1, abort_flag, timeout_ns)
+                                                 : warp_wait_phase(mma(b), (t >> 1) & 1, abort_flag, timeout_ns);
+      if (!got) {
         give_up();
         break;
       }
       ptx::tc_fence_after();
       if (q == 0 && lane == 0) stamp[0] = clock64();
       uint32_t rif[2][4 * CPW], rgo[2][4 * CPW];
-#pragma unroll
-      for (int tau = 0; tau < 2; ++tau) {
-        const uint32_t col = dcol + (uint32_t)(tau * NH);
-        tmem_ld_chunks<CPW>(col + ((uint32_t)(32 * q) << 16), rif[tau]);
-        tmem_ld_chunks<CPW>(col + ((uint32_t)(32 * q + 16) << 16), rgo[tau]);
-      }
-      ptx::tmem_wait_ld();
-      ptx::tc_fence_before();
-      if (q == 0 && lane == 0) stamp[1] = clock64();
       uint16_t hw[2][CPW][2];
-      lstm_cells<CPW, false, false>(rif, rgo, bz, c_st, h_st, len_c, t, hw);
+      if (variant & kProbeSplitLoad) {
+        // Tile 0's accumulators first; tile 1's load runs under tile 0's gate math.
+        tmem_ld_chunks<CPW>(dcol + ((uint32_t)(32 * q) << 16), rif[0]);
+        tmem_ld_chunks<CPW>(dcol + ((uint32_t)(32 * q + 16) << 16), rgo[0]);
+        ptx::tmem_wait_ld();
+        if (q == 0 && lane == 0) stamp[1] = clock64();
+        tmem_ld_chunks<CPW>(dcol + (uint32_t)NH + ((uint32_t)(32 * q) << 16), rif[1]);
+        tmem_ld_chunks<CPW>(dcol + (uint32_t)NH + ((uint32_t)(32 * q + 16) << 16), rgo[1]);
+        lstm_cells_tile<CPW, false, false>(0, rif, rgo, bz, c_st, h_st, len_c, t, hw);
+        ptx::tmem_wait_ld();
+        reg_after_wait<4 * CPW>(rif[1]);  // tile 1's registers are read only after the wait
+        reg_after_wait<4 * CPW>(rgo[1]);
+        ptx::tc_fence_before();
+        lstm_cells_tile<CPW, false, false>(1, rif, rgo, bz, c_st, h_st, len_c, t, hw);
+      } else {
+#pragma unroll
+        for (int tau = 0; tau < 2; ++tau) {
+          const uint32_t col = dcol + (uint32_t)(tau * NH);
+          tmem_ld_chunks<CPW>(col + ((uint32_t)(32 * q) << 16), rif[tau]);
+          tmem_ld_chunks<CPW>(col + ((uint32_t)(32 * q + 16) << 16), rgo[tau]);
+        }
+        ptx::tmem_wait_ld();
+        ptx::tc_fence_before();
+        if (q == 0 && lane == 0) stamp[1] = clock64();
+        lstm_cells<CPW, false, false>(rif, rgo, bz, c_st, h_st, len_c, t, hw);
+      }
       uint8_t* dst = sm + (size_t)(2 * (b ^ 1) + s) * kHalf;
 #pragma unroll
       for (int tau = 0; tau < 2; ++tau)
@@ -2052,18 +2145,37 @@ __global__ void __launch_bounds__(160, 1) step_probe_kernel(int steps, unsigned 
 #pragma unroll
           for (int e = 0; e < 2; ++e)
             *reinterpret_cast<uint16_t*>(dst + sw128_off(8 * jc + cpair + e, 8 * (4 * tau + q) + j8)) = hw[tau][jc][e];
-      ptx::fence_proxy_async_smem();
-      if (q == 0 && lane == 0) stamp[2] = clock64();
-      __syncwarp();
-      if (lane == 0) {
-        if (ptx::atom_add_acq_rel_smem(ptx::smem_u32(counter), 1u) % 4u == 3u) {
-          stamp[3] = clock64();
-          if (t + 1 < steps) {
-            const uint32_t src = hbuf(b ^ 1, s);
-            ptx::bulk_s2c(ptx::mapa(src, (uint32_t)(s ^ 1)), src, kHalf, ptx::mapa(full(b ^ 1), (uint32_t)(s ^ 1)));
+      if (variant & kProbeStAsync) {
+        // All four warps' h in place, then every thread forwards 16-byte pieces of the tile.
+        if (q == 0 && lane == 0) stamp[2] = clock64();
+        ptx::named_bar_sync(1, 128);
+        if (q == 0 && lane == 0) stamp[3] = clock64();
+        if (t + 1 < steps) {
+          const uint32_t peer = (uint32_t)(s ^ 1);
+          const uint32_t rbar = ptx::mapa(full(b ^ 1), peer);
+          const uint32_t src = hbuf(b ^ 1, s);
+#pragma unroll
+          for (int c = tid; c < (int)(kHalf / 16); c += 128) {
+            const uint4 v = *reinterpret_cast<const uint4*>(sm + (src - sbase) + 16 * c);
+            ptx::st_async_v4(ptx::mapa(src + 16u * c, peer), v, rbar);
           }
         }
-        ptx::mbar_arrive(hready(b));
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(hready(b));
+      } else {
+        ptx::fence_proxy_async_smem();
+        if (q == 0 && lane == 0) stamp[2] = clock64();
+        __syncwarp();
+        if (lane == 0) {
+          if (ptx::atom_add_acq_rel_smem(ptx::smem_u32(counter), 1u) % 4u == 3u) {
+            stamp[3] = clock64();
+            if (t + 1 < steps) {
+              const uint32_t src = hbuf(b ^ 1, s);
+              ptx::bulk_s2c(ptx::mapa(src, (uint32_t)(s ^ 1)), src, kHalf, ptx::mapa(full(b ^ 1), (uint32_t)(s ^ 1)));
+            }
+          }
+          ptx::mbar_arrive(hready(b));
+        }
       }
     }
   }
@@ -2295,13 +2407,14 @@ using namespace plstm::tc;
 
 // Dependent-step latency probe (see step_probe_kernel).  out: device buffer of
 // kProbeOut uint64 words.
-extern "C" int32_t plstm_diag_step_latency(int32_t rows, int32_t steps, uint64_t* out, int32_t timeout_ms,
-                                           void* stream) {
+extern "C" int32_t plstm_diag_step_latency(int32_t rows, int32_t steps, int32_t variant, uint64_t* out,
+                                           int32_t timeout_ms, void* stream) {
   clear_error();
   PLSTM_CHECK_ARG(rows == 16 || rows == 32, "rows must be 16 or 32");
   PLSTM_CHECK_ARG(steps >= 8 && steps <= 1000000, "steps must be in [8, 1000000]");
   PLSTM_CHECK_ARG(out != nullptr, "out is NULL");
   PLSTM_CHECK_ARG(timeout_ms >= 0, "timeout_ms must be >= 0");
+  PLSTM_CHECK_ARG(variant >= 0 && variant < 16, "variant must be in [0, 16)");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   void* k = rows == 16 ? (void*)step_probe_kernel<16> : (void*)step_probe_kernel<32>;
   const int smem = 4 * rows * 128 + 1024 + 1024;
@@ -2321,7 +2434,8 @@ extern "C" int32_t plstm_diag_step_latency(int32_t rows, int32_t steps, uint64_t
   cfg.numAttrs = 1;
   int st = steps;
   unsigned long long tns = (unsigned long long)(timeout_ms > 0 ? timeout_ms : 2000) * 1000000ull;
-  void* args[] = {&st, &tns, &out};
+  int var = variant;
+  void* args[] = {&st, &var, &tns, &out};
   PLSTM_TRY_CUDA(cudaLaunchKernelExC(&cfg, k, args));
   note_launches(1);
   return PLSTM_OK;

@@ -83,7 +83,7 @@ def step(args) -> dict:
             "us_per_step": k_ms * 1e3 / (args.seq + 4)}
 
 
-def step_latency(rows: int = 16, steps: int = 20000, device: int = 0) -> dict:
+def step_latency(rows: int = 16, steps: int = 20000, device: int = 0, variant: int = 0) -> dict:
     """The dependent-step latency probe (plstm_diag_step_latency): cycles and microseconds of one
     wavefront layer-step's dependency chain run alone, with its phases."""
     from . import _lib
@@ -93,10 +93,10 @@ def step_latency(rows: int = 16, steps: int = 20000, device: int = 0) -> dict:
     out = torch.zeros(16, dtype=torch.int64, device=dev)
     stream = torch.cuda.current_stream(dev)
     for _ in range(2):  # warm-up (module load, clocks)
-        _lib.check(lib.plstm_diag_step_latency(rows, 1000, out.data_ptr(), 0, stream.cuda_stream))
+        _lib.check(lib.plstm_diag_step_latency(rows, 1000, variant, out.data_ptr(), 0, stream.cuda_stream))
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record(stream)
-    _lib.check(lib.plstm_diag_step_latency(rows, steps, out.data_ptr(), 0, stream.cuda_stream))
+    _lib.check(lib.plstm_diag_step_latency(rows, steps, variant, out.data_ptr(), 0, stream.cuda_stream))
     b.record(stream)
     torch.cuda.synchronize(dev)
     o = [int(v) for v in out.cpu().tolist()]
@@ -105,7 +105,7 @@ def step_latency(rows: int = 16, steps: int = 20000, device: int = 0) -> dict:
     n = max(o[2], 1)
     phases = ["landed->commit issued", "commit->accumulator seen", "seen->loaded", "loaded->h written",
               "h written->copy issued", "copy issued->next h landed"]
-    return {"rows": rows, "steps": steps, "cycles_per_step": o[1] / n,
+    return {"rows": rows, "steps": steps, "variant": variant, "cycles_per_step": o[1] / n,
             "us_per_step": a.elapsed_time(b) * 1e3 / steps,
             "phase_cycles": {k: o[3 + i] / n for i, k in enumerate(phases)},
             "method": "plstm_diag_step_latency: 2-CTA cluster; per step the sibling's h lands, 8 tcgen05 MMAs "
@@ -114,7 +114,7 @@ def step_latency(rows: int = 16, steps: int = 20000, device: int = 0) -> dict:
 
 
 def probe(args) -> dict:
-    return step_latency(args.rows, args.steps)
+    return step_latency(args.rows, args.steps, variant=args.variant)
 
 
 def forward(args) -> dict:
@@ -172,6 +172,7 @@ def main() -> None:
     pr = sub.add_parser("probe")
     pr.add_argument("--rows", type=int, choices=[16, 32], default=16)
     pr.add_argument("--steps", type=int, default=20000)
+    pr.add_argument("--variant", type=int, default=0, help="bits of plstm_diag_step_latency's variants")
     args = ap.parse_args()
     print(json.dumps({"gemm": gemm, "step": step, "forward": forward, "probe": probe}[args.cmd](args)))
 

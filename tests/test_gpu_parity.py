@@ -357,20 +357,21 @@ def test_timeout_is_reported_not_hung(cuda_device):
     assert_close16(out, r_out, "after timeout")
 
 
+@pytest.mark.parametrize("variant", [0, 15])
 @pytest.mark.parametrize("rows", [16, 32])
-def test_step_latency_probe(cuda_device, rows):
+def test_step_latency_probe(cuda_device, rows, variant):
     """The dependent-step probe finishes, reports its phases, and its step time is plausible:
     at least the sum of its own phases' MMA issue and no longer than a full wavefront step."""
     from persistent_lstm_hip_b200 import microbench
 
-    r = microbench.step_latency(rows=rows, steps=4000)
+    r = microbench.step_latency(rows=rows, steps=4000, variant=variant)
     ph = r["phase_cycles"]
     assert 300 < r["cycles_per_step"] < 20000, r
     assert abs(sum(ph.values()) - r["cycles_per_step"]) < 0.05 * r["cycles_per_step"], r
     assert 0.1 < r["us_per_step"] < 10, r
     lib = _lib.load()
     out = torch.zeros(16, dtype=torch.int64, device=cuda_device)
-    assert lib.plstm_diag_step_latency(24, 100, out.data_ptr(), 0, None) == _lib.EINVAL
+    assert lib.plstm_diag_step_latency(24, 100, 0, out.data_ptr(), 0, None) == _lib.EINVAL
 
 
 def test_unchecked_timeout_raises_by_the_next_call(cuda_device):

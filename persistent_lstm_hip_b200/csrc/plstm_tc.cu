@@ -1942,7 +1942,26 @@ constexpr int kProbeOut = 16;
 //      barrier) instead of one bulk copy;
 //   8: the two tiles' accumulators are loaded one after the other, the second load in flight
 //      under the first tile's gate math.
-constexpr int kProbeSpinLanded = 1, kProbeSpinMma = 2, kProbeStAsync = 4, kProbeSplitLoad = 8;
+//  16: the hand-off is plain 16-byte remote stores (st.shared::cluster) by all 128 compute
+//      threads, a proxy fence and one cluster-scope release arrival per warp on the sibling's
+//      barrier (no transaction bytes), waited for with cluster-scope acquire.
+constexpr int kProbeSpinLanded = 1, kProbeSpinMma = 2, kProbeStAsync = 4, kProbeSplitLoad = 8, kProbeRemoteSt = 16;
+
+__device__ __forceinline__ bool warp_wait_phase_cluster(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                                        unsigned long long timeout_ns) {
+  int ok = 0;
+  if ((threadIdx.x & 31) == 0) {
+    const unsigned long long t0 = ptx::globaltimer();
+    while (true) {
+      if (ptx::mbar_try_wait_cluster(bar, parity)) {
+        ok = 1;
+        break;
+      }
+      if (*abort_flag || ptx::globaltimer() - t0 > timeout_ns) break;
+    }
+  }
+  return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
 
 __device__ __forceinline__ bool warp_spin_phase(uint32_t bar, uint32_t parity, volatile int* abort_flag,
                                                 unsigned long long timeout_ns) {
@@ -1984,7 +2003,7 @@ __global__ void __launch_bounds__(160, 1) step_probe_kernel(int steps, int varia
   for (int i = tid; i < (int)(4 * kHalf / 4); i += blockDim.x) reinterpret_cast<uint32_t*>(sm)[i] = 0u;  // h0 = 0
   if (tid == 0) {
     for (int b = 0; b < 2; ++b) {
-      ptx::mbar_init(full(b), 1);
+      ptx::mbar_init(full(b), (variant & kProbeRemoteSt) ? 4 : 1);
       ptx::mbar_init(mma(b), 1);
       ptx::mbar_init(hready(b), 4);
     }
@@ -1992,8 +2011,10 @@ __global__ void __launch_bounds__(160, 1) step_probe_kernel(int steps, int varia
     *abort_flag = 0;
     ptx::fence_mbar_init_cluster();
     // The sibling's h of steps 1 and 2.
-    if (steps > 1) ptx::mbar_arrive_expect_tx(full(1), kHalf);
-    if (steps > 2) ptx::mbar_arrive_expect_tx(full(0), kHalf);
+    if (!(variant & kProbeRemoteSt)) {
+      if (steps > 1) ptx::mbar_arrive_expect_tx(full(1), kHalf);
+      if (steps > 2) ptx::mbar_arrive_expect_tx(full(0), kHalf);
+    }
   }
   if (warp == 0) {
     ptx::tmem_alloc(sbase + kBar + 56, 128);
@@ -2036,13 +2057,16 @@ __global__ void __launch_bounds__(160, 1) step_probe_kernel(int steps, int varia
     for (int t = 0; t < steps && ok; ++t) {
       const int b = t & 1;
       if (t >= 1) {
-        const bool got = (variant & kProbeSpinLanded) ? warp_spin_phase(full(b), ((t - 1) >> 1) & 1, abort_flag, timeout_ns)
-                                                      : warp_wait_phase(full(b), ((t - 1) >> 1) & 1, abort_flag, timeout_ns);
+        const uint32_t par = ((t - 1) >> 1) & 1;
+        const bool got = (variant & kProbeRemoteSt)     ? warp_wait_phase_cluster(full(b), par, abort_flag, timeout_ns)
+                         : (variant & kProbeSpinLanded) ? warp_spin_phase(full(b), par, abort_flag, timeout_ns)
+                                                        : warp_wait_phase(full(b), par, abort_flag, timeout_ns);
         if (!got) {
           give_up();
           break;
         }
-        if (t + 2 < steps && ptx::elect_one()) ptx::mbar_arrive_expect_tx(full(b), kHalf);
+        if (!(variant & kProbeRemoteSt) && t + 2 < steps && ptx::elect_one())
+          ptx::mbar_arrive_expect_tx(full(b), kHalf);
         __syncwarp();
       }
       landed = clock64();
@@ -2145,7 +2169,25 @@ __global__ void __launch_bounds__(160, 1) step_probe_kernel(int steps, int varia
 #pragma unroll
           for (int e = 0; e < 2; ++e)
             *reinterpret_cast<uint16_t*>(dst + sw128_off(8 * jc + cpair + e, 8 * (4 * tau + q) + j8)) = hw[tau][jc][e];
-      if (variant & kProbeStAsync) {
+      if (variant & kProbeRemoteSt) {
+        if (q == 0 && lane == 0) stamp[2] = clock64();
+        ptx::named_bar_sync(1, 128);
+        if (q == 0 && lane == 0) stamp[3] = clock64();
+        if (t + 1 < steps) {
+          const uint32_t peer = (uint32_t)(s ^ 1);
+          const uint32_t src = hbuf(b ^ 1, s);
+#pragma unroll
+          for (int c = tid; c < (int)(kHalf / 16); c += 128) {
+            const uint4 v = *reinterpret_cast<const uint4*>(sm + (src - sbase) + 16 * c);
+            ptx::st_cluster_v4(ptx::mapa(src + 16u * c, peer), v);
+          }
+          ptx::fence_proxy_async_cluster();
+          __syncwarp();
+          if (lane == 0) ptx::mbar_arrive_remote(ptx::mapa(full(b ^ 1), peer));
+        }
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(hready(b));
+      } else if (variant & kProbeStAsync) {
         // All four warps' h in place, then every thread forwards 16-byte pieces of the tile.
         if (q == 0 && lane == 0) stamp[2] = clock64();
         ptx::named_bar_sync(1, 128);
@@ -2180,6 +2222,208 @@ __global__ void __launch_bounds__(160, 1) step_probe_kernel(int steps, int varia
     }
   }
   if (*abort_flag) {  // copies already in flight toward the sibling land before either CTA leaves
+    const unsigned long long w0 = ptx::globaltimer();
+    while (ptx::globaltimer() - w0 < 50000ull) {
+    }
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem, 128);
+  }
+  ptx::cluster_sync();
+}
+
+// The same chain with each layer split over four CTAs (variant 32 of the probe): CTA r owns
+// 32 hidden units (one M = 128 tile of gate rows); per step it waits for the other three
+// CTAs' 32-unit pieces of h (NH rows x 64 bytes each, K-major 8 x 16-byte core matrices, no
+// swizzle, so that a piece is contiguous), issues 6 MMAs over them (3 pieces x 2 K steps),
+// runs the gate math of its 32 units and pushes its own piece to the three others.
+constexpr int kProbeQuad = 32;
+
+template <int NH>
+__global__ void __launch_bounds__(160, 1) step_probe4_kernel(int steps, unsigned long long timeout_ns,
+                                                              unsigned long long* out) {
+  constexpr int CPW = NH / 8;
+  constexpr uint32_t kPiece = NH * 64;    // 32 units x NH rows, 16-bit
+  constexpr uint32_t kBuf = 4 * kPiece;   // one step parity: the four pieces
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = ptx::smem_u32(sm);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int r = (int)ptx::cluster_ctarank();
+  constexpr uint32_t kBar = 2 * kBuf;
+  auto full = [&](int b) { return sbase + kBar + 8u * b; };
+  auto mma = [&](int b) { return sbase + kBar + 16u + 8u * b; };
+  auto hready = [&](int b) { return sbase + kBar + 32u + 8u * b; };
+  auto piece = [&](int b, int pc) { return sbase + (uint32_t)b * kBuf + (uint32_t)pc * kPiece; };
+  uint32_t* counter = reinterpret_cast<uint32_t*>(sm + kBar + 48);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + kBar + 52);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + kBar + 56);
+  volatile unsigned long long* stamp = reinterpret_cast<volatile unsigned long long*>(sm + kBar + 64);
+
+  for (int i = tid; i < (int)(kBar / 4); i += blockDim.x) reinterpret_cast<uint32_t*>(sm)[i] = 0u;
+  if (tid == 0) {
+    for (int b = 0; b < 2; ++b) {
+      ptx::mbar_init(full(b), 1);
+      ptx::mbar_init(mma(b), 1);
+      ptx::mbar_init(hready(b), 4);
+    }
+    *counter = 0;
+    *abort_flag = 0;
+    ptx::fence_mbar_init_cluster();
+    if (steps > 1) ptx::mbar_arrive_expect_tx(full(1), 3 * kPiece);
+    if (steps > 2) ptx::mbar_arrive_expect_tx(full(0), 3 * kPiece);
+  }
+  if (warp == 0) {
+    ptx::tmem_alloc(sbase + kBar + 56, 128);
+    ptx::tmem_relinquish();
+  }
+  ptx::fence_proxy_async_smem();
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(tslot);
+  if (warp < 4) {  // A: one tile, K = 128 (64 columns)
+    uint32_t v[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = ((i + lane) & 1) ? 0x20002000u : 0xa000a000u;
+#pragma unroll
+    for (int c = 0; c < 2; ++c) ptx::tmem_st_32x32b_x32(tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)(32 * c), v);
+    ptx::tmem_wait_st();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  ptx::cluster_sync();
+  const uint32_t dcol = tmem + 64;
+  bool ok = true;
+  auto give_up = [&]() {
+    if (lane == 0 && !*abort_flag) {
+      for (int q = 0; q < 4; ++q) ptx::st_cluster_u32(ptx::mapa(ptx::smem_u32((void*)abort_flag), (uint32_t)q), 1u);
+      if (r == 0) out[0] = 1ull;
+    }
+    ok = false;
+  };
+
+  if (warp == 4) {
+    constexpr uint32_t idesc = ptx::idesc_f16(128, NH, false);
+    const int t0 = steps / 4;
+    unsigned long long sum[6] = {0, 0, 0, 0, 0, 0}, first = 0, prev_push = 0, landed = 0;
+    int counted = 0;
+    for (int t = 0; t < steps && ok; ++t) {
+      const int b = t & 1;
+      if (t >= 1) {
+        if (!warp_wait_phase(full(b), ((t - 1) >> 1) & 1, abort_flag, timeout_ns)) {
+          give_up();
+          break;
+        }
+        if (t + 2 < steps && ptx::elect_one()) ptx::mbar_arrive_expect_tx(full(b), 3 * kPiece);
+        __syncwarp();
+      }
+      landed = clock64();
+      if (t == t0) first = landed;
+      if (t > t0) sum[5] += landed - prev_push;
+      if (ptx::elect_one()) {
+        ptx::tc_fence_after();
+        bool acc = false;
+        for (int pc = 0; pc < 4; ++pc) {
+          if (pc == r) continue;
+#pragma unroll
+          for (int ks = 0; ks < 2; ++ks) {
+            ptx::mma_f16_ts(dcol, tmem + (uint32_t)(16 * pc + 8 * ks),
+                            ptx::desc_k_none(piece(b, pc) + 256u * ks, 128, 512), idesc, acc ? 1u : 0u);
+            acc = true;
+          }
+        }
+        ptx::mma_commit(mma(b));
+      }
+      __syncwarp();
+      const unsigned long long committed = clock64();
+      if (!warp_wait_phase(hready(b), (t >> 1) & 1, abort_flag, timeout_ns)) {
+        give_up();
+        break;
+      }
+      if (t >= t0) {
+        sum[0] += committed - landed;
+        sum[1] += stamp[0] - committed;
+        sum[2] += stamp[1] - stamp[0];
+        sum[3] += stamp[2] - stamp[1];
+        sum[4] += stamp[3] - stamp[2];
+        prev_push = stamp[3];
+        ++counted;
+      }
+    }
+    if (r == 0 && lane == 0 && ok) {
+      out[0] = 0ull;
+      out[1] = landed - first;
+      out[2] = (unsigned long long)max(counted - 1, 0);
+      for (int i = 0; i < 6; ++i) out[3 + i] = sum[i];
+    }
+  } else {
+    const int q = warp, j8 = lane >> 2, cpair = (lane & 3) * 2;
+    float c_st[2][CPW][2];
+    uint16_t h_st[2][CPW][2];
+    int len_c[CPW][2];
+    const float bz[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+    for (int tau = 0; tau < 2; ++tau)
+#pragma unroll
+      for (int jc = 0; jc < CPW; ++jc)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          c_st[tau][jc][e] = 0.f;
+          h_st[tau][jc][e] = 0;
+          len_c[jc][e] = steps;
+        }
+    const int u = 8 * q + j8;  // unit within this CTA's 32
+    for (int t = 0; t < steps && ok; ++t) {
+      const int b = t & 1;
+      if (!warp_wait_phase(mma(b), (t >> 1) & 1, abort_flag, timeout_ns)) {
+        give_up();
+        break;
+      }
+      ptx::tc_fence_after();
+      if (q == 0 && lane == 0) stamp[0] = clock64();
+      uint32_t rif[2][4 * CPW], rgo[2][4 * CPW];
+      tmem_ld_chunks<CPW>(dcol + ((uint32_t)(32 * q) << 16), rif[0]);
+      tmem_ld_chunks<CPW>(dcol + ((uint32_t)(32 * q + 16) << 16), rgo[0]);
+      ptx::tmem_wait_ld();
+      reg_after_wait<4 * CPW>(rif[0]);
+      reg_after_wait<4 * CPW>(rgo[0]);
+      ptx::tc_fence_before();
+      if (q == 0 && lane == 0) stamp[1] = clock64();
+      uint16_t hw[2][CPW][2];
+      lstm_cells_tile<CPW, false, false>(0, rif, rgo, bz, c_st, h_st, len_c, t, hw);
+      uint8_t* dst = sm + (size_t)(b ^ 1) * kBuf + (size_t)r * kPiece;
+#pragma unroll
+      for (int jc = 0; jc < CPW; ++jc)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int row = 8 * jc + cpair + e;
+          *reinterpret_cast<uint16_t*>(dst + (row >> 3) * 512 + (u >> 3) * 128 + (row & 7) * 16 + (u & 7) * 2) =
+              hw[0][jc][e];
+        }
+      ptx::fence_proxy_async_smem();
+      if (q == 0 && lane == 0) stamp[2] = clock64();
+      __syncwarp();
+      if (lane == 0) {
+        if (ptx::atom_add_acq_rel_smem(ptx::smem_u32(counter), 1u) % 4u == 3u) {
+          stamp[3] = clock64();
+          if (t + 1 < steps) {
+            const uint32_t src = piece(b ^ 1, r);
+            for (int pr = 1; pr < 4; ++pr) {
+              const uint32_t peer = (uint32_t)((r + pr) & 3);
+              ptx::bulk_s2c(ptx::mapa(src, peer), src, kPiece, ptx::mapa(full(b ^ 1), peer));
+            }
+          }
+        }
+        ptx::mbar_arrive(hready(b));
+      }
+    }
+  }
+  if (*abort_flag) {
     const unsigned long long w0 = ptx::globaltimer();
     while (ptx::globaltimer() - w0 < 50000ull) {
     }
@@ -2414,20 +2658,23 @@ extern "C" int32_t plstm_diag_step_latency(int32_t rows, int32_t steps, int32_t 
   PLSTM_CHECK_ARG(steps >= 8 && steps <= 1000000, "steps must be in [8, 1000000]");
   PLSTM_CHECK_ARG(out != nullptr, "out is NULL");
   PLSTM_CHECK_ARG(timeout_ms >= 0, "timeout_ms must be >= 0");
-  PLSTM_CHECK_ARG(variant >= 0 && variant < 16, "variant must be in [0, 16)");
+  PLSTM_CHECK_ARG(variant == kProbeQuad || (variant >= 0 && variant < 32 && !((variant & 4) && (variant & 16))),
+                  "variant must be in [0, 32) (not both 4 and 16) or 32");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  void* k = rows == 16 ? (void*)step_probe_kernel<16> : (void*)step_probe_kernel<32>;
+  const bool quad = variant == kProbeQuad;
+  void* k = quad ? (rows == 16 ? (void*)step_probe4_kernel<16> : (void*)step_probe4_kernel<32>)
+                 : (rows == 16 ? (void*)step_probe_kernel<16> : (void*)step_probe_kernel<32>);
   const int smem = 4 * rows * 128 + 1024 + 1024;
   PLSTM_TRY_CUDA(cudaMemsetAsync(out, 0, kProbeOut * sizeof(uint64_t), s));
   PLSTM_TRY_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(2, 1, 1);
+  cfg.gridDim = dim3(quad ? 4 : 2, 1, 1);
   cfg.blockDim = dim3(160, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   cudaLaunchAttribute attr;
   attr.id = cudaLaunchAttributeClusterDimension;
-  attr.val.clusterDim.x = 2;
+  attr.val.clusterDim.x = quad ? 4 : 2;
   attr.val.clusterDim.y = 1;
   attr.val.clusterDim.z = 1;
   cfg.attrs = &attr;
@@ -2435,8 +2682,9 @@ extern "C" int32_t plstm_diag_step_latency(int32_t rows, int32_t steps, int32_t 
   int st = steps;
   unsigned long long tns = (unsigned long long)(timeout_ms > 0 ? timeout_ms : 2000) * 1000000ull;
   int var = variant;
-  void* args[] = {&st, &var, &tns, &out};
-  PLSTM_TRY_CUDA(cudaLaunchKernelExC(&cfg, k, args));
+  void* args2[] = {&st, &var, &tns, &out};
+  void* args4[] = {&st, &tns, &out};
+  PLSTM_TRY_CUDA(cudaLaunchKernelExC(&cfg, k, quad ? args4 : args2));
   note_launches(1);
   return PLSTM_OK;
 }

@@ -48,6 +48,7 @@
 //     records PLSTM_ETIMEOUT in the workspace status word, raises the abort
 //     flag of every CTA of the cluster and the kernel unwinds without trapping.
 #include <algorithm>
+#include <cstdio>
 #include <cstdlib>
 #include <mutex>
 #include <string>
@@ -876,40 +877,43 @@ __global__ void __launch_bounds__(Smem<N>::kThreads, 1) wavefront_kernel(const P
 // read by one output warp per slot (warps 10 / 11, TMEM lane quadrants 2 / 3, where
 // the head's rows are replicated), so neither the gate math nor the global stores of
 // the outputs sit on the recurrence's critical path.
-template <int NH>
+template <int NH, int NSL = 2>
 struct Smem2 {
   static constexpr int kBKB = NH * 128;             // one 64-wide K block of a slot's B operand
   static constexpr int kBufBytes = 4 * kBKB;        // [in0 | in1 | rec0 | rec1]
   static constexpr int kSlotBytes = 2 * kBufBytes;  // step-parity double buffer
   static constexpr int kB = 0;
-  static constexpr int kALin = kB + 2 * kSlotBytes;
+  static constexpr int kALin = kB + NSL * kSlotBytes;
   static constexpr int kBar = kALin + kALinBytes;
   // Per slot: eight barrier kinds, one per buffer parity (8 bytes each).
   static constexpr int kFullIn = 0, kFullRec = 16, kEmpty = 32, kHReady = 48, kMma = 64, kDFree = 80, kLin = 96,
                        kLinFree = 112;
   static constexpr int kBarSlot = 128;
-  static constexpr int kTmemSlot = kBar + 2 * kBarSlot, kAbort = kTmemSlot + 4, kDone = kTmemSlot + 8;
-  static constexpr int kPerm = kTmemSlot + 64, kLens = kPerm + 4 * 2 * NH;
-  static constexpr int kEnd = kLens + 4 * 2 * NH;
+  static constexpr int kTmemSlot = kBar + NSL * kBarSlot, kAbort = kTmemSlot + 4, kDone = kTmemSlot + 8;
+  static constexpr int kPerm = kTmemSlot + 64, kLens = kPerm + 4 * NSL * NH;
+  static constexpr int kEnd = kLens + 4 * NSL * NH;
   static constexpr int kDynBytes = kEnd + 1024;  // + alignment slack
   static constexpr int CPW = NH / 8;               // 8-column chunks per compute warp (all NH columns)
   static constexpr int kSlotWarps = 4;             // compute warps per slot: one per TMEM lane quadrant
-  static constexpr int kComputeWarps = 2 * kSlotWarps;
-  static constexpr int kOutWarp0 = kComputeWarps + 2;        // after one control warp per slot
-  static constexpr int kThreads = (kComputeWarps + 4) * 32;  // + one output warp per slot
+  static constexpr int kComputeWarps = NSL * kSlotWarps;
+  static constexpr int kOutWarp0 = kComputeWarps + NSL;  // after one control warp per slot
+  // + one output warp per slot in [B][T][O] mode (the only mode in which they work)
+  static constexpr int threads(int mode) { return (kOutWarp0 + (mode == kModeSeq ? NSL : 0)) * 32; }
   static constexpr bool kSplitLinear = (NH / 2) % 16 == 0;
   static constexpr int kNL = kSplitLinear ? NH / 2 : NH;
   static constexpr int kD = kTmemACols;            // D[slot][tau] at kD + (2 slot + tau) NH
-  static constexpr int kDLin = kD + 4 * NH;        // D_lin[slot][buffer] at kDLin + (2 slot + buffer) NL
-  static constexpr int kTmemCols = tmem_cols_for(kDLin + 4 * kNL);
-  static_assert(kDLin + 4 * kNL <= 512, "tile too wide for tensor memory");
+  static constexpr int kDLin = kD + 2 * NSL * NH;  // D_lin[slot][buffer] at kDLin + (2 slot + buffer) NL
+  static constexpr int kTmemCols = tmem_cols_for(kDLin + 2 * NSL * kNL);
+  static_assert(kDLin + 2 * NSL * kNL <= 512, "tile too wide for tensor memory");
   static_assert(NH % 16 == 0 && CPW >= 2 && CPW <= 4, "slot width must be 16 or 32");
+  static_assert(NSL >= 2 && NSL <= 3 && kDone + 4 * NSL <= kPerm, "two or three slots");
 };
 
-template <int NH, bool BF16, bool VARLEN, int MODE>
-__global__ void __launch_bounds__(Smem2<NH>::kThreads, 1) wavefront2_kernel(const Params p) {
-  using S = Smem2<NH>;
-  constexpr int N = 2 * NH;
+template <int NH, int NSL, bool BF16, bool VARLEN, int MODE>
+__global__ void __launch_bounds__(Smem2<NH, NSL>::threads(MODE), 1) wavefront2_kernel(const Params p) {
+  using S = Smem2<NH, NSL>;
+  constexpr int N = NSL * NH;
+  constexpr int kThreads = S::threads(MODE);
   constexpr int CPW = S::CPW;
   constexpr int NL = S::kNL;
   constexpr int kComputeWarps = S::kComputeWarps;
@@ -927,8 +931,11 @@ __global__ void __launch_bounds__(Smem2<NH>::kThreads, 1) wavefront2_kernel(cons
   const int tile = blockIdx.x / ncta;
   const bool last_layer = l == p.L - 1;
   const bool drain = kHasLinear && last_layer;
-  const bool does_linear = drain && (S::kSplitLinear || s == 0);
-  const bool sibling_linear = drain && (S::kSplitLinear || s == 1);
+  // The Linear head of a slot: split over both last-layer CTAs when half the slot is a legal
+  // MMA width, else computed by the CTA of the slot's parity (so the slots' heads are spread
+  // over both CTAs).
+  auto does_lin = [&](int sl) { return drain && (S::kSplitLinear || s == (sl & 1)); };
+  auto sibling_lin = [&](int sl) { return drain && (S::kSplitLinear || s != (sl & 1)); };
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + S::kAbort);
   int32_t* perm_s = reinterpret_cast<int32_t*>(sm + S::kPerm);
   int32_t* lens_s = reinterpret_cast<int32_t*>(sm + S::kLens);
@@ -941,7 +948,7 @@ __global__ void __launch_bounds__(Smem2<NH>::kThreads, 1) wavefront2_kernel(cons
 
   // ---- set-up ------------------------------------------------------------------
   if (tid == 0) {
-    for (int sl = 0; sl < 2; ++sl)
+    for (int sl = 0; sl < NSL; ++sl)
       for (int b = 0; b < 2; ++b) {
         ptx::mbar_init(bar(sl, S::kFullIn, b), 1);
         ptx::mbar_init(bar(sl, S::kFullRec, b), 1);
@@ -953,34 +960,33 @@ __global__ void __launch_bounds__(Smem2<NH>::kThreads, 1) wavefront2_kernel(cons
         ptx::mbar_init(bar(sl, S::kLinFree, b), 1);
       }
     *abort_flag = 0;
-    reinterpret_cast<uint32_t*>(sm + S::kDone)[0] = 0;
-    reinterpret_cast<uint32_t*>(sm + S::kDone)[1] = 0;
+    for (int sl = 0; sl < NSL; ++sl) reinterpret_cast<uint32_t*>(sm + S::kDone)[sl] = 0;
     ptx::fence_mbar_init_cluster();
   }
   if (warp == 0) {
     ptx::tmem_alloc(sbase + S::kTmemSlot, S::kTmemCols);
     ptx::tmem_relinquish();
   }
-  for (int i = tid; i < N; i += S::kThreads) {
+  for (int i = tid; i < N; i += kThreads) {
     const int b = p.perm[tile * N + i];
     perm_s[i] = b;
     int len = 0;
     if (b >= 0) len = VARLEN ? min(max(p.lengths[b], 0), p.T) : p.T;
     lens_s[i] = len;
   }
-  if (does_linear) {
+  if (drain) {
     // The head's rows (O <= 32, rows 0-31 of the packed image) are replicated into
     // every 32-row lane quadrant; 8-row swizzle groups keep their XOR pattern.
     const uint4* srcl = reinterpret_cast<const uint4*>(p.packed + packed_alin_off(p.L));
     uint4* dstl = reinterpret_cast<uint4*>(sm + S::kALin);
-    for (int i = tid; i < kALinBytes / 16; i += S::kThreads) {
+    for (int i = tid; i < kALinBytes / 16; i += kThreads) {
       const int kb = i / (kATileKB / 16), r = (i / 8) % 128, c = i % 8;
       dstl[i] = srcl[kb * (kATileKB / 16) + (r & 31) * 8 + c];
     }
   }
   __syncthreads();  // perm_s / lens_s / tmem slot visible
   // Initial recurrent state h0 -> both recurrent K blocks of each slot's B buffer 0.
-  for (int i = tid; i < N * kH; i += S::kThreads) {
+  for (int i = tid; i < N * kH; i += kThreads) {
     const int n = i / kH, k = i % kH;
     const int sl = n / NH, nn = n % NH;
     float v = 0.0f;
@@ -997,7 +1003,7 @@ __global__ void __launch_bounds__(Smem2<NH>::kThreads, 1) wavefront2_kernel(cons
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(sm + S::kTmemSlot);
   // This CTA's weight slice -> TMEM columns [0, 256): warps 0-3 store tile 0, warps
   // 4-7 tile 1, each its lane quadrant's 32 rows.
-  if (warp < kComputeWarps) {
+  if (warp < 8) {
     const int row = 32 * (warp & 3) + lane;
     const uint32_t lane_off = (uint32_t)(32 * (warp & 3)) << 16;
     const int tau = warp >> 2;
@@ -1050,6 +1056,7 @@ __global__ void __launch_bounds__(Smem2<NH>::kThreads, 1) wavefront2_kernel(cons
     // [B][T][O] mode: the Linear outputs of every step, read from the slot's Linear
     // accumulator in this warp's lane quadrant and stored, off the critical path.
     const int sl = warp - S::kOutWarp0;
+    const bool does_linear = does_lin(sl);
     bool active = false;
     const int Tt = slot_len(sl, &active);
     if (MODE == kModeSeq && does_linear && active) {
@@ -1098,6 +1105,7 @@ __global__ void __launch_bounds__(Smem2<NH>::kThreads, 1) wavefront2_kernel(cons
   } else if (warp >= kComputeWarps) {
     // ============================ control warps ==========================
     const int sl = warp - kComputeWarps;
+    const bool does_linear = does_lin(sl);
     bool active = false;
     const int Tt = slot_len(sl, &active);
     // A slot's layer-0 x tile: NH rows x kx, no swizzle (fits the slot's two input K blocks).
@@ -1286,9 +1294,12 @@ __global__ void __launch_bounds__(Smem2<NH>::kThreads, 1) wavefront2_kernel(cons
   } else {
     // =========================== compute warps ===========================
     const int sl = warp >> 2, q = warp & 3;
+    const bool does_linear = does_lin(sl), sibling_linear = sibling_lin(sl);
     bool active = false, other_active = false;
     const int Tt = slot_len(sl, &active);
-    const int T_other = slot_len(sl ^ 1, &other_active);
+    // The slot whose gate math precedes this one's on the MUFU pipes (round robin).
+    const int prev_sl = (sl + NSL - 1) % NSL;
+    const int T_other = slot_len(prev_sl, &other_active);
     const int j8 = lane >> 2;          // unit within the quadrant's group of 8
     const int cpair = (lane & 3) * 2;  // first of the two batch columns in a chunk
     const bool tracer = sl == p.trace_slot;
@@ -1394,13 +1405,13 @@ __global__ void __launch_bounds__(Smem2<NH>::kThreads, 1) wavefront2_kernel(cons
             break;
           }
         }
-        // The slots take turns on the MUFU pipes: slot 1 runs its gate math after
-        // slot 0's of the same step, slot 0 after slot 1's previous step, so that one
-        // slot's MMA / hand-off latency overlaps the other's gate math.
+        // The slots take turns on the MUFU pipes: slot sl > 0 runs its gate math after
+        // slot sl - 1's of the same step, slot 0 after the last slot's previous step, so
+        // that one slot's MMA / hand-off latency overlaps the others' gate math.
         {
-          const int tt = sl == 1 ? t : t - 1;
+          const int tt = sl > 0 ? t : t - 1;
           if (other_active && tt >= 0 && tt < T_other &&
-              !wait_phase(bar(sl ^ 1, S::kHReady, tt & 1), (tt >> 1) & 1, abort_flag, p.timeout_ns)) {
+              !wait_phase(bar(prev_sl, S::kHReady, tt & 1), (tt >> 1) & 1, abort_flag, p.timeout_ns)) {
             if (lane == 0) raise_abort(p, sm + S::kAbort, ncta, t);
             break;
           }
@@ -1763,14 +1774,14 @@ int threads_for(int N) {
   }
 }
 
-template <int NH, bool BF16, bool VARLEN, int MODE>
+template <int NH, int NSL, bool BF16, bool VARLEN, int MODE>
 void* kernel2_ptr() {
-  return reinterpret_cast<void*>(&wavefront2_kernel<NH, BF16, VARLEN, MODE>);
+  return reinterpret_cast<void*>(&wavefront2_kernel<NH, NSL, BF16, VARLEN, MODE>);
 }
-template <int NH>
+template <int NH, int NSL>
 void* pick_kernel2(bool bf16, bool varlen, int mode) {
 #define PLSTM_TC_K(B, V, M) \
-  if (bf16 == B && varlen == V && mode == M) return kernel2_ptr<NH, B, V, M>();
+  if (bf16 == B && varlen == V && mode == M) return kernel2_ptr<NH, NSL, B, V, M>();
   PLSTM_TC_K(false, false, kModeSeq) PLSTM_TC_K(false, false, kModeLast) PLSTM_TC_K(false, false, kModeHSeq)
   PLSTM_TC_K(false, true, kModeSeq) PLSTM_TC_K(false, true, kModeLast) PLSTM_TC_K(false, true, kModeHSeq)
   PLSTM_TC_K(true, false, kModeSeq) PLSTM_TC_K(true, false, kModeLast) PLSTM_TC_K(true, false, kModeHSeq)
@@ -1780,15 +1791,19 @@ void* pick_kernel2(bool bf16, bool varlen, int mode) {
 }
 // Kernel, dynamic shared memory and block size of a plan's launch.
 void* plan_kernel(const Plan& pl, bool bf16, bool varlen, int mode) {
-  if (pl.slots == 2) return pl.N == 32 ? pick_kernel2<16>(bf16, varlen, mode) : pick_kernel2<32>(bf16, varlen, mode);
+  if (pl.slots == 3) return pick_kernel2<16, 3>(bf16, varlen, mode);
+  if (pl.slots == 2)
+    return pl.N == 32 ? pick_kernel2<16, 2>(bf16, varlen, mode) : pick_kernel2<32, 2>(bf16, varlen, mode);
   return pick_kernel_n(pl.N, bf16, varlen, mode);
 }
 int plan_smem(const Plan& pl) {
-  if (pl.slots == 2) return pl.N == 32 ? Smem2<16>::kDynBytes : Smem2<32>::kDynBytes;
+  if (pl.slots == 3) return Smem2<16, 3>::kDynBytes;
+  if (pl.slots == 2) return pl.N == 32 ? Smem2<16, 2>::kDynBytes : Smem2<32, 2>::kDynBytes;
   return smem_bytes_for(pl.N);
 }
-int plan_threads(const Plan& pl) {
-  if (pl.slots == 2) return pl.N == 32 ? Smem2<16>::kThreads : Smem2<32>::kThreads;
+int plan_threads(const Plan& pl, int mode) {
+  if (pl.slots == 3) return Smem2<16, 3>::threads(mode);
+  if (pl.slots == 2) return pl.N == 32 ? Smem2<16, 2>::threads(mode) : Smem2<32, 2>::threads(mode);
   return threads_for(pl.N);
 }
 
@@ -1804,7 +1819,7 @@ cudaError_t allow_cluster(void* k, int L) {
 // (0: the cluster does not fit); cached.
 int max_active_clusters(int device, int L, const Plan& pl) {
   static std::mutex mu;
-  static int cache[64][kMaxLayers + 1][4][2];
+  static int cache[64][kMaxLayers + 1][4][3];  // [device][L][tile rows / 16 - 1][slots - 1]
   static bool init = false;
   std::lock_guard<std::mutex> g(mu);
   if (!init) {
@@ -1818,57 +1833,84 @@ int max_active_clusters(int device, int L, const Plan& pl) {
   if (device < 0 || device >= 64 || L < 1 || L > kMaxLayers) return 0;
   int& slot = cache[device][L][ni][pl.slots - 1];
   if (slot >= 0) return slot;
-  void* k = plan_kernel(pl, false, false, kModeLast);
-  cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, plan_smem(pl));
-  allow_cluster(k, L);
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(2 * L * 64, 1, 1);
-  cfg.blockDim = dim3((unsigned)plan_threads(pl), 1, 1);
-  cfg.dynamicSmemBytes = plan_smem(pl);
-  cudaLaunchAttribute attr;
-  attr.id = cudaLaunchAttributeClusterDimension;
-  attr.val.clusterDim.x = 2 * L;
-  attr.val.clusterDim.y = 1;
-  attr.val.clusterDim.z = 1;
-  cfg.attrs = &attr;
-  cfg.numAttrs = 1;
-  int n = 0;
-  if (cudaOccupancyMaxActiveClusters(&n, k, &cfg) != cudaSuccess || n < 0) {
-    cudaGetLastError();
-    n = 0;
+  // The fewest co-resident clusters of the three output modes' kernels (their block sizes and
+  // register counts differ), so that the plan does not depend on the output mode.
+  int n = 1 << 30;
+  for (int mode : {kModeSeq, kModeLast, kModeHSeq}) {
+    void* k = plan_kernel(pl, false, false, mode);
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, plan_smem(pl));
+    allow_cluster(k, L);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * L * 64, 1, 1);
+    cfg.blockDim = dim3((unsigned)plan_threads(pl, mode), 1, 1);
+    cfg.dynamicSmemBytes = plan_smem(pl);
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 2 * L;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    int m = 0;
+    if (cudaOccupancyMaxActiveClusters(&m, k, &cfg) != cudaSuccess || m < 0) {
+      cudaGetLastError();
+      m = 0;
+    }
+    n = std::min(n, m);
   }
   slot = n;
   return n;
 }
 
-Plan make_plan(const Problem& p) {
+Plan make_plan(const Problem& p, bool varlen) {
   Plan pl;
-  // Two-slot tiles of 32 or 64 rows by default (PLSTM_TC_KERNEL=1 selects the
-  // single-slot kernel with 16 / 32 / 48-row tiles).  The smallest tile whose
-  // clusters all fit on the GPU at once (one wave); beyond that the widest tile (of
-  // those whose cluster fits at all: 16-CTA clusters for L > 4 need one 16-SM group).
+  // Multi-slot tiles by default: 32 rows (two 16-row slots), 48 (three 16-row slots) or
+  // 64 (two 32-row slots); PLSTM_TC_KERNEL=1 selects the single-slot kernel with 16 / 32 /
+  // 48-row tiles.  The smallest tile whose clusters all fit on the GPU at once (one wave);
+  // beyond that the widest tile (of those whose cluster fits at all: 16-CTA clusters for
+  // L > 4 need one 16-SM group).  Slots of 16 rows have the shortest step (their gate math
+  // is half as long), so a batch that 15 clusters of 32 rows cannot hold (B = 512) runs as
+  // 11 clusters of three 16-row slots rather than 8 clusters of two 32-row slots.
   pl.slots = 2;
   if (const char* e = std::getenv("PLSTM_TC_KERNEL"))
     if (std::atoi(e) == 1 && tc_kx(p) == kXK) pl.slots = 1;  // the single-slot kernel reads x 16 wide
-  static constexpr int kTile2Ns[2] = {32, 64};
-  const int* ns = pl.slots == 2 ? kTile2Ns : kTileNs;
-  const int nn = pl.slots == 2 ? 2 : 3;
-  int N = ns[0];
+  static constexpr int kTile2Ns[3] = {32, 48, 64};
+  static constexpr int kTile2Slots[3] = {2, 3, 2};
+  const bool multi = pl.slots == 2;
+  const int* ns = multi ? kTile2Ns : kTileNs;
+  const int nn = 3;
+  auto slots_of = [&](int i) { return multi ? kTile2Slots[i] : 1; };
+  // Three 16-row slots measured faster than two 32-row slots for uniform lengths with [B][O] or
+  // [B][T][H] output (B = 512: 1.57 / 1.53 ms against 1.83 / 2.00 ms) but slower with [B][T][O]
+  // output and for variable lengths, where 32-row tiles whose shortest tiles run in a second
+  // wave's slack win (dual_plan).
+  const bool allow48 = !varlen && !p.out_seq();
+  int N = ns[0], slots = slots_of(0);
   for (int i = 0; i < nn; ++i) {
+    if (multi && ns[i] == 48 && !allow48) continue;
     Plan c = pl;
     c.N = ns[i];
+    c.slots = slots_of(i);
     const int m = max_active_clusters(p.device, p.L, c);
     if (m < 1) continue;
     N = ns[i];
+    slots = c.slots;
     if ((p.B + ns[i] - 1) / ns[i] <= m) break;
   }
   if (const char* e = std::getenv("PLSTM_TC_NTILE")) {
     const int v = std::atoi(e);
     for (int i = 0; i < nn; ++i)
-      if (v == ns[i]) N = v;
+      if (v == ns[i]) {
+        N = v;
+        slots = slots_of(i);
+      }
   }
+  pl.slots = slots;
   pl.N = N;
   pl.tiles = (p.B + N - 1) / N;
+  if (const char* dbg = std::getenv("PLSTM_TC_DEBUG"))
+    if (std::atoi(dbg) != 0)
+      std::fprintf(stderr, "plstm tc: %d-slot kernel, %d-row tiles, %d tiles\n", pl.slots, N, pl.tiles);
   return pl;
 }
 
@@ -2509,7 +2551,10 @@ bool tc_supported(const Problem& p, std::string* why) {
 size_t tc_packed_size(const Problem& p) { return wavefront_shape(p) ? packed_total(p.L) : tcl_packed_size(p); }
 
 size_t tc_workspace_size(const Problem& p) {
-  return wavefront_shape(p) ? tc_ws(p, make_plan(p)).total : tcl_workspace_size(p);
+  // The workspace is sized before the call says whether lengths come: the larger of the
+  // fixed- and variable-length plans.
+  if (!wavefront_shape(p)) return tcl_workspace_size(p);
+  return std::max(tc_ws(p, make_plan(p, false)).total, tc_ws(p, make_plan(p, true)).total);
 }
 
 int32_t tc_pack(const Problem& p, int ih_layout, int hh_layout, const void* const* w_ih,
@@ -2543,7 +2588,7 @@ int32_t tc_forward(const Problem& p, const void* packed, const void* x, const in
                    const void* h0, const void* c0, void* out, void* h_n, void* c_n, void* ws,
                    cudaStream_t s) {
   if (!wavefront_shape(p)) return tcl_forward(p, packed, x, lengths, h0, c0, out, h_n, c_n, ws, s);
-  const Plan pl = make_plan(p);
+  const Plan pl = make_plan(p, lengths != nullptr);
   const TcWs w = tc_ws(p, pl);
   uint8_t* wsb = static_cast<uint8_t*>(ws);
   int32_t* perm = reinterpret_cast<int32_t*>(wsb + w.perm);
@@ -2615,7 +2660,7 @@ int32_t tc_forward(const Problem& p, const void* packed, const void* x, const in
     PLSTM_TRY_CUDA(allow_cluster(k, p.L));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(lp.tiles * 2 * p.L), 1, 1);
-    cfg.blockDim = dim3((unsigned)plan_threads(lp), 1, 1);
+    cfg.blockDim = dim3((unsigned)plan_threads(lp, mode), 1, 1);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
     cudaLaunchAttribute attr;

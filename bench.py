@@ -490,14 +490,14 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     lat = None
     if rank == 0 and not args.no_latency:
         probes = {r: microbench.step_latency(rows=r, steps=20000, device=local_rank) for r in (16, 32)}
-        t_step = probes[32]["us_per_step"]  # the config-2 kernel runs 32-row slots
+        t_step = probes[16]["us_per_step"]  # the config-2 kernel runs 16-row slots (three per 48-row tile)
         wave_ms = t_step * (T + L - 1) / 1e3
         serial_ms = t_step * T * L / 1e3
         lat = {"t_step_us": t_step, "probe": probes,
                "floor_wavefront_ms": wave_ms, "frac_wavefront": wave_ms / kernel_ms,
                "floor_layer_serial_ms": serial_ms, "frac_layer_serial": serial_ms / kernel_ms,
-               "method": "(T + L - 1) x t_step of the 32-row probe (a wavefront of T + L - 1 dependent steps); "
-                         "T x L x t_step is the north star's layer-serial form"}
+               "method": "(T + L - 1) x t_step of the 16-row probe, the kernel's slot height (a wavefront of "
+                         "T + L - 1 dependent steps); T x L x t_step is the north star's layer-serial form"}
 
     if rank != 0:
         return

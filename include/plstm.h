@@ -102,7 +102,7 @@ typedef struct plstm_desc {
   int32_t w_layout;    /* PLSTM_W_* of w_ih / w_hh given to plstm_pack / plstm_forward */
   int32_t flags;       /* PLSTM_FLAG_* */
   int32_t backend;     /* PLSTM_BACKEND_* */
-  int32_t timeout_ms;  /* bound of every inter-CTA wait; 0 = 2000 ms */
+  int32_t timeout_ms;  /* bound of every inter-CTA wait; 0 = $PLSTM_TIMEOUT_MS, else 2000 ms */
   int32_t device;      /* CUDA device ordinal the pointers live on */
 } plstm_desc;
 

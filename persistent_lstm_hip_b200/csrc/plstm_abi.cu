@@ -1,6 +1,7 @@
 // plstm_abi.cu — the C ABI (include/plstm.h): validation, backend dispatch,
 // workspace layout and the reference-named entry points.
 #include <atomic>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -70,9 +71,19 @@ int32_t make_problem(const plstm_desc* d, Problem* p) {
   p->O = (d->flags & PLSTM_FLAG_NO_LINEAR) ? 0 : d->output_size;
   p->dtype = d->dtype;
   p->flags = d->flags;
-  p->timeout_ms = d->timeout_ms > 0 ? d->timeout_ms : 2000;
+  p->timeout_ms = d->timeout_ms > 0 ? d->timeout_ms : default_timeout_ms();
   p->device = d->device;
   return PLSTM_OK;
+}
+
+// Bound of every inter-CTA wait when the descriptor leaves it 0: PLSTM_TIMEOUT_MS if set (a
+// profiler that replays each launch dozens of times can stretch a step well past 2 s), else 2 s.
+int32_t default_timeout_ms() {
+  if (const char* e = std::getenv("PLSTM_TIMEOUT_MS")) {
+    const long v = std::strtol(e, nullptr, 10);
+    if (v > 0 && v <= 3600000) return (int32_t)v;
+  }
+  return 2000;
 }
 
 namespace {

@@ -133,6 +133,8 @@ struct Problem {
 // Validates a descriptor and fills the Problem every backend reads (plstm_abi.cu);
 // PLSTM_EINVAL with the message set on a bad field.
 int32_t make_problem(const plstm_desc* d, Problem* p);
+// Default bound of the inter-CTA waits: PLSTM_TIMEOUT_MS, else 2000 ms.
+int32_t default_timeout_ms();
 
 // Generic layer-sequential FFMA backend (any shape, f32/f16/bf16).
 size_t simt_packed_size(const Problem& p);

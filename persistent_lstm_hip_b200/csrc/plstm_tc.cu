@@ -1880,11 +1880,11 @@ Plan make_plan(const Problem& p, bool varlen) {
   const int* ns = multi ? kTile2Ns : kTileNs;
   const int nn = 3;
   auto slots_of = [&](int i) { return multi ? kTile2Slots[i] : 1; };
-  // Three 16-row slots measured faster than two 32-row slots for uniform lengths with [B][O] or
-  // [B][T][H] output (B = 512: 1.57 / 1.53 ms against 1.83 / 2.00 ms) but slower with [B][T][O]
-  // output and for variable lengths, where 32-row tiles whose shortest tiles run in a second
-  // wave's slack win (dual_plan).
-  const bool allow48 = !varlen && !p.out_seq();
+  // Three 16-row slots measured faster than two 32-row slots for uniform lengths (B = 512:
+  // [B][O] 1.54 against 1.83 ms, [B][T][H] 1.54 against 2.00, [B][T][O] 1.97 against 1.99) but
+  // slower for variable lengths, where 32-row tiles whose shortest tiles run in a second wave's
+  // slack win (dual_plan).
+  const bool allow48 = !varlen;
   int N = ns[0], slots = slots_of(0);
   for (int i = 0; i < nn; ++i) {
     if (multi && ns[i] == 48 && !allow48) continue;

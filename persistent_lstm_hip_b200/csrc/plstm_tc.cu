@@ -113,7 +113,9 @@ struct Smem {
 
 struct Params {
   const uint8_t* packed;
-  const uint8_t* xp;        // [tiles][T][N * kx * 2 bytes]
+  const uint8_t* xp;        // [tiles][T][N * kx * 2 bytes], or null: the kernel reads x itself (x_raw)
+  const uint16_t* x_raw;    // x[B][T][I] 16-bit, read by the layer-0 x warp of the multi-slot kernel when xp is null
+  int I;                    // input columns of x_raw (<= 16, so that kx = 16)
   const int32_t* perm;      // [tiles * N], -1 = padding row
   const int32_t* lengths;   // [B] (varlen) or null
   const int32_t* tile_len;  // [tiles]
@@ -897,8 +899,11 @@ struct Smem2 {
   static constexpr int kSlotWarps = 4;             // compute warps per slot: one per TMEM lane quadrant
   static constexpr int kComputeWarps = NSL * kSlotWarps;
   static constexpr int kOutWarp0 = kComputeWarps + NSL;  // after one control warp per slot
-  // + one output warp per slot in [B][T][O] mode (the only mode in which they work)
-  static constexpr int threads(int mode) { return (kOutWarp0 + (mode == kModeSeq ? NSL : 0)) * 32; }
+  // + one output warp per slot in [B][T][O] mode (the only mode in which they work, and only in
+  // the last layer), else one warp for x: the layer-0 x warp reads x[B][T][I] into the input tiles
+  // (in [B][T][O] mode the last output warp takes that role in a layer 0 that is not the last).
+  static constexpr int xwarp(int mode) { return kOutWarp0 + (mode == kModeSeq ? NSL - 1 : 0); }
+  static constexpr int threads(int mode) { return (kOutWarp0 + (mode == kModeSeq ? NSL : 1)) * 32; }
   static constexpr bool kSplitLinear = (NH / 2) % 16 == 0;
   static constexpr int kNL = kSplitLinear ? NH / 2 : NH;
   static constexpr int kD = kTmemACols;            // D[slot][tau] at kD + (2 slot + tau) NH
@@ -1051,7 +1056,78 @@ __global__ void __launch_bounds__(Smem2<NH, NSL>::threads(MODE), 1) wavefront2_k
     return tmem + (uint32_t)(S::kDLin + (2 * sl + lin_buf(t)) * NL);
   };
 
-  if (warp >= S::kOutWarp0) {
+  const bool x_warp = warp == S::xwarp(MODE) && l == 0 && p.xp == nullptr && !(MODE == kModeSeq && last_layer);
+  if (x_warp) {
+    // ============================== x warp ===============================
+    // Layer 0 without a repacked x (xp null, I <= 16): lane n < NH holds row n of every slot
+    // and writes x_t of it into the slot's input tile (kx = 16: K group 0 = columns 0-7 at
+    // 8-row groups 256 bytes apart, K group 1 = columns 8-15 128 bytes further), two steps
+    // ahead of the MMAs that read it (the tile of step t + 2 reuses step t's buffer once step
+    // t's gate math has started, i.e. its MMAs are done: HReady).  The global loads of x_{t+3}
+    // are issued right after x_{t+2} is written, so their latency hides under a whole step.
+    {
+      const int I = p.I;
+      int Tt[NSL];
+      for (int sl = 0; sl < NSL; ++sl) {
+        bool a = false;
+        Tt[sl] = slot_len(sl, &a);
+      }
+      // Rows / columns never written stay zero: clear both parity tiles of every slot.
+      for (int sl = 0; sl < NSL; ++sl)
+        for (int b = 0; b < 2; ++b)
+          for (int i = lane; i < NH * 16 * 2 / 16; i += 32)
+            reinterpret_cast<uint4*>(sm + S::kB + sl * S::kSlotBytes + b * S::kBufBytes)[i] = make_uint4(0, 0, 0, 0);
+      auto load_row = [&](int sl, int t, uint32_t (&o)[8]) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[i] = 0u;
+        const int b = lane < NH ? perm_s[sl * NH + lane] : -1;
+        if (b < 0 || t >= Tt[sl]) return;
+        const uint16_t* src = p.x_raw + ((size_t)b * p.T + t) * I;
+#pragma unroll
+        for (int k = 0; k < 16; ++k)
+          if (k < I) o[k >> 1] |= (uint32_t)__ldg(src + k) << (16 * (k & 1));
+      };
+      auto write_row = [&](int sl, int b, const uint32_t (&o)[8]) {
+        if (lane >= NH) return;
+        uint8_t* dst = sm + S::kB + sl * S::kSlotBytes + b * S::kBufBytes + (lane >> 3) * 256 + (lane & 7) * 16;
+        *reinterpret_cast<uint4*>(dst) = make_uint4(o[0], o[1], o[2], o[3]);
+        if (I > 8) *reinterpret_cast<uint4*>(dst + 128) = make_uint4(o[4], o[5], o[6], o[7]);
+      };
+      uint32_t v[NSL][8];
+      // Steps 0 and 1, then x_2 into registers.
+      for (int t = 0; t < 2; ++t)
+        for (int sl = 0; sl < NSL; ++sl) {
+          if (t >= Tt[sl]) continue;
+          load_row(sl, t, v[sl]);
+          write_row(sl, t, v[sl]);
+          ptx::fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) ptx::mbar_arrive(bar(sl, S::kFullIn, t));
+        }
+      int Tmax = 0;
+      for (int sl = 0; sl < NSL; ++sl) {
+        load_row(sl, 2, v[sl]);
+        Tmax = max(Tmax, Tt[sl]);
+      }
+      bool ok = true;
+      for (int t = 0; ok && t + 2 < Tmax; ++t) {
+        const int b = t & 1;
+        for (int sl = 0; sl < NSL; ++sl) {
+          if (t + 2 >= Tt[sl]) continue;
+          if (!warp_wait_phase(bar(sl, S::kHReady, b), (t >> 1) & 1, abort_flag, p.timeout_ns)) {
+            if (lane == 0 && !*abort_flag) raise_abort(p, sm + S::kAbort, ncta, t);
+            ok = false;
+            break;
+          }
+          write_row(sl, b, v[sl]);
+          ptx::fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) ptx::mbar_arrive(bar(sl, S::kFullIn, b));
+          load_row(sl, t + 3, v[sl]);
+        }
+      }
+    }
+  } else if (warp >= S::kOutWarp0) {
     // ============================ output warps ===========================
     // [B][T][O] mode: the Linear outputs of every step, read from the slot's Linear
     // accumulator in this warp's lane quadrant and stored, off the critical path.
@@ -1111,6 +1187,9 @@ __global__ void __launch_bounds__(Smem2<NH, NSL>::threads(MODE), 1) wavefront2_k
     // A slot's layer-0 x tile: NH rows x kx, no swizzle (fits the slot's two input K blocks).
     const uint32_t xbytes = (uint32_t)(NH * p.kx * 2), bkb = S::kBKB;
     const uint32_t in_bytes = (l == 0) ? xbytes : 2 * bkb;
+    // Layer 0 whose x tiles the x warp writes: FullIn completes on that warp's arrival
+    // (no transaction bytes to expect, nothing to copy).
+    const bool x_by_warp = l == 0 && p.xp == nullptr;
     constexpr uint32_t idesc_g = ptx::idesc_f16(128, NH, BF16);
     constexpr uint32_t idesc_l = ptx::idesc_f16(128, NL, BF16);
     const uint16_t up_mask = l > 0 ? (uint16_t)(3u << (2 * (l - 1))) : 0;
@@ -1199,7 +1278,7 @@ __global__ void __launch_bounds__(Smem2<NH, NSL>::threads(MODE), 1) wavefront2_k
     // (h(t) itself is pushed by the slot's last compute warp to finish the step).
     auto hand_off = [&](int t) {
       const int b = t & 1;
-      if (l == 0 && t + 2 < Tt && ptx::elect_one())
+      if (l == 0 && !x_by_warp && t + 2 < Tt && ptx::elect_one())
         ptx::bulk_g2s(bbuf(sl, b), x_src(t + 2), xbytes, bar(sl, S::kFullIn, b));
       __syncwarp();
     };
@@ -1207,7 +1286,7 @@ __global__ void __launch_bounds__(Smem2<NH, NSL>::threads(MODE), 1) wavefront2_k
     if (active) {
       // Prologue: expected bytes of steps 0 / 1 (inputs) and 1 / 2 (sibling h), x of steps 0 / 1.
       if (ptx::elect_one()) {
-        for (int t = 0; t < 2 && t < Tt; ++t) {
+        for (int t = 0; t < 2 && t < Tt && !x_by_warp; ++t) {
           ptx::mbar_arrive_expect_tx(bar(sl, S::kFullIn, t), in_bytes);
           if (l == 0) ptx::bulk_g2s(bbuf(sl, t), x_src(t), xbytes, bar(sl, S::kFullIn, t));
         }
@@ -1220,7 +1299,7 @@ __global__ void __launch_bounds__(Smem2<NH, NSL>::threads(MODE), 1) wavefront2_k
           fail(0);
         } else {
           issue_in(0);
-          if (2 < Tt && ptx::elect_one()) ptx::mbar_arrive_expect_tx(bar(sl, S::kFullIn, 0), in_bytes);
+          if (2 < Tt && !x_by_warp && ptx::elect_one()) ptx::mbar_arrive_expect_tx(bar(sl, S::kFullIn, 0), in_bytes);
           __syncwarp();
         }
       }
@@ -1269,7 +1348,8 @@ __global__ void __launch_bounds__(Smem2<NH, NSL>::threads(MODE), 1) wavefront2_k
           if (in_pending && warp_test_wait(bar(sl, S::kDFree, b), (t >> 1) & 1) &&
               warp_test_wait(bar(sl, S::kFullIn, b ^ 1), ((t + 1) >> 1) & 1)) {
             issue_in(t + 1);
-            if (t + 3 < Tt && ptx::elect_one()) ptx::mbar_arrive_expect_tx(bar(sl, S::kFullIn, b ^ 1), in_bytes);
+            if (t + 3 < Tt && !x_by_warp && ptx::elect_one())
+              ptx::mbar_arrive_expect_tx(bar(sl, S::kFullIn, b ^ 1), in_bytes);
             __syncwarp();
             in_pending = false;
             continue;
@@ -2598,9 +2678,14 @@ int32_t tc_forward(const Problem& p, const void* packed, const void* x, const in
   int* choice = dual.on ? reinterpret_cast<int*>(len32 + dual.tiles32) : nullptr;
   int32_t* hist = reinterpret_cast<int32_t*>(wsb + w.hist);
   int32_t* sorted = reinterpret_cast<int32_t*>(wsb + w.sorted);
+  // The multi-slot kernels read x[B][T][I] themselves when it is at most 16 columns wide (one
+  // 16-wide K step: the layer-0 x warp fills the input tiles); otherwise x is repacked into
+  // per-tile K-major tiles first.  PLSTM_TC_XPACK=1 forces the repack (for comparisons).
+  const bool fuse_x = pl.slots >= 2 && tc_kx(p) == kXK && !(p.out_seq() && p.L == 1) &&
+                      std::getenv("PLSTM_TC_XPACK") == nullptr;
   if (!dual.on) {
     int32_t rc = tc_make_perm(p, pl.N, pl.tiles, lengths, perm, tile_len, hist, sorted, s);
-    if (rc == PLSTM_OK) rc = tc_xpack(p, pl.N, pl.tiles, x, perm, wsb + w.xp, tc_kx(p), s);
+    if (rc == PLSTM_OK && !fuse_x) rc = tc_xpack(p, pl.N, pl.tiles, x, perm, wsb + w.xp, tc_kx(p), s);
     if (rc != PLSTM_OK) return rc;
   } else {
     // One length-sorted order serves both heights (64-row tile j = 32-row tiles 2j, 2j+1);
@@ -2612,13 +2697,17 @@ int32_t tc_forward(const Problem& p, const void* packed, const void* x, const in
     tc_tile_choice_kernel<<<1, 32, 0, s>>>(len32, dual.tiles32, pl.tiles, p.L, dual.m32, dual.m64, tile_len, choice);
     PLSTM_TRY_CUDA(cudaGetLastError());
     note_launches(1);
-    rc = tc_xpack(p, 32, dual.tiles32, x, perm, wsb + w.xp, tc_kx(p), s, choice);
-    if (rc == PLSTM_OK) rc = tc_xpack(p, 64, pl.tiles, x, perm, wsb + w.xp, tc_kx(p), s, choice);
+    if (!fuse_x) {
+      rc = tc_xpack(p, 32, dual.tiles32, x, perm, wsb + w.xp, tc_kx(p), s, choice);
+      if (rc == PLSTM_OK) rc = tc_xpack(p, 64, pl.tiles, x, perm, wsb + w.xp, tc_kx(p), s, choice);
+    }
     if (rc != PLSTM_OK) return rc;
   }
   Params kp = {};
   kp.packed = static_cast<const uint8_t*>(packed);
-  kp.xp = wsb + w.xp;
+  kp.xp = fuse_x ? nullptr : wsb + w.xp;
+  kp.x_raw = static_cast<const uint16_t*>(x);
+  kp.I = p.I;
   kp.perm = perm;
   kp.lengths = lengths;
   kp.tile_len = tile_len;

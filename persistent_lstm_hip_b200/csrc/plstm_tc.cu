@@ -1064,7 +1064,9 @@ __global__ void __launch_bounds__(Smem2<NH, NSL>::threads(MODE), 1) wavefront2_k
     // 8-row groups 256 bytes apart, K group 1 = columns 8-15 128 bytes further), two steps
     // ahead of the MMAs that read it (the tile of step t + 2 reuses step t's buffer once step
     // t's gate math has started, i.e. its MMAs are done: HReady).  The global loads of x_{t+3}
-    // are issued right after x_{t+2} is written, so their latency hides under a whole step.
+    // are issued right after x_{t+2} is written, so their latency hides under a whole step,
+    // and every row is prefetched into L2 kXPrefetch steps ahead, so that those loads hit L2
+    // even when x starts out in HBM (a step is shorter than an HBM miss).
     {
       const int I = p.I;
       int Tt[NSL];
@@ -1077,23 +1079,33 @@ __global__ void __launch_bounds__(Smem2<NH, NSL>::threads(MODE), 1) wavefront2_k
         for (int b = 0; b < 2; ++b)
           for (int i = lane; i < NH * 16 * 2 / 16; i += 32)
             reinterpret_cast<uint4*>(sm + S::kB + sl * S::kSlotBytes + b * S::kBufBytes)[i] = make_uint4(0, 0, 0, 0);
-      auto load_row = [&](int sl, int t, uint32_t (&o)[8]) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) o[i] = 0u;
+      // Loads leave the 16-bit values raw in registers; they are packed only when the tile is
+      // written (the next iteration), so the warp never waits for its own loads in between.
+      auto load_row = [&](int sl, int t, uint32_t (&raw)[16]) {
         const int b = lane < NH ? perm_s[sl * NH + lane] : -1;
-        if (b < 0 || t >= Tt[sl]) return;
-        const uint16_t* src = p.x_raw + ((size_t)b * p.T + t) * I;
+        const bool live = b >= 0 && t < Tt[sl];
+        const uint16_t* src = p.x_raw + ((size_t)max(b, 0) * p.T + t) * I;
 #pragma unroll
-        for (int k = 0; k < 16; ++k)
-          if (k < I) o[k >> 1] |= (uint32_t)__ldg(src + k) << (16 * (k & 1));
+        for (int k = 0; k < 16; ++k) raw[k] = (live && k < I) ? (uint32_t)__ldg(src + k) : 0u;
       };
-      auto write_row = [&](int sl, int b, const uint32_t (&o)[8]) {
+      constexpr int kXPrefetch = 24;
+      auto prefetch_row = [&](int sl, int t) {
+        const int b = lane < NH ? perm_s[sl * NH + lane] : -1;
+        if (b >= 0 && t < Tt[sl]) ptx::prefetch_l2(p.x_raw + ((size_t)b * p.T + t) * I);
+      };
+      auto write_row = [&](int sl, int b, const uint32_t (&raw)[16]) {
         if (lane >= NH) return;
         uint8_t* dst = sm + S::kB + sl * S::kSlotBytes + b * S::kBufBytes + (lane >> 3) * 256 + (lane & 7) * 16;
-        *reinterpret_cast<uint4*>(dst) = make_uint4(o[0], o[1], o[2], o[3]);
-        if (I > 8) *reinterpret_cast<uint4*>(dst + 128) = make_uint4(o[4], o[5], o[6], o[7]);
+        *reinterpret_cast<uint4*>(dst) = make_uint4(raw[0] | raw[1] << 16, raw[2] | raw[3] << 16,
+                                                    raw[4] | raw[5] << 16, raw[6] | raw[7] << 16);
+        if (I > 8)
+          *reinterpret_cast<uint4*>(dst + 128) = make_uint4(raw[8] | raw[9] << 16, raw[10] | raw[11] << 16,
+                                                            raw[12] | raw[13] << 16, raw[14] | raw[15] << 16);
       };
-      uint32_t v[NSL][8];
+      uint32_t v[NSL][16];
+      // The first kXPrefetch steps of every row into L2 (one prefetch per 64 bytes of a row).
+      for (int sl = 0; sl < NSL; ++sl)
+        for (int t = 0; t < kXPrefetch; t += max(1, 64 / (2 * I))) prefetch_row(sl, t);
       // Steps 0 and 1, then x_2 into registers.
       for (int t = 0; t < 2; ++t)
         for (int sl = 0; sl < NSL; ++sl) {
@@ -1124,6 +1136,7 @@ __global__ void __launch_bounds__(Smem2<NH, NSL>::threads(MODE), 1) wavefront2_k
           __syncwarp();
           if (lane == 0) ptx::mbar_arrive(bar(sl, S::kFullIn, b));
           load_row(sl, t + 3, v[sl]);
+          prefetch_row(sl, t + 3 + kXPrefetch);
         }
       }
     }

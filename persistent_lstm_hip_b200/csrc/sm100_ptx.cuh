@@ -123,6 +123,9 @@ __device__ __forceinline__ void st_cluster_u32(uint32_t cluster_addr, uint32_t v
                : "memory");
 }
 
+// Prefetches the L2 line holding `p` (global memory) into L2.
+__device__ __forceinline__ void prefetch_l2(const void* p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
+
 // ---- bulk async copies -------------------------------------------------------
 // global -> this CTA's shared memory, completion as tx bytes on `bar`.
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {

@@ -490,14 +490,19 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     lat = None
     if rank == 0 and not args.no_latency:
         probes = {r: microbench.step_latency(rows=r, steps=20000, device=local_rank) for r in (16, 32)}
-        t_step = probes[16]["us_per_step"]  # the config-2 kernel runs 16-row slots (three per 48-row tile)
+        # The config-2 kernel runs 16-row slots (three per 48-row tile).  The probe's step in SM cycles,
+        # at the SM clock sampled during the timed region (a lone 2-CTA launch may run at another clock).
+        sm_mhz = clocks.get("sm_mhz") or 1965.0
+        t_step = probes[16]["cycles_per_step"] / sm_mhz
         wave_ms = t_step * (T + L - 1) / 1e3
         serial_ms = t_step * T * L / 1e3
         lat = {"t_step_us": t_step, "probe": probes,
                "floor_wavefront_ms": wave_ms, "frac_wavefront": wave_ms / kernel_ms,
                "floor_layer_serial_ms": serial_ms, "frac_layer_serial": serial_ms / kernel_ms,
-               "method": "(T + L - 1) x t_step of the 16-row probe, the kernel's slot height (a wavefront of "
-                         "T + L - 1 dependent steps); T x L x t_step is the north star's layer-serial form"}
+               "sm_mhz": sm_mhz,
+               "method": "(T + L - 1) x t_step, t_step = the 16-row probe's cycles per step (the kernel's slot "
+                         "height) at the SM clock sampled during the timed region (a wavefront of T + L - 1 "
+                         "dependent steps); T x L x t_step is the north star's layer-serial form"}
 
     if rank != 0:
         return

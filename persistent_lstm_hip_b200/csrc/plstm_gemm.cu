@@ -87,14 +87,16 @@ __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.comm
 __device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
+// Two values rounded to 16 bits in one conversion (lo -> bits [0, 16)): the paired
+// cvt.rn.{f16x2,bf16x2}.f32 runs at ALU rate, the single-value one at the MUFU rate.
 template <bool BF16>
-__device__ __forceinline__ uint16_t bits16(float v) {
+__device__ __forceinline__ uint32_t bits16x2(float lo, float hi) {
   if (BF16) {
-    __nv_bfloat16 h = __float2bfloat16_rn(v);
-    return *reinterpret_cast<uint16_t*>(&h);
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
   }
-  __half h = __float2half_rn(v);
-  return *reinterpret_cast<uint16_t*>(&h);
+  __half2 v = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
 }
 
 template <bool BF16>
@@ -143,7 +145,40 @@ __global__ void __launch_bounds__(kThreads, 1)
   ptx::tc_fence_after();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
 
-  if (warp < 4) {
+  if (warp < 4 && kp == 16) {
+    // ---------------- producers, K <= 16 ----------------
+    // Thread = row.  A row is at most 16 values, so its loads stay raw in registers and the
+    // loads of tile it + 1 are issued before tile it is written (and rows 4 tiles ahead are
+    // prefetched into L2): the producers never wait a whole memory latency per tile.
+    const int m_local = tid;
+    const int ns = lo.stages;
+    auto row_of = [&](int it) { return (first_m + it * ctas_per_n) * kBM + m_local; };
+    auto load = [&](int it, uint32_t (&raw)[16]) {
+      const int m = row_of(it);
+      const bool valid = it < my_tiles && m < M;
+      const uint16_t* src = x + (size_t)(valid ? m : 0) * K;
+#pragma unroll
+      for (int k = 0; k < 16; ++k) raw[k] = (valid && k < K) ? (uint32_t)__ldg(src + k) : 0u;
+    };
+    uint32_t cur[16], nxt[16];
+    load(0, cur);
+    for (int it = 0; it < my_tiles; ++it) {
+      const int s = it % ns;
+      if (it + 4 < my_tiles && row_of(it + 4) < M) ptx::prefetch_l2(x + (size_t)row_of(it + 4) * K);
+      load(it + 1, nxt);
+      if (it >= ns && !wait_bounded(a_empty + 8 * s, ((it / ns) - 1) & 1)) break;
+      uint8_t* a = sm + lo.a_off + s * lo.a_stage;
+      *reinterpret_cast<uint4*>(a + none16_off(m_local, 0)) =
+          make_uint4(cur[0] | cur[1] << 16, cur[2] | cur[3] << 16, cur[4] | cur[5] << 16, cur[6] | cur[7] << 16);
+      *reinterpret_cast<uint4*>(a + none16_off(m_local, 8)) = make_uint4(
+          cur[8] | cur[9] << 16, cur[10] | cur[11] << 16, cur[12] | cur[13] << 16, cur[14] | cur[15] << 16);
+      ptx::fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(a_full + 8 * s);
+#pragma unroll
+      for (int k = 0; k < 16; ++k) cur[k] = nxt[k];
+    }
+  } else if (warp < 4) {
     // ---------------- producers ----------------
     const int m_local = tid;  // 0..127
     const int ns = lo.stages;
@@ -229,8 +264,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t pk[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i)
-          pk[i] = (uint32_t)bits16<BF16>(__uint_as_float(r[8 * c + 2 * i])) |
-                  ((uint32_t)bits16<BF16>(__uint_as_float(r[8 * c + 2 * i + 1])) << 16);
+          pk[i] = bits16x2<BF16>(__uint_as_float(r[8 * c + 2 * i]), __uint_as_float(r[8 * c + 2 * i + 1]));
         *reinterpret_cast<uint4*>(row + 16 * c) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
       }
       ptx::fence_proxy_async_smem();  // the staged rows are read by the bulk copies below

@@ -14,13 +14,19 @@
 //              for Kp = 64 .. 256) into one of two A stages;
 //   warp 4     issues tcgen05.mma M=128 N=128 into one of two TMEM accumulators;
 //   warps 5-12 epilogue: two warps per TMEM lane quadrant, 64 accumulator
-//              columns each: tcgen05.ld, convert to 16-bit, stage the tile in
-//              one of two shared-memory buffers, then one bulk shared->global
-//              copy per output row segment (128 rows x 256 bytes), which drains
-//              to HBM while the next tile is loaded (per-thread 16-byte stores
-//              of the staged tile reached 2.7 TB/s).
+//              columns each: tcgen05.ld, convert to 16-bit in pairs, stage the
+//              tile in one of two shared-memory buffers as two 128 x 64 boxes in
+//              the 128-byte swizzle, then two TMA tensor stores
+//              (cp.async.bulk.tensor.2d) write it out and drain to HBM while the
+//              next tile is loaded.  Without a tensor map (driver entry point
+//              unavailable) the tile goes out as one bulk copy per 256-byte row.
 // All waits are bounded.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include <algorithm>
+#include <cstring>
+#include <mutex>
 
 #include "plstm_common.cuh"
 #include "sm100_ptx.cuh"
@@ -31,7 +37,8 @@ namespace gemm {
 constexpr int kBM = 128, kBN = 128;
 constexpr int kEpiWarps = 8;
 constexpr int kThreads = (4 + 1 + kEpiWarps) * 32;
-constexpr int kStageRowPad = kBN * 2 + 16;  // staging row stride (bank-conflict padding)
+constexpr int kStageRowPad = kBN * 2 + 16;  // staging row stride of the row-copy path (bank-conflict padding)
+constexpr int kStageBytes = kBM * kStageRowPad;  // one stage buffer (>= the TMA path's two 16 KB boxes)
 
 __host__ __device__ constexpr int kpad_of(int K) { return K <= 16 ? 16 : ((K + 63) / 64) * 64; }
 
@@ -51,8 +58,8 @@ __host__ __device__ inline Layout layout_for(int K) {
   lo.b_off = 0;
   lo.a_off = kBN * lo.kp * 2;  // B tile [128 x Kp]
   for (lo.stages = 2; lo.stages >= 1; --lo.stages) {
-    lo.stage_off = lo.a_off + lo.stages * lo.a_stage;
-    lo.bar_off = lo.stage_off + 2 * kBM * kStageRowPad;
+    lo.stage_off = (lo.a_off + lo.stages * lo.a_stage + 1023) / 1024 * 1024;  // swizzle atoms: 1 KB aligned
+    lo.bar_off = lo.stage_off + 2 * kStageBytes;
     lo.total = lo.bar_off + 128 + 1024;
     if (lo.total <= kMaxSmem) break;
   }
@@ -99,10 +106,19 @@ __device__ __forceinline__ uint32_t bits16x2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
+// TMA store of one box of the tensor map at element coordinates (x = column, y = row) from
+// this CTA's shared memory, tracked by the issuing thread's bulk groups.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t ssrc, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(map), "r"(x),
+               "r"(y), "r"(ssrc)
+               : "memory");
+}
+
 template <bool BF16>
 __global__ void __launch_bounds__(kThreads, 1)
     input_gemm_kernel(const uint16_t* __restrict__ x, int M, int K, const uint16_t* __restrict__ w_t, int N,
-                      uint16_t* __restrict__ gate, int n_tiles_n, int m_tiles) {
+                      uint16_t* __restrict__ gate, int n_tiles_n, int m_tiles, const __grid_constant__ CUtensorMap gmap,
+                      int use_tma) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = ptx::smem_u32(sm);
@@ -257,25 +273,33 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::tc_fence_before();
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(d_empty + 8 * db);
-      uint8_t* stage = sm + lo.stage_off + db * (kBM * kStageRowPad);
-      uint8_t* row = stage + m_local * kStageRowPad + hc * 128;
+      uint8_t* stage = sm + lo.stage_off + db * kStageBytes;
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
         uint32_t pk[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i)
           pk[i] = bits16x2<BF16>(__uint_as_float(r[8 * c + 2 * i]), __uint_as_float(r[8 * c + 2 * i + 1]));
-        *reinterpret_cast<uint4*>(row + 16 * c) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        // TMA: box hc (columns 64 hc ..), 128-byte rows with 16-byte chunks swizzled by row % 8;
+        // row copies: padded rows of kStageRowPad bytes.
+        uint8_t* dst = use_tma ? stage + hc * (kBM * 128) + m_local * 128 + ((c ^ (m_local & 7)) << 4)
+                               : stage + m_local * kStageRowPad + hc * 128 + 16 * c;
+        *reinterpret_cast<uint4*>(dst) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
       }
-      ptx::fence_proxy_async_smem();  // the staged rows are read by the bulk copies below
-      // The previous tile's copies (other stage buffer) have read their rows: the buffer this
+      ptx::fence_proxy_async_smem();  // the staged tile is read by the async copies below
+      // The previous tile's copies (other stage buffer) have read their data: the buffer this
       // tile's successor writes is free once everyone is past the barrier.
       if (etid < kBM) bulk_wait_read0();
       asm volatile("bar.sync 1, %0;" ::"n"(kEpiWarps * 32) : "memory");
-      // One bulk copy per output row segment (up to 256 contiguous bytes): the tile drains to
-      // HBM asynchronously while the next tile is loaded from tensor memory.
+      // The tile drains to HBM asynchronously while the next tile is loaded from tensor memory.
       const int m0 = (first_m + it * ctas_per_n) * kBM;
-      if (etid < kBM && m0 + etid < M) {
+      if (use_tma) {
+        if (etid == 0) {  // rows past M and columns past N are clipped by the tensor map
+          tma_store_2d(&gmap, ptx::smem_u32(stage), n0, m0);
+          if (ncols > 64) tma_store_2d(&gmap, ptx::smem_u32(stage + kBM * 128), n0 + 64, m0);
+          bulk_commit();
+        }
+      } else if (etid < kBM && m0 + etid < M) {
         bulk_s2g(gate + (size_t)(m0 + etid) * N + n0, ptx::smem_u32(stage + etid * kStageRowPad),
                  (uint32_t)(ncols * 2));
         bulk_commit();
@@ -289,6 +313,35 @@ __global__ void __launch_bounds__(kThreads, 1)
     ptx::tc_fence_after();
     ptx::tmem_dealloc(tmem, 2 * kBN);
   }
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link against libcuda).
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static std::once_flag once;
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    cudaGetLastError();
+  });
+  return fn;
+}
+
+// Tensor map of gate[M][N] (16-bit) with 128-row x 64-column boxes in the 128-byte swizzle;
+// false if it cannot be made (the kernel then stores rows with plain bulk copies).
+bool make_gate_map(void* gate, int M, int N, CUtensorMap* map) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc = encode_fn();
+  if (enc == nullptr) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)N, (cuuint64_t)M};
+  const cuuint64_t strides[1] = {(cuuint64_t)N * 2};
+  const cuuint32_t box[2] = {64, (cuuint32_t)kBM};
+  const cuuint32_t estr[2] = {1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, gate, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 }  // namespace gemm
@@ -317,19 +370,13 @@ extern "C" int32_t plstm_input_gemm(const void* x, int32_t m, int32_t k, const v
   const int m_tiles = (m + gemm::kBM - 1) / gemm::kBM;
   const int grid = std::max(n_tiles_n, std::min(m_tiles * n_tiles_n, (sms / n_tiles_n) * n_tiles_n));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (dtype == PLSTM_BF16) {
-    auto kern = gemm::input_gemm_kernel<true>;
-    PLSTM_TRY_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, lo.total));
-    kern<<<grid, gemm::kThreads, lo.total, s>>>(static_cast<const uint16_t*>(x), m, k,
-                                                static_cast<const uint16_t*>(w_t), n,
-                                                static_cast<uint16_t*>(gate), n_tiles_n, m_tiles);
-  } else {
-    auto kern = gemm::input_gemm_kernel<false>;
-    PLSTM_TRY_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, lo.total));
-    kern<<<grid, gemm::kThreads, lo.total, s>>>(static_cast<const uint16_t*>(x), m, k,
-                                                static_cast<const uint16_t*>(w_t), n,
-                                                static_cast<uint16_t*>(gate), n_tiles_n, m_tiles);
-  }
+  CUtensorMap gmap;
+  std::memset(&gmap, 0, sizeof(gmap));
+  const int use_tma = gemm::make_gate_map(gate, m, n, &gmap) ? 1 : 0;
+  auto kern = dtype == PLSTM_BF16 ? gemm::input_gemm_kernel<true> : gemm::input_gemm_kernel<false>;
+  PLSTM_TRY_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, lo.total));
+  kern<<<grid, gemm::kThreads, lo.total, s>>>(static_cast<const uint16_t*>(x), m, k, static_cast<const uint16_t*>(w_t),
+                                              n, static_cast<uint16_t*>(gate), n_tiles_n, m_tiles, gmap, use_tma);
   PLSTM_TRY_CUDA(cudaGetLastError());
   note_launches(1);
   return PLSTM_OK;

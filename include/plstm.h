@@ -46,6 +46,8 @@ extern "C" {
 #define PLSTM_ETIMEOUT 3   /* a bounded inter-CTA wait gave up (device status) */
 #define PLSTM_ECUDA 4      /* a CUDA runtime call failed */
 #define PLSTM_EWORKSPACE 5 /* workspace smaller than plstm_workspace_size() */
+#define PLSTM_EBOUNDS 6    /* bounds-check build only: an index was outside its buffer (device status; the
+                              detail word is the checking site) */
 
 /* ---- element types ------------------------------------------------------ */
 #define PLSTM_F32 0

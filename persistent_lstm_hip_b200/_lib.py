@@ -12,7 +12,7 @@ import threading
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.environ.get("PLSTM_LIB", os.path.join(HERE, "lib", "libplstm.so"))
 
-OK, EINVAL, ENOTSUP, ETIMEOUT, ECUDA, EWORKSPACE = 0, 1, 2, 3, 4, 5
+OK, EINVAL, ENOTSUP, ETIMEOUT, ECUDA, EWORKSPACE, EBOUNDS = 0, 1, 2, 3, 4, 5, 6
 F32, F16, BF16 = 0, 1, 2
 W_NATIVE, W_TRANSPOSED, W_KPAIR, W_MMAC = 0, 1, 2, 3
 HU_SEQ_MAJOR, HU_WRITE_SEQUENCE = 0x1, 0x2
@@ -28,7 +28,7 @@ FLAG_TEST_DROP = 0x100
 FLAG_TRACE = 0x200
 
 _CODE_NAMES = {EINVAL: "PLSTM_EINVAL", ENOTSUP: "PLSTM_ENOTSUP", ETIMEOUT: "PLSTM_ETIMEOUT",
-               ECUDA: "PLSTM_ECUDA", EWORKSPACE: "PLSTM_EWORKSPACE"}
+               ECUDA: "PLSTM_ECUDA", EWORKSPACE: "PLSTM_EWORKSPACE", EBOUNDS: "PLSTM_EBOUNDS"}
 
 # Every symbol include/plstm.h declares, with its ctypes prototype.
 _P = ctypes.c_void_p

@@ -18,6 +18,8 @@ CSRC = os.path.join(HERE, "csrc")
 LIB_DIR = os.path.join(HERE, "lib")
 OBJ_DIR = os.path.join(HERE, "lib", "obj")
 LIB = os.path.join(LIB_DIR, "libplstm.so")
+OBJ_DIR_BC = os.path.join(HERE, "lib", "obj_bc")
+LIB_BC = os.path.join(LIB_DIR, "libplstm_bc.so")
 SOURCES = ["plstm_abi.cu", "plstm_simt.cu", "plstm_tc.cu", "plstm_tcl.cu", "plstm_gemm.cu", "plstm_misc.cu",
            "plstm_noalloc.cu", "plstm_dedupe.cu"]
 HEADERS = ["plstm_common.cuh", "sm100_ptx.cuh"]
@@ -34,34 +36,41 @@ def _stale(target: str, deps) -> bool:
     return any(os.path.getmtime(d) > t for d in deps)
 
 
-def _compile(src: str, verbose: bool) -> str:
-    obj = os.path.join(OBJ_DIR, os.path.splitext(src)[0] + ".o")
+def _compile(src: str, verbose: bool, bounds_check: bool = False) -> str:
+    obj_dir = OBJ_DIR_BC if bounds_check else OBJ_DIR
+    obj = os.path.join(obj_dir, os.path.splitext(src)[0] + ".o")
     deps = [os.path.join(CSRC, src)] + [os.path.join(CSRC, h) for h in HEADERS] + \
         [os.path.join(ROOT, "include", "plstm.h")]
     if _stale(obj, deps):
-        cmd = [NVCC, *FLAGS, "-c", os.path.join(CSRC, src), "-o", obj]
+        cmd = [NVCC, *FLAGS, *(["-DPLSTM_BOUNDS_CHECK"] if bounds_check else []), "-c", os.path.join(CSRC, src),
+               "-o", obj]
         if verbose:
             print(" ".join(cmd), file=sys.stderr)
         subprocess.run(cmd, check=True)
     return obj
 
 
-def build(force: bool = False, verbose: bool = False) -> str:
-    os.makedirs(OBJ_DIR, exist_ok=True)
+def build(force: bool = False, verbose: bool = False, bounds_check: bool = False) -> str:
+    """Builds lib/libplstm.so, or with bounds_check=True lib/libplstm_bc.so: the same sources
+    compiled with -DPLSTM_BOUNDS_CHECK, whose kernels test the indices of their global, shared
+    and distributed-shared accesses and report PLSTM_EBOUNDS instead of faulting (the tests run
+    small shapes through it)."""
+    obj_dir, lib = (OBJ_DIR_BC, LIB_BC) if bounds_check else (OBJ_DIR, LIB)
+    os.makedirs(obj_dir, exist_ok=True)
     if force:
-        for f in os.listdir(OBJ_DIR):
-            os.remove(os.path.join(OBJ_DIR, f))
+        for f in os.listdir(obj_dir):
+            os.remove(os.path.join(obj_dir, f))
     with cf.ThreadPoolExecutor(max_workers=len(SOURCES)) as ex:
-        objs = list(ex.map(lambda s: _compile(s, verbose), SOURCES))
-    if force or _stale(LIB, objs):
-        cmd = [NVCC, "-shared", "-gencode", "arch=compute_100a,code=sm_100a", "-o", LIB + ".tmp", *objs,
+        objs = list(ex.map(lambda s: _compile(s, verbose, bounds_check), SOURCES))
+    if force or _stale(lib, objs):
+        cmd = [NVCC, "-shared", "-gencode", "arch=compute_100a,code=sm_100a", "-o", lib + ".tmp", *objs,
                "-lcudart"]
         if verbose:
             print(" ".join(cmd), file=sys.stderr)
         subprocess.run(cmd, check=True)
-        os.replace(LIB + ".tmp", LIB)
-    return LIB
+        os.replace(lib + ".tmp", lib)
+    return lib
 
 
 if __name__ == "__main__":
-    print(build(force="--force" in sys.argv, verbose=True))
+    print(build(force="--force" in sys.argv, verbose=True, bounds_check="--bounds-check" in sys.argv))

@@ -135,6 +135,11 @@ int32_t finish(const Problem& p, void* ws, cudaStream_t s) {
   int32_t st = 0, detail = 0;
   const int32_t rc = plstm_read_status(ws, s, &st, &detail);
   if (rc != PLSTM_OK) return rc;
+  if (st == PLSTM_EBOUNDS) {
+    set_error("device status " + std::to_string(st) + " (site " + std::to_string(detail) +
+              "): the bounds-check build found an index outside its buffer");
+    return st;
+  }
   if (st != PLSTM_OK) {
     set_error("device status " + std::to_string(st) + " (cta " + std::to_string(detail >> 16) +
               ", step " + std::to_string(detail & 0xffff) + "): a bounded inter-CTA wait gave up");

@@ -113,6 +113,19 @@ __device__ __forceinline__ void report_status(int* status, int code, int detail)
   if (status != nullptr && atomicCAS(status, 0, code) == 0) status[1] = detail;
 }
 
+// Checked accesses of the bounds-check build (compiled with -DPLSTM_BOUNDS_CHECK, the
+// library lib/libplstm_bc.so): each checked site tests its index against its buffer's
+// extent; a failure records PLSTM_EBOUNDS with the site number as the detail word and the
+// caller skips the access instead of faulting.  In the normal build the test is compiled out.
+#ifdef PLSTM_BOUNDS_CHECK
+__device__ __forceinline__ bool bc_ok(int* status, bool ok, int site) {
+  if (!ok) report_status(status, PLSTM_EBOUNDS, site);
+  return ok;
+}
+#else
+__device__ __forceinline__ bool bc_ok(int*, bool, int) { return true; }
+#endif
+
 // ---- entry points implemented per backend ---------------------------------
 struct Problem {
   int B, T, I, H, L, O;

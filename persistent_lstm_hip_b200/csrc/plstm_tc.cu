@@ -935,6 +935,11 @@ __global__ void __launch_bounds__(Smem2<NH, NSL>::threads(MODE), 1) wavefront2_k
   const int l = rank >> 1, s = rank & 1;
   const int tile = blockIdx.x / ncta;
   const bool last_layer = l == p.L - 1;
+  // Extents the bounds-check build tests indices against (bc_ok; compiled out otherwise).
+  int* const st = p.status;
+  const size_t n_tiles = gridDim.x / ncta;
+  const size_t packed_bytes = packed_total(p.L);
+  const size_t state_elems = (size_t)p.L * p.B * p.hid;
   const bool drain = kHasLinear && last_layer;
   // The Linear head of a slot: split over both last-layer CTAs when half the slot is a legal
   // MMA width, else computed by the CTA of the slot's parity (so the slots' heads are spread
@@ -973,10 +978,10 @@ __global__ void __launch_bounds__(Smem2<NH, NSL>::threads(MODE), 1) wavefront2_k
     ptx::tmem_relinquish();
   }
   for (int i = tid; i < N; i += kThreads) {
-    const int b = p.perm[tile * N + i];
+    const int b = bc_ok(st, (size_t)tile * N + i < n_tiles * N, 1) ? p.perm[tile * N + i] : -1;
     perm_s[i] = b;
     int len = 0;
-    if (b >= 0) len = VARLEN ? min(max(p.lengths[b], 0), p.T) : p.T;
+    if (b >= 0 && bc_ok(st, b < p.B, 2)) len = VARLEN ? min(max(p.lengths[b], 0), p.T) : p.T;
     lens_s[i] = len;
   }
   if (drain) {
@@ -986,7 +991,8 @@ __global__ void __launch_bounds__(Smem2<NH, NSL>::threads(MODE), 1) wavefront2_k
     uint4* dstl = reinterpret_cast<uint4*>(sm + S::kALin);
     for (int i = tid; i < kALinBytes / 16; i += kThreads) {
       const int kb = i / (kATileKB / 16), r = (i / 8) % 128, c = i % 8;
-      dstl[i] = srcl[kb * (kATileKB / 16) + (r & 31) * 8 + c];
+      const size_t si = (size_t)kb * (kATileKB / 16) + (r & 31) * 8 + c;
+      if (bc_ok(st, packed_alin_off(p.L) + 16 * (si + 1) <= packed_bytes, 3)) dstl[i] = srcl[si];
     }
   }
   __syncthreads();  // perm_s / lens_s / tmem slot visible
@@ -996,12 +1002,12 @@ __global__ void __launch_bounds__(Smem2<NH, NSL>::threads(MODE), 1) wavefront2_k
     const int sl = n / NH, nn = n % NH;
     float v = 0.0f;
     const int b = perm_s[n];
-    if (p.h0 != nullptr && b >= 0 && k < p.hid) {
+    if (p.h0 != nullptr && b >= 0 && k < p.hid && bc_ok(st, ((size_t)l * p.B + b) * p.hid + k < state_elems, 4)) {
       const uint16_t* h0 = static_cast<const uint16_t*>(p.h0);
       v = from_bits<BF16>(h0[((size_t)l * p.B + b) * p.hid + k]);
     }
-    *reinterpret_cast<uint16_t*>(sm + S::kB + sl * S::kSlotBytes + (2 + (k >> 6)) * S::kBKB +
-                                 sw128_off(nn, k & 63)) = to_bits<BF16>(v);
+    const uint32_t off = S::kB + sl * S::kSlotBytes + (2 + (k >> 6)) * S::kBKB + sw128_off(nn, k & 63);
+    if (bc_ok(st, off + 2 <= (uint32_t)S::kALin, 5)) *reinterpret_cast<uint16_t*>(sm + off) = to_bits<BF16>(v);
   }
   ptx::fence_proxy_async_smem();
   ptx::tc_fence_after();
@@ -1017,6 +1023,10 @@ __global__ void __launch_bounds__(Smem2<NH, NSL>::threads(MODE), 1) wavefront2_k
 #pragma unroll 1
     for (int c = 0; c < kAK / 2; c += 32) {
       uint32_t r[32];
+      const bool a_in = bc_ok(st, (size_t)rank * kABytes + ((size_t)tau * 128 + row) * kAK * 2 + 16 * (c / 4 + 8) <=
+                                      packed_alin_off(p.L), 6) &&
+                        bc_ok(st, tau * 128 + c + 32 <= S::kTmemCols, 7);
+      if (!a_in) continue;
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const uint4 v = src[c / 4 + i];
@@ -1083,7 +1093,7 @@ __global__ void __launch_bounds__(Smem2<NH, NSL>::threads(MODE), 1) wavefront2_k
       // written (the next iteration), so the warp never waits for its own loads in between.
       auto load_row = [&](int sl, int t, uint32_t (&raw)[16]) {
         const int b = lane < NH ? perm_s[sl * NH + lane] : -1;
-        const bool live = b >= 0 && t < Tt[sl];
+        const bool live = b >= 0 && t < Tt[sl] && bc_ok(st, b < p.B && t < p.T, 8);
         const uint16_t* src = p.x_raw + ((size_t)max(b, 0) * p.T + t) * I;
 #pragma unroll
         for (int k = 0; k < 16; ++k) raw[k] = (live && k < I) ? (uint32_t)__ldg(src + k) : 0u;
@@ -1095,6 +1105,7 @@ __global__ void __launch_bounds__(Smem2<NH, NSL>::threads(MODE), 1) wavefront2_k
       };
       auto write_row = [&](int sl, int b, const uint32_t (&raw)[16]) {
         if (lane >= NH) return;
+        if (!bc_ok(st, (lane >> 3) * 256 + (lane & 7) * 16 + (I > 8 ? 144 : 16) <= 2 * S::kBKB, 9)) return;
         uint8_t* dst = sm + S::kB + sl * S::kSlotBytes + b * S::kBufBytes + (lane >> 3) * 256 + (lane & 7) * 16;
         *reinterpret_cast<uint4*>(dst) = make_uint4(raw[0] | raw[1] << 16, raw[2] | raw[3] << 16,
                                                     raw[4] | raw[5] << 16, raw[6] | raw[7] << 16);
@@ -1177,7 +1188,8 @@ __global__ void __launch_bounds__(Smem2<NH, NSL>::threads(MODE), 1) wavefront2_k
               const int b = perm_s[n];
               if (b < 0) continue;
               const float v = __uint_as_float(r[c][i]) + blin_o;
-              out16[((size_t)b * p.T + (t - 1)) * p.O + o] = to_bits<BF16>(t - 1 < lens_s[n] ? v : 0.0f);
+              if (bc_ok(st, b < p.B && t - 1 < p.T, 10))
+                out16[((size_t)b * p.T + (t - 1)) * p.O + o] = to_bits<BF16>(t - 1 < lens_s[n] ? v : 0.0f);
             }
         }
       }
@@ -1187,7 +1199,8 @@ __global__ void __launch_bounds__(Smem2<NH, NSL>::threads(MODE), 1) wavefront2_k
           const int n = lin_n0 + i;
           const int b = perm_s[n];
           if (b < 0) continue;
-          for (int ts = Tt; ts < p.T; ++ts) out16[((size_t)b * p.T + ts) * p.O + o] = 0;
+          if (bc_ok(st, b < p.B, 10))
+            for (int ts = Tt; ts < p.T; ++ts) out16[((size_t)b * p.T + ts) * p.O + o] = 0;
         }
       }
     }
@@ -1219,6 +1232,11 @@ __global__ void __launch_bounds__(Smem2<NH, NSL>::threads(MODE), 1) wavefront2_k
     const bool tracer = sl == p.trace_slot;
 
     auto x_src = [&](int t) { return p.xp + (((size_t)tile * p.T + t) * N + (size_t)sl * NH) * (size_t)(p.kx * 2); };
+    // The repacked x ends at n_tiles * T * N * kx * 2 bytes.
+    auto x_in = [&](int t) {
+      return bc_ok(st, (((size_t)tile * p.T + t) * N + (size_t)sl * NH) * (size_t)(p.kx * 2) + xbytes <=
+                           n_tiles * p.T * N * (size_t)(p.kx * 2) && xbytes <= 2 * bkb, 11);
+    };
     auto issue_in = [&](int t) {
       const int b = t & 1;
       if (ptx::elect_one()) {
@@ -1291,7 +1309,7 @@ __global__ void __launch_bounds__(Smem2<NH, NSL>::threads(MODE), 1) wavefront2_k
     // (h(t) itself is pushed by the slot's last compute warp to finish the step).
     auto hand_off = [&](int t) {
       const int b = t & 1;
-      if (l == 0 && !x_by_warp && t + 2 < Tt && ptx::elect_one())
+      if (l == 0 && !x_by_warp && t + 2 < Tt && x_in(t + 2) && ptx::elect_one())
         ptx::bulk_g2s(bbuf(sl, b), x_src(t + 2), xbytes, bar(sl, S::kFullIn, b));
       __syncwarp();
     };
@@ -1301,7 +1319,7 @@ __global__ void __launch_bounds__(Smem2<NH, NSL>::threads(MODE), 1) wavefront2_k
       if (ptx::elect_one()) {
         for (int t = 0; t < 2 && t < Tt && !x_by_warp; ++t) {
           ptx::mbar_arrive_expect_tx(bar(sl, S::kFullIn, t), in_bytes);
-          if (l == 0) ptx::bulk_g2s(bbuf(sl, t), x_src(t), xbytes, bar(sl, S::kFullIn, t));
+          if (l == 0 && x_in(t)) ptx::bulk_g2s(bbuf(sl, t), x_src(t), xbytes, bar(sl, S::kFullIn, t));
         }
         for (int t = 1; t <= 2; ++t)
           if (t < Tt || (does_linear && t == Tt)) ptx::mbar_arrive_expect_tx(bar(sl, S::kFullRec, t & 1), bkb);
@@ -1418,7 +1436,7 @@ __global__ void __launch_bounds__(Smem2<NH, NSL>::threads(MODE), 1) wavefront2_k
           const int b = bidx[jc][e];
           uint16_t hv = 0;
           float cv = 0.0f;
-          if (b >= 0 && p.h0 != nullptr && u < p.hid) {
+          if (b >= 0 && p.h0 != nullptr && u < p.hid && bc_ok(st, ((size_t)l * p.B + b) * p.hid + u < state_elems, 12)) {
             hv = static_cast<const uint16_t*>(p.h0)[((size_t)l * p.B + b) * p.hid + u];
             cv = from_bits<BF16>(static_cast<const uint16_t*>(p.c0)[((size_t)l * p.B + b) * p.hid + u]);
           }
@@ -1434,7 +1452,9 @@ __global__ void __launch_bounds__(Smem2<NH, NSL>::threads(MODE), 1) wavefront2_k
 #pragma unroll
       for (int tau = 0; tau < 2; ++tau)
 #pragma unroll
-        for (int g = 0; g < 4; ++g) bz[tau][g] = bias_img[tau * 128 + 32 * q + 8 * g + j8];
+        for (int g = 0; g < 4; ++g)
+          bz[tau][g] = bc_ok(st, rank * 256 + tau * 128 + 32 * q + 8 * g + j8 < ncta * 256, 13)
+                           ? bias_img[tau * 128 + 32 * q + 8 * g + j8] : 0.0f;
     }
     const float* blin = reinterpret_cast<const float*>(p.packed + packed_blin_off(p.L));
     const bool lin_warp = does_linear && q == 0;
@@ -1463,7 +1483,7 @@ __global__ void __launch_bounds__(Smem2<NH, NSL>::threads(MODE), 1) wavefront2_k
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           const int b = perm_s[lin_n0 + 8 * c + i];
-          if (b >= 0) out16[(size_t)b * p.O + o] = to_bits<BF16>(__uint_as_float(r[c][i]) + blin_o);
+          if (b >= 0 && bc_ok(st, b < p.B, 14)) out16[(size_t)b * p.O + o] = to_bits<BF16>(__uint_as_float(r[c][i]) + blin_o);
         }
     };
 
@@ -1519,7 +1539,8 @@ __global__ void __launch_bounds__(Smem2<NH, NSL>::threads(MODE), 1) wavefront2_k
           for (int jc = 0; jc < CPW; ++jc)
 #pragma unroll
             for (int e = 0; e < 2; ++e)
-              *reinterpret_cast<uint16_t*>(dst + sw128_off(8 * jc + cpair + e, ul)) = hw[tau][jc][e];
+              if (bc_ok(st, (uint32_t)(dst - sm) + sw128_off(8 * jc + cpair + e, ul) + 2 <= (uint32_t)S::kALin, 15))
+                *reinterpret_cast<uint16_t*>(dst + sw128_off(8 * jc + cpair + e, ul)) = hw[tau][jc][e];
         }
         ptx::fence_proxy_async_smem();
         if (tracer && q == 0 && lane == 0) trace_mark(p, rank, t, 6);
@@ -1538,7 +1559,8 @@ __global__ void __launch_bounds__(Smem2<NH, NSL>::threads(MODE), 1) wavefront2_k
             if (MODE == kModeSeq && does_linear && t >= 1 &&
                 !wait_phase(bar(sl, S::kLin, lin_buf(t)), lin_phase(t), abort_flag, p.timeout_ns)) {
               raise_abort(p, sm + S::kAbort, ncta, t);
-            } else {
+            } else if (bc_ok(st, (uint32_t)(b ^ 1) * S::kBufBytes + sl * S::kSlotBytes + (3 + s) * S::kBKB <=
+                                     (uint32_t)S::kALin, 20)) {
               push_h(bbuf(sl, b ^ 1) + (uint32_t)((2 + s) * S::kBKB), S::kBKB, rank, to_sibling,
                      bar(sl, S::kFullRec, b ^ 1), l + 1 < p.L, 2 * (l + 1), bbuf(sl, b) + (uint32_t)(s * S::kBKB),
                      bar(sl, S::kFullIn, b));
@@ -1555,7 +1577,7 @@ __global__ void __launch_bounds__(Smem2<NH, NSL>::threads(MODE), 1) wavefront2_k
             for (int jc = 0; jc < CPW; ++jc)
 #pragma unroll
               for (int e = 0; e < 2; ++e)
-                if (bidx[jc][e] >= 0 && 64 * s + ul < p.hid)
+                if (bidx[jc][e] >= 0 && 64 * s + ul < p.hid && bc_ok(st, bidx[jc][e] < p.B, 16))
                   out16[((size_t)bidx[jc][e] * p.T + t) * p.hid + 64 * s + ul] =
                       (!VARLEN || t < len_c[jc][e]) ? hw[tau][jc][e] : (uint16_t)0;
           }
@@ -1578,7 +1600,7 @@ __global__ void __launch_bounds__(Smem2<NH, NSL>::threads(MODE), 1) wavefront2_k
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
               const int bb = bidx[jc][e];
-              if (bb < 0 || u >= p.hid) continue;
+              if (bb < 0 || u >= p.hid || !bc_ok(st, bb < p.B, 16)) continue;
               for (int ts = Tt; ts < p.T; ++ts) out16[((size_t)bb * p.T + ts) * p.hid + u] = 0;
             }
         }
@@ -1594,6 +1616,7 @@ __global__ void __launch_bounds__(Smem2<NH, NSL>::threads(MODE), 1) wavefront2_k
             const int bb = bidx[jc][e];
             if (bb < 0 || u >= p.hid) continue;
             const size_t idx = ((size_t)l * p.B + bb) * p.hid + u;
+            if (!bc_ok(st, idx < state_elems, 17)) continue;
             if (p.h_n != nullptr) static_cast<uint16_t*>(p.h_n)[idx] = h_st[tau][jc][e];
             if (p.c_n != nullptr) {
               if (p.flags & PLSTM_FLAG_CN_F32)

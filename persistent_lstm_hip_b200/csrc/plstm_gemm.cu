@@ -120,7 +120,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                       uint16_t* __restrict__ gate, int n_tiles_n, int m_tiles, const __grid_constant__ CUtensorMap gmap,
                       int use_tma) {
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sm = ptx::smem_align1024(smem_raw);
   const uint32_t sbase = ptx::smem_u32(sm);
   const Layout lo = layout_for(K);
   const int kp = lo.kp;

@@ -362,7 +362,7 @@ __global__ void __launch_bounds__(Smem<N>::kThreads, 1) wavefront_kernel(const P
   constexpr int NL = S::kNL;
   constexpr bool kHasLinear = MODE != kModeHSeq;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sm = ptx::smem_align1024(smem_raw);
   const uint32_t sbase = ptx::smem_u32(sm);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -694,19 +694,29 @@ __global__ void __launch_bounds__(Smem<N>::kThreads, 1) wavefront_kernel(const P
     // semantics and would wait for global stores issued before it to complete.
     auto write_linear = [&](int ts, const uint32_t (&r)[kLinChunks][8], bool last_mode) {
       if (o >= p.O) return;
+      // Two columns rounded to 16 bits per instruction (the single-value conversion issues on
+      // the pipe the gate math's tanh runs on).
 #pragma unroll
       for (int c = 0; c < kLinChunks; ++c)
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
+        for (int i = 0; i < 8; i += 2) {
           const int n = lin_n0 + 8 * c + i;
-          const int b = perm_s[n];
-          if (b < 0) continue;
-          const float v = __uint_as_float(r[c][i]) + blin_o;
-          if (last_mode) {
-            out16[(size_t)b * p.O + o] = to_bits<BF16>(v);
-          } else {
-            const bool live = ts < lens_s[n];
-            out16[((size_t)b * p.T + ts) * p.O + o] = to_bits<BF16>(live ? v : 0.0f);
+          float v[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            v[e] = __uint_as_float(r[c][i + e]) + blin_o;
+            if (!last_mode && ts >= lens_s[n + e]) v[e] = 0.0f;
+          }
+          const uint32_t bits = pack2_bits<BF16>(v[0], v[1]);
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int b = perm_s[n + e];
+            if (b < 0) continue;
+            const uint16_t hb = (uint16_t)(e == 0 ? bits & 0xffffu : bits >> 16);
+            if (last_mode)
+              out16[(size_t)b * p.O + o] = hb;
+            else
+              out16[((size_t)b * p.T + ts) * p.O + o] = hb;
           }
         }
     };
@@ -875,10 +885,11 @@ __global__ void __launch_bounds__(Smem<N>::kThreads, 1) wavefront_kernel(const P
 // Each slot's gate accumulator is single-buffered (TMEM holds A + 2 slots x 2 tiles x
 // NH columns + the Linear tiles): the next step's input MMAs wait until the compute
 // warps have loaded the current accumulator ("dfree").  With [B][T][O] output the
-// Linear head's MMAs have their own commit barrier and a double-buffered accumulator,
-// read by one output warp per slot (warps 10 / 11, TMEM lane quadrants 2 / 3, where
-// the head's rows are replicated), so neither the gate math nor the global stores of
-// the outputs sit on the recurrence's critical path.
+// Linear head's MMAs have their own commit barrier and a double-buffered accumulator;
+// each slot's head runs whole on the last-layer CTA of the slot's parity and is read by
+// that CTA's output warp (the head's rows are replicated into every TMEM lane quadrant),
+// so neither the gate math nor the global stores of the outputs sit on the recurrence's
+// critical path.
 template <int NH, int NSL = 2>
 struct Smem2 {
   static constexpr int kBKB = NH * 128;             // one 64-wide K block of a slot's B operand
@@ -893,19 +904,32 @@ struct Smem2 {
   static constexpr int kBarSlot = 128;
   static constexpr int kTmemSlot = kBar + NSL * kBarSlot, kAbort = kTmemSlot + 4, kDone = kTmemSlot + 8;
   static constexpr int kPerm = kTmemSlot + 64, kLens = kPerm + 4 * NSL * NH;
-  static constexpr int kEnd = kLens + 4 * NSL * NH;
+  // [B][T][O] mode: one step's Linear outputs of an output warp's slot, [row][o] 16-bit with a
+  // 64-byte row pitch (O <= 32), staged for 16-byte global stores.
+  static constexpr int kOutPitch = 64;
+  static constexpr int kOutStage = kLens + 4 * NSL * NH;
+  static constexpr int kEnd = kOutStage + ((NSL + 1) / 2) * NH * kOutPitch;
   static constexpr int kDynBytes = kEnd + 1024;  // + alignment slack
   static constexpr int CPW = NH / 8;               // 8-column chunks per compute warp (all NH columns)
   static constexpr int kSlotWarps = 4;             // compute warps per slot: one per TMEM lane quadrant
   static constexpr int kComputeWarps = NSL * kSlotWarps;
   static constexpr int kOutWarp0 = kComputeWarps + NSL;  // after one control warp per slot
-  // + one output warp per slot in [B][T][O] mode (the only mode in which they work, and only in
-  // the last layer), else one warp for x: the layer-0 x warp reads x[B][T][I] into the input tiles
-  // (in [B][T][O] mode the last output warp takes that role in a layer 0 that is not the last).
-  static constexpr int xwarp(int mode) { return kOutWarp0 + (mode == kModeSeq ? NSL - 1 : 0); }
-  static constexpr int threads(int mode) { return (kOutWarp0 + (mode == kModeSeq ? NSL : 1)) * 32; }
-  static constexpr bool kSplitLinear = (NH / 2) % 16 == 0;
-  static constexpr int kNL = kSplitLinear ? NH / 2 : NH;
+  // + one more warp: in [B][T][O] mode a last-layer CTA's output warp (it stores the Linear outputs
+  // of the slots s, s + 2, ... whose heads the CTA computes), in layer 0 the x warp, which reads
+  // x[B][T][I] into the input tiles (a layer 0 that is also the last layer in [B][T][O] mode takes
+  // the repacked x instead).
+  static constexpr int xwarp(int) { return kOutWarp0; }
+  static constexpr int threads(int mode) { return (kOutWarp0 + (mode == kModeSeq ? kOutWarps : 1)) * 32; }
+  // The Linear head of a slot runs whole on the last-layer CTA of the slot's parity (kSplitLinear
+  // false; splitting a 32-row slot's head over both CTAs gave each CTA's output warp two slots).
+  static constexpr bool kSplitLinear = false;
+  static constexpr int kNL = NH;
+  // [B][T][O] mode: output warps per CTA, each storing the heads of kOutSlotsPerWarp of the
+  // ceil(NSL / 2) slots the CTA owns the heads of.  One warp for all: a second one would take the
+  // three-slot block past 16 warps and cap its registers at 96, which slows every layer's gate math
+  // more than the output warp's work costs.
+  static constexpr int kOutSlotsPerWarp = (NSL + 1) / 2;
+  static constexpr int kOutWarps = (NSL + 1) / 2 / kOutSlotsPerWarp;
   static constexpr int kD = kTmemACols;            // D[slot][tau] at kD + (2 slot + tau) NH
   static constexpr int kDLin = kD + 2 * NSL * NH;  // D_lin[slot][buffer] at kDLin + (2 slot + buffer) NL
   static constexpr int kTmemCols = tmem_cols_for(kDLin + 2 * NSL * kNL);
@@ -926,7 +950,7 @@ __global__ void __launch_bounds__(Smem2<NH, NSL>::threads(MODE), 1) wavefront2_k
   // The launch of the tile height not chosen ends here, before any barrier, TMEM or cluster traffic.
   if (p.choice != nullptr && *p.choice != N) return;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sm = ptx::smem_align1024(smem_raw);
   const uint32_t sbase = ptx::smem_u32(sm);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -1153,54 +1177,132 @@ __global__ void __launch_bounds__(Smem2<NH, NSL>::threads(MODE), 1) wavefront2_k
     }
   } else if (warp >= S::kOutWarp0) {
     // ============================ output warps ===========================
-    // [B][T][O] mode: the Linear outputs of every step, read from the slot's Linear
-    // accumulator in this warp's lane quadrant and stored, off the critical path.
-    const int sl = warp - S::kOutWarp0;
-    const bool does_linear = does_lin(sl);
-    bool active = false;
-    const int Tt = slot_len(sl, &active);
-    if (MODE == kModeSeq && does_linear && active) {
+    // [B][T][O] mode: the output warp of a last-layer CTA stores the Linear outputs of every step
+    // of the slots whose heads this CTA computes, read from each slot's Linear accumulator in this
+    // warp's lane quadrant (the head's rows are replicated into all four), off the critical path.
+    if (MODE == kModeSeq) {
       const int o = lane;
       const float blin_o = o < p.O ? reinterpret_cast<const float*>(p.packed + packed_blin_off(p.L))[o] : 0.0f;
       uint16_t* out16 = static_cast<uint16_t*>(p.out);
-      const int lin_n0 = sl * NH + (S::kSplitLinear ? s * NL : 0);
       const uint32_t qlane = (uint32_t)(32 * (warp & 3)) << 16;
-      for (int t = 1; t <= Tt; ++t) {
-        if (*abort_flag) break;
-        if (!wait_phase(bar(sl, S::kLin, lin_buf(t)), lin_phase(t), abort_flag, p.timeout_ns)) {
-          if (lane == 0) raise_abort(p, sm + S::kAbort, ncta, t);
-          break;
-        }
-        ptx::tc_fence_after();
-        uint32_t r[NL / 8][8];
+      // A step's outputs go out as few wide stores: each row's O values are staged in shared
+      // memory and copied in chunks of cb bytes (16 when O % 8 == 0), one chunk per lane, with the
+      // chunks' addresses worked out once.  (A 2-byte store per row and lane cost ~130 cycles a
+      // row, longer than a step for 32 rows.)
+      const uintptr_t oaddr = reinterpret_cast<uintptr_t>(p.out);
+      const int cb = (p.O % 8 == 0 && oaddr % 16 == 0) ? 16
+                     : (p.O % 4 == 0 && oaddr % 8 == 0) ? 8
+                     : (p.O % 2 == 0 && oaddr % 4 == 0) ? 4 : 2;
+      const int cpr = 2 * p.O / cb;  // chunks per row
+      const int nchunks = NL * cpr;
+      constexpr int kPer = S::kOutSlotsPerWarp;
+      constexpr int kPlan = 4;  // chunks per lane with precomputed addresses (the rest: per step)
+      const size_t row_bytes = (size_t)p.T * p.O * 2;
+      auto copy_chunk = [&](uint32_t src, uint8_t* dst) {
+        if (cb == 16)
+          *reinterpret_cast<uint4*>(dst) = ptx::ld_shared_v4(src);
+        else if (cb == 8)
+          *reinterpret_cast<uint2*>(dst) = ptx::ld_shared_v2(src);
+        else if (cb == 4)
+          *reinterpret_cast<uint32_t*>(dst) = ptx::ld_shared_u32(src);
+        else
+          *reinterpret_cast<uint16_t*>(dst) = ptx::ld_shared_u16(src);
+      };
+      // The slots this warp stores: sl = s + 2 (w kPer + k) for output warp w; lane i holds the
+      // batch row and length of head column i of each.
+      // A slot whose rows all have length 0 has Tts 0 but still owns rows (written as zeros).
+      int sls[kPer], Tts[kPer], my_b[kPer], my_len[kPer];
+      bool owns[kPer];
+      uint32_t stage[kPer], ch_src[kPer][kPlan];
+      long long ch_dst[kPer][kPlan];  // byte offset of the chunk in out at t = 0, or -1
+      int Tmax = 0;
 #pragma unroll
-        for (int c = 0; c < NL / 8; ++c) ptx::tmem_ld_32x32b_x8(dlin_at(sl, t) + qlane + (uint32_t)(8 * c), r[c]);
-        ptx::tmem_wait_ld();
-        ptx::tc_fence_before();
-        __syncwarp();
-        if (lane == 0) ptx::mbar_arrive(bar(sl, S::kLinFree, lin_buf(t)));
-        if (o < p.O) {
+      for (int k = 0; k < kPer; ++k) {
+        sls[k] = s + 2 * ((warp - S::kOutWarp0) * kPer + k);
+        bool active = false;
+        Tts[k] = (sls[k] < NSL && does_lin(sls[k])) ? slot_len(sls[k], &active) : 0;
+        owns[k] = sls[k] < NSL && does_lin(sls[k]) && active;
+        if (!owns[k]) Tts[k] = 0;
+        Tmax = max(Tmax, Tts[k]);
+        const int lin_n0 = min(sls[k], NSL - 1) * NH;
+        my_b[k] = (owns[k] && lane < NL) ? perm_s[lin_n0 + lane] : -1;
+        my_len[k] = (owns[k] && lane < NL) ? lens_s[lin_n0 + lane] : 0;
+        stage[k] = sbase + (uint32_t)(S::kOutStage + ((warp - S::kOutWarp0) * kPer + k) * NH * S::kOutPitch);
+#pragma unroll
+        for (int it = 0; it < kPlan; ++it) {
+          const int jj = 32 * it + lane;
+          const int n = jj < nchunks ? jj / cpr : 0;
+          const int b = __shfl_sync(0xffffffffu, my_b[k], n);
+          const int kc = jj - n * cpr;
+          ch_src[k][it] = stage[k] + (uint32_t)(n * S::kOutPitch + kc * cb);
+          ch_dst[k][it] = (jj < nchunks && b >= 0 && bc_ok(st, b < p.B, 10)) ? (long long)b * row_bytes + kc * cb : -1;
+        }
+      }
+      bool ok = true;
+      for (int t = 1; ok && t <= Tmax; ++t) {
+#pragma unroll
+        for (int k = 0; k < kPer; ++k) {
+          if (t > Tts[k]) continue;
+          const int sl = sls[k];
+          if (!wait_phase(bar(sl, S::kLin, lin_buf(t)), lin_phase(t), abort_flag, p.timeout_ns)) {
+            if (lane == 0 && !*abort_flag) raise_abort(p, sm + S::kAbort, ncta, t);
+            ok = false;
+            break;
+          }
+          ptx::tc_fence_after();
+          uint32_t r[NL / 8][8];
+#pragma unroll
+          for (int c = 0; c < NL / 8; ++c) ptx::tmem_ld_32x32b_x8(dlin_at(sl, t) + qlane + (uint32_t)(8 * c), r[c]);
+          ptx::tmem_wait_ld();
+#pragma unroll
+          for (int c = 0; c < NL / 8; ++c) reg_after_wait<8>(r[c]);
+          ptx::tc_fence_before();
+          __syncwarp();
+          // Relaxed: a release arrive would first wait for the previous step's output stores.
+          if (lane == 0) ptx::mbar_arrive_relaxed(bar(sl, S::kLinFree, lin_buf(t)));
+          const uint32_t live = __ballot_sync(0xffffffffu, t - 1 < my_len[k]);  // bit n: row n not finished
+          // Two rows rounded to 16 bits per instruction (the single-value conversion issues on
+          // the pipe the gate math's tanh runs on, and this warp shares schedulers with it).
 #pragma unroll
           for (int c = 0; c < NL / 8; ++c)
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              const int n = lin_n0 + 8 * c + i;
-              const int b = perm_s[n];
-              if (b < 0) continue;
-              const float v = __uint_as_float(r[c][i]) + blin_o;
-              if (bc_ok(st, b < p.B && t - 1 < p.T, 10))
-                out16[((size_t)b * p.T + (t - 1)) * p.O + o] = to_bits<BF16>(t - 1 < lens_s[n] ? v : 0.0f);
+            for (int i = 0; i < 8; i += 2) {
+              float v[2];
+#pragma unroll
+              for (int e = 0; e < 2; ++e)
+                v[e] = (live >> (8 * c + i + e)) & 1u ? __uint_as_float(r[c][i + e]) + blin_o : 0.0f;
+              const uint32_t bits = pack2_bits<BF16>(v[0], v[1]);
+              if (o < p.O) {
+                const uint32_t row = stage[k] + (uint32_t)((8 * c + i) * S::kOutPitch + 2 * o);
+                ptx::st_shared_u16(row, (uint16_t)(bits & 0xffffu));
+                ptx::st_shared_u16(row + S::kOutPitch, (uint16_t)(bits >> 16));
+              }
             }
+          __syncwarp();
+          uint8_t* const out_t = reinterpret_cast<uint8_t*>(p.out) + (size_t)(t - 1) * p.O * 2;
+#pragma unroll
+          for (int it = 0; it < kPlan; ++it)
+            if (ch_dst[k][it] >= 0) copy_chunk(ch_src[k][it], out_t + ch_dst[k][it]);
+          for (int j0 = 32 * kPlan; j0 < nchunks; j0 += 32) {  // wide plans only (cb < 16)
+            const int jj = j0 + lane;
+            const int n = jj < nchunks ? jj / cpr : 0, kc = jj - n * cpr;
+            const int b = __shfl_sync(0xffffffffu, my_b[k], n);
+            if (jj < nchunks && b >= 0 && bc_ok(st, b < p.B, 10))
+              copy_chunk(stage[k] + (uint32_t)(n * S::kOutPitch + kc * cb), out_t + (size_t)b * row_bytes + kc * cb);
+          }
+          __syncwarp();  // the stage is rewritten next step
         }
       }
-      // Outputs past the slot's last step are zero.
-      if (o < p.O && !*abort_flag) {
-        for (int i = 0; i < NL; ++i) {
-          const int n = lin_n0 + i;
-          const int b = perm_s[n];
-          if (b < 0) continue;
-          if (bc_ok(st, b < p.B, 10))
-            for (int ts = Tt; ts < p.T; ++ts) out16[((size_t)b * p.T + ts) * p.O + o] = 0;
+      // Outputs past each slot's last step are zero.
+      if (ok && !*abort_flag) {
+#pragma unroll
+        for (int k = 0; k < kPer; ++k) {
+          if (!owns[k]) continue;
+          for (int i = 0; i < NL; ++i) {
+            const int b = __shfl_sync(0xffffffffu, my_b[k], i);
+            if (o < p.O && b >= 0 && bc_ok(st, b < p.B, 10))
+              for (int ts = Tts[k]; ts < p.T; ++ts) out16[((size_t)b * p.T + ts) * p.O + o] = 0;
+          }
         }
       }
     }
@@ -1278,25 +1380,30 @@ __global__ void __launch_bounds__(Smem2<NH, NSL>::threads(MODE), 1) wavefront2_k
       }
       __syncwarp();
     };
-    // Commits the step's gate MMAs, then issues and commits the Linear MMAs on h_{t-1}
-    // (behind the gate MMAs in the tensor pipe, tracked by their own barrier).
-    auto issue_lin_commit = [&](int t, bool lin) {
+    // Commits the step's gate MMAs.
+    auto commit_gates = [&](int t) {
+      if (ptx::elect_one()) {
+        ptx::tc_fence_after();
+        ptx::mma_commit(bar(sl, S::kMma, t & 1));
+      }
+      __syncwarp();
+    };
+    // Issues and commits the Linear MMAs on h_{t-1} (behind the gate MMAs in the tensor pipe,
+    // tracked by their own barrier).
+    auto issue_linear = [&](int t) {
       const int b = t & 1;
       if (ptx::elect_one()) {
         ptx::tc_fence_after();
-        ptx::mma_commit(bar(sl, S::kMma, b));
-        if (lin) {
-          const uint64_t dB = dB0 + kBufStep * b;
-          const uint32_t dlin = dlin_at(sl, t);
+        const uint64_t dB = dB0 + kBufStep * b;
+        const uint32_t dlin = dlin_at(sl, t);
 #pragma unroll
-          for (int kb = 0; kb < 2; ++kb)
+        for (int kb = 0; kb < 2; ++kb)
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-              ptx::mma_f16_ss(dlin, dAl + (uint64_t)((kb * kATileKB + kk * 32) >> 4),
-                              dB + (uint64_t)(((2 + kb) * S::kBKB + lin_row_off + kk * 32) >> 4), idesc_l,
-                              (kb | kk) != 0 ? 1u : 0u);
-          ptx::mma_commit(bar(sl, S::kLin, lin_buf(t)));
-        }
+          for (int kk = 0; kk < 4; ++kk)
+            ptx::mma_f16_ss(dlin, dAl + (uint64_t)((kb * kATileKB + kk * 32) >> 4),
+                            dB + (uint64_t)(((2 + kb) * S::kBKB + lin_row_off + kk * 32) >> 4), idesc_l,
+                            (kb | kk) != 0 ? 1u : 0u);
+        ptx::mma_commit(bar(sl, S::kLin, lin_buf(t)));
       }
       __syncwarp();
     };
@@ -1351,15 +1458,17 @@ __global__ void __launch_bounds__(Smem2<NH, NSL>::threads(MODE), 1) wavefront2_k
         }
         if (tracer && lane == 0) trace_mark(p, rank, t, 0);
         if (gates) issue_rec_half(t, 1 - s);
-        // The output warp must have read the Linear accumulator buffer this step reuses.
+        commit_gates(t);
+        last_commit = t;
+        // The output warp must have read the Linear accumulator buffer this step reuses (the gate
+        // MMAs are committed first, so that the compute warps never wait for the output warp).
         if (MODE == kModeSeq && lin && t >= 3 &&
             !warp_wait_phase(bar(sl, S::kLinFree, lin_buf(t)), (uint32_t)((t - 3) >> 1) & 1u, abort_flag,
                              p.timeout_ns)) {
           fail(t);
           break;
         }
-        issue_lin_commit(t, lin);
-        last_commit = t;
+        if (lin) issue_linear(t);
         if (lin) last_lin = t;
         if (tracer && lane == 0) trace_mark(p, rank, t, 1);
         if (!gates) break;  // drain step issued
@@ -1408,9 +1517,23 @@ __global__ void __launch_bounds__(Smem2<NH, NSL>::threads(MODE), 1) wavefront2_k
     const bool does_linear = does_lin(sl), sibling_linear = sibling_lin(sl);
     bool active = false, other_active = false;
     const int Tt = slot_len(sl, &active);
-    // The slot whose gate math precedes this one's on the MUFU pipes (round robin).
-    const int prev_sl = (sl + NSL - 1) % NSL;
-    const int T_other = slot_len(prev_sl, &other_active);
+    // The slot whose gate math precedes this one's on the MUFU pipes: the nearest active slot
+    // before it in the ring.  Skipping inactive slots keeps the ring closed, which bounds how far
+    // one slot can run ahead of the next: with an open ring (slot 2 of a partial tile empty) slot
+    // 0 could finish step t + 2 before slot 1 polled the parity of step t, and that poll would
+    // then wait for step t + 4.  (Rings that open when a slot finishes early are why three-slot
+    // tiles take uniform lengths only.)
+    int prev_sl = sl;
+    for (int k = 1; k < NSL; ++k) {
+      const int c = (sl + NSL - k) % NSL;
+      bool a = false;
+      slot_len(c, &a);
+      if (a) {
+        prev_sl = c;
+        break;
+      }
+    }
+    const int T_other = prev_sl != sl ? slot_len(prev_sl, &other_active) : 0;
     const int j8 = lane >> 2;          // unit within the quadrant's group of 8
     const int cpair = (lane & 3) * 2;  // first of the two batch columns in a chunk
     const bool tracer = sl == p.trace_slot;
@@ -1518,11 +1641,12 @@ __global__ void __launch_bounds__(Smem2<NH, NSL>::threads(MODE), 1) wavefront2_k
             break;
           }
         }
-        // The slots take turns on the MUFU pipes: slot sl > 0 runs its gate math after
-        // slot sl - 1's of the same step, slot 0 after the last slot's previous step, so
-        // that one slot's MMA / hand-off latency overlaps the others' gate math.
+        // The slots take turns on the MUFU pipes: a slot runs its gate math after that of
+        // the preceding active slot's same step (its previous step if that slot comes later
+        // in the ring, i.e. for the first active slot), so that one slot's MMA / hand-off
+        // latency overlaps the others' gate math.
         {
-          const int tt = sl > 0 ? t : t - 1;
+          const int tt = prev_sl < sl ? t : t - 1;
           if (other_active && tt >= 0 && tt < T_other &&
               !wait_phase(bar(prev_sl, S::kHReady, tt & 1), (tt >> 1) & 1, abort_flag, p.timeout_ns)) {
             if (lane == 0) raise_abort(p, sm + S::kAbort, ncta, t);
@@ -2144,7 +2268,7 @@ __global__ void __launch_bounds__(160, 1) step_probe_kernel(int steps, int varia
   constexpr int CPW = NH / 8;
   constexpr uint32_t kHalf = NH * 128;  // one 64-unit K block of h: NH rows x 128 bytes (128-byte swizzle)
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sm = ptx::smem_align1024(smem_raw);
   const uint32_t sbase = ptx::smem_u32(sm);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int s = (int)ptx::cluster_ctarank();
@@ -2407,7 +2531,7 @@ __global__ void __launch_bounds__(160, 1) step_probe4_kernel(int steps, unsigned
   constexpr uint32_t kPiece = NH * 64;    // 32 units x NH rows, 16-bit
   constexpr uint32_t kBuf = 4 * kPiece;   // one step parity: the four pieces
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sm = ptx::smem_align1024(smem_raw);
   const uint32_t sbase = ptx::smem_u32(sm);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int r = (int)ptx::cluster_ctarank();

@@ -289,7 +289,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) proj_kernel(const GemmArgs a)
   using S = GemmSmem<KP, XIN, NT>;
   PLSTM_TCL_TILE_CONSTANTS(NT);
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sm = ptx::smem_align1024(smem_raw);
   const uint32_t sbase = ptx::smem_u32(sm);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int C = ctas_of(a.H);
@@ -542,7 +542,7 @@ __global__ void __launch_bounds__(RecSmem<H, NCW, NT>::kThreads, 1) rec_kernel(c
   constexpr int CPW = kNT * 4 / (NCW * 8);  // 8-column chunks per compute warp
   static_assert(CPW * NCW * 8 == kNT * 4, "tile rows must split evenly over the compute warps");
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sm = ptx::smem_align1024(smem_raw);
   const uint32_t sbase = ptx::smem_u32(sm);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int r = (int)ptx::cluster_ctarank();

@@ -5,6 +5,7 @@ max |err| <= 1e-4."""
 from __future__ import annotations
 
 import ctypes
+import os
 
 import numpy as np
 import pytest
@@ -533,3 +534,40 @@ def test_tc_small_hidden_varlen_state_bf16(cuda_device):
         assert_close16(out, r_out, "out")
         assert_close16(h_n, r_h, "h_n")
         assert_close16(c_n, r_c, "c_n")
+
+
+def test_every_output_element_written(cuda_device):
+    """[B,T,O], [B,O] and [B,T,H] outputs land in a buffer pre-filled with NaN: every element must
+    be written (zeros past each row's length included), also for a tile slot whose rows all have
+    length 0 and for output widths whose rows are stored in 16-, 8-, 4- and 2-byte pieces."""
+    lib = _lib.load()
+    for (B, T, H, L, O, ntile) in [(40, 9, 128, 2, 24, "32"), (70, 7, 128, 3, 12, "64"), (50, 6, 128, 2, 10, None),
+                                   (33, 5, 96, 2, 7, "64"), (45, 5, 96, 2, 5, "32"), (200, 5, 128, 2, 24, "48")]:
+        m = make_model(5, H, L, O, seed=B)
+        w = weights_of(m, L, torch.float16, cuda_device)
+        x = _rand_x(B, T, 5, torch.float16, cuda_device, seed=B + 1)
+        lens = _rand_lengths(B, T, seed=B + 2, lo=0)
+        lens[B - 20:] = 0  # the last rows (a whole 16-row slot) have length 0
+        varlen = ntile != "48"  # 48-row tiles take uniform lengths only
+        os.environ.pop("PLSTM_TC_NTILE", None)
+        if ntile:
+            os.environ["PLSTM_TC_NTILE"] = ntile
+        try:
+            for mode, shape in (("seq", (B, T, O)), ("last", (B, O)), ("hseq", (B, T, H))):
+                pw = core.PackedWeights(*w, out_mode=mode, backend="tc")
+                d = pw.desc(batch=B, seq_len=T, extra_flags=_lib.FLAG_SYNC_CHECK)
+                nb = ctypes.c_size_t(0)
+                _lib.check(lib.plstm_workspace_size(ctypes.byref(d), ctypes.byref(nb)))
+                ws = torch.zeros(max(int(nb.value), 256), dtype=torch.uint8, device=cuda_device)
+                out = torch.full(shape, float("nan"), dtype=torch.float16, device=cuda_device)
+                ld = lens.to(cuda_device) if varlen else None
+                _lib.check(lib.plstm_forward_packed(ctypes.byref(d), pw.blob.data_ptr(), x.data_ptr(),
+                                                    ld.data_ptr() if ld is not None else None, None, None,
+                                                    out.data_ptr(), None, None, ws.data_ptr(), ws.numel(),
+                                                    torch.cuda.current_stream().cuda_stream))
+                torch.cuda.synchronize()
+                assert not torch.isnan(out).any(), f"{mode} B={B} O={O} ntile={ntile}: unwritten elements"
+                r_out, _, _ = oracle_of(x, *w, lengths=lens if varlen else None, out_mode=mode)
+                assert_close16(out, r_out, f"{mode} B={B} O={O}")
+        finally:
+            os.environ.pop("PLSTM_TC_NTILE", None)

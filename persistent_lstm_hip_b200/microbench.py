@@ -141,9 +141,20 @@ def forward(args) -> dict:
         steps = int(lengths.sum())
         lengths = lengths.to(dev)
     ms = _time(lambda: pw.forward(x, lengths=lengths, need_state=False), args.iters, 2)
+    # The recurrent kernel alone (plstm_profile: CUDA events around its launches, mean).
+    from . import _lib
+    lib = _lib.load()
+    lib.plstm_profile(1)
+    k_ms, n = ctypes.c_float(0), ctypes.c_int32(0)
+    lib.plstm_profile_read(ctypes.byref(k_ms), ctypes.byref(n))
+    for _ in range(args.iters):
+        pw.forward(x, lengths=lengths, need_state=False)
+    torch.cuda.synchronize()
+    lib.plstm_profile_read(ctypes.byref(k_ms), ctypes.byref(n))
+    lib.plstm_profile(0)
     return {"backend": pw.backend, "hidden": args.hidden, "layers": L, "batch": args.batch, "seq": args.seq,
             "input": args.input, "dtype": args.dtype, "out": args.out, "min_len": args.min_len, "ms": ms,
-            "seq_timesteps_per_s": steps / (ms / 1e3)}
+            "kernel_ms": k_ms.value / max(n.value, 1), "seq_timesteps_per_s": steps / (ms / 1e3)}
 
 
 def main() -> None:

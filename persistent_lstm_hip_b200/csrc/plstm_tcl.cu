@@ -32,6 +32,7 @@
 //   3. the Linear head (or the h sequence output) from the last layer's h.
 // Layers run one after the other; every wait in the kernels is bounded.
 #include <algorithm>
+#include <cstdio>
 #include <cstdlib>
 #include <mutex>
 #include <string>
@@ -790,9 +791,7 @@ __global__ void __launch_bounds__(RecSmem<H, NCW, NT>::kThreads, 1) rec_kernel(c
             c_st[jc][e] = cn[e];
             h_st[jc][e] = (uint16_t)(e == 0 ? bits & 0xffffu : bits >> 16);
           }
-          const uint32_t off = hoff<NT>(u, n0 + 8 * jc + cpair + e);
-          *reinterpret_cast<uint16_t*>(dst + off) = h_st[jc][e];
-          if (gdst != nullptr) *reinterpret_cast<uint16_t*>(gdst + off) = h_st[jc][e];
+          *reinterpret_cast<uint16_t*>(dst + hoff<NT>(u, n0 + 8 * jc + cpair + e)) = h_st[jc][e];
         }
       }
       ptx::fence_proxy_async_smem();
@@ -818,6 +817,15 @@ __global__ void __launch_bounds__(RecSmem<H, NCW, NT>::kThreads, 1) rec_kernel(c
           }
           trace_mark(a, tile, r, t, 7);
         }
+      }
+      // The layer's h sequence, after the step's arrivals: a release arrive (and the pusher's
+      // acquire-release counter) would first wait for these global stores to complete.
+      if (gdst != nullptr) {
+#pragma unroll
+        for (int jc = 0; jc < CPW; ++jc)
+#pragma unroll
+          for (int e = 0; e < 2; ++e)
+            *reinterpret_cast<uint16_t*>(gdst + hoff<NT>(u, n0 + 8 * jc + cpair + e)) = h_st[jc][e];
       }
     }
     // Final state of this CTA's units.
@@ -1144,9 +1152,64 @@ int rec_max_clusters(int device, int H, int nt) {
   return n;
 }
 
-// Tile rows of a forward: 32 for H <= 256 when 32-row tiles still fit in one wave of
-// clusters; 80 when 64-row tiles need more clusters than fit at once and 80-row tiles
-// need fewer waves (B = 512 at H = 384..512: 8 tiles of 64 but 7 clusters); else 64.
+// Recurrence CTAs (of both length variants of `dtype`) that one SM holds at once, at most two, by
+// whole-SM registers, shared memory and tensor memory (H / 2 + NT columns, 256 or 512 allocated);
+// cached.  The cluster occupancy query counts one CTA per SM (15 clusters of 8 on a B200), but
+// measured: 32 clusters of 8 CTAs of 32-row H = 256 tiles (f16 and bf16) ran in one wave, two CTAs
+// on most SMs, 2.82 ms per layer at B = 1024 against 2.65 ms at B = 512.
+int rec_ctas_per_sm(int device, int H, int nt, int dtype) {
+  static std::mutex mu;
+  static int cache[64][8][4][2];
+  static bool init = false;
+  std::lock_guard<std::mutex> g(mu);
+  if (!init) {
+    for (auto& a : cache)
+      for (auto& b : a)
+        for (auto& c : b) c[0] = c[1] = -1;
+    init = true;
+  }
+  if (device < 0 || device >= 64 || !rec_hidden_ok(H)) return 0;
+  const bool bf16 = dtype == PLSTM_BF16;
+  int& slot = cache[device][H / 64 - 1][nt == 80 ? 1 : nt == 32 ? 2 : nt == 48 ? 3 : 0][bf16 ? 1 : 0];
+  if (slot >= 0) return slot;
+  int smem_sm = 0;
+  int n = (H / 2 + nt <= 256) ? 2 : 1;
+  if (cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, device) != cudaSuccess) n = 1;
+  else n = std::min(n, smem_sm / (rec_smem(H, nt) + 1024));
+  for (bool varlen : {false, true}) {
+    cudaFuncAttributes fa = {};
+    if (cudaFuncGetAttributes(&fa, pick_rec(H, bf16, varlen, nt)) != cudaSuccess) {
+      n = 1;
+      continue;
+    }
+    const int regs = (fa.numRegs + 7) / 8 * 8;
+    n = std::min(n, 65536 / std::max(1, regs * rec_threads(H, nt)));
+  }
+  cudaGetLastError();
+  slot = std::max(n, 1);
+  return slot;
+}
+
+// Clusters of the recurrence that run at once: the occupancy query's count where one CTA fits an
+// SM; with two, 7/8 of the SMs' CTA slots in whole clusters (a cluster must fit one GPC; 32
+// clusters of 8 ran in one wave on 148 SMs), at least twice the query's count.
+int rec_resident_clusters(int device, int H, int nt, int dtype) {
+  const int m = rec_max_clusters(device, H, nt);
+  const int k = rec_ctas_per_sm(device, H, nt, dtype);
+  if (m < 1 || k < 2) return m;
+  int sms = 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) {
+    cudaGetLastError();
+    return m;
+  }
+  return std::max(k * m, sms * k * 7 / (8 * ctas_of(H)));
+}
+
+// Tile rows of a forward: 32 or 48 for H <= 256 when those tiles still fit in one wave of
+// clusters (32 first: at B = 512, H = 256 its 16 clusters run at once, 2.65 ms per layer
+// against 2.86 ms with 11 clusters of 48 rows); 80 when 64-row tiles need more clusters than fit
+// at once and 80-row tiles need fewer waves (B = 512 at H = 384..512: 8 tiles of 64 but 7
+// clusters); else 64.
 // PLSTM_TCL_NT=32|48|64|80 forces a tile height the hidden size has (tests, diagnostics).
 int choose_nt(const Problem& q) {
   if (const char* e = std::getenv("PLSTM_TCL_NT")) {
@@ -1156,7 +1219,7 @@ int choose_nt(const Problem& q) {
   }
   if (rec_nt32(q.H)) {
     for (int nt : {32, 48}) {
-      const int m = rec_max_clusters(q.device, q.H, nt);
+      const int m = rec_resident_clusters(q.device, q.H, nt, q.dtype);
       if (m >= 1 && (q.B + nt - 1) / nt <= m) return nt;
     }
     return 64;
@@ -1425,6 +1488,11 @@ int32_t tcl_forward(const Problem& p, const void* packed, const void* x, const i
   const int H = tcl_hp(p.H), L = p.L, C = ctas_of(H);
   const int nt = choose_nt(padded(p));
   const int tiles = (p.B + nt - 1) / nt;
+  if (const char* dbg = std::getenv("PLSTM_TC_DEBUG"))
+    if (std::atoi(dbg) != 0)
+      std::fprintf(stderr, "plstm tcl: H %d, %d-row tiles, %d tiles; clusters of %d CTAs at once (32/48/64 rows): %d/%d/%d\n",
+                   H, nt, tiles, C, rec_resident_clusters(p.device, H, 32, p.dtype),
+                   rec_resident_clusters(p.device, H, 48, p.dtype), rec_resident_clusters(p.device, H, 64, p.dtype));
   const Ws w = ws_layout(padded(p), nt);
   uint8_t* wsb = static_cast<uint8_t*>(ws);
   const uint8_t* pk = static_cast<const uint8_t*>(packed);

@@ -491,10 +491,14 @@ struct RecSmem {
   static constexpr int kEnd = kLens + 4 * NT;
   static constexpr int kDyn = kEnd + 1024;
   static constexpr int kComputeWarps = NCW;  // NCW / 4 per TMEM lane quadrant, 256 / NCW columns each
-  static constexpr int kThreads = (kComputeWarps + 1) * 32;
+  // + the control warp (own-piece MMAs and the first half of the peer-piece MMAs) + the helper
+  // warp (the second half, into its own accumulator).
+  static constexpr int kThreads = (kComputeWarps + 2) * 32;
   static constexpr int kACols = H / 2;  // W_hh slice: 128 lanes x H 16-bit values
   static constexpr int kD = kACols;     // gate accumulator [128 x NT] (single buffer)
-  static constexpr int kTmemCols = kACols + NT <= 256 ? 256 : 512;
+  static constexpr int kD1 = kD + NT;   // the helper warp's partial accumulator [128 x NT]
+  static constexpr int kTmemCols = kACols + 2 * NT <= 256 ? 256 : 512;
+  static_assert(kACols + 2 * NT <= 512, "tensor memory");
   static_assert(kDyn <= 232448, "shared memory");
 };
 
@@ -535,7 +539,7 @@ __device__ __forceinline__ void rec_abort(const RecArgs& a, uint8_t* sm_abort, i
 }
 
 template <int H, int NCW, bool BF16, bool VARLEN, int NT>
-__global__ void __launch_bounds__(RecSmem<H, NCW, NT>::kThreads, 1) rec_kernel(const RecArgs a) {
+__global__ void __launch_bounds__(RecSmem<H, NCW, NT>::kThreads, NT <= 32 ? 2 : 1) rec_kernel(const RecArgs a) {
   using S = RecSmem<H, NCW, NT>;
   PLSTM_TCL_TILE_CONSTANTS(NT);
   constexpr int C = S::C;
@@ -560,7 +564,7 @@ __global__ void __launch_bounds__(RecSmem<H, NCW, NT>::kThreads, 1) rec_kernel(c
   if (tid == 0) {
     for (int b = 0; b < 2; ++b) {
       ptx::mbar_init(bar_rec + 8 * b, 1);
-      ptx::mbar_init(bar_mma + 8 * b, 1);
+      ptx::mbar_init(bar_mma + 8 * b, 2);  // the control and the helper warp's commits
       ptx::mbar_init(bar_hready + 8 * b, S::kComputeWarps);
     }
     for (int s = 0; s < GS; ++s) ptx::mbar_init(bar_g + 8 * s, 1);
@@ -617,7 +621,13 @@ __global__ void __launch_bounds__(RecSmem<H, NCW, NT>::kThreads, 1) rec_kernel(c
   ptx::cluster_sync();  // every CTA's barriers are initialised before any remote copy
 
   const int Tt = a.tile_len[tile];
-  const uint32_t dcol = tmem + (uint32_t)S::kD;
+  const uint32_t dcol = tmem + (uint32_t)S::kD, dcol1 = tmem + (uint32_t)S::kD1;
+  // The peer-piece MMAs of a step, K steps j in [0, H / 16) but this CTA's own two (units [32 r,
+  // 32 r + 32)), are issued by two warps in parallel (one thread issues an MMA every ~45-100
+  // cycles): index i < kHalfO by the control warp into D, the rest by the helper warp into D1,
+  // which the compute warps add.  Each accumulator sums its K steps in a fixed order.
+  constexpr int kOthers = H / 16 - 2, kHalfO = kOthers / 2;
+  auto kstep = [&](int i) { return i < 2 * r ? i : i + 2; };
   auto gates_src = [&](int t) {
     return reinterpret_cast<const uint8_t*>(a.gates) + (((size_t)t * gridDim.x / C + tile) * C + r) * (size_t)kGBlock;
   };
@@ -638,14 +648,17 @@ __global__ void __launch_bounds__(RecSmem<H, NCW, NT>::kThreads, 1) rec_kernel(c
       }
       __syncwarp();
     };
-    auto issue_others = [&](int t, bool init) {
-      // every K step but this CTA's own two (units [32 r, 32 r + 32))
-      bool first = init;
-      if (2 * r > 0) {
-        issue(t, 0, 2 * r, first);
-        first = false;
+    auto issue_others = [&](int t) {  // the control warp's half of the peer-piece K steps, into D
+      const int b = t & 1;
+      if (ptx::elect_one()) {
+        ptx::tc_fence_after();
+        for (int i = 0; i < kHalfO; ++i) {
+          const int j = kstep(i);
+          const uint64_t dB = ptx::desc_k_none(bbuf(b) + (uint32_t)(2 * j * kKG), kKG, 128);
+          ptx::mma_f16_ts(dcol, tmem + (uint32_t)(8 * j), dB, idesc, 1u);
+        }
       }
-      if (2 * r + 2 < H / 16) issue(t, 2 * r + 2, H / 16, first);
+      __syncwarp();
     };
     auto commit = [&](int t) {
       if (ptx::elect_one()) ptx::mma_commit(bar_mma + 8 * (t & 1));
@@ -672,7 +685,7 @@ __global__ void __launch_bounds__(RecSmem<H, NCW, NT>::kThreads, 1) rec_kernel(c
       __syncwarp();
       // Step 0 runs on h0, already complete in buffer 0.
       issue(0, 2 * r, 2 * r + 2, true);
-      issue_others(0, false);
+      issue_others(0);
       commit(0);
     }
     for (int t = 0; ok && t < Tt; ++t) {
@@ -685,7 +698,7 @@ __global__ void __launch_bounds__(RecSmem<H, NCW, NT>::kThreads, 1) rec_kernel(c
         if (lane == 0) trace_mark(a, tile, r, t, 0);
         if (t + 2 < Tt && ptx::elect_one()) ptx::mbar_arrive_expect_tx(bar_rec + 8 * b, rec_bytes);
         __syncwarp();
-        issue_others(t, false);
+        issue_others(t);
         commit(t);
         if (lane == 0) trace_mark(a, tile, r, t, 1);
       }
@@ -700,6 +713,30 @@ __global__ void __launch_bounds__(RecSmem<H, NCW, NT>::kThreads, 1) rec_kernel(c
         issue(t + 1, 2 * r, 2 * r + 2, true);
         if (lane == 0) trace_mark(a, tile, r, t, 3);
       }
+    }
+  } else if (warp == S::kComputeWarps + 1) {
+    // ============================ helper warp ==============================
+    // The second half of each step's peer-piece MMAs into D1: once the peers' pieces have landed
+    // and the compute warps have loaded D1 of the previous step.
+    constexpr uint32_t idesc = ptx::idesc_f16(128, kNT, BF16);
+    for (int t = 0; t < Tt; ++t) {
+      const int b = t & 1;
+      if (t >= 1 && (!warp_wait(bar_rec + 8 * b, ((t - 1) >> 1) & 1, abort_flag, a.timeout_ns) ||
+                     !warp_wait(bar_hready + 8 * ((t - 1) & 1), ((t - 1) >> 1) & 1, abort_flag, a.timeout_ns))) {
+        if (ptx::elect_one()) rec_abort(a, sm + S::kAbort, C, t);
+        __syncwarp();
+        break;
+      }
+      if (ptx::elect_one()) {
+        ptx::tc_fence_after();
+        for (int i = kHalfO; i < kOthers; ++i) {
+          const int j = kstep(i);
+          const uint64_t dB = ptx::desc_k_none(bbuf(b) + (uint32_t)(2 * j * kKG), kKG, 128);
+          ptx::mma_f16_ts(dcol1, tmem + (uint32_t)(8 * j), dB, idesc, i > kHalfO ? 1u : 0u);
+        }
+        ptx::mma_commit(bar_mma + 8 * b);
+      }
+      __syncwarp();
     }
   } else {
     // ============================ compute warps ============================
@@ -754,6 +791,28 @@ __global__ void __launch_bounds__(RecSmem<H, NCW, NT>::kThreads, 1) rec_kernel(c
         }
       }
       ptx::tmem_wait_ld();
+      {  // + the helper warp's partial accumulator
+        uint32_t p1[4 * CPW], p2[4 * CPW];
+#pragma unroll
+        for (int i = 0; i < CPW / 4; ++i) {
+          ptx::tmem_ld_16x256b_x4(dcol1 + lo + (uint32_t)(n0 + 32 * i), *reinterpret_cast<uint32_t(*)[16]>(&p1[16 * i]));
+          ptx::tmem_ld_16x256b_x4(dcol1 + hi + (uint32_t)(n0 + 32 * i), *reinterpret_cast<uint32_t(*)[16]>(&p2[16 * i]));
+        }
+        if (CPW % 4 != 0) {
+          constexpr int c0 = CPW / 4 * 4;
+#pragma unroll
+          for (int c = c0; c < CPW; ++c) {
+            ptx::tmem_ld_16x256b_x1(dcol1 + lo + (uint32_t)(n0 + 8 * c), *reinterpret_cast<uint32_t(*)[4]>(&p1[4 * c]));
+            ptx::tmem_ld_16x256b_x1(dcol1 + hi + (uint32_t)(n0 + 8 * c), *reinterpret_cast<uint32_t(*)[4]>(&p2[4 * c]));
+          }
+        }
+        ptx::tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 4 * CPW; ++i) {
+          rif[i] = __float_as_uint(__uint_as_float(rif[i]) + __uint_as_float(p1[i]));
+          rgo[i] = __float_as_uint(__uint_as_float(rgo[i]) + __uint_as_float(p2[i]));
+        }
+      }
       ptx::tc_fence_before();
       if (warp == 0 && lane == 0) trace_mark(a, tile, r, t, 5);
       // Projected input + bias of the four gates of this thread's cells.
@@ -1106,7 +1165,7 @@ int rec_smem(int H, int nt) {
   }
 }
 bool rec_hidden_ok(int H) { return H >= 64 && H <= 512 && H % 64 == 0; }
-int rec_threads(int H, int nt) { return ((nt != 64 ? 8 : rec_warps()) + 1) * 32; }
+int rec_threads(int H, int nt) { return ((nt != 64 ? 8 : rec_warps()) + 2) * 32; }
 
 cudaError_t config_rec(void* k, int H, int nt) {
   if (k == nullptr) return cudaErrorInvalidDeviceFunction;
@@ -1153,7 +1212,7 @@ int rec_max_clusters(int device, int H, int nt) {
 }
 
 // Recurrence CTAs (of both length variants of `dtype`) that one SM holds at once, at most two, by
-// whole-SM registers, shared memory and tensor memory (H / 2 + NT columns, 256 or 512 allocated);
+// whole-SM registers, shared memory and tensor memory (H / 2 + 2 NT columns, 256 or 512 allocated);
 // cached.  The cluster occupancy query counts one CTA per SM (15 clusters of 8 on a B200), but
 // measured: 32 clusters of 8 CTAs of 32-row H = 256 tiles (f16 and bf16) ran in one wave, two CTAs
 // on most SMs, 2.82 ms per layer at B = 1024 against 2.65 ms at B = 512.
@@ -1173,7 +1232,7 @@ int rec_ctas_per_sm(int device, int H, int nt, int dtype) {
   int& slot = cache[device][H / 64 - 1][nt == 80 ? 1 : nt == 32 ? 2 : nt == 48 ? 3 : 0][bf16 ? 1 : 0];
   if (slot >= 0) return slot;
   int smem_sm = 0;
-  int n = (H / 2 + nt <= 256) ? 2 : 1;
+  int n = (H / 2 + 2 * nt <= 256) ? 2 : 1;
   if (cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, device) != cudaSuccess) n = 1;
   else n = std::min(n, smem_sm / (rec_smem(H, nt) + 1024));
   for (bool varlen : {false, true}) {

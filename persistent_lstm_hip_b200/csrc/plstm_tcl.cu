@@ -497,14 +497,21 @@ struct RecSmem {
   static constexpr int kACols = H / 2;  // W_hh slice: 128 lanes x H 16-bit values
   static constexpr int kD = kACols;     // gate accumulator [128 x NT] (single buffer)
   static constexpr int kD1 = kD + NT;   // the helper warp's partial accumulator [128 x NT]
-  static constexpr int kTmemCols = kACols + 2 * NT <= 256 ? 256 : 512;
-  static_assert(kACols + 2 * NT <= 512, "tensor memory");
+  static constexpr int kX = kD1 + NT;   // layer 0's W_ih slice (fused input projection, kx / 2 <= 64 columns)
+  static constexpr int kTmemCols = kX + kMaxXK / 2 <= 256 ? 256 : 512;
+  static_assert(kX + kMaxXK / 2 <= 512, "tensor memory");
   static_assert(kDyn <= 232448, "shared memory");
 };
 
 struct RecArgs {
   const uint8_t* whh;      // this layer's W_hh images [C][128][H]
-  const uint16_t* gates;   // [T][tiles][C][128][kGRow]
+  const uint16_t* gates;   // [T][tiles][C][128][kGRow] (unless xp is set)
+  // Layer 0 with its input projection fused in (no gate blocks): packed x tiles [tiles][T]
+  // (NT rows x kx, core matrices), the layer's W_ih image [4H][kx] and f32 bias [4H]; else null.
+  const uint8_t* xp;
+  const uint16_t* wih0;
+  const float* bias0;
+  int kx;
   const int32_t* perm;     // [tiles * kNT]
   const int32_t* lengths;  // [B] or null
   const int32_t* tile_len; // [tiles]
@@ -613,6 +620,16 @@ __global__ void __launch_bounds__(RecSmem<H, NCW, NT>::kThreads, NT <= 32 ? 2 : 
       }
       ptx::tmem_st_32x32b_x32(tmem + lane_off + (uint32_t)c, v);
     }
+    if (a.xp != nullptr) {  // layer 0's W_ih slice [128 x kx] -> columns [kX, kX + kx / 2)
+      const uint32_t* wsrc = reinterpret_cast<const uint32_t*>(a.wih0 + ((size_t)r * kRows + row) * a.kx);
+#pragma unroll 1
+      for (int c = 0; c < a.kx / 2; c += 8) {
+        uint32_t v[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = wsrc[c + i];
+        ptx::tmem_st_32x32b_x8(tmem + lane_off + (uint32_t)(S::kX + c), v);
+      }
+    }
     ptx::tmem_wait_st();
   }
   ptx::tc_fence_before();
@@ -628,7 +645,12 @@ __global__ void __launch_bounds__(RecSmem<H, NCW, NT>::kThreads, NT <= 32 ? 2 : 
   // which the compute warps add.  Each accumulator sums its K steps in a fixed order.
   constexpr int kOthers = H / 16 - 2, kHalfO = kOthers / 2;
   auto kstep = [&](int i) { return i < 2 * r ? i : i + 2; };
-  auto gates_src = [&](int t) {
+  // Each step's input block, prefetched GS steps ahead into the gate ring: the projected gate block,
+  // or with the fused layer-0 projection the step's x tile (the input MMAs' B operand).
+  const bool fused_x = a.xp != nullptr;
+  const uint32_t blk_bytes = fused_x ? (uint32_t)(kNT * a.kx * 2) : (uint32_t)kGBlock;
+  auto gates_src = [&](int t) -> const uint8_t* {
+    if (fused_x) return a.xp + ((size_t)tile * a.T + t) * (size_t)blk_bytes;
     return reinterpret_cast<const uint8_t*>(a.gates) + (((size_t)t * gridDim.x / C + tile) * C + r) * (size_t)kGBlock;
   };
 
@@ -667,10 +689,26 @@ __global__ void __launch_bounds__(RecSmem<H, NCW, NT>::kThreads, NT <= 32 ? 2 : 
     auto load_gates = [&](int t) {
       if (ptx::elect_one()) {
         const int s = t % GS;
-        ptx::mbar_arrive_expect_tx(bar_g + 8 * s, kGBlock);
-        ptx::bulk_g2s(gslot(s), gates_src(t), kGBlock, bar_g + 8 * s);
+        ptx::mbar_arrive_expect_tx(bar_g + 8 * s, blk_bytes);
+        ptx::bulk_g2s(gslot(s), gates_src(t), blk_bytes, bar_g + 8 * s);
       }
       __syncwarp();
+    };
+    // Fused layer 0: D = W_ih . x_t (kx / 16 MMAs, initialising D) once the x tile has landed; the
+    // own-piece MMAs then accumulate.
+    auto issue_x = [&](int t) -> bool {
+      if (!fused_x) return true;
+      const int s = t % GS;
+      if (!warp_wait(bar_g + 8 * s, (t / GS) & 1, abort_flag, a.timeout_ns)) return false;
+      if (ptx::elect_one()) {
+        ptx::tc_fence_after();
+        for (int i = 0; i < a.kx / 16; ++i)
+          ptx::mma_f16_ts(dcol, tmem + (uint32_t)(S::kX + 8 * i),
+                          ptx::desc_k_none(gslot(s) + (uint32_t)(256 * i), 128, (uint32_t)(a.kx * 16)), idesc,
+                          i != 0 ? 1u : 0u);
+      }
+      __syncwarp();
+      return true;
     };
     bool ok = true;
     auto fail = [&](int t) {
@@ -684,7 +722,8 @@ __global__ void __launch_bounds__(RecSmem<H, NCW, NT>::kThreads, NT <= 32 ? 2 : 
         for (int t = 1; t <= 2 && t < Tt; ++t) ptx::mbar_arrive_expect_tx(bar_rec + 8 * (t & 1), rec_bytes);
       __syncwarp();
       // Step 0 runs on h0, already complete in buffer 0.
-      issue(0, 2 * r, 2 * r + 2, true);
+      if (!issue_x(0)) fail(0);
+      issue(0, 2 * r, 2 * r + 2, !fused_x);
       issue_others(0);
       commit(0);
     }
@@ -710,7 +749,11 @@ __global__ void __launch_bounds__(RecSmem<H, NCW, NT>::kThreads, NT <= 32 ? 2 : 
       }
       if (lane == 0) trace_mark(a, tile, r, t, 2);
       if (t + 1 < Tt) {
-        issue(t + 1, 2 * r, 2 * r + 2, true);
+        if (!issue_x(t + 1)) {
+          fail(t + 1);
+          break;
+        }
+        issue(t + 1, 2 * r, 2 * r + 2, !fused_x);
         if (lane == 0) trace_mark(a, tile, r, t, 3);
       }
     }
@@ -745,6 +788,11 @@ __global__ void __launch_bounds__(RecSmem<H, NCW, NT>::kThreads, NT <= 32 ? 2 : 
     const int n0 = 8 * CPW * cg;
     const int ul = 8 * q + j8;  // unit within this CTA's 32
     const int u = kU * r + ul;  // unit within the layer
+    float bias_x[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // fused layer 0: f32 bias of this thread's four gate rows
+    if (fused_x) {
+#pragma unroll
+      for (int g = 0; g < 4; ++g) bias_x[g] = a.bias0[r * kRows + 32 * q + 8 * g + j8];
+    }
     float c_st[CPW][2];
     uint16_t h_st[CPW][2];
     int len_c[CPW][2], bidx[CPW][2];
@@ -768,7 +816,7 @@ __global__ void __launch_bounds__(RecSmem<H, NCW, NT>::kThreads, NT <= 32 ? 2 : 
     for (int t = 0; t < Tt; ++t) {
       const int b = t & 1, gs = t % GS;
       if (*abort_flag) break;
-      if (!wait_bar(bar_g + 8 * gs, (t / GS) & 1, abort_flag, a.timeout_ns) ||
+      if ((!fused_x && !wait_bar(bar_g + 8 * gs, (t / GS) & 1, abort_flag, a.timeout_ns)) ||
           !wait_bar(bar_mma + 8 * b, (t >> 1) & 1, abort_flag, a.timeout_ns)) {
         if (lane == 0) rec_abort(a, sm + S::kAbort, C, t);
         break;
@@ -815,7 +863,8 @@ __global__ void __launch_bounds__(RecSmem<H, NCW, NT>::kThreads, NT <= 32 ? 2 : 
       }
       ptx::tc_fence_before();
       if (warp == 0 && lane == 0) trace_mark(a, tile, r, t, 5);
-      // Projected input + bias of the four gates of this thread's cells.
+      // Projected input + bias of the four gates of this thread's cells (with the fused layer-0
+      // projection the accumulator holds the input part, and the f32 bias is added here).
       const uint8_t* gsl = sm + S::kG + gs * kGBlock;
       float pre[4][CPW][2];
 #pragma unroll
@@ -823,7 +872,8 @@ __global__ void __launch_bounds__(RecSmem<H, NCW, NT>::kThreads, NT <= 32 ? 2 : 
         const uint8_t* grow = gsl + (size_t)(32 * q + 8 * g + j8) * kGRow * 2;
 #pragma unroll
         for (int jc = 0; jc < CPW; ++jc) {
-          const float2 gv = from_bits2<BF16>(*reinterpret_cast<const uint32_t*>(grow + (n0 + 8 * jc + cpair) * 2));
+          const float2 gv = fused_x ? make_float2(bias_x[g], bias_x[g])
+                                    : from_bits2<BF16>(*reinterpret_cast<const uint32_t*>(grow + (n0 + 8 * jc + cpair) * 2));
           const uint32_t* acc = g < 2 ? rif : rgo;
           const int base = 4 * jc + (g & 1) * 2;
           pre[g][jc][0] = __uint_as_float(acc[base]) + gv.x;
@@ -871,8 +921,8 @@ __global__ void __launch_bounds__(RecSmem<H, NCW, NT>::kThreads, NT <= 32 ? 2 : 
                           ptx::mapa(bar_rec + 8 * (b ^ 1), (uint32_t)pr));
           }
           if (t + GS < Tt) {
-            ptx::mbar_arrive_expect_tx(bar_g + 8 * gs, kGBlock);
-            ptx::bulk_g2s(gslot(gs), gates_src(t + GS), kGBlock, bar_g + 8 * gs);
+            ptx::mbar_arrive_expect_tx(bar_g + 8 * gs, blk_bytes);
+            ptx::bulk_g2s(gslot(gs), gates_src(t + GS), blk_bytes, bar_g + 8 * gs);
           }
           trace_mark(a, tile, r, t, 7);
         }
@@ -1232,7 +1282,7 @@ int rec_ctas_per_sm(int device, int H, int nt, int dtype) {
   int& slot = cache[device][H / 64 - 1][nt == 80 ? 1 : nt == 32 ? 2 : nt == 48 ? 3 : 0][bf16 ? 1 : 0];
   if (slot >= 0) return slot;
   int smem_sm = 0;
-  int n = (H / 2 + 2 * nt <= 256) ? 2 : 1;
+  int n = (H / 2 + 2 * nt + kMaxXK / 2 <= 256) ? 2 : 1;
   if (cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, device) != cudaSuccess) n = 1;
   else n = std::min(n, smem_sm / (rec_smem(H, nt) + 1024));
   for (bool varlen : {false, true}) {
@@ -1574,6 +1624,10 @@ int32_t tcl_forward(const Problem& p, const void* packed, const void* x, const i
   void* rk = pick_rec(H, bf16, varlen, nt);
   PLSTM_TRY_CUDA(config_rec(rk, H, nt));
   const bool seq_out = !p.has_linear() || p.out_seq();
+  // Layer 0's input projection runs inside its recurrence for tile heights of 64 / 80 rows (one CTA per
+  // SM; config 4: 23.8 -> 23.2 ms); with 32-row tiles, two CTAs sharing an SM, the separate projection
+  // measured as fast (config 3: 10.12 against 10.16 ms).  PLSTM_TCL_PROJ0 forces the separate one.
+  const bool fuse_x0 = nt >= 64 && std::getenv("PLSTM_TCL_PROJ0") == nullptr;
   for (int l = 0; l < L; ++l) {
     GemmArgs ga = {};
     ga.xp = wsb + w.xp;
@@ -1585,13 +1639,13 @@ int32_t tcl_forward(const Problem& p, const void* packed, const void* x, const i
     ga.T = p.T;
     ga.H = H;
     ga.tiles = tiles;
-    int32_t rc;
-    if (l == 0)
+    int32_t rc = PLSTM_OK;
+    if (l == 0 && !fuse_x0)
       rc = nt == 80   ? launch_proj_x<80>(ga, kx_of(p.I), bf16, sms, s)
            : nt == 32 ? launch_proj_x<32>(ga, kx_of(p.I), bf16, sms, s)
            : nt == 48 ? launch_proj_x<48>(ga, kx_of(p.I), bf16, sms, s)
                       : launch_proj_x<64>(ga, kx_of(p.I), bf16, sms, s);
-    else
+    else if (l > 0)
       rc = nt == 80   ? launch_proj_h80(ga, bf16, sms, s)
            : nt == 32 ? launch_proj_hs<32>(ga, bf16, sms, s)
            : nt == 48 ? launch_proj_hs<48>(ga, bf16, sms, s)
@@ -1601,6 +1655,12 @@ int32_t tcl_forward(const Problem& p, const void* packed, const void* x, const i
     RecArgs ra = {};
     ra.whh = pk + off_whh(l, H);
     ra.gates = reinterpret_cast<const uint16_t*>(wsb + w.gates);
+    if (l == 0 && fuse_x0) {
+      ra.xp = wsb + w.xp;
+      ra.wih0 = reinterpret_cast<const uint16_t*>(pk + off_wih(0, H, L));
+      ra.bias0 = reinterpret_cast<const float*>(pk + off_bias(H, L));
+      ra.kx = kx_of(p.I);
+    }
     ra.perm = perm;
     ra.lengths = lengths;
     ra.tile_len = tile_len;

@@ -16,13 +16,16 @@
 //      The W_ih slice of the CTA's 128 gate rows stays resident in shared memory;
 //      the epilogue writes one 128-row x 64-column block per (step, batch tile,
 //      recurrent CTA), already in the order the recurrence reads it.
-//   2. rec_kernel: one cluster of C = H / 32 CTAs per 64-row batch tile; CTA r owns
+//   2. rec_kernel: one cluster of C = H / 32 CTAs per batch tile (32-80 rows); CTA r owns
 //      hidden units [32 r, 32 r + 32), i.e. 128 gate rows = one M = 128 MMA tile.
 //      Its W_hh slice [128 x H] stays resident in tensor memory (H / 2 columns) for
-//      the whole sequence.  Per step: D[128 x 64] = W_hh . h_{t-1}^T as H / 16
+//      the whole sequence.  Per step: D[128 x NT] = W_hh . h_{t-1}^T as H / 16
 //      tcgen05.mma (A from TMEM, B = h_{t-1} from shared memory), the MMAs over the
 //      CTA's own 32 units issued as soon as it has written them, the rest once the
-//      other C - 1 pieces have landed; the compute warps add the projected gate
+//      other C - 1 pieces have landed, split between the control warp and a helper
+//      warp that accumulates into a second TMEM accumulator (one thread issues an MMA
+//      only every ~45-100 cycles); with 64- / 80-row tiles layer 0's input projection
+//      runs here too (W_ih slice in TMEM, x tiles streamed in); the compute warps add the projected gate
 //      block (prefetched three steps ahead by bulk copy), apply the gate math in
 //      registers (c in f32), write their h piece (and store it to the layer's h
 //      sequence in global memory, the next layer's projection input); the last

@@ -1398,12 +1398,18 @@ int32_t launch_proj_h80(const GemmArgs& ga, bool bf16, int sms, cudaStream_t s) 
 
 template <int KP, bool BF16, bool XIN, int NT>
 int32_t launch_proj(const GemmArgs& ga, int sms, cudaStream_t s) {
+  using G = GemmSmem<KP, XIN, NT>;
   auto k = proj_kernel<KP, BF16, XIN, NT>;
-  PLSTM_TRY_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmSmem<KP, XIN, NT>::kDyn));
+  // Two CTAs per SM where tensor memory holds both (small jobs: their per-job latency chains
+  // overlap); the shared-memory request then keeps a third off the SM (its allocation of tensor
+  // memory would wait for one of the two to finish).
+  const int per_sm = (G::kTmemCols <= 256 && getenv("PLSTM_TCL_PROJ1") == nullptr) ? 2 : 1;
+  const int smem = per_sm == 2 ? std::max(G::kDyn, 80 * 1024) : G::kDyn;
+  PLSTM_TRY_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
   const int C = ctas_of(ga.H);
   const long long jobs = (long long)ga.T * ga.tiles * C;
-  const int grid = (int)std::max<long long>(C, std::min<long long>((sms / C) * C, jobs));
-  k<<<grid, kGemmThreads, GemmSmem<KP, XIN, NT>::kDyn, s>>>(ga);
+  const int grid = (int)std::max<long long>(C, std::min<long long>((per_sm * sms / C) * C, jobs));
+  k<<<grid, kGemmThreads, smem, s>>>(ga);
   PLSTM_TRY_CUDA(cudaGetLastError());
   note_launches(1);
   return PLSTM_OK;
